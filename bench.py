@@ -1,0 +1,262 @@
+#!/usr/bin/env python
+"""GPT-2 small DDP training throughput with the predictive-residual hook.
+
+    python bench.py [--gpus N --steps K --warmup W]            # this framework
+    python bench.py --impl reference ...                       # reference hook
+    torchrun --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N ...
+
+Workload: GPT-2 small (12 layers, d 768, 12 heads, FFN 3072, vocab 50257),
+seq 1024, micro-batch 8 per GPU, fp32 master weights with bf16 autocast,
+AdamW lr 6e-4, DDP buckets of 25 MB, random-init N(0, 0.02) weights,
+tokens uniform over the vocabulary from a seed (synthetic data).
+
+Timing: W untimed warm-up steps, then exactly K steps between a barrier +
+synchronize on both sides, CUDA events on the launching stream, max over
+ranks.  A step touches ~2 GB of weights, gradients and optimizer state, far
+more than the 126 MB L2, so no flush is needed between steps.  The
+end-to-end figure runs the same K steps through ``DDPTrainer.step_host``:
+H2D copy of the step's tokens from pinned memory, the step, and a D2H read
+of the loss, timed on the host between synchronized points (max over ranks).
+
+Rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import contextlib
+import json
+import os
+import sys
+
+import torch
+import torch.distributed as dist
+
+METRIC = "GPT-2 DDP tokens/s + compressed-allreduce GB/s at 1–8 B200; compression ratio"
+ROOT = os.path.dirname(os.path.abspath(__file__))
+
+
+def parse():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--hook", choices=["fused", "nccl", "compat"], default="fused")
+    ap.add_argument("--mode", choices=["int4", "int8", "topk"], default="int4")
+    ap.add_argument("--topk", type=float, default=0.05, help="keep fraction for --mode topk")
+    ap.add_argument("--variant", default="auto", choices=["auto", "oneshot", "twoshot"])
+    ap.add_argument("--model", choices=["gpt2", "llama"], default="gpt2")
+    ap.add_argument("--micro-batch", type=int, default=None)
+    ap.add_argument("--seq", type=int, default=None)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-clocks", action="store_true")
+    ap.add_argument("--max-ctas", type=int, default=0)
+    return ap.parse_args()
+
+
+def visible_gpu_indices(n: int) -> list[int] | None:
+    v = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if v:
+        parts = [p.strip() for p in v.split(",") if p.strip()]
+        if all(p.isdigit() for p in parts):
+            return [int(p) for p in parts[:n]]
+        return None
+    return list(range(n))
+
+
+def make_batches(vocab: int, mb: int, seq: int, count: int, seed: int, device) -> list[tuple]:
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    out = []
+    for _ in range(count):
+        t = torch.randint(0, vocab, (mb, seq + 1), generator=g, device=device)
+        out.append((t[:, :-1].contiguous(), t[:, 1:].contiguous()))
+    return out
+
+
+class _HFLoss(torch.nn.Module):
+    """forward(x, y) -> loss adapter around a transformers causal LM."""
+
+    def __init__(self, m):
+        super().__init__()
+        self.m = m
+
+    def forward(self, x, y):
+        logits = self.m(input_ids=x).logits
+        return torch.nn.functional.cross_entropy(logits.view(-1, logits.size(-1)).float(), y.reshape(-1))
+
+
+def build_reference(args, device):
+    """Reference arm: unmodified nangila_ddp hook from baseline/_ref on a stock
+    transformers GPT-2 small (the reference ships no GPT-2 model)."""
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "nangila_ddp")):
+        return None, "baseline/_ref/nangila_ddp is not installed"
+    sys.path.insert(0, ref)
+    from nangila_ddp import register_nangila_hook as ref_register  # noqa: E402
+    from transformers import GPT2Config, GPT2LMHeadModel  # noqa: E402
+
+    cfg = GPT2Config(vocab_size=50257, n_positions=1024, n_embd=768, n_layer=12, n_head=12, n_inner=3072,
+                     resid_pdrop=0.0, embd_pdrop=0.0, attn_pdrop=0.0, initializer_range=0.02)
+    cfg._attn_implementation = "sdpa"
+    model = _HFLoss(GPT2LMHeadModel(cfg)).to(device)
+    ddp = torch.nn.parallel.DistributedDataParallel(model, device_ids=[device.index], bucket_cap_mb=25)
+    # Same call the reference's trainer makes (train_nano.py:133-143), with
+    # the per-bucket EMA predictor enabled.
+    ref_register(ddp, beta=0.9, bits=4, stochastic=True, use_fp16_transport=False, use_momentum=True)
+    opt = torch.optim.AdamW(ddp.parameters(), lr=6e-4)
+
+    def step(x, y):
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            loss = ddp(x, y)
+        opt.zero_grad(set_to_none=True)
+        loss.backward()
+        opt.step()
+        return loss.detach()
+
+    return step, None
+
+
+def main():
+    args = parse()
+    from mini_nangila_b200.train import DDPTrainer, init_distributed
+    from mini_nangila_b200.utils import ClockSampler, barrier_sync, max_over_ranks
+
+    rank, world, local = init_distributed("nccl", timeout_s=300)
+    device = torch.device("cuda", local)
+    torch.manual_seed(1234)
+    torch.backends.cuda.matmul.allow_tf32 = True
+    if args.model == "gpt2":
+        from mini_nangila_b200.models import GPT2, GPT2Config
+
+        mcfg = GPT2Config.small()
+        vocab, mb, seq = mcfg.vocab_size, args.micro_batch or 8, args.seq or 1024
+        model_name = "gpt2-small-124M"
+    else:
+        from mini_nangila_b200.models import Llama, LlamaConfig
+
+        mcfg = LlamaConfig.b1_1()
+        vocab, mb, seq = mcfg.vocab_size, args.micro_batch or 4, args.seq or 2048
+        model_name = "llama-1.1B"
+
+    quiet = contextlib.redirect_stdout(open(os.devnull, "w")) if args.impl == "reference" else contextlib.nullcontext()
+    trainer = None
+    if args.impl == "reference":
+        if args.model != "gpt2":
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "the reference arm is defined for GPT-2 small"}))
+            dist.destroy_process_group()
+            return
+        step_fn, why = build_reference(args, device)
+        if step_fn is None:
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": why}))
+            dist.destroy_process_group()
+            return
+        hook_name = "reference-nangila_ddp-int4-momentum"
+    else:
+        model = GPT2(mcfg) if args.model == "gpt2" else Llama(mcfg)
+        if args.model == "llama":
+            model = model.to(torch.bfloat16)
+        hk = None
+        if args.hook in ("fused", "compat"):
+            hk = dict(beta=0.9, bits=8 if args.mode == "int8" else 4, stochastic=True, use_momentum=True,
+                      topk_percent=args.topk if args.mode == "topk" else 0.0, seed=12345,
+                      error_feedback=True, variant=args.variant, max_ctas=args.max_ctas)
+        trainer = DDPTrainer(model, lr=6e-4, hook=args.hook, hook_kwargs=hk, bucket_cap_mb=25.0,
+                             autocast_dtype=torch.bfloat16 if args.model == "gpt2" else None, device=device)
+        step_fn = trainer.step
+        hook_name = {"fused": f"fused-{args.mode}", "nccl": "nccl-fp32-allreduce", "compat": f"compat-{args.mode}"}[args.hook]
+
+    batches = make_batches(vocab, mb, seq, 4, 1000 + rank, device)
+    with quiet:
+        for i in range(args.warmup):
+            step_fn(*batches[i % len(batches)])
+        barrier_sync(device)
+        sampler = ClockSampler(visible_gpu_indices(world)).start() if (rank == 0 and not args.no_clocks) else None
+        launches0 = trainer.kernel_launches() if trainer else 0
+        barrier_sync(device)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for i in range(args.steps):
+            step_fn(*batches[i % len(batches)])
+        e.record()
+        barrier_sync(device)
+        ms_local = s.elapsed_time(e)
+        launches = (trainer.kernel_launches() - launches0) if trainer else 0
+        clocks = sampler.stop() if sampler else None
+        ms = max_over_ranks(ms_local, device)
+        e2e = None
+        if not args.no_e2e:
+            host_batches = [(x.cpu().pin_memory(), y.cpu().pin_memory()) for x, y in batches]
+            barrier_sync(device)
+            import time
+
+            t0 = time.perf_counter()
+            for i in range(args.steps):
+                x, y = host_batches[i % len(host_batches)]
+                if trainer is not None:
+                    trainer.step_host(x, y)
+                else:
+                    float(step_fn(x.to(device, non_blocking=True), y.to(device, non_blocking=True)).item())
+            barrier_sync(device)
+            e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1000.0, device)
+            xb, yb = host_batches[0]
+            e2e = {
+                "value": world * mb * seq * args.steps / (e2e_ms / 1000.0),
+                "unit": "tokens/s",
+                "ms_per_step": e2e_ms / args.steps,
+                "h2d_bytes_per_step": int(xb.numel() * xb.element_size() + yb.numel() * yb.element_size()),
+                "d2h_bytes_per_step": 4,
+            }
+    hs = trainer.hook_state if trainer else None
+    if trainer is not None and hs is not None and getattr(hs, "comm", None) is not None:
+        hs.comm.check()
+    tokens = world * mb * seq * args.steps
+    value = tokens / (ms / 1000.0)
+    if rank == 0:
+        out = {
+            "metric": METRIC,
+            "value": value,
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms / args.steps,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (uniform random tokens from a seed; random-init weights)",
+            "config": {
+                "model": model_name,
+                "global_batch": world * mb,
+                "micro_batch": mb,
+                "seq_len": seq,
+                "parallelism": f"dp{world}",
+                "hook": hook_name,
+                "bucket_mb": 25,
+                "optimizer": "AdamW lr 6e-4",
+                "precision": "fp32 master weights, bf16 autocast" if args.model == "gpt2" else "bf16",
+                "l2": "no flush: each step reads/writes ~2 GB of weights, grads and optimizer state (> 126 MB L2)",
+            },
+            "gpu_launches": launches,
+        }
+        if args.impl == "reference":
+            out["impl"] = "reference"
+        if hs is not None and hs.raw_bytes:
+            out["compression_ratio"] = hs.compression_ratio()
+            out["config"]["variant"] = hs.last_variant
+        if clocks is not None:
+            out["clocks"] = clocks
+        if e2e is not None:
+            out["e2e"] = e2e
+        print(json.dumps(out), flush=True)
+    if hs is not None and getattr(hs, "comm", None) is not None:
+        hs.comm.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

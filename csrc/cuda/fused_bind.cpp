@@ -1,0 +1,233 @@
+// Torch-facing side of the fused compressed all-reduce: tensor checks,
+// geometry, epoch bookkeeping and launches on the current CUDA stream.
+#include <torch/extension.h>
+
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include <cstring>
+
+#include "common/ngl_product.h"
+#include "fused.h"
+
+namespace {
+using namespace ngl::dev;
+
+int num_sms(int device) {
+  static int cached[64] = {0};
+  if (device >= 0 && device < 64 && cached[device]) return cached[device];
+  int v = 0;
+  cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device);
+  if (device >= 0 && device < 64) cached[device] = v;
+  return v;
+}
+
+int64_t dense_payload_bytes(int64_t n, int bits) {
+  const int64_t nblk = (n + 255) / 256;
+  return ((nblk * 4 + 15) & ~int64_t(15)) + nblk * (bits == 4 ? 128 : 256);
+}
+int64_t topk_payload_bytes(int64_t n, int64_t k) { return ((n + 255) / 256) * ngl::topk_record_bytes((int)k); }
+
+void check_dev(const torch::Tensor& t, const char* what) {
+  TORCH_CHECK(t.is_cuda(), what, " must be a CUDA tensor");
+  TORCH_CHECK(t.is_contiguous(), what, " must be contiguous");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, what, " must be 16-byte aligned");
+}
+int dtype_code(torch::ScalarType t) {
+  if (t == torch::kFloat32) return kF32;
+  if (t == torch::kBFloat16) return kBF16;
+  TORCH_CHECK(false, "bucket dtype must be float32 or bfloat16");
+  return -1;
+}
+void check_launch(cudaError_t e, const char* what) {
+  TORCH_CHECK(e == cudaSuccess, what, " launch failed: ", cudaGetErrorString(e));
+}
+
+// Persistent state of one process's fused communicator: the symmetric-region
+// pointers of every rank, the geometry, the epoch counter, the status word.
+class FusedComm {
+ public:
+  FusedComm(int64_t world, int64_t rank, std::vector<int64_t> sym_ptrs, int64_t flags_off, int64_t rflags_off,
+            int64_t inbox_off, int64_t slot_bytes, int64_t result_off, int64_t result_bytes, int64_t max_chunks,
+            torch::Tensor status)
+      : world_(world), rank_(rank), status_(status) {
+    TORCH_CHECK(world >= 1 && world <= kMaxWorld, "world size must be in [1, 8]");
+    TORCH_CHECK(world == 1 || (int64_t)sym_ptrs.size() == world, "need one symmetric pointer per rank");
+    TORCH_CHECK(status.is_cuda() && status.scalar_type() == torch::kInt32 && status.numel() >= 4,
+                "status must be int32[>=4] on the device");
+    std::memset(&base_, 0, sizeof(base_));
+    for (int i = 0; i < (int)sym_ptrs.size() && i < kMaxWorld; ++i)
+      base_.sym[i] = reinterpret_cast<uint8_t*>(sym_ptrs[i]);
+    base_.world = (int)world;
+    base_.rank = (int)rank;
+    base_.flags_off = flags_off;
+    base_.rflags_off = rflags_off;
+    base_.inbox_off = inbox_off;
+    base_.slot_bytes = slot_bytes;
+    base_.result_off = result_off;
+    base_.result_bytes = result_bytes;
+    base_.max_chunks = (int)max_chunks;
+    base_.status = status.data_ptr<int>();
+  }
+
+  // Launch the fused kernel on the current stream; returns the epoch used.
+  // variant: 0 = auto-single (world 1), 1 = one-shot, 2 = two-shot.
+  int64_t run(torch::Tensor grad, c10::optional<torch::Tensor> pred, c10::optional<torch::Tensor> ef, int64_t mode,
+              int64_t k, int64_t variant, bool stochastic, int64_t seed, int64_t bucket, int64_t step, double beta,
+              bool first, int64_t max_ctas, int64_t timeout_ns, int64_t tag) {
+    check_dev(grad, "bucket");
+    const int64_t n = grad.numel();
+    FusedParams P = base_;
+    P.grad = grad.data_ptr();
+    P.pred = nullptr;
+    P.ef = nullptr;
+    if (pred.has_value()) {
+      check_dev(*pred, "predictor state");
+      TORCH_CHECK(pred->scalar_type() == torch::kFloat32 && pred->numel() == n, "predictor state must be fp32[n]");
+      P.pred = pred->data_ptr<float>();
+    }
+    if (ef.has_value()) {
+      check_dev(*ef, "error feedback");
+      TORCH_CHECK(ef->scalar_type() == torch::kFloat32 && ef->numel() == n, "error feedback must be fp32[n]");
+      P.ef = ef->data_ptr<float>();
+    }
+    TORCH_CHECK(mode >= 0 && mode <= 2, "mode must be 0 (int4), 1 (int8) or 2 (top-k)");
+    P.n = n;
+    P.nblk = (int)((n + ngl::kBlock - 1) / ngl::kBlock);
+    P.nchunks = (P.nblk + kChunkBlocks - 1) / kChunkBlocks;
+    P.k = (int)k;
+    P.rec_bytes = ngl::topk_record_bytes((int)k);
+    if (world_ == 1) variant = kVariantSingle;
+    TORCH_CHECK(variant != kVariantSingle || world_ == 1, "the single-rank kernel needs world size 1");
+    if (mode == kTopK) {
+      TORCH_CHECK(k >= 1 && k <= 256, "top-k per block must be in [1, 256]");
+      TORCH_CHECK(variant != kVariantTwoShot, "two-shot is implemented for dense modes only");
+    }
+    if (world_ > 1) {
+      TORCH_CHECK(P.nchunks <= base_.max_chunks, "bucket larger than the communicator capacity");
+      const int64_t need = mode == kTopK ? topk_payload_bytes(n, k) : dense_payload_bytes(n, mode == kInt4 ? 4 : 8);
+      TORCH_CHECK(need <= base_.slot_bytes, "payload (", need, " B) exceeds the inbox slot (", base_.slot_bytes, " B)");
+      if (variant == kVariantTwoShot)
+        TORCH_CHECK(dense_payload_bytes(n, 8) <= base_.result_bytes, "two-shot result exceeds its region");
+    }
+    epoch_ += 1;
+    P.epoch = (uint32_t)epoch_;
+    P.parity = (int)(epoch_ & 1);
+    P.tag = (uint32_t)tag;
+    P.q.seed = (uint64_t)seed;
+    P.q.step = (uint64_t)step;
+    P.q.bucket = (uint32_t)bucket;
+    P.q.rank = (uint32_t)rank_;
+    P.q.stochastic = stochastic ? 1 : 0;
+    P.q.use_ef = P.ef != nullptr;
+    P.q.use_pred = P.pred != nullptr;
+    P.f.inv_world = 1.0f / (float)world_;
+    P.f.beta = (float)beta;
+    P.f.omb = 1.0f - (float)beta;
+    P.f.first = first ? 1 : 0;
+    P.f.use_pred = P.pred != nullptr;
+    P.timeout_ns = (uint64_t)timeout_ns;
+    if (P.nblk == 0) return epoch_;
+    const c10::cuda::CUDAGuard guard(grad.device());
+    cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+    const int dev = grad.get_device();
+    int grid;
+    if (variant == kVariantSingle) {
+      grid = std::max(1, std::min((P.nblk + kWarps - 1) / kWarps, 4 * num_sms(dev)));
+    } else {
+      const int cap = (int)(max_ctas > 0 ? max_ctas : 2 * num_sms(dev));
+      grid = std::max(1, std::min(P.nchunks, cap));
+    }
+    check_launch(launch_fused(P, (int)mode, dtype_code(grad.scalar_type()), (int)variant, grid, stream), "fused");
+    return epoch_;
+  }
+
+  int64_t epoch() const { return epoch_; }
+  void set_epoch(int64_t e) { epoch_ = e; }
+
+ private:
+  int64_t world_, rank_;
+  torch::Tensor status_;
+  FusedParams base_;
+  int64_t epoch_ = 0;
+};
+
+// Encode one rank's payload on the device (same layout as an inbox slot).
+std::vector<torch::Tensor> product_encode_cuda(torch::Tensor g, c10::optional<torch::Tensor> pred,
+                                               c10::optional<torch::Tensor> ef, int64_t mode, int64_t k,
+                                               bool stochastic, int64_t seed, int64_t rank, int64_t bucket,
+                                               int64_t step) {
+  check_dev(g, "g");
+  const int64_t n = g.numel();
+  const int nblk = (int)((n + 255) / 256);
+  const int64_t bytes = mode == kTopK ? topk_payload_bytes(n, k) : dense_payload_bytes(n, mode == kInt4 ? 4 : 8);
+  auto out = torch::zeros({bytes}, g.options().dtype(torch::kUInt8));
+  torch::Tensor ef_out =
+      ef.has_value() ? torch::empty_like(*ef) : torch::empty({0}, g.options().dtype(torch::kFloat32));
+  QParams qp;
+  qp.seed = (uint64_t)seed;
+  qp.step = (uint64_t)step;
+  qp.bucket = (uint32_t)bucket;
+  qp.rank = (uint32_t)rank;
+  qp.stochastic = stochastic;
+  qp.use_ef = ef.has_value();
+  qp.use_pred = pred.has_value();
+  if (pred.has_value()) check_dev(*pred, "pred");
+  if (ef.has_value()) check_dev(*ef, "ef");
+  if (nblk == 0) return {out, ef_out};
+  const c10::cuda::CUDAGuard guard(g.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  const int grid = std::min((nblk + kWarps - 1) / kWarps, 4 * num_sms(g.get_device()));
+  check_launch(launch_encode(g.data_ptr(), pred.has_value() ? pred->data_ptr<float>() : nullptr,
+                             ef.has_value() ? ef->data_ptr<float>() : nullptr,
+                             ef.has_value() ? ef_out.data_ptr<float>() : nullptr, n, (int)k, qp,
+                             out.data_ptr<uint8_t>(), (int)mode, dtype_code(g.scalar_type()), grid, stream),
+               "encode");
+  return {out, ef_out};
+}
+
+// Rank-ordered reduction of W payloads on one device; updates `pred` (EMA)
+// in place when given and returns the averaged bucket.
+torch::Tensor product_reduce_cuda(std::vector<torch::Tensor> payloads, int64_t n, int64_t mode, int64_t k,
+                                  c10::optional<torch::Tensor> pred, double beta, bool first, double inv_world,
+                                  torch::ScalarType out_dtype) {
+  TORCH_CHECK(!payloads.empty() && (int)payloads.size() <= kMaxWorld, "1..8 payloads");
+  ReduceSrcs s;
+  std::memset(&s, 0, sizeof(s));
+  for (size_t i = 0; i < payloads.size(); ++i) {
+    check_dev(payloads[i], "payload");
+    s.p[i] = payloads[i].data_ptr<uint8_t>();
+  }
+  auto out = torch::empty({n}, payloads[0].options().dtype(out_dtype));
+  const int nblk = (int)((n + 255) / 256);
+  if (nblk == 0) return out;
+  FParams fp;
+  fp.inv_world = (float)inv_world;
+  fp.beta = (float)beta;
+  fp.omb = 1.0f - (float)beta;
+  fp.first = first;
+  fp.use_pred = pred.has_value();
+  if (pred.has_value()) check_dev(*pred, "pred");
+  const c10::cuda::CUDAGuard guard(payloads[0].device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  const int grid = std::min((nblk + kWarps - 1) / kWarps, 4 * num_sms(payloads[0].get_device()));
+  check_launch(launch_reduce(s, (int)payloads.size(), out.data_ptr(),
+                             pred.has_value() ? pred->data_ptr<float>() : nullptr, n, (int)k, fp, (int)mode,
+                             dtype_code(out_dtype), grid, stream),
+               "reduce");
+  return out;
+}
+
+}  // namespace
+
+void register_fused(pybind11::module& m) {
+  pybind11::class_<FusedComm>(m, "FusedComm")
+      .def(pybind11::init<int64_t, int64_t, std::vector<int64_t>, int64_t, int64_t, int64_t, int64_t, int64_t,
+                          int64_t, int64_t, torch::Tensor>())
+      .def("run", &FusedComm::run)
+      .def_property("epoch", &FusedComm::epoch, &FusedComm::set_epoch);
+  m.def("product_encode", &product_encode_cuda);
+  m.def("product_reduce", &product_reduce_cuda);
+  m.def("dense_payload_bytes", &dense_payload_bytes);
+  m.def("topk_payload_bytes", &topk_payload_bytes);
+}

@@ -1,0 +1,156 @@
+// Device-side helpers shared by the sm_100a kernels: memory-ordering PTX for
+// cross-GPU flags, bounded waits, vector I/O for fp32/bf16 buckets.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common/ngl_product.h"
+
+namespace ngl {
+namespace dev {
+
+constexpr unsigned kFull = 0xffffffffu;
+
+__device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
+__device__ __forceinline__ int64_t max64(int64_t a, int64_t b) { return a > b ? a : b; }
+
+// Error codes written to the status word (never a trap).
+enum Status : int {
+  kOk = 0,
+  kTimeoutPayload = 1,   // a peer's payload flag never arrived
+  kTimeoutResult = 2,    // a two-shot result flag never arrived
+  kBadHeader = 3,        // payload header did not match (n / epoch)
+  kBounds = 4,           // bounds check failed (NGL_BOUNDS_CHECK builds)
+};
+
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_volatile_i32(const int* p) {
+  int v;
+  asm volatile("ld.volatile.global.s32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+
+// Record the first error (code + two context words) without trapping.
+__device__ __forceinline__ void set_status(int* status, int code, int a, int b) {
+  if (status == nullptr) return;
+  if (atomicCAS(status, 0, code) == 0) {
+    status[1] = a;
+    status[2] = b;
+  }
+}
+
+// Spin until *flag == want, a deadline passes, or another CTA reports an
+// error.  Returns false on give-up (caller records the status).
+__device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t want, uint64_t timeout_ns,
+                                          const int* status) {
+  if (ld_acquire_sys(flag) == want) return true;
+  const uint64_t t0 = globaltimer();
+  uint32_t spins = 0;
+  while (true) {
+    if (ld_acquire_sys(flag) == want) return true;
+    if ((++spins & 63u) == 0) {
+      if (globaltimer() - t0 > timeout_ns) return false;
+      if (status != nullptr && ld_volatile_i32(status) != 0) return false;
+    }
+    __nanosleep(64);
+  }
+}
+
+// Warp reductions.
+__device__ __forceinline__ float warp_absmax(float v) {
+  float m = fabsf(v);
+  if (m != m) m = 0.0f;  // NaN ignored, like fmax
+  uint32_t u = __reduce_max_sync(kFull, __float_as_uint(m));
+  return __uint_as_float(u);
+}
+__device__ __forceinline__ int warp_excl_scan(int v, int lane) {
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    int y = __shfl_up_sync(kFull, x, o);
+    if (lane >= o) x += y;
+  }
+  return x - v;
+}
+
+// ---- 8 consecutive elements per lane: vector loads of fp32 / bf16 ----
+template <typename T>
+struct Vec8;
+
+template <>
+struct Vec8<float> {
+  static __device__ __forceinline__ void load(const float* p, float (&v)[8]) {
+    float4 a = *reinterpret_cast<const float4*>(p);
+    float4 b = *reinterpret_cast<const float4*>(p + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  }
+  static __device__ __forceinline__ void store(float* p, const float (&v)[8]) {
+    *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+    *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
+  }
+  static __device__ __forceinline__ float get(const float* p) { return *p; }
+  static __device__ __forceinline__ void put(float* p, float v) { *p = v; }
+};
+
+template <>
+struct Vec8<__nv_bfloat16> {
+  static __device__ __forceinline__ void load(const __nv_bfloat16* p, float (&v)[8]) {
+    uint4 u = *reinterpret_cast<const uint4*>(p);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      v[2 * i] = __uint_as_float(w[i] << 16);
+      v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+  }
+  static __device__ __forceinline__ void store(__nv_bfloat16* p, const float (&v)[8]) {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+      w[i] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+  static __device__ __forceinline__ float get(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+  static __device__ __forceinline__ void put(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
+};
+
+// Load 8 elements starting at element `e0` of which `valid` (0..8) are in
+// range; out-of-range lanes read 0.  `vec_ok` selects the vector path.
+template <typename T>
+__device__ __forceinline__ void load8(const T* base, int64_t e0, int valid, bool vec_ok, float (&v)[8]) {
+  if (valid == 8 && vec_ok) {
+    Vec8<T>::load(base + e0, v);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = (j < valid) ? Vec8<T>::get(base + e0 + j) : 0.0f;
+  }
+}
+template <typename T>
+__device__ __forceinline__ void store8(T* base, int64_t e0, int valid, bool vec_ok, const float (&v)[8]) {
+  if (valid == 8 && vec_ok) {
+    Vec8<T>::store(base + e0, v);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (j < valid) Vec8<T>::put(base + e0 + j, v[j]);
+  }
+}
+
+}  // namespace dev
+}  // namespace ngl

@@ -1,0 +1,221 @@
+// pybind11 bindings of the native host library (module mini_nangila_b200._host).
+#include <pybind11/numpy.h>
+#include <pybind11/pybind11.h>
+#include <pybind11/stl.h>
+
+#include "nangila_host.hpp"
+
+namespace py = pybind11;
+using namespace ngl::host;
+
+namespace {
+template <typename T>
+using carr = py::array_t<T, py::array::c_style | py::array::forcecast>;
+
+// Hand a std::vector to numpy without a copy.
+template <typename T>
+py::array_t<T> to_np(std::vector<T>&& v) {
+  auto* heap = new std::vector<T>(std::move(v));
+  py::capsule owner(heap, [](void* p) { delete reinterpret_cast<std::vector<T>*>(p); });
+  return py::array_t<T>({(py::ssize_t)heap->size()}, {(py::ssize_t)sizeof(T)}, heap->data(), owner);
+}
+template <typename T>
+const T* ptr(const carr<T>& a) {
+  return a.size() ? a.data() : nullptr;
+}
+py::tuple qout(QuantOut&& q) { return py::make_tuple(to_np(std::move(q.bytes)), q.scale); }
+}  // namespace
+
+PYBIND11_MODULE(_host, m) {
+  m.doc() = "Native host library: bit-exact codecs, predictors, topology, NZCP, product-format oracle";
+  py::register_exception<ShapeMismatch>(m, "ShapeMismatch", PyExc_ValueError);
+
+  // nangila-math / nangila-edge
+  m.def("q823_from_f32", [](carr<float> x) { return to_np(q823_from_f32(ptr(x), x.size())); });
+  m.def("q823_to_f32", [](carr<int32_t> q) { return to_np(q823_to_f32(ptr(q), q.size())); });
+  m.def("q823_add", [](carr<int32_t> a, carr<int32_t> b) { return to_np(q823_add(ptr(a), a.size(), ptr(b), b.size())); });
+  m.def("q823_sub", [](carr<int32_t> a, carr<int32_t> b) { return to_np(q823_sub(ptr(a), a.size(), ptr(b), b.size())); });
+  m.def("q823_mul_scalar", [](carr<int32_t> a, float s) { return to_np(q823_mul_scalar(ptr(a), a.size(), s)); });
+  m.def("fixedq_from_f32", [](carr<float> x) { return to_np(fixedq_from_f32(ptr(x), x.size())); });
+  m.def("fixedq_to_f32", [](carr<int32_t> q) { return to_np(fixedq_to_f32(ptr(q), q.size())); });
+
+  // UnifiedQuantizer
+  m.def("stochastic_quantize", [](carr<int32_t> r, int bits, uint64_t seed, uint64_t counter) {
+    QuantOut q = stochastic_quantize(ptr(r), r.size(), bits, seed, &counter);
+    return py::make_tuple(to_np(std::move(q.bytes)), q.scale, counter);
+  });
+  m.def("stochastic_dequantize", [](carr<uint8_t> b, float scale, int bits) {
+    return to_np(stochastic_dequantize(ptr(b), b.size(), scale, bits));
+  });
+  m.def("topk_quantize", [](carr<int32_t> r, float k) { return qout(topk_quantize(ptr(r), r.size(), k)); });
+  m.def("topk_dequantize", [](carr<uint8_t> b, float s) { return to_np(topk_dequantize(ptr(b), b.size(), s)); });
+  m.def("topk_threshold", [](carr<float> x, float k) { return topk_threshold(ptr(x), x.size(), k); });
+
+  // nangila-hpc
+  m.def("eb_quantize", [](carr<int32_t> r, float eps) { return qout(eb_quantize(ptr(r), r.size(), eps)); });
+  m.def("eb_dequantize", [](carr<uint8_t> b, float s) { return to_np(eb_dequantize(ptr(b), b.size(), s)); });
+  m.def("rle_quantize", [](carr<int32_t> r, float eps) { return qout(rle_quantize(ptr(r), r.size(), eps)); });
+  m.def("rle_dequantize", [](carr<uint8_t> b, float s) { return to_np(rle_dequantize(ptr(b), b.size(), s)); });
+  m.def("bs_quantize", [](carr<int32_t> r, float eps) { return qout(bs_quantize(ptr(r), r.size(), eps)); });
+  m.def("bs_dequantize", [](carr<uint8_t> b, float s) { return to_np(bs_dequantize(ptr(b), b.size(), s)); });
+  m.def("bsrle_quantize", [](carr<int32_t> r, float eps) { return qout(bsrle_quantize(ptr(r), r.size(), eps)); });
+  m.def("bsrle_dequantize", [](carr<uint8_t> b, float s) { return to_np(bsrle_dequantize(ptr(b), b.size(), s)); });
+  m.def("rle_encode_i16", [](carr<int16_t> q) { return to_np(rle_encode_i16(ptr(q), q.size())); });
+  m.def("rle_decode_i16", [](carr<uint8_t> b) { return to_np(rle_decode_i16(ptr(b), b.size())); });
+
+  // Predictors
+  py::class_<MomentumPredictor>(m, "MomentumPredictor")
+      .def(py::init<float>())
+      .def("predict", [](const MomentumPredictor& p) { return to_np(p.predict()); })
+      .def("update", [](MomentumPredictor& p, carr<int32_t> o) { p.update(ptr(o), o.size()); })
+      .def("reset", &MomentumPredictor::reset)
+      .def_property_readonly("beta", &MomentumPredictor::beta)
+      .def_property_readonly("has_state", &MomentumPredictor::has_state)
+      .def("get_state", [](const MomentumPredictor& p) { return py::make_tuple(to_np(Fixed(p.state())), p.has_state()); })
+      .def("set_state", [](MomentumPredictor& p, carr<int32_t> s, bool has) {
+        p.set_state(Fixed(ptr(s), ptr(s) + s.size()), has);
+      });
+  py::class_<LinearPredictor>(m, "LinearPredictor")
+      .def(py::init<>())
+      .def("predict", [](const LinearPredictor& p) { return to_np(p.predict()); })
+      .def("update", [](LinearPredictor& p, carr<int32_t> o) { p.update(ptr(o), o.size()); })
+      .def("reset", &LinearPredictor::reset)
+      .def_property_readonly("history", &LinearPredictor::history)
+      .def("get_state", [](const LinearPredictor& p) {
+        return py::make_tuple(to_np(Fixed(p.s_t())), to_np(Fixed(p.s_tm1())), p.history());
+      })
+      .def("set_state", [](LinearPredictor& p, carr<int32_t> st, carr<int32_t> stm1, int n) {
+        p.set_history(Fixed(ptr(st), ptr(st) + st.size()), Fixed(ptr(stm1), ptr(stm1) + stm1.size()), n);
+      });
+
+  // TopologyMask
+  py::class_<TopologyMask>(m, "TopologyMask")
+      .def(py::init<>())
+      .def_static("from_variance_threshold",
+                  [](carr<float> v, float d) { return TopologyMask::from_variance_threshold(ptr(v), v.size(), d); })
+      .def_static("all_drivers", &TopologyMask::all_drivers)
+      .def_readwrite("driver_indices", &TopologyMask::driver_indices)
+      .def_readwrite("passenger_indices", &TopologyMask::passenger_indices)
+      .def_readwrite("threshold", &TopologyMask::threshold)
+      .def_readwrite("total_layers", &TopologyMask::total_layers)
+      .def("is_driver", &TopologyMask::is_driver)
+      .def("is_passenger", &TopologyMask::is_passenger)
+      .def("compression_factor", &TopologyMask::compression_factor)
+      .def("passenger_percentage", &TopologyMask::passenger_percentage)
+      .def("to_bytes", [](const TopologyMask& t) {
+        Bytes b = t.to_bytes();
+        return py::bytes(reinterpret_cast<const char*>(b.data()), b.size());
+      })
+      .def_static("from_bytes", [](py::bytes b) {
+        std::string s = b;
+        return TopologyMask::from_bytes(reinterpret_cast<const uint8_t*>(s.data()), s.size());
+      });
+
+  // NZCP
+  m.def("nz_compress", [](carr<float> data, size_t particles, size_t steps, int codec, float eps) {
+    if (particles * steps > (size_t)data.size()) throw std::runtime_error("data shorter than particles*steps");
+    NzStats st;
+    Bytes b;
+    {
+      py::gil_scoped_release nogil;
+      b = nz_compress(ptr(data), particles, steps, codec, eps, &st);
+    }
+    py::dict stats;
+    stats["total_raw"] = st.total_raw;
+    stats["total_comp"] = st.total_comp;
+    stats["max_abs_err"] = st.max_abs_err;
+    return py::make_tuple(to_np(std::move(b)), stats);
+  });
+  m.def("nz_read_header", [](carr<uint8_t> b) {
+    NzHeader h = nz_read_header(ptr(b), b.size());
+    return py::make_tuple(h.version, h.codec, h.particles, h.steps);
+  });
+  m.def("nz_decompress", [](carr<uint8_t> b, bool add_back) {
+    Floats f;
+    {
+      py::gil_scoped_release nogil;
+      f = nz_decompress(ptr(b), b.size(), add_back);
+    }
+    return to_np(std::move(f));
+  });
+  m.def("lammps_generate_synthetic", [](size_t p, size_t s) { return to_np(lammps_generate_synthetic(p, s)); });
+
+  // Product format oracle
+  m.def("product_encode", [](carr<float> g, py::object pred, py::object e_in, int bits, bool stochastic, bool ef,
+                             uint64_t seed, uint32_t rank, uint32_t bucket, uint64_t step) {
+    const size_t n = g.size();
+    const size_t nblk = (n + 255) / 256;
+    carr<float> pr = pred.is_none() ? carr<float>() : pred.cast<carr<float>>();
+    carr<float> ei = e_in.is_none() ? carr<float>() : e_in.cast<carr<float>>();
+    if (!pred.is_none() && (size_t)pr.size() != n) throw std::runtime_error("pred size mismatch");
+    if (!e_in.is_none() && (size_t)ei.size() != n) throw std::runtime_error("e size mismatch");
+    std::vector<float> scales(nblk);
+    std::vector<uint8_t> codes(nblk * (bits == 4 ? 128 : 256));
+    std::vector<float> e_out(ef ? n : 0);
+    ProductParams p;
+    p.bits = bits;
+    p.stochastic = stochastic;
+    p.error_feedback = ef;
+    p.seed = seed;
+    p.rank = rank;
+    p.bucket = bucket;
+    p.step = step;
+    product_encode(ptr(g), pred.is_none() ? nullptr : ptr(pr), e_in.is_none() ? nullptr : ptr(ei), n, p,
+                   scales.data(), codes.data(), ef ? e_out.data() : nullptr);
+    return py::make_tuple(to_np(std::move(scales)), to_np(std::move(codes)), to_np(std::move(e_out)));
+  });
+  m.def("product_reduce", [](std::vector<carr<float>> scales, std::vector<carr<uint8_t>> codes, size_t n, int bits,
+                             py::object pred, float inv_world) {
+    const int W = (int)scales.size();
+    std::vector<const float*> sp(W);
+    std::vector<const uint8_t*> cp(W);
+    for (int r = 0; r < W; ++r) {
+      sp[r] = ptr(scales[r]);
+      cp[r] = ptr(codes[r]);
+    }
+    carr<float> pr = pred.is_none() ? carr<float>() : pred.cast<carr<float>>();
+    std::vector<float> avg(n);
+    product_reduce(sp.data(), cp.data(), W, n, bits, pred.is_none() ? nullptr : ptr(pr), inv_world, avg.data());
+    return to_np(std::move(avg));
+  });
+  m.def("product_reduce_twoshot", [](std::vector<carr<float>> scales, std::vector<carr<uint8_t>> codes, size_t n,
+                                     int bits, py::object pred, float inv_world) {
+    const int W = (int)scales.size();
+    std::vector<const float*> sp(W);
+    std::vector<const uint8_t*> cp(W);
+    for (int r = 0; r < W; ++r) {
+      sp[r] = ptr(scales[r]);
+      cp[r] = ptr(codes[r]);
+    }
+    carr<float> pr = pred.is_none() ? carr<float>() : pred.cast<carr<float>>();
+    std::vector<float> avg(n);
+    product_reduce_twoshot(sp.data(), cp.data(), W, n, bits, pred.is_none() ? nullptr : ptr(pr), inv_world,
+                           avg.data());
+    return to_np(std::move(avg));
+  });
+  m.def("product_ema", [](carr<float> state, carr<float> avg, float beta, bool first) {
+    std::vector<float> s(state.data(), state.data() + state.size());
+    product_ema(s.data(), ptr(avg), s.size(), beta, first);
+    return to_np(std::move(s));
+  });
+  m.def("product_topk_encode", [](carr<float> g, py::object pred, py::object e_in, int k, bool ef) {
+    const size_t n = g.size();
+    const size_t nblk = (n + 255) / 256;
+    carr<float> pr = pred.is_none() ? carr<float>() : pred.cast<carr<float>>();
+    carr<float> ei = e_in.is_none() ? carr<float>() : e_in.cast<carr<float>>();
+    std::vector<uint8_t> rec(nblk * ngl::host::Bytes::size_type(((4 + 2 * k + 3) & ~3)));
+    std::vector<float> e_out(ef ? n : 0);
+    product_topk_encode(ptr(g), pred.is_none() ? nullptr : ptr(pr), e_in.is_none() ? nullptr : ptr(ei), n, k, ef,
+                        rec.data(), ef ? e_out.data() : nullptr);
+    return py::make_tuple(to_np(std::move(rec)), to_np(std::move(e_out)));
+  });
+  m.def("product_topk_reduce", [](std::vector<carr<uint8_t>> recs, size_t n, int k, py::object pred, float inv_world) {
+    const int W = (int)recs.size();
+    std::vector<const uint8_t*> rp(W);
+    for (int r = 0; r < W; ++r) rp[r] = ptr(recs[r]);
+    carr<float> pr = pred.is_none() ? carr<float>() : pred.cast<carr<float>>();
+    std::vector<float> avg(n);
+    product_topk_reduce(rp.data(), W, n, k, pred.is_none() ? nullptr : ptr(pr), inv_world, avg.data());
+    return to_np(std::move(avg));
+  });
+}

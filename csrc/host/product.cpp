@@ -1,0 +1,211 @@
+// Host oracle of the product wire format used by the fused all-reduce kernel
+// (csrc/cuda/fused_allreduce.cu).  Same per-element arithmetic
+// (csrc/common/ngl_product.h) in plain sequential loops.
+#include <algorithm>
+#include <cstring>
+
+#include "../common/ngl_product.h"
+#include "nangila_host.hpp"
+
+namespace ngl {
+namespace host {
+
+void product_encode(const float* g, const float* pred, const float* e_in, size_t n, const ProductParams& p,
+                    float* scales, uint8_t* codes, float* e_out) {
+  const int32_t qmax = p.bits == 4 ? 7 : 127;
+  const float qmaxf = (float)qmax;
+  const size_t nblk = (n + kBlock - 1) / kBlock;
+  const size_t bpb = p.bits == 4 ? kInt4BlockBytes : kInt8BlockBytes;
+  std::memset(codes, 0, nblk * bpb);
+  float c[kBlock];
+  int32_t q[kBlock];
+  for (size_t b = 0; b < nblk; ++b) {
+    const size_t base = b * kBlock;
+    const size_t len = std::min<size_t>(kBlock, n - base);
+    float absmax = 0.0f;
+    for (size_t i = 0; i < kBlock; ++i) {
+      if (i < len) {
+        float pr = pred ? pred[base + i] : 0.0f;
+        float e = (p.error_feedback && e_in) ? e_in[base + i] : 0.0f;
+        c[i] = product_residual(g[base + i], pr, e);
+        absmax = f_max(absmax, f_abs(c[i]));
+      } else {
+        c[i] = 0.0f;
+      }
+    }
+    const float s = product_scale(absmax, qmaxf);
+    const float inv = product_inv(s);
+    scales[b] = s;
+    for (size_t i = 0; i < kBlock; i += 4) {
+      U32x4 r = {0, 0, 0, 0};
+      if (p.stochastic) r = product_noise4(p.seed, p.rank, p.bucket, p.step, (uint32_t)((base + i) / 4));
+      const uint32_t rb[4] = {r.x, r.y, r.z, r.w};
+      for (int j = 0; j < 4; ++j) {
+        const size_t k = i + j;
+        if (k >= len) {
+          q[k] = 0;
+          continue;
+        }
+        q[k] = p.stochastic ? product_code_sr(c[k], inv, u01_from_bits(rb[j]), qmax) : product_code_rn(c[k], inv, qmax);
+        if (p.error_feedback && e_out) e_out[base + k] = NGL_FSUB(c[k], product_deq(q[k], s));
+      }
+    }
+    uint8_t* out = codes + b * bpb;
+    if (p.bits == 4) {
+      for (size_t j = 0; j < kInt4BlockBytes; ++j) out[j] = (uint8_t)((nib(q[2 * j]) << 4) | nib(q[2 * j + 1]));
+    } else {
+      for (size_t j = 0; j < kInt8BlockBytes; ++j) out[j] = (uint8_t)(int8_t)q[j];
+    }
+  }
+}
+
+void product_reduce(const float* const* scales, const uint8_t* const* codes, int world, size_t n, int bits,
+                    const float* pred, float inv_world, float* avg_out) {
+  const size_t bpb = bits == 4 ? kInt4BlockBytes : kInt8BlockBytes;
+  for (size_t i = 0; i < n; ++i) {
+    const size_t b = i / kBlock, k = i % kBlock;
+    float acc = 0.0f;
+    for (int r = 0; r < world; ++r) {
+      const uint8_t* blk = codes[r] + b * bpb;
+      int32_t q;
+      if (bits == 4) {
+        uint32_t byte = blk[k / 2];
+        q = sext4((k & 1) ? (byte & 0xF) : (byte >> 4));
+      } else {
+        q = (int8_t)blk[k];
+      }
+      acc = product_accum(acc, q, scales[r][b]);
+    }
+    avg_out[i] = product_average(pred ? pred[i] : 0.0f, acc, inv_world);
+  }
+}
+
+void product_ema(float* state, const float* avg, size_t n, float beta, bool first) {
+  const float omb = 1.0f - beta;
+  for (size_t i = 0; i < n; ++i) state[i] = ngl::product_ema(state[i], avg[i], beta, omb, first);
+}
+
+namespace {
+inline uint32_t fbits(float x) {
+  uint32_t u;
+  std::memcpy(&u, &x, 4);
+  return u;
+}
+}  // namespace
+
+void product_topk_encode(const float* g, const float* pred, const float* e_in, size_t n, int k, bool ef,
+                         uint8_t* records, float* e_out) {
+  const size_t nblk = (n + kBlock - 1) / kBlock;
+  const int rb = topk_record_bytes(k);
+  std::memset(records, 0, nblk * rb);
+  float c[kBlock];
+  uint32_t mag[kBlock];
+  for (size_t b = 0; b < nblk; ++b) {
+    const size_t base = b * kBlock;
+    const int len = (int)std::min<size_t>(kBlock, n - base);
+    float absmax = 0.0f;
+    for (int i = 0; i < len; ++i) {
+      c[i] = product_residual(g[base + i], pred ? pred[base + i] : 0.0f, (ef && e_in) ? e_in[base + i] : 0.0f);
+      mag[i] = fbits(f_abs(c[i]));
+      absmax = f_max(absmax, f_abs(c[i]));
+    }
+    const int keff = std::min(k, len);
+    // Threshold: largest T with count(mag >= T) >= keff (bitwise search).
+    uint32_t T = 0;
+    for (int bit = 31; bit >= 0; --bit) {
+      uint32_t cand = T | (1u << bit);
+      int cnt = 0;
+      for (int i = 0; i < len; ++i) cnt += mag[i] >= cand;
+      if (cnt >= keff) T = cand;
+    }
+    int gt = 0;
+    for (int i = 0; i < len; ++i) gt += mag[i] > T;
+    int eq_budget = keff - gt;
+    const float s = product_scale(absmax, 127.0f);
+    const float inv = product_inv(s);
+    uint8_t* rec = records + b * rb;
+    std::memcpy(rec, &s, 4);
+    int out = 0;
+    for (int i = 0; i < len; ++i) {
+      bool sel = mag[i] > T;
+      if (!sel && mag[i] == T && eq_budget > 0) {
+        sel = true;
+        --eq_budget;
+      }
+      if (sel) {
+        int32_t q = product_code_rn(c[i], inv, 127);
+        rec[4 + out] = (uint8_t)i;
+        rec[4 + k + out] = (uint8_t)(int8_t)q;
+        ++out;
+        if (ef && e_out) e_out[base + i] = NGL_FSUB(c[i], product_deq(q, s));
+      } else if (ef && e_out) {
+        e_out[base + i] = c[i];
+      }
+    }
+  }
+}
+
+void product_topk_reduce(const uint8_t* const* records, int world, size_t n, int k, const float* pred,
+                         float inv_world, float* avg_out) {
+  const size_t nblk = (n + kBlock - 1) / kBlock;
+  const int rb = topk_record_bytes(k);
+  float acc[kBlock];
+  for (size_t b = 0; b < nblk; ++b) {
+    const size_t base = b * kBlock;
+    const int len = (int)std::min<size_t>(kBlock, n - base);
+    for (int i = 0; i < kBlock; ++i) acc[i] = 0.0f;
+    for (int r = 0; r < world; ++r) {
+      const uint8_t* rec = records[r] + b * rb;
+      float s;
+      std::memcpy(&s, rec, 4);
+      const int keff = std::min(k, len);  // records of a short last block are padded
+      for (int j = 0; j < keff; ++j) {
+        int idx = rec[4 + j];
+        int32_t q = (int8_t)rec[4 + k + j];
+        acc[idx] = product_accum(acc[idx], q, s);
+      }
+    }
+    for (int i = 0; i < len; ++i) avg_out[base + i] = product_average(pred ? pred[base + i] : 0.0f, acc[i], inv_world);
+  }
+}
+
+// Two-shot: the chunk owner reduces, re-encodes the mean residual as INT8
+// with per-block scales (round to nearest), every rank decodes that.
+void product_reduce_twoshot(const float* const* scales, const uint8_t* const* codes, int world, size_t n, int bits,
+                            const float* pred, float inv_world, float* avg_out) {
+  const size_t bpb = bits == 4 ? kInt4BlockBytes : kInt8BlockBytes;
+  const size_t nblk = (n + kBlock - 1) / kBlock;
+  float m[kBlock];
+  for (size_t b = 0; b < nblk; ++b) {
+    const size_t base = b * kBlock;
+    const size_t len = std::min<size_t>(kBlock, n - base);
+    float absmax = 0.0f;
+    for (size_t k = 0; k < kBlock; ++k) {
+      float acc = 0.0f;
+      if (k < len) {
+        for (int r = 0; r < world; ++r) {
+          const uint8_t* blk = codes[r] + b * bpb;
+          int32_t q;
+          if (bits == 4) {
+            uint32_t byte = blk[k / 2];
+            q = sext4((k & 1) ? (byte & 0xF) : (byte >> 4));
+          } else {
+            q = (int8_t)blk[k];
+          }
+          acc = product_accum(acc, q, scales[r][b]);
+        }
+      }
+      m[k] = NGL_FMUL(acc, inv_world);
+      absmax = f_max(absmax, f_abs(m[k]));
+    }
+    const float s2 = product_scale(absmax, 127.0f);
+    const float inv2 = product_inv(s2);
+    for (size_t k = 0; k < len; ++k) {
+      const float d = product_accum(0.0f, product_code_rn(m[k], inv2, 127), s2);
+      avg_out[base + k] = product_average(pred ? pred[base + k] : 0.0f, d, 1.0f);
+    }
+  }
+}
+
+}  // namespace host
+}  // namespace ngl

@@ -1,0 +1,298 @@
+"""PyTorch DDP communication hook with predictive-residual compression.
+
+``register_nangila_hook`` accepts the keyword arguments of the reference's
+hook (``python/nangila_ddp/comm_hook.py:47-60``) and adds:
+
+* ``impl``: ``"fused"`` (default on CUDA) runs one sm_100a kernel per bucket
+  that predicts, compresses, exchanges over NVLink, decodes, sums, adds the
+  prediction back and updates the predictor and the error feedback; the
+  returned future completes on the communication stream, so the exchange
+  overlaps the rest of backward.  ``"host"`` runs the same product format
+  through the C++ oracle and ``all_gather`` (CPU / gloo ranks).  ``"compat"``
+  reproduces the reference's algorithm and payload (global absmax scale,
+  ``floor(x + U - 0.5)`` rounding, hi/lo nibbles, LSB-first top-k mask,
+  static randperm topology) with torch ops.
+* ``error_feedback`` (fused/host; the reference has none), ``variant``
+  (``auto|oneshot|twoshot``), ``timeout_s``, ``verbose``, ``max_ctas``.
+
+The hook state object returned by ``register_nangila_hook`` exposes
+``state_dict()/load_state_dict()`` (predictor and error-feedback buffers,
+call counters) so a resumed run continues bit-identically.
+"""
+from __future__ import annotations
+
+import time
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from .fused import FusedAllReduce, payload_bytes, topk_per_block
+
+
+@dataclass
+class _BucketState:
+    numel: int
+    sig: tuple
+    pred: torch.Tensor | None
+    ef: torch.Tensor | None
+    calls: int = 0
+
+
+@dataclass
+class HookConfig:
+    beta: float = 0.9
+    bits: int = 4
+    stochastic: bool = True
+    use_fp16_transport: bool = True  # accepted for API compatibility; unused (as in the reference)
+    seed: int = 12345
+    metrics_path: str | None = None
+    use_momentum: bool = False
+    topk_percent: float = 0.0
+    topo_drop_percent: float = 0.0
+    topo_seed: int = 424242
+    impl: str = "fused"
+    error_feedback: bool = True
+    variant: str = "auto"
+    timeout_s: float = 10.0
+    verbose: bool = False
+    max_ctas: int = 0
+
+    @property
+    def mode(self) -> str:
+        if self.topk_percent > 0.0:
+            return "topk"
+        return "int8" if self.bits == 8 else "int4"
+
+    @property
+    def k(self) -> int:
+        return topk_per_block(self.topk_percent) if self.topk_percent > 0.0 else 0
+
+
+@dataclass
+class NangilaHookState:
+    config: HookConfig
+    group: object = None
+    comm: FusedAllReduce | None = None
+    buckets: dict = field(default_factory=dict)
+    stream: torch.cuda.Stream | None = None
+    raw_bytes: int = 0
+    comp_bytes: int = 0
+    calls: int = 0
+    last_variant: str = ""
+
+    def compression_ratio(self) -> float:
+        return self.raw_bytes / max(1, self.comp_bytes)
+
+    def state_dict(self) -> dict:
+        out = {"calls": self.calls, "buckets": {}}
+        for b, st in self.buckets.items():
+            out["buckets"][b] = {
+                "numel": st.numel,
+                "calls": st.calls,
+                "pred": None if st.pred is None else st.pred.detach().cpu().clone(),
+                "ef": None if st.ef is None else st.ef.detach().cpu().clone(),
+            }
+        if self.comm is not None:
+            out["epoch"] = int(self.comm.comm.epoch)
+        return out
+
+    def load_state_dict(self, sd: dict) -> None:
+        self.calls = int(sd.get("calls", 0))
+        for b, d in sd["buckets"].items():
+            st = self.buckets.get(int(b))
+            if st is None or st.numel != d["numel"]:
+                st = _BucketState(d["numel"], ("restored", d["numel"]), None, None)
+                self.buckets[int(b)] = st
+            st.calls = int(d["calls"])
+            dev = self.comm.device if self.comm is not None else torch.device("cpu")
+            st.pred = None if d["pred"] is None else d["pred"].to(dev).clone()
+            st.ef = None if d["ef"] is None else d["ef"].to(dev).clone()
+        if self.comm is not None and "epoch" in sd:
+            self.comm.comm.epoch = int(sd["epoch"])
+
+
+def _bucket_sig(bucket) -> tuple:
+    try:
+        ps = bucket.parameters()
+        return (bucket.buffer().numel(), tuple(p.data_ptr() for p in ps[:2]), len(ps))
+    except Exception:
+        return (bucket.buffer().numel(),)
+
+
+def _get_state(hs: NangilaHookState, bidx: int, buf: torch.Tensor, sig: tuple, want_pred: bool,
+               want_ef: bool) -> tuple[_BucketState, bool]:
+    st = hs.buckets.get(bidx)
+    fresh = st is None or st.numel != buf.numel() or (st.sig != sig and st.sig[0] != "restored")
+    if fresh:
+        pred = torch.zeros(buf.numel(), dtype=torch.float32, device=buf.device) if want_pred else None
+        ef = torch.zeros(buf.numel(), dtype=torch.float32, device=buf.device) if want_ef else None
+        st = _BucketState(buf.numel(), sig, pred, ef, 0)
+        hs.buckets[bidx] = st
+    elif st.sig != sig:
+        st.sig = sig
+    first = st.calls == 0
+    st.calls += 1
+    return st, first
+
+
+def _log(hs: NangilaHookState, bidx: int, numel: int, comp: int, res_mean_abs: float = float("nan")) -> None:
+    cfg = hs.config
+    rank = dist.get_rank(hs.group) if dist.is_initialized() else 0
+    if rank != 0 or not (cfg.metrics_path or cfg.verbose):
+        return
+    raw = numel * 4
+    ratio = raw / max(comp, 1)
+    if cfg.verbose:
+        print(f"[nangila-b200-{cfg.mode}] bucket={numel} raw={raw/1e6:.3f}MB comp_local={comp/1e6:.3f}MB "
+              f"ratio={ratio:.2f}x pred_mode={'EMA' if cfg.use_momentum else 'none'} bits={cfg.bits}")
+    if cfg.metrics_path:
+        # Same key,value layout as the reference's metrics CSV (comm_hook.py:307-319)
+        line = (f"ts,{time.time():.6f},hook_idx,{hs.calls},bucket_elems,{numel},raw_bytes,{raw},"
+                f"comp_bytes,{comp},ratio,{ratio:.6f},res_mean_abs,{res_mean_abs:.6e}\n")
+        try:
+            with open(cfg.metrics_path, "a") as fh:
+                fh.write(line)
+        except OSError:
+            pass
+
+
+# --------------------------------------------------------------- fused (GPU)
+def _fused_hook(hs: NangilaHookState, bucket):
+    cfg = hs.config
+    buf = bucket.buffer()
+    bidx = bucket.index()
+    st, first = _get_state(hs, bidx, buf, _bucket_sig(bucket), cfg.use_momentum, cfg.error_feedback)
+    hs.calls += 1
+    cur = torch.cuda.current_stream(buf.device)
+    hs.stream.wait_stream(cur)
+    with torch.cuda.stream(hs.stream):
+        hs.last_variant = hs.comm.allreduce_(
+            buf, st.pred, st.ef, mode=cfg.mode, k=cfg.k, variant=cfg.variant, stochastic=cfg.stochastic,
+            seed=cfg.seed, bucket=bidx, step=st.calls, beta=cfg.beta, first=first,
+        )
+        fut = torch.futures.Future(devices=[buf.device])
+        fut.set_result(buf)
+    comp = payload_bytes(buf.numel(), cfg.mode, cfg.k)
+    hs.raw_bytes += buf.numel() * 4
+    hs.comp_bytes += comp
+    _log(hs, bidx, buf.numel(), comp)
+    return fut
+
+
+# ------------------------------------------------------- host (CPU, gloo)
+def _host_hook(hs: NangilaHookState, bucket):
+    from .._ext import host
+
+    h = host()
+    cfg = hs.config
+    buf = bucket.buffer()
+    bidx = bucket.index()
+    world = dist.get_world_size(hs.group)
+    rank = dist.get_rank(hs.group)
+    st, first = _get_state(hs, bidx, buf, _bucket_sig(bucket), cfg.use_momentum, cfg.error_feedback)
+    hs.calls += 1
+    g = buf.detach().float().cpu().numpy()
+    pred = st.pred.cpu().numpy() if st.pred is not None else None
+    ef = st.ef.cpu().numpy() if st.ef is not None else None
+    n = g.size
+    if cfg.mode == "topk":
+        rec, e_out = h.product_topk_encode(g, pred, ef, cfg.k, cfg.error_feedback)
+        payload = torch.from_numpy(np.ascontiguousarray(rec))
+    else:
+        bits = 4 if cfg.mode == "int4" else 8
+        scales, codes, e_out = h.product_encode(g, pred, ef, bits, cfg.stochastic, cfg.error_feedback,
+                                                cfg.seed & 0x7FFFFFFFFFFFFFFF, rank, bidx, st.calls)
+        payload = torch.cat([torch.from_numpy(scales).view(torch.uint8), torch.from_numpy(codes)])
+    gathered = [torch.empty_like(payload) for _ in range(world)]
+    dist.all_gather(gathered, payload, group=hs.group)
+    inv_world = np.float32(1.0) / np.float32(world)
+    if cfg.mode == "topk":
+        avg = h.product_topk_reduce([x.numpy() for x in gathered], n, cfg.k, pred, float(inv_world))
+    else:
+        nblk = (n + 255) // 256
+        sc = [x[: nblk * 4].view(torch.float32).numpy() for x in gathered]
+        cd = [x[nblk * 4:].numpy() for x in gathered]
+        avg = h.product_reduce(sc, cd, n, bits, pred, float(inv_world))
+    if st.pred is not None:
+        st.pred.copy_(torch.from_numpy(h.product_ema(st.pred.cpu().numpy(), avg, cfg.beta, first)))
+    if st.ef is not None:
+        st.ef.copy_(torch.from_numpy(e_out))
+    buf.copy_(torch.from_numpy(avg).to(buf.dtype))
+    comp = payload.numel()
+    hs.raw_bytes += n * 4
+    hs.comp_bytes += comp
+    _log(hs, bidx, n, comp)
+    fut = torch.futures.Future()
+    fut.set_result(buf)
+    return fut
+
+
+def register_nangila_hook(
+    model: torch.nn.Module,
+    *,
+    beta: float = 0.9,
+    bits: int = 4,
+    stochastic: bool = True,
+    use_fp16_transport: bool = True,
+    seed: int = 12345,
+    metrics_path: str | None = None,
+    use_momentum: bool = False,
+    topk_percent: float = 0.0,
+    topo_drop_percent: float = 0.0,
+    topo_seed: int = 424242,
+    impl: str | None = None,
+    error_feedback: bool | None = None,
+    variant: str = "auto",
+    timeout_s: float = 10.0,
+    verbose: bool = False,
+    max_ctas: int = 0,
+    process_group=None,
+) -> NangilaHookState:
+    """Register a predictive-residual compression comm hook on a DDP model.
+
+    Returns the hook state (metrics, ``state_dict``/``load_state_dict``).
+    """
+    if not hasattr(model, "register_comm_hook"):
+        raise RuntimeError("Model is not DDP-wrapped; call torch.nn.parallel.DistributedDataParallel first.")
+    if bits not in (4, 8):
+        raise ValueError("bits must be 4 or 8")
+    dev = next(model.parameters()).device
+    if impl is None:
+        impl = "fused" if dev.type == "cuda" else "host"
+    if impl == "compat":
+        from .compat_hook import make_compat_hook
+
+        cfg = HookConfig(beta, bits, stochastic, use_fp16_transport, seed, metrics_path, use_momentum, topk_percent,
+                         topo_drop_percent, topo_seed, impl, bool(error_feedback), variant, timeout_s, verbose)
+        hs = NangilaHookState(cfg, process_group)
+        model.register_comm_hook(state=None, hook=make_compat_hook(hs))
+        return hs
+    if topo_drop_percent > 0.0:
+        raise NotImplementedError("static topology drop is provided by impl='compat'")
+    cfg = HookConfig(beta, bits, stochastic, use_fp16_transport, seed, metrics_path, use_momentum, topk_percent,
+                     topo_drop_percent, topo_seed, impl, True if error_feedback is None else bool(error_feedback),
+                     variant, timeout_s, verbose, max_ctas)
+    hs = NangilaHookState(cfg, process_group)
+    if impl == "fused":
+        if dev.type != "cuda":
+            raise RuntimeError("impl='fused' needs a CUDA model; use impl='host' on CPU")
+        bucket_cap = int(getattr(model, "bucket_bytes_cap", 25 * 1024 * 1024))
+        max_numel = max([p.numel() for p in model.parameters()] + [bucket_cap // 4]) + 8192
+        # Buckets may concatenate several parameters above the cap; size for
+        # the cap plus the largest parameter.
+        max_numel = max_numel + max(p.numel() for p in model.parameters())
+        hs.comm = FusedAllReduce(max_numel, group=process_group, device=dev, topk_k=max(cfg.k, 1),
+                                 timeout_s=timeout_s, max_ctas=max_ctas)
+        hs.stream = torch.cuda.Stream(device=dev, priority=-1)
+
+        def hook(_state, bucket):
+            return _fused_hook(hs, bucket)
+    elif impl == "host":
+        def hook(_state, bucket):
+            return _host_hook(hs, bucket)
+    else:
+        raise ValueError(f"unknown impl {impl!r}")
+    model.register_comm_hook(state=None, hook=hook)
+    return hs

@@ -1,0 +1,112 @@
+"""Data-parallel training engine: the public API a user calls.
+
+``DDPTrainer`` wraps a model in ``DistributedDataParallel`` (25 MB buckets,
+gradient buckets as views), registers a gradient communication hook and runs
+AdamW steps under bf16 autocast with fp32 master weights:
+
+* ``hook="fused"``: predictive-residual compression, one sm_100a kernel per
+  bucket (``register_nangila_hook``);
+* ``hook="nccl"``: stock DDP all-reduce (plain NCCL fp32), the baseline;
+* ``hook="compat"`` / ``"host"``: the reference-compatible and the CPU paths.
+
+``step(x, y)`` trains on device-resident tokens and returns the loss tensor;
+``step_host(x_pinned, y_pinned)`` copies the step's inputs from pinned host
+memory, trains, and reads the loss back (the end-to-end path).
+
+Reference: python/nangila_ddp/train_nano.py:126-181 (DDP + hook + AdamW loop).
+"""
+from __future__ import annotations
+
+import os
+from datetime import timedelta
+
+import torch
+import torch.distributed as dist
+from torch.nn.parallel import DistributedDataParallel as DDP
+
+from .parallel.hook import register_nangila_hook
+
+
+def init_distributed(backend: str | None = None, timeout_s: float = 300.0) -> tuple[int, int, int]:
+    """Initialise torch.distributed from torchrun's environment (or as a
+    single rank on 127.0.0.1).  Returns (rank, world, local_rank)."""
+    if not dist.is_initialized():
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        if "MASTER_PORT" not in os.environ:
+            import socket
+
+            s = socket.socket()
+            s.bind(("127.0.0.1", 0))
+            os.environ["MASTER_PORT"] = str(s.getsockname()[1])
+            s.close()
+        os.environ.setdefault("RANK", "0")
+        os.environ.setdefault("WORLD_SIZE", "1")
+        os.environ.setdefault("LOCAL_RANK", "0")
+        if backend is None:
+            backend = "nccl" if torch.cuda.is_available() else "gloo"
+        local = int(os.environ["LOCAL_RANK"])
+        if backend == "nccl":
+            torch.cuda.set_device(local)
+            dist.init_process_group(backend, timeout=timedelta(seconds=timeout_s),
+                                    device_id=torch.device("cuda", local))
+        else:
+            dist.init_process_group(backend, timeout=timedelta(seconds=timeout_s))
+    return dist.get_rank(), dist.get_world_size(), int(os.environ.get("LOCAL_RANK", "0"))
+
+
+class DDPTrainer:
+    def __init__(
+        self,
+        model: torch.nn.Module,
+        *,
+        lr: float = 6e-4,
+        hook: str = "fused",
+        hook_kwargs: dict | None = None,
+        bucket_cap_mb: float = 25.0,
+        autocast_dtype: torch.dtype | None = torch.bfloat16,
+        device: torch.device | None = None,
+        fused_optimizer: bool = True,
+    ):
+        self.device = device or (torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available()
+                                 else torch.device("cpu"))
+        model = model.to(self.device)
+        kw = dict(bucket_cap_mb=bucket_cap_mb, gradient_as_bucket_view=True)
+        if self.device.type == "cuda":
+            kw["device_ids"] = [self.device.index]
+        self.ddp = DDP(model, **kw)
+        self.hook_state = None
+        if hook in ("fused", "compat", "host"):
+            hk = dict(hook_kwargs or {})
+            hk.setdefault("impl", hook)
+            self.hook_state = register_nangila_hook(self.ddp, **hk)
+        elif hook != "nccl":
+            raise ValueError(f"unknown hook {hook!r}")
+        use_fused = fused_optimizer and self.device.type == "cuda"
+        self.opt = torch.optim.AdamW(self.ddp.parameters(), lr=lr, fused=use_fused)
+        self.autocast_dtype = autocast_dtype if self.device.type == "cuda" else None
+
+    @property
+    def model(self) -> torch.nn.Module:
+        return self.ddp.module
+
+    def step(self, x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
+        if self.autocast_dtype is not None:
+            with torch.autocast(self.device.type, dtype=self.autocast_dtype):
+                loss = self.ddp(x, y)
+        else:
+            loss = self.ddp(x, y)
+        self.opt.zero_grad(set_to_none=False)
+        loss.backward()
+        self.opt.step()
+        return loss.detach()
+
+    def step_host(self, x_host: torch.Tensor, y_host: torch.Tensor) -> float:
+        x = x_host.to(self.device, non_blocking=True)
+        y = y_host.to(self.device, non_blocking=True)
+        return float(self.step(x, y).item())
+
+    def kernel_launches(self) -> int:
+        hs = self.hook_state
+        if hs is not None and getattr(hs, "comm", None) is not None:
+            return hs.comm.launches
+        return 0

@@ -1,0 +1,82 @@
+"""Sample SM clocks and throttle reasons with ``nvidia-smi`` while a timed
+region runs (read-only queries; no GPU setting is changed)."""
+from __future__ import annotations
+
+import os
+import signal
+import statistics
+import subprocess
+import tempfile
+
+FIELDS = [
+    "index", "clocks.sm", "clocks.max.sm", "power.draw", "clocks_event_reasons.active",
+    "clocks_event_reasons.hw_slowdown", "clocks_event_reasons.hw_thermal_slowdown",
+    "clocks_event_reasons.sw_thermal_slowdown", "clocks_event_reasons.sw_power_cap",
+]
+REASON_KEYS = {
+    "clocks_event_reasons.hw_slowdown": "hw_slowdown",
+    "clocks_event_reasons.hw_thermal_slowdown": "hw_thermal_slowdown",
+    "clocks_event_reasons.sw_thermal_slowdown": "sw_thermal_slowdown",
+    "clocks_event_reasons.sw_power_cap": "sw_power_cap",
+}
+
+
+class ClockSampler:
+    def __init__(self, gpus: list[int] | None = None, period_ms: int = 200):
+        self.gpus = gpus
+        self.period_ms = period_ms
+        self.proc = None
+        self.path = None
+
+    def start(self) -> "ClockSampler":
+        fd, self.path = tempfile.mkstemp(prefix="ngl_clocks_", suffix=".csv")
+        os.close(fd)
+        cmd = ["nvidia-smi", f"--query-gpu={','.join(FIELDS)}", "--format=csv,noheader,nounits", f"-lms", str(self.period_ms)]
+        if self.gpus:
+            cmd += ["-i", ",".join(str(g) for g in self.gpus)]
+        try:
+            self.proc = subprocess.Popen(cmd, stdout=open(self.path, "w"), stderr=subprocess.DEVNULL,
+                                         start_new_session=True)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def stop(self) -> dict:
+        if self.proc is not None:
+            try:
+                os.killpg(self.proc.pid, signal.SIGTERM)
+            except ProcessLookupError:
+                pass
+            self.proc.wait(timeout=10)
+        out = {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        if not self.path or not os.path.exists(self.path):
+            return out
+        rows = []
+        with open(self.path) as fh:
+            for line in fh:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) == len(FIELDS):
+                    rows.append(dict(zip(FIELDS, parts)))
+        os.unlink(self.path)
+        if not rows:
+            return out
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+        sm = [num(r["clocks.sm"]) for r in rows if num(r["clocks.sm"])]
+        mx = [num(r["clocks.max.sm"]) for r in rows if num(r["clocks.max.sm"])]
+        pw = [num(r["power.draw"]) for r in rows if num(r["power.draw"])]
+        reasons = set()
+        for r in rows:
+            for k, name in REASON_KEYS.items():
+                if r.get(k, "").lower().startswith("active"):
+                    reasons.add(name)
+        # Median under load: samples above 50% of max (idle samples at the
+        # edges of the window excluded).
+        peak = max(mx) if mx else None
+        loaded = [s for s in sm if peak is None or s >= 0.5 * peak] or sm
+        out.update(sm_mhz=statistics.median(loaded) if loaded else None, sm_max_mhz=peak,
+                   reasons=sorted(reasons), samples=len(rows), power_w_max=max(pw) if pw else None)
+        return out

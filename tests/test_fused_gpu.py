@@ -1,0 +1,191 @@
+"""sm_100a fused compressed all-reduce vs the C++ host oracle (bitwise)."""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+SIZES = [1, 31, 255, 256, 257, 1000, 8 * 256 * 3 + 17, 65536 + 3]
+
+
+def _ext():
+    from mini_nangila_b200 import _ext
+
+    return _ext.host(), _ext.cuda()
+
+
+def _data(n, seed, scale=1e-3):
+    g = np.random.default_rng(seed)
+    x = (g.standard_normal(n) * scale).astype(np.float32)
+    x[g.random(n) < 0.3] *= 0.01
+    return x
+
+
+def _bits(a):
+    return np.asarray(a, dtype=np.float32).view(np.uint32)
+
+
+@pytest.mark.parametrize("n", SIZES)
+@pytest.mark.parametrize("mode", ["int4", "int8", "topk"])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_encode_matches_oracle(n, mode, dtype):
+    h, c = _ext()
+    g = torch.from_numpy(_data(n, 1)).to(dtype)
+    gf = g.float().numpy()
+    pred = _data(n, 2)
+    ef = _data(n, 3, 1e-4)
+    dev = torch.device("cuda")
+    mcode = {"int4": 0, "int8": 1, "topk": 2}[mode]
+    k = 13
+    out, ef_out = c.product_encode(g.to(dev), torch.from_numpy(pred).to(dev), torch.from_numpy(ef).to(dev),
+                                   mcode, k, True, 777, 3, 5, 9)
+    if mode == "topk":
+        rec, e_ref = h.product_topk_encode(gf, pred, ef, k, True)
+        assert bytes(out.cpu().numpy()) == bytes(rec)
+    else:
+        bits = 4 if mode == "int4" else 8
+        sc, cd, e_ref = h.product_encode(gf, pred, ef, bits, True, True, 777, 3, 5, 9)
+        nblk = (n + 255) // 256
+        o = out.cpu().numpy()
+        assert np.array_equal(o[: nblk * 4].view(np.float32).view(np.uint32), sc.view(np.uint32))
+        off = (nblk * 4 + 15) & ~15
+        assert bytes(o[off:]) == bytes(cd)
+    assert np.array_equal(_bits(ef_out.cpu().numpy()), _bits(e_ref))
+
+
+@pytest.mark.parametrize("n", [257, 1000, 65536 + 3])
+@pytest.mark.parametrize("mode", ["int4", "int8", "topk"])
+def test_reduce_matches_oracle(n, mode):
+    h, c = _ext()
+    dev = torch.device("cuda")
+    W = 3
+    k = 26
+    bits = 8 if mode == "int8" else 4
+    mcode = {"int4": 0, "int8": 1, "topk": 2}[mode]
+    pred = _data(n, 50)
+    payloads_dev, sc_l, cd_l, rec_l = [], [], [], []
+    for r in range(W):
+        g = _data(n, 10 + r)
+        if mode == "topk":
+            rec, _ = h.product_topk_encode(g, pred, None, k, False)
+            rec_l.append(rec)
+            payloads_dev.append(torch.from_numpy(rec).to(dev))
+        else:
+            sc, cd, _ = h.product_encode(g, pred, None, bits, True, False, 1, r, 0, 0)
+            sc_l.append(sc)
+            cd_l.append(cd)
+            nblk = (n + 255) // 256
+            buf = np.zeros(((nblk * 4 + 15) & ~15) + cd.size, np.uint8)
+            buf[: nblk * 4] = sc.view(np.uint8)
+            buf[((nblk * 4 + 15) & ~15):] = cd
+            payloads_dev.append(torch.from_numpy(buf).to(dev))
+    inv = float(np.float32(1.0) / np.float32(W))
+    state = torch.from_numpy(pred.copy()).to(dev)
+    avg = c.product_reduce(payloads_dev, n, mcode, k, state, 0.9, False, inv, torch.float32)
+    if mode == "topk":
+        ref = h.product_topk_reduce(rec_l, n, k, pred, inv)
+    else:
+        ref = h.product_reduce(sc_l, cd_l, n, bits, pred, inv)
+    assert np.array_equal(_bits(avg.cpu().numpy()), _bits(ref))
+    ema = h.product_ema(pred, ref, 0.9, False)
+    assert np.array_equal(_bits(state.cpu().numpy()), _bits(ema))
+
+
+@pytest.mark.parametrize("mode", ["int4", "int8", "topk"])
+@pytest.mark.parametrize("n", [1000, 65536 + 3])
+def test_fused_single_rank_matches_oracle(mode, n):
+    from mini_nangila_b200.parallel.fused import FusedAllReduce
+
+    h, _ = _ext()
+    dev = torch.device("cuda")
+    comm = FusedAllReduce(n, device=dev)
+    k = 26
+    bits = 8 if mode == "int8" else 4
+    pred = _data(n, 7)
+    ef = _data(n, 8, 1e-4)
+    pred_d, ef_d = torch.from_numpy(pred.copy()).to(dev), torch.from_numpy(ef.copy()).to(dev)
+    for step in range(3):
+        g = _data(n, 100 + step)
+        gd = torch.from_numpy(g).to(dev)
+        comm.allreduce_(gd, pred_d, ef_d, mode=mode, k=k, seed=42, bucket=2, step=step, beta=0.9, first=(step == 0))
+        if mode == "topk":
+            rec, e_new = h.product_topk_encode(g, pred, ef, k, True)
+            avg = h.product_topk_reduce([rec], n, k, pred, 1.0)
+        else:
+            sc, cd, e_new = h.product_encode(g, pred, ef, bits, True, True, 42, 0, 2, step)
+            avg = h.product_reduce([sc], [cd], n, bits, pred, 1.0)
+        pred = h.product_ema(pred, avg, 0.9, step == 0)
+        ef = e_new
+        assert np.array_equal(_bits(gd.cpu().numpy()), _bits(avg)), f"avg mismatch at step {step}"
+        assert np.array_equal(_bits(pred_d.cpu().numpy()), _bits(pred))
+        assert np.array_equal(_bits(ef_d.cpu().numpy()), _bits(ef))
+    comm.check()
+
+
+def _two_rank_emulation(n, mode, k, bad_tag=False, deliver=True, timeout_s=0.2):
+    """Run rank 0 of a 2-rank one-shot all-reduce on one GPU with rank 1's
+    payload and flags pre-delivered into rank 0's region."""
+    from mini_nangila_b200.parallel.fused import (MODES, VARIANTS, FusedAllReduce, make_layout,
+                                                  payload_bytes)
+
+    h, c = _ext()
+    dev = torch.device("cuda")
+    L = make_layout(2, n, k)
+    reg0 = torch.zeros(L.total, dtype=torch.uint8, device=dev)
+    reg1 = torch.zeros(L.total, dtype=torch.uint8, device=dev)
+    status = torch.zeros(4, dtype=torch.int32, device=dev)
+    comm = c.FusedComm(2, 0, [reg0.data_ptr(), reg1.data_ptr()], L.flags_off, L.rflags_off, L.inbox_off,
+                       L.slot_bytes, L.result_off, L.result_bytes, L.max_chunks, status)
+    epoch = comm.epoch + 1
+    parity = epoch & 1
+    tag = FusedAllReduce.tag_for(n, 4)
+    g0, g1 = _data(n, 1), _data(n, 2)
+    bits = 8 if mode == "int8" else 4
+    mcode = MODES[mode]
+    if deliver:
+        p1, _ = c.product_encode(torch.from_numpy(g1).to(dev), None, None, mcode, k, True, 99, 1, 4, 7)
+        slot = L.inbox_off + (parity * 2 + 1) * L.slot_bytes
+        reg0[slot: slot + p1.numel()] = p1
+        nchunks = ((n + 255) // 256 + 7) // 8
+        flags = reg0[L.flags_off:].view(torch.int64)
+        val = ((tag ^ (1 if bad_tag else 0)) << 32) | epoch
+        if val >= 1 << 63:
+            val -= 1 << 64
+        base = (parity * 2 + 1) * L.max_chunks
+        flags[base: base + nchunks] = val
+    torch.cuda.synchronize()
+    gd = torch.from_numpy(g0).to(dev)
+    comm.run(gd, None, None, mcode, k, VARIANTS["oneshot"], True, 99, 4, 7, 0.9, True, 0, int(timeout_s * 1e9), tag)
+    torch.cuda.synchronize()
+    st = status.cpu().tolist()
+    inv = float(np.float32(0.5))
+    if mode == "topk":
+        r0, _ = h.product_topk_encode(g0, None, None, k, False)
+        r1, _ = h.product_topk_encode(g1, None, None, k, False)
+        ref = h.product_topk_reduce([r0, r1], n, k, None, inv)
+    else:
+        s0, c0, _ = h.product_encode(g0, None, None, bits, True, False, 99, 0, 4, 7)
+        s1, c1, _ = h.product_encode(g1, None, None, bits, True, False, 99, 1, 4, 7)
+        ref = h.product_reduce([s0, s1], [c0, c1], n, bits, None, inv)
+    return st, gd.cpu().numpy(), ref
+
+
+@pytest.mark.parametrize("mode", ["int4", "int8", "topk"])
+def test_oneshot_kernel_with_predelivered_peer(mode):
+    st, out, ref = _two_rank_emulation(50000, mode, 13)
+    assert st[0] == 0, st
+    assert np.array_equal(_bits(out), _bits(ref))
+
+
+def test_wait_times_out_and_reports_status():
+    """A flag that nothing sets: the bounded wait gives up, records the status
+    and the context stays usable."""
+    st, _, _ = _two_rank_emulation(5000, "int4", 13, deliver=False, timeout_s=0.05)
+    assert st[0] == 1, st  # timeout waiting for a peer's payload
+    x = torch.ones(10, device="cuda")
+    assert float(x.sum()) == 10.0
+
+
+def test_bad_tag_is_reported():
+    st, _, _ = _two_rank_emulation(5000, "int4", 13, bad_tag=True)
+    assert st[0] == 3, st
