@@ -114,6 +114,17 @@ NGL_HD float product_ema(float state, float avg, float beta, float one_minus_bet
 // Top-k record size in bytes for k kept elements of a 256-block:
 // fp32 scale, k uint8 indices, k int8 values, padded to 4 bytes.
 NGL_HD int topk_record_bytes(int k) { return (4 + 2 * k + 3) & ~3; }
+// Wire payloads are sequences of chunk records, one per 8 consecutive
+// 256-blocks (the last chunk is padded with empty blocks):
+//   INT4 / INT8: [8 x f32 scale][8 x 128 | 256 code bytes]
+//   top-k:       8 x top-k block record
+constexpr int kChunkBlocks = 8;
+NGL_HD int chunk_record_bytes(int mode, int k) {
+  return mode == 0 ? 4 * kChunkBlocks + kChunkBlocks * kInt4BlockBytes
+       : mode == 1 ? 4 * kChunkBlocks + kChunkBlocks * kInt8BlockBytes
+                   : kChunkBlocks * topk_record_bytes(k);
+}
+
 // Kept elements per 256-block for a keep fraction.
 inline int topk_per_block(double frac) {
   int k = (int)(frac * kBlock + 0.5);

@@ -10,11 +10,13 @@ namespace dev {
 
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
-constexpr int kChunkBlocks = kWarps;  // one 256-block per warp per chunk
 constexpr int kMaxWorld = 8;
-constexpr int kTopkMaxRec = 520;      // topk_record_bytes(256) rounded up
+constexpr int kMaxCols = 2048;        // max CTAs of one launch (flag columns)
+constexpr int kTopkMaxRec = 520;      // topk_record_bytes(256)
+constexpr int kMaxChunkRec = 8 * kTopkMaxRec;
 
 enum Mode : int { kInt4 = 0, kInt8 = 1, kTopK = 2 };
+enum FlagKind : int { kFlagPayload = 0, kFlagResult = 1 };
 
 struct QParams {
   uint64_t seed;
@@ -33,6 +35,10 @@ struct FParams {
   int use_pred;
 };
 
+// Symmetric region of every rank (same layout on all ranks):
+//   flags_off : u64 flags [2 parity][2 kinds][world src][kMaxCols]
+//   inbox_off : [2 parity][world src] slots of slot_bytes (chunk records)
+//   result_off: [2 parity] two-shot result regions of result_bytes
 struct FusedParams {
   void* grad;
   float* pred;
@@ -40,18 +46,17 @@ struct FusedParams {
   int64_t n;
   int nblk;
   int nchunks;
-  int k;          // top-k per block
-  int rec_bytes;  // top-k record bytes
+  int k;           // top-k per block
+  int rec_bytes;   // top-k block record bytes
+  int chunk_bytes; // wire bytes per chunk record for this mode
   int world;
   int rank;
   uint8_t* sym[kMaxWorld];
-  int64_t flags_off;   // u64 flags [2][world][max_chunks]
-  int64_t rflags_off;  // u64 result flags [2][max_chunks]
-  int64_t inbox_off;   // [2][world] slots of slot_bytes
+  int64_t flags_off;
+  int64_t inbox_off;
   int64_t slot_bytes;
-  int64_t result_off;  // [2] result regions of result_bytes
+  int64_t result_off;
   int64_t result_bytes;
-  int max_chunks;
   uint32_t epoch;
   uint32_t tag;
   int parity;
@@ -68,6 +73,9 @@ struct ReduceSrcs {
 enum DType : int { kF32 = 0, kBF16 = 1 };
 enum Variant : int { kVariantSingle = 0, kVariantOneShot = 1, kVariantTwoShot = 2 };
 
+// Grid used for a launch: a pure function of (nchunks, mode, dtype, variant,
+// cap) on a given GPU model, so every rank launches the same grid.
+int fused_grid(int nchunks, int mode, int dtype, int variant, int cap, int device);
 cudaError_t launch_fused(const FusedParams& P, int mode, int dtype, int variant, int grid, cudaStream_t stream);
 cudaError_t launch_encode(const void* g, const float* pred, const float* ef_in, float* ef_out, int64_t n, int k,
                           const QParams& qp, uint8_t* out, int mode, int dtype, int grid, cudaStream_t stream);

@@ -22,11 +22,11 @@ int num_sms(int device) {
   return v;
 }
 
-int64_t dense_payload_bytes(int64_t n, int bits) {
-  const int64_t nblk = (n + 255) / 256;
-  return ((nblk * 4 + 15) & ~int64_t(15)) + nblk * (bits == 4 ? 128 : 256);
+int64_t nchunks_of(int64_t n) { return ((n + 255) / 256 + ngl::kChunkBlocks - 1) / ngl::kChunkBlocks; }
+// Wire bytes of one rank's payload for a bucket of n elements.
+int64_t payload_bytes(int64_t n, int64_t mode, int64_t k) {
+  return nchunks_of(n) * ngl::chunk_record_bytes((int)mode, (int)k);
 }
-int64_t topk_payload_bytes(int64_t n, int64_t k) { return ((n + 255) / 256) * ngl::topk_record_bytes((int)k); }
 
 void check_dev(const torch::Tensor& t, const char* what) {
   TORCH_CHECK(t.is_cuda(), what, " must be a CUDA tensor");
@@ -47,9 +47,8 @@ void check_launch(cudaError_t e, const char* what) {
 // pointers of every rank, the geometry, the epoch counter, the status word.
 class FusedComm {
  public:
-  FusedComm(int64_t world, int64_t rank, std::vector<int64_t> sym_ptrs, int64_t flags_off, int64_t rflags_off,
-            int64_t inbox_off, int64_t slot_bytes, int64_t result_off, int64_t result_bytes, int64_t max_chunks,
-            torch::Tensor status)
+  FusedComm(int64_t world, int64_t rank, std::vector<int64_t> sym_ptrs, int64_t flags_off, int64_t inbox_off,
+            int64_t slot_bytes, int64_t result_off, int64_t result_bytes, torch::Tensor status)
       : world_(world), rank_(rank), status_(status) {
     TORCH_CHECK(world >= 1 && world <= kMaxWorld, "world size must be in [1, 8]");
     TORCH_CHECK(world == 1 || (int64_t)sym_ptrs.size() == world, "need one symmetric pointer per rank");
@@ -61,12 +60,10 @@ class FusedComm {
     base_.world = (int)world;
     base_.rank = (int)rank;
     base_.flags_off = flags_off;
-    base_.rflags_off = rflags_off;
     base_.inbox_off = inbox_off;
     base_.slot_bytes = slot_bytes;
     base_.result_off = result_off;
     base_.result_bytes = result_bytes;
-    base_.max_chunks = (int)max_chunks;
     base_.status = status.data_ptr<int>();
   }
 
@@ -94,9 +91,10 @@ class FusedComm {
     TORCH_CHECK(mode >= 0 && mode <= 2, "mode must be 0 (int4), 1 (int8) or 2 (top-k)");
     P.n = n;
     P.nblk = (int)((n + ngl::kBlock - 1) / ngl::kBlock);
-    P.nchunks = (P.nblk + kChunkBlocks - 1) / kChunkBlocks;
+    P.nchunks = (P.nblk + ngl::kChunkBlocks - 1) / ngl::kChunkBlocks;
     P.k = (int)k;
     P.rec_bytes = ngl::topk_record_bytes((int)k);
+    P.chunk_bytes = ngl::chunk_record_bytes((int)mode, (int)k);
     if (world_ == 1) variant = kVariantSingle;
     TORCH_CHECK(variant != kVariantSingle || world_ == 1, "the single-rank kernel needs world size 1");
     if (mode == kTopK) {
@@ -104,11 +102,10 @@ class FusedComm {
       TORCH_CHECK(variant != kVariantTwoShot, "two-shot is implemented for dense modes only");
     }
     if (world_ > 1) {
-      TORCH_CHECK(P.nchunks <= base_.max_chunks, "bucket larger than the communicator capacity");
-      const int64_t need = mode == kTopK ? topk_payload_bytes(n, k) : dense_payload_bytes(n, mode == kInt4 ? 4 : 8);
+      const int64_t need = payload_bytes(n, mode, k);
       TORCH_CHECK(need <= base_.slot_bytes, "payload (", need, " B) exceeds the inbox slot (", base_.slot_bytes, " B)");
       if (variant == kVariantTwoShot)
-        TORCH_CHECK(dense_payload_bytes(n, 8) <= base_.result_bytes, "two-shot result exceeds its region");
+        TORCH_CHECK(payload_bytes(n, kInt8, 0) <= base_.result_bytes, "two-shot result exceeds its region");
     }
     epoch_ += 1;
     P.epoch = (uint32_t)epoch_;
@@ -131,13 +128,7 @@ class FusedComm {
     const c10::cuda::CUDAGuard guard(grad.device());
     cudaStream_t stream = at::cuda::getCurrentCUDAStream();
     const int dev = grad.get_device();
-    int grid;
-    if (variant == kVariantSingle) {
-      grid = std::max(1, std::min((P.nblk + kWarps - 1) / kWarps, 4 * num_sms(dev)));
-    } else {
-      const int cap = (int)(max_ctas > 0 ? max_ctas : 2 * num_sms(dev));
-      grid = std::max(1, std::min(P.nchunks, cap));
-    }
+    const int grid = fused_grid(P.nchunks, (int)mode, dtype_code(grad.scalar_type()), (int)variant, (int)max_ctas, dev);
     check_launch(launch_fused(P, (int)mode, dtype_code(grad.scalar_type()), (int)variant, grid, stream), "fused");
     return epoch_;
   }
@@ -160,7 +151,7 @@ std::vector<torch::Tensor> product_encode_cuda(torch::Tensor g, c10::optional<to
   check_dev(g, "g");
   const int64_t n = g.numel();
   const int nblk = (int)((n + 255) / 256);
-  const int64_t bytes = mode == kTopK ? topk_payload_bytes(n, k) : dense_payload_bytes(n, mode == kInt4 ? 4 : 8);
+  const int64_t bytes = payload_bytes(n, mode, k);
   auto out = torch::zeros({bytes}, g.options().dtype(torch::kUInt8));
   torch::Tensor ef_out =
       ef.has_value() ? torch::empty_like(*ef) : torch::empty({0}, g.options().dtype(torch::kFloat32));
@@ -223,11 +214,14 @@ torch::Tensor product_reduce_cuda(std::vector<torch::Tensor> payloads, int64_t n
 void register_fused(pybind11::module& m) {
   pybind11::class_<FusedComm>(m, "FusedComm")
       .def(pybind11::init<int64_t, int64_t, std::vector<int64_t>, int64_t, int64_t, int64_t, int64_t, int64_t,
-                          int64_t, int64_t, torch::Tensor>())
+                          torch::Tensor>())
       .def("run", &FusedComm::run)
       .def_property("epoch", &FusedComm::epoch, &FusedComm::set_epoch);
   m.def("product_encode", &product_encode_cuda);
   m.def("product_reduce", &product_reduce_cuda);
-  m.def("dense_payload_bytes", &dense_payload_bytes);
-  m.def("topk_payload_bytes", &topk_payload_bytes);
+  m.def("payload_bytes", &payload_bytes);
+  m.def("fused_grid", [](int64_t n, int64_t mode, bool bf16, int64_t variant, int64_t cap, int64_t device) {
+    const int nchunks = (int)nchunks_of(n);
+    return fused_grid(nchunks, (int)mode, bf16 ? kBF16 : kF32, (int)variant, (int)cap, (int)device);
+  });
 }

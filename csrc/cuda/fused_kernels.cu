@@ -1,26 +1,35 @@
 // Fused compressed all-reduce for DDP gradient buckets (sm_100a).
 //
-// One kernel per bucket does, chunk by chunk (8 blocks of 256 elements per
-// CTA iteration, one block per warp):
-//   predict (EMA state) -> residual with error feedback -> per-block absmax
-//   scale -> Philox stochastic INT4/INT8 codes (or per-block top-k select and
-//   index packing) -> P2P stores of the payload into every peer's inbox over
-//   NVLink -> a release flag per (chunk, peer) -> bounded acquire-wait on the
-//   peers' flags -> rank-ordered decode + sum -> predictor add-back -> EMA
-//   update -> write the averaged gradient back into the bucket.
+// One kernel per bucket.  Every CTA owns the chunks c = b, b + G, b + 2G, ...
+// (8 blocks of 256 elements per chunk, one block per warp), and CTA b of
+// every rank owns the same chunks, so the ranks synchronise per CTA
+// "column" instead of per chunk:
 //
-// The reference does the same work as ~20 eager PyTorch ops, five NCCL
+// one-shot
+//   phase 1  for each owned chunk: predict (EMA state) -> residual with error
+//            feedback -> per-block absmax scale -> Philox stochastic INT4/INT8
+//            codes (or per-block top-k selection + index packing) -> chunk
+//            record staged in shared memory -> 16-byte P2P stores of the
+//            record into every peer's inbox over NVLink
+//   signal   one release flag per peer for this column
+//   phase 2  one bounded acquire-wait on the peers' column flags, then for
+//            each owned chunk: rank-ordered decode + sum of the W records ->
+//            predictor add-back -> EMA update -> averaged gradient written
+//            back into the bucket
+// two-shot (dense modes)
+//   phase A  chunk i of the column goes only to its owner rank i mod W
+//   phase B  the owner sums its chunks' W records, re-encodes the mean
+//            residual as INT8 with per-block scales and pushes that record
+//            to every rank
+//   phase C  every rank decodes the owners' INT8 records
+//
+// The reference does this work as ~20 eager PyTorch ops, five NCCL
 // all_gathers and nine host syncs per bucket
 // (python/nangila_ddp/comm_hook.py:125-324).
 //
-// Two-shot variant (dense INT4/INT8 only): each rank owns the chunks
-// c = rank (mod W); phase A pushes every chunk's payload to its owner,
-// phase B reduces the owned chunks and broadcasts them re-encoded as INT8 with
-// per-block scales, phase C decodes the owners' results.  NVLink bytes per
-// rank drop from (W-1)*P to about 2*P*(W-1)/W.
-//
-// Every peer access is a plain global load/store through an IPC mapping;
-// there is no TMA and no multicast anywhere in this file.
+// Every peer access is a plain global load/store through an IPC mapping:
+// there is no TMA and no multicast in this file.  Every wait is bounded and
+// reports through the status word instead of trapping.
 #include "fused.h"
 #include "ngl_cuda.cuh"
 
@@ -30,23 +39,21 @@ namespace dev {
 __device__ __forceinline__ int64_t align16(int64_t x) { return (x + 15) & ~int64_t(15); }
 
 // ------------------------------------------------------------ warp encoders
-// Load the residual c = g - pred + e of 8 consecutive elements of a block.
+// Residual c = g - pred + e of the lane's 8 consecutive elements of a block.
 template <typename T>
 __device__ __forceinline__ int load_residual(const T* g, const float* pred, const float* ef, int64_t n, int blk,
                                              int lane, const QParams& qp, float (&c)[8]) {
   const int64_t e0 = (int64_t)blk * kBlock + lane * 8;
-  int valid = (int)min64(8, max64(0, n - e0));
+  const int valid = (int)min64(8, max64(0, n - e0));
   float gv[8], pv[8], ev[8];
   load8<T>(g, e0, valid, true, gv);
   if (qp.use_pred) load8<float>(pred, e0, valid, true, pv);
-#pragma unroll
-  for (int j = 0; j < 8; ++j)
-    if (!qp.use_pred) pv[j] = 0.0f;
   if (qp.use_ef) load8<float>(ef, e0, valid, true, ev);
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    if (!qp.use_ef) ev[j] = 0.0f;
-    c[j] = (j < valid) ? product_residual(gv[j], pv[j], ev[j]) : 0.0f;
+    const float p = qp.use_pred ? pv[j] : 0.0f;
+    const float e = qp.use_ef ? ev[j] : 0.0f;
+    c[j] = (j < valid) ? product_residual(gv[j], p, e) : 0.0f;
   }
   return valid;
 }
@@ -58,18 +65,18 @@ __device__ __forceinline__ float block_absmax(const float (&c)[8]) {
   return __uint_as_float(__reduce_max_sync(kFull, __float_as_uint(m)));
 }
 
-// Dense INT4/INT8 encode of one block.  Returns the block scale; codes for the
-// lane's 8 elements in w[0] (INT4) or w[0..1] (INT8); writes the new EF.
+// Dense INT4/INT8 encode of one block: returns the scale; the lane's codes in
+// w[0] (INT4) or w[0..1] (INT8); q[] holds the integer codes; writes new EF.
 template <int BITS>
 __device__ __forceinline__ float encode_dense(const float (&c)[8], int valid, int blk, int lane, const QParams& qp,
-                                              float* ef_out, int64_t n, uint32_t (&w)[2], int32_t (&q)[8]) {
+                                              float* ef_out, uint32_t (&w)[2], int32_t (&q)[8]) {
   constexpr int32_t qmax = BITS == 4 ? 7 : 127;
   const float s = product_scale(block_absmax(c), (float)qmax);
   const float inv = product_inv(s);
   if (qp.stochastic) {
     const uint32_t g0 = (uint32_t)((int64_t)blk * (kBlock / 4) + lane * 2);
-    U32x4 r0 = product_noise4(qp.seed, qp.rank, qp.bucket, qp.step, g0);
-    U32x4 r1 = product_noise4(qp.seed, qp.rank, qp.bucket, qp.step, g0 + 1);
+    const U32x4 r0 = product_noise4(qp.seed, qp.rank, qp.bucket, qp.step, g0);
+    const U32x4 r1 = product_noise4(qp.seed, qp.rank, qp.bucket, qp.step, g0 + 1);
     const uint32_t rb[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
 #pragma unroll
     for (int j = 0; j < 8; ++j) q[j] = product_code_sr(c[j], inv, u01_from_bits(rb[j]), qmax);
@@ -102,22 +109,22 @@ __device__ __forceinline__ float encode_dense(const float (&c)[8], int valid, in
   return s;
 }
 
-// Store one lane's dense codes + the block scale into a payload slot laid out
-// as [scales (nblk f32, 16B-aligned)][codes (nblk * 128|256 B)].
+// Dense chunk record: [8 x f32 scale][8 x bpb codes]; warp w owns block w.
 template <int BITS>
-__device__ __forceinline__ void put_dense(uint8_t* slot, int nblk, int blk, int lane, float s, const uint32_t (&w)[2]) {
+__device__ __forceinline__ void put_dense(uint8_t* rec, int warp, int lane, float s, const uint32_t (&w)[2]) {
   constexpr int bpb = BITS == 4 ? kInt4BlockBytes : kInt8BlockBytes;
-  uint8_t* codes = slot + align16((int64_t)nblk * 4) + (int64_t)blk * bpb;
-  if (lane == 0) reinterpret_cast<float*>(slot)[blk] = s;
+  uint8_t* codes = rec + 4 * kChunkBlocks + warp * bpb;
+  if (lane == 0) reinterpret_cast<float*>(rec)[warp] = s;
   if (BITS == 4) reinterpret_cast<uint32_t*>(codes)[lane] = w[0];
   else reinterpret_cast<uint2*>(codes)[lane] = make_uint2(w[0], w[1]);
 }
 
+// Accumulate warp `warp`'s block of one dense chunk record (global memory).
 template <int BITS>
-__device__ __forceinline__ void accum_dense(const uint8_t* slot, int nblk, int blk, int lane, float (&acc)[8]) {
+__device__ __forceinline__ void accum_dense(const uint8_t* rec, int warp, int lane, float (&acc)[8]) {
   constexpr int bpb = BITS == 4 ? kInt4BlockBytes : kInt8BlockBytes;
-  const uint8_t* codes = slot + align16((int64_t)nblk * 4) + (int64_t)blk * bpb;
-  const float s = __ldcg(reinterpret_cast<const float*>(slot) + blk);
+  const uint8_t* codes = rec + 4 * kChunkBlocks + warp * bpb;
+  const float s = __ldcg(reinterpret_cast<const float*>(rec) + warp);
   if (BITS == 4) {
     const uint32_t x = __ldcg(reinterpret_cast<const unsigned int*>(codes) + lane);
 #pragma unroll
@@ -161,13 +168,13 @@ __device__ __forceinline__ void finalize(T* grad, float* pred, int64_t n, int bl
 // --------------------------------------------------------------- top-k warp
 struct TopkSel {
   float s;
-  uint32_t selmask;  // bit j: element j of this lane selected
+  uint32_t selmask;  // bit j: element j of this lane kept
   int32_t q[8];
 };
 
-// Select the k largest |c| of one block (ties -> lower index), quantize the
-// selected ones to int8 with scale absmax/127, build the record in `rec`
-// (per-warp shared memory) and write the new EF.
+// Keep the k largest |c| of one block (ties -> lower index), int8 codes with
+// scale absmax/127, record [f32 s][k idx ascending][k int8] written to `rec`
+// (shared memory of this warp), new EF written.
 __device__ __forceinline__ TopkSel topk_select(const float (&c)[8], int valid, int blk, int lane, int k, int64_t n,
                                                const QParams& qp, float* ef_out, uint8_t* rec, int rec_bytes) {
   TopkSel r;
@@ -176,6 +183,7 @@ __device__ __forceinline__ TopkSel topk_select(const float (&c)[8], int valid, i
   uint32_t m[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) m[j] = __float_as_uint(fabsf(c[j]));
+  // Largest T with |{j : m_j >= T}| >= keff, one bit at a time (MSB first).
   uint32_t T = 0;
   for (int bit = 31; bit >= 0; --bit) {
     const uint32_t cand = T | (1u << bit);
@@ -191,8 +199,7 @@ __device__ __forceinline__ TopkSel topk_select(const float (&c)[8], int valid, i
     gt += (m[j] > T);
     eq += (m[j] == T && j < valid);
   }
-  const int gt_total = (int)__reduce_add_sync(kFull, (unsigned)gt);
-  const int budget = keff - gt_total;
+  const int budget = keff - (int)__reduce_add_sync(kFull, (unsigned)gt);
   int eq_rank = warp_excl_scan(eq, lane);
   uint32_t sel = 0;
 #pragma unroll
@@ -230,31 +237,100 @@ __device__ __forceinline__ TopkSel topk_select(const float (&c)[8], int valid, i
   return r;
 }
 
-// Accumulate one rank's record (already staged in shared memory) into the
-// per-warp accumulator acc[256].
-__device__ __forceinline__ void topk_accum(const uint8_t* rec, int k, int keff, float* acc, int lane) {
-  const float s = reinterpret_cast<const float*>(rec)[0];
+// Add one rank's block record (global memory) into the warp accumulator,
+// staging it through shared memory.
+__device__ __forceinline__ void topk_accum_global(const uint8_t* rec_g, uint8_t* stage, int k, int keff,
+                                                  int rec_bytes, float* acc, int lane) {
+  for (int w = lane; w < rec_bytes / 4; w += 32)
+    reinterpret_cast<uint32_t*>(stage)[w] = __ldcg(reinterpret_cast<const unsigned int*>(rec_g) + w);
+  __syncwarp();
+  const float s = reinterpret_cast<const float*>(stage)[0];
   for (int j = lane; j < keff; j += 32) {
-    const int idx = rec[4 + j];
-    const int32_t q = (int8_t)rec[4 + k + j];
-    acc[idx] = product_accum(acc[idx], q, s);
+    const int idx = stage[4 + j];
+    acc[idx] = product_accum(acc[idx], (int32_t)(int8_t)stage[4 + k + j], s);
   }
   __syncwarp();
 }
 
+// ------------------------------------------------------------- chunk level
+// Encode chunk c into the shared-memory record `rec` (all threads; ends
+// with __syncthreads).  Blocks past the end are written as empty blocks.
+template <int MODE, typename T>
+__device__ __forceinline__ void encode_chunk(const T* g, const float* pred, const float* ef, int64_t n, int nblk,
+                                             int k, int rec_bytes, const QParams& qp, int c, uint8_t* rec) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int blk = c * kChunkBlocks + warp;
+  if (MODE == kTopK) {
+    uint8_t* r = rec + warp * rec_bytes;
+    if (blk < nblk) {
+      float cv[8];
+      const int valid = load_residual<T>(g, pred, ef, n, blk, lane, qp, cv);
+      topk_select(cv, valid, blk, lane, k, n, qp, const_cast<float*>(ef), r, rec_bytes);
+    } else {
+      for (int w = lane; w < rec_bytes / 4; w += 32) reinterpret_cast<uint32_t*>(r)[w] = 0u;
+    }
+  } else {
+    constexpr int BITS = MODE == kInt4 ? 4 : 8;
+    uint32_t w[2] = {0u, 0u};
+    float s = 0.0f;
+    if (blk < nblk) {
+      float cv[8];
+      int32_t q[8];
+      const int valid = load_residual<T>(g, pred, ef, n, blk, lane, qp, cv);
+      s = encode_dense<BITS>(cv, valid, blk, lane, qp, const_cast<float*>(ef), w, q);
+    }
+    put_dense<BITS>(rec, warp, lane, s, w);
+  }
+  __syncthreads();
+}
+
+__device__ __forceinline__ void copy_record(uint8_t* dst, const uint8_t* rec, int bytes) {
+  const uint4* s = reinterpret_cast<const uint4*>(rec);
+  uint4* d = reinterpret_cast<uint4*>(dst);
+  for (int i = threadIdx.x; i < bytes / 16; i += blockDim.x) d[i] = s[i];
+}
+
+// Decode chunk c: accumulate the W records in rank order, finalize.
+template <int MODE, typename T, typename RecOf>
+__device__ __forceinline__ void decode_chunk(const RecOf& rec_of, int world, T* grad, float* pred, int64_t n, int nblk,
+                                             int k, int rec_bytes, const FParams& fp, int c, uint8_t* stage_smem,
+                                             float* acc_smem) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int blk = c * kChunkBlocks + warp;
+  if (blk >= nblk) return;
+  float acc[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+  if (MODE == kTopK) {
+    float* a = acc_smem + warp * kBlock;
+    uint8_t* stage = stage_smem + warp * kTopkMaxRec;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) a[lane * 8 + j] = 0.0f;
+    __syncwarp();
+    const int keff = min(k, (int)min64(kBlock, n - (int64_t)blk * kBlock));
+    for (int src = 0; src < world; ++src)
+      topk_accum_global(rec_of(src) + warp * rec_bytes, stage, k, keff, rec_bytes, a, lane);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = a[lane * 8 + j];
+    __syncwarp();
+  } else {
+    constexpr int BITS = MODE == kInt4 ? 4 : 8;
+    for (int src = 0; src < world; ++src) accum_dense<BITS>(rec_of(src), warp, lane, acc);
+  }
+  finalize<T>(grad, pred, n, blk, lane, acc, fp);
+}
+
 // ---------------------------------------------------------- flag addressing
-__device__ __forceinline__ uint64_t* flag_ptr(const FusedParams& P, int r, int src, int c) {
+__device__ __forceinline__ uint64_t* col_flag(const FusedParams& P, int r, int kind, int src, int col) {
   return reinterpret_cast<uint64_t*>(P.sym[r] + P.flags_off) +
-         ((int64_t)(P.parity * P.world + src) * P.max_chunks + c);
+         ((int64_t)((P.parity * 2 + kind) * P.world + src) * kMaxCols + col);
 }
-__device__ __forceinline__ uint64_t* rflag_ptr(const FusedParams& P, int r, int c) {
-  return reinterpret_cast<uint64_t*>(P.sym[r] + P.rflags_off) + ((int64_t)P.parity * P.max_chunks + c);
+__device__ __forceinline__ uint8_t* slot_rec(const FusedParams& P, int r, int src, int c) {
+  return P.sym[r] + P.inbox_off + (int64_t)(P.parity * P.world + src) * P.slot_bytes + (int64_t)c * P.chunk_bytes;
 }
-__device__ __forceinline__ uint8_t* slot_ptr(const FusedParams& P, int r, int src) {
-  return P.sym[r] + P.inbox_off + (int64_t)(P.parity * P.world + src) * P.slot_bytes;
-}
-__device__ __forceinline__ uint8_t* result_ptr(const FusedParams& P, int r) {
-  return P.sym[r] + P.result_off + (int64_t)P.parity * P.result_bytes;
+__device__ __forceinline__ uint8_t* result_rec(const FusedParams& P, int r, int c) {
+  return P.sym[r] + P.result_off + (int64_t)P.parity * P.result_bytes +
+         (int64_t)c * chunk_record_bytes(kInt8, 0);
 }
 __device__ __forceinline__ void st_release_u64(uint64_t* p, uint64_t v) {
   asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
@@ -264,222 +340,159 @@ __device__ __forceinline__ uint64_t ld_acquire_u64(const uint64_t* p) {
   asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ uint64_t flag_value(const FusedParams& P) { return ((uint64_t)P.tag << 32) | P.epoch; }
+// The flag carries the epoch (low word) and a tag of (bucket size, bucket
+// id, grid) so ranks that disagree are reported instead of mixing buckets.
+__device__ __forceinline__ uint32_t flag_tag(const FusedParams& P) { return P.tag ^ (gridDim.x * 0x9E3779B1u); }
+__device__ __forceinline__ uint64_t flag_value(const FusedParams& P) {
+  return ((uint64_t)flag_tag(P) << 32) | P.epoch;
+}
 
-// Wait for a flag carrying this call's epoch; verify the tag.  0 = ok.
+// Wait for a flag of this epoch and check its tag: 0 ok, -1 timeout,
+// -2 another CTA failed, 1 tag mismatch.
 __device__ int wait_tagged(const FusedParams& P, const uint64_t* f) {
   uint64_t v = ld_acquire_u64(f);
   if ((uint32_t)v != P.epoch) {
     const uint64_t t0 = globaltimer();
     uint32_t spins = 0;
     while (true) {
-      __nanosleep(64);
+      __nanosleep(32);
       v = ld_acquire_u64(f);
       if ((uint32_t)v == P.epoch) break;
-      if ((++spins & 63u) == 0) {
+      if ((++spins & 31u) == 0) {
         if (globaltimer() - t0 > P.timeout_ns) return -1;
         if (ld_volatile_i32(P.status) != 0) return -2;
       }
     }
   }
-  return ((uint32_t)(v >> 32) == P.tag) ? 0 : 1;
+  return ((uint32_t)(v >> 32) == flag_tag(P)) ? 0 : 1;
 }
 
-// All threads: wait until every peer's flag for chunk c has arrived.  Returns
-// false (uniformly across the CTA) if the CTA must stop.
-__device__ bool wait_chunk(const FusedParams& P, int c, int* s_abort, bool include_self) {
-  const int t = threadIdx.x;
-  if (t < P.world && (include_self || t != P.rank)) {
-    const int rc = wait_tagged(P, flag_ptr(P, P.rank, t, c));
-    if (rc != 0) {
-      if (rc == -1) set_status(P.status, kTimeoutPayload, c, t);
-      else if (rc == 1) set_status(P.status, kBadHeader, c, t);
-      atomicExch(s_abort, 1);
-    }
-  }
+// Release this CTA's column flag of `kind` on every peer (after a barrier
+// that orders all of the CTA's stores before it).
+__device__ __forceinline__ void signal_column(const FusedParams& P, int kind) {
   __syncthreads();
-  return *s_abort == 0;
-}
-__device__ bool wait_result(const FusedParams& P, int c, int* s_abort) {
-  const int owner = c % P.world;
-  if (threadIdx.x == 0) {
-    const int rc = wait_tagged(P, rflag_ptr(P, P.rank, c));
-    if (rc != 0) {
-      if (rc == -1) set_status(P.status, kTimeoutResult, c, owner);
-      else if (rc == 1) set_status(P.status, kBadHeader, c, owner);
-      atomicExch(s_abort, 1);
-    }
-  }
-  __syncthreads();
-  return *s_abort == 0;
-}
-
-// After the CTA's stores for chunk c: release the chunk's flag on the peers.
-// only_peer >= 0 signals just that rank (itself included: the two-shot owner
-// of a chunk may be this rank, read back by another CTA).
-__device__ __forceinline__ void signal_chunk(const FusedParams& P, int c, int only_peer) {
   const int t = threadIdx.x;
-  if (t < P.world && (only_peer < 0 ? t != P.rank : t == only_peer)) {
+  if (t < P.world && t != P.rank) {
     __threadfence_system();
-    st_release_u64(flag_ptr(P, t, P.rank, c), flag_value(P));
+    st_release_u64(col_flag(P, t, kind, P.rank, blockIdx.x), flag_value(P));
   }
+}
+
+// All threads: wait for every peer's column flag of `kind`.  Returns false
+// (uniformly) if the CTA must stop.
+__device__ bool wait_column(const FusedParams& P, int kind, int* s_abort) {
+  const int t = threadIdx.x;
+  if (t < P.world && t != P.rank) {
+    const int rc = wait_tagged(P, col_flag(P, P.rank, kind, t, blockIdx.x));
+    if (rc != 0) {
+      if (rc == -1) set_status(P.status, kind == kFlagPayload ? kTimeoutPayload : kTimeoutResult, blockIdx.x, t);
+      else if (rc == 1) set_status(P.status, kBadHeader, blockIdx.x, t);
+      atomicExch(s_abort, 1);
+    }
+  }
+  __syncthreads();
+  return *s_abort == 0;
 }
 
 // ------------------------------------------------------------------ kernels
-template <int MODE, typename T>
-__device__ __forceinline__ void encode_push(const FusedParams& P, int blk, int lane, int warp, uint8_t* rec_smem,
-                                            int only_peer) {
-  float c[8];
-  const int valid = load_residual<T>(reinterpret_cast<const T*>(P.grad), P.pred, P.ef, P.n, blk, lane, P.q, c);
-  if (MODE == kTopK) {
-    uint8_t* rec = rec_smem + warp * kTopkMaxRec;
-    topk_select(c, valid, blk, lane, P.k, P.n, P.q, P.ef, rec, P.rec_bytes);
-    const int nw = P.rec_bytes / 4;
-    for (int i = 0; i < P.world; ++i) {
-      const int r = (P.rank + 1 + i) % P.world;
-      uint32_t* dst = reinterpret_cast<uint32_t*>(slot_ptr(P, r, P.rank) + (int64_t)blk * P.rec_bytes);
-      for (int w = lane; w < nw; w += 32) dst[w] = reinterpret_cast<const uint32_t*>(rec)[w];
-    }
-  } else {
-    constexpr int BITS = MODE == kInt4 ? 4 : 8;
-    uint32_t w[2];
-    int32_t q[8];
-    const float s = encode_dense<BITS>(c, valid, blk, lane, P.q, P.ef, P.n, w, q);
-    if (only_peer >= 0) {
-      put_dense<BITS>(slot_ptr(P, only_peer, P.rank), P.nblk, blk, lane, s, w);
-    } else {
-      for (int i = 0; i < P.world; ++i) {
-        const int r = (P.rank + 1 + i) % P.world;
-        put_dense<BITS>(slot_ptr(P, r, P.rank), P.nblk, blk, lane, s, w);
-      }
-    }
-  }
-}
+template <int MODE>
+struct Smem {
+  static constexpr int kRec = MODE == kTopK ? kMaxChunkRec : (MODE == kInt4 ? 1056 : 2080);
+  static constexpr int kStage = MODE == kTopK ? kWarps * kTopkMaxRec : 16;
+  static constexpr int kAcc = MODE == kTopK ? kWarps * kBlock : 4;
+};
 
-template <int MODE, typename T>
-__device__ __forceinline__ void decode_finalize(const FusedParams& P, int blk, int lane, int warp, uint8_t* rec_smem,
-                                                float* acc_smem) {
-  float acc[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
-  if (MODE == kTopK) {
-    float* a = acc_smem + warp * kBlock;
-    uint8_t* rec = rec_smem + warp * kTopkMaxRec;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) a[lane * 8 + j] = 0.0f;
-    __syncwarp();
-    const int len = (int)min64(kBlock, P.n - (int64_t)blk * kBlock);
-    const int keff = min(P.k, len);
-    const int nw = P.rec_bytes / 4;
-    for (int src = 0; src < P.world; ++src) {
-      const uint32_t* s = reinterpret_cast<const uint32_t*>(slot_ptr(P, P.rank, src) + (int64_t)blk * P.rec_bytes);
-      for (int w = lane; w < nw; w += 32) reinterpret_cast<uint32_t*>(rec)[w] = __ldcg(s + w);
-      __syncwarp();
-      topk_accum(rec, P.k, keff, a, lane);
-    }
-#pragma unroll
-    for (int j = 0; j < 8; ++j) acc[j] = a[lane * 8 + j];
-    __syncwarp();
-  } else {
-    constexpr int BITS = MODE == kInt4 ? 4 : 8;
-    for (int src = 0; src < P.world; ++src) accum_dense<BITS>(slot_ptr(P, P.rank, src), P.nblk, blk, lane, acc);
-  }
-  finalize<T>(reinterpret_cast<T*>(P.grad), P.pred, P.n, blk, lane, acc, P.f);
-}
-
-// One-shot: every rank pushes its payload to every peer, then reduces all.
 template <int MODE, typename T>
 __global__ void __launch_bounds__(kThreads) oneshot_kernel(FusedParams P) {
   __shared__ int s_abort;
-  __shared__ __align__(16) uint8_t rec_smem[MODE == kTopK ? kWarps * kTopkMaxRec : 16];
-  __shared__ __align__(16) float acc_smem[MODE == kTopK ? kWarps * kBlock : 4];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __shared__ __align__(16) uint8_t rec[Smem<MODE>::kRec];
+  __shared__ __align__(16) uint8_t stage[Smem<MODE>::kStage];
+  __shared__ __align__(16) float acc_smem[Smem<MODE>::kAcc];
   if (threadIdx.x == 0) s_abort = 0;
-  __syncthreads();
-  int prev = -1;
+  const T* g = reinterpret_cast<const T*>(P.grad);
+  // Phase 1: encode each owned chunk and push its record to every rank.
   for (int c = blockIdx.x; c < P.nchunks; c += gridDim.x) {
-    const int blk = c * kChunkBlocks + warp;
-    if (blk < P.nblk) encode_push<MODE, T>(P, blk, lane, warp, rec_smem, -1);
-    __syncthreads();
-    signal_chunk(P, c, -1);
-    if (prev >= 0) {
-      if (!wait_chunk(P, prev, &s_abort, false)) return;
-      const int pb = prev * kChunkBlocks + warp;
-      if (pb < P.nblk) decode_finalize<MODE, T>(P, pb, lane, warp, rec_smem, acc_smem);
+    encode_chunk<MODE, T>(g, P.pred, P.ef, P.n, P.nblk, P.k, P.rec_bytes, P.q, c, rec);
+    for (int i = 0; i < P.world; ++i) {
+      const int r = (P.rank + 1 + i) % P.world;  // self last
+      copy_record(slot_rec(P, r, P.rank, c), rec, P.chunk_bytes);
     }
-    prev = c;
+    __syncthreads();
   }
-  if (prev >= 0) {
-    if (!wait_chunk(P, prev, &s_abort, false)) return;
-    const int pb = prev * kChunkBlocks + warp;
-    if (pb < P.nblk) decode_finalize<MODE, T>(P, pb, lane, warp, rec_smem, acc_smem);
+  signal_column(P, kFlagPayload);
+  // Phase 2: wait for the peers' records of this column, reduce.
+  if (!wait_column(P, kFlagPayload, &s_abort)) return;
+  auto rec_of = [&](int src) { return slot_rec(P, P.rank, src, 0); };
+  for (int c = blockIdx.x; c < P.nchunks; c += gridDim.x) {
+    auto rc = [&](int src) { return rec_of(src) + (int64_t)c * P.chunk_bytes; };
+    decode_chunk<MODE, T>(rc, P.world, reinterpret_cast<T*>(P.grad), P.pred, P.n, P.nblk, P.k, P.rec_bytes, P.f, c,
+                          stage, acc_smem);
   }
 }
 
-// Two-shot for dense modes: reduce-scatter of the compressed payload to the
-// chunk owners, INT8 re-encode of the owned mean residual, all-gather of it.
 template <int MODE, typename T>
 __global__ void __launch_bounds__(kThreads) twoshot_kernel(FusedParams P) {
   constexpr int BITS = MODE == kInt4 ? 4 : 8;
   __shared__ int s_abort;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __shared__ __align__(16) uint8_t rec[2080];
   if (threadIdx.x == 0) s_abort = 0;
-  __syncthreads();
-  // Phase A: encode every chunk, push it to its owner.
-  for (int c = blockIdx.x; c < P.nchunks; c += gridDim.x) {
-    const int owner = c % P.world;
-    const int blk = c * kChunkBlocks + warp;
-    if (blk < P.nblk) encode_push<MODE, T>(P, blk, lane, warp, nullptr, owner);
-    __syncthreads();
-    signal_chunk(P, c, owner);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const T* g = reinterpret_cast<const T*>(P.grad);
+  // Phase A: chunk i of this column goes to its owner rank i mod W.
+  {
+    int i = 0;
+    for (int c = blockIdx.x; c < P.nchunks; c += gridDim.x, ++i) {
+      encode_chunk<MODE, T>(g, P.pred, P.ef, P.n, P.nblk, P.k, P.rec_bytes, P.q, c, rec);
+      copy_record(slot_rec(P, i % P.world, P.rank, c), rec, P.chunk_bytes);
+      __syncthreads();
+    }
   }
-  // Phase B: reduce owned chunks, re-encode as INT8, push to every rank.
-  const int n_owned = (P.nchunks - P.rank + P.world - 1) / P.world;
-  for (int o = blockIdx.x; o < n_owned; o += gridDim.x) {
-    const int c = o * P.world + P.rank;
-    if (!wait_chunk(P, c, &s_abort, true)) return;
-    const int blk = c * kChunkBlocks + warp;
-    if (blk < P.nblk) {
+  signal_column(P, kFlagPayload);
+  if (!wait_column(P, kFlagPayload, &s_abort)) return;
+  // Phase B: reduce owned chunks, re-encode the mean residual as INT8.
+  {
+    int i = 0;
+    for (int c = blockIdx.x; c < P.nchunks; c += gridDim.x, ++i) {
+      if (i % P.world != P.rank) continue;
+      const int blk = c * kChunkBlocks + warp;
       float acc[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
-      for (int src = 0; src < P.world; ++src) accum_dense<BITS>(slot_ptr(P, P.rank, src), P.nblk, blk, lane, acc);
+      if (blk < P.nblk)
+        for (int src = 0; src < P.world; ++src) accum_dense<BITS>(slot_rec(P, P.rank, src, c), warp, lane, acc);
       float m[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) m[j] = NGL_FMUL(acc[j], P.f.inv_world);
       const float s2 = product_scale(block_absmax(m), 127.0f);
       const float inv2 = product_inv(s2);
-      uint32_t lo = 0, hi = 0;
+      uint32_t w[2] = {0u, 0u};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        lo |= ((uint32_t)product_code_rn(m[j], inv2, 127) & 0xffu) << (8 * j);
-        hi |= ((uint32_t)product_code_rn(m[4 + j], inv2, 127) & 0xffu) << (8 * j);
+        w[0] |= ((uint32_t)product_code_rn(m[j], inv2, 127) & 0xffu) << (8 * j);
+        w[1] |= ((uint32_t)product_code_rn(m[4 + j], inv2, 127) & 0xffu) << (8 * j);
       }
-      const uint32_t w[2] = {lo, hi};
-      for (int i = 0; i < P.world; ++i) {
-        const int r = (P.rank + 1 + i) % P.world;
-        put_dense<8>(result_ptr(P, r), P.nblk, blk, lane, s2, w);
+      put_dense<8>(rec, warp, lane, s2, w);
+      __syncthreads();
+      for (int t = 0; t < P.world; ++t) {
+        const int r = (P.rank + 1 + t) % P.world;
+        copy_record(result_rec(P, r, c), rec, chunk_record_bytes(kInt8, 0));
       }
-    }
-    __syncthreads();
-    if (threadIdx.x < P.world) {
-      __threadfence_system();
-      st_release_u64(rflag_ptr(P, threadIdx.x, c), flag_value(P));
+      __syncthreads();
     }
   }
-  // Phase C: decode the owners' INT8 results.
+  signal_column(P, kFlagResult);
+  if (!wait_column(P, kFlagResult, &s_abort)) return;
+  // Phase C: decode the owners' INT8 records.
+  FParams f = P.f;
+  f.inv_world = 1.0f;
   for (int c = blockIdx.x; c < P.nchunks; c += gridDim.x) {
-    if (!wait_result(P, c, &s_abort)) return;
     const int blk = c * kChunkBlocks + warp;
-    if (blk < P.nblk) {
-      float acc[8];
+    if (blk >= P.nblk) continue;
+    float acc[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
-      accum_dense<8>(result_ptr(P, P.rank), P.nblk, blk, lane, acc);
-      FParams f = P.f;
-      f.inv_world = 1.0f;
-      finalize<T>(reinterpret_cast<T*>(P.grad), P.pred, P.n, blk, lane, acc, f);
-    }
+    for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+    accum_dense<8>(result_rec(P, P.rank, c), warp, lane, acc);
+    finalize<T>(reinterpret_cast<T*>(P.grad), P.pred, P.n, blk, lane, acc, f);
   }
 }
 
@@ -499,7 +512,7 @@ __global__ void __launch_bounds__(kThreads) single_kernel(FusedParams P) {
       constexpr int BITS = MODE == kInt4 ? 4 : 8;
       uint32_t w[2];
       int32_t q[8];
-      const float s = encode_dense<BITS>(c, valid, blk, lane, P.q, P.ef, P.n, w, q);
+      const float s = encode_dense<BITS>(c, valid, blk, lane, P.q, P.ef, w, q);
 #pragma unroll
       for (int j = 0; j < 8; ++j) acc[j] = product_accum(0.0f, q[j], s);
     }
@@ -508,76 +521,43 @@ __global__ void __launch_bounds__(kThreads) single_kernel(FusedParams P) {
 }
 
 // ------------------------------------------ single-GPU building-block kernels
-// Encode one rank's payload into a local buffer (test oracle comparisons and
-// multi-rank emulation on one GPU).
+// Encode one rank's wire payload into a local buffer (oracle comparisons
+// and multi-rank emulation on one GPU).
 template <int MODE, typename T>
 __global__ void __launch_bounds__(kThreads) encode_kernel(const T* g, const float* pred, const float* ef_in,
-                                                          float* ef_out, int64_t n, int nblk, int k, int rec_bytes,
-                                                          QParams qp, uint8_t* out) {
-  __shared__ __align__(16) uint8_t rec_smem[MODE == kTopK ? kWarps * kTopkMaxRec : 16];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int blk = blockIdx.x * kWarps + warp; blk < nblk; blk += gridDim.x * kWarps) {
-    float c[8];
-    const int valid = load_residual<T>(g, pred, ef_in, n, blk, lane, qp, c);
-    if (MODE == kTopK) {
-      uint8_t* rec = rec_smem + warp * kTopkMaxRec;
-      topk_select(c, valid, blk, lane, k, n, qp, ef_out, rec, rec_bytes);
-      uint32_t* dst = reinterpret_cast<uint32_t*>(out + (int64_t)blk * rec_bytes);
-      for (int w = lane; w < rec_bytes / 4; w += 32) dst[w] = reinterpret_cast<const uint32_t*>(rec)[w];
-      __syncwarp();
-    } else {
-      constexpr int BITS = MODE == kInt4 ? 4 : 8;
-      uint32_t w[2];
-      int32_t q[8];
-      const float s = encode_dense<BITS>(c, valid, blk, lane, qp, ef_out, n, w, q);
-      put_dense<BITS>(out, nblk, blk, lane, s, w);
+                                                          float* ef_out, int64_t n, int nblk, int nchunks, int k,
+                                                          int rec_bytes, int chunk_bytes, QParams qp, uint8_t* out) {
+  __shared__ __align__(16) uint8_t rec[Smem<MODE>::kRec];
+  // ef_in and ef_out may differ here: copy-through by encoding from ef_in and
+  // storing into ef_out (the fused kernels update in place).
+  for (int c = blockIdx.x; c < nchunks; c += gridDim.x) {
+    if (ef_in != ef_out && ef_in != nullptr) {
+      // The encoders read EF through `ef` and write through the same pointer;
+      // stage the chunk's EF into ef_out first so the in-place path applies.
+      const int64_t e0 = (int64_t)c * kChunkBlocks * kBlock;
+      const int64_t e1 = min64(n, e0 + (int64_t)kChunkBlocks * kBlock);
+      for (int64_t i = e0 + threadIdx.x; i < e1; i += blockDim.x) ef_out[i] = ef_in[i];
+      __syncthreads();
     }
+    encode_chunk<MODE, T>(g, pred, ef_out, n, nblk, k, rec_bytes, qp, c, rec);
+    copy_record(out + (int64_t)c * chunk_bytes, rec, chunk_bytes);
+    __syncthreads();
   }
 }
 
 template <int MODE, typename T>
 __global__ void __launch_bounds__(kThreads) reduce_kernel(ReduceSrcs srcs, int world, T* out, float* pred, int64_t n,
-                                                          int nblk, int k, int rec_bytes, FParams fp) {
-  __shared__ __align__(16) uint8_t rec_smem[MODE == kTopK ? kWarps * kTopkMaxRec : 16];
-  __shared__ __align__(16) float acc_smem[MODE == kTopK ? kWarps * kBlock : 4];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int blk = blockIdx.x * kWarps + warp; blk < nblk; blk += gridDim.x * kWarps) {
-    float acc[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
-    if (MODE == kTopK) {
-      float* a = acc_smem + warp * kBlock;
-      uint8_t* rec = rec_smem + warp * kTopkMaxRec;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) a[lane * 8 + j] = 0.0f;
-      __syncwarp();
-      const int len = (int)min64(kBlock, n - (int64_t)blk * kBlock);
-      const int keff = min(k, len);
-      for (int src = 0; src < world; ++src) {
-        const uint32_t* s = reinterpret_cast<const uint32_t*>(srcs.p[src] + (int64_t)blk * rec_bytes);
-        for (int w = lane; w < rec_bytes / 4; w += 32) reinterpret_cast<uint32_t*>(rec)[w] = s[w];
-        __syncwarp();
-        topk_accum(rec, k, keff, a, lane);
-      }
-#pragma unroll
-      for (int j = 0; j < 8; ++j) acc[j] = a[lane * 8 + j];
-      __syncwarp();
-    } else {
-      constexpr int BITS = MODE == kInt4 ? 4 : 8;
-      for (int src = 0; src < world; ++src) accum_dense<BITS>(srcs.p[src], nblk, blk, lane, acc);
-    }
-    finalize<T>(out, pred, n, blk, lane, acc, fp);
+                                                          int nblk, int nchunks, int k, int rec_bytes,
+                                                          int chunk_bytes, FParams fp) {
+  __shared__ __align__(16) uint8_t stage[Smem<MODE>::kStage];
+  __shared__ __align__(16) float acc_smem[Smem<MODE>::kAcc];
+  for (int c = blockIdx.x; c < nchunks; c += gridDim.x) {
+    auto rc = [&](int src) { return srcs.p[src] + (int64_t)c * chunk_bytes; };
+    decode_chunk<MODE, T>(rc, world, out, pred, n, nblk, k, rec_bytes, fp, c, stage, acc_smem);
   }
 }
 
-}  // namespace dev
-}  // namespace ngl
-
-
 // ------------------------------------------------------------- launchers
-namespace ngl {
-namespace dev {
-
 #define NGL_DISPATCH(MODE, DT, ...)                                               \
   [&] {                                                                           \
     if ((DT) == kF32) {                                                           \
@@ -592,6 +572,36 @@ namespace dev {
       else { constexpr int M = kTopK; __VA_ARGS__(); }                            \
     }                                                                             \
   }()
+
+int fused_grid(int nchunks, int mode, int dtype, int variant, int cap, int device) {
+  static int occ_cache[3][2][3] = {};
+  static int sms = 0;
+  if (sms == 0) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  int& occ = occ_cache[variant][dtype][mode];
+  if (occ == 0) {
+    int v = 1;
+    NGL_DISPATCH(mode, dtype, [&] {
+      if (variant == kVariantTwoShot) {
+        if constexpr (M != kTopK) cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, twoshot_kernel<M, T>, kThreads, 0);
+      } else if (variant == kVariantOneShot) {
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, oneshot_kernel<M, T>, kThreads, 0);
+      } else {
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, single_kernel<M, T>, kThreads, 0);
+      }
+    });
+    occ = v > 0 ? v : 1;
+  }
+  int g = occ * sms;
+  if (variant == kVariantSingle) {
+    g = 4 * sms;
+    const int need = nchunks;  // one chunk = kWarps blocks = one CTA iteration
+    return need < g ? (need > 0 ? need : 1) : g;
+  }
+  if (cap > 0 && cap < g) g = cap;
+  if (g > kMaxCols) g = kMaxCols;
+  if (nchunks < g) g = nchunks;
+  return g > 0 ? g : 1;
+}
 
 cudaError_t launch_fused(const FusedParams& P, int mode, int dtype, int variant, int grid, cudaStream_t stream) {
   if (variant == kVariantSingle) {
@@ -609,10 +619,12 @@ cudaError_t launch_fused(const FusedParams& P, int mode, int dtype, int variant,
 cudaError_t launch_encode(const void* g, const float* pred, const float* ef_in, float* ef_out, int64_t n, int k,
                           const QParams& qp, uint8_t* out, int mode, int dtype, int grid, cudaStream_t stream) {
   const int nblk = (int)((n + kBlock - 1) / kBlock);
+  const int nchunks = (nblk + kChunkBlocks - 1) / kChunkBlocks;
   const int rec = topk_record_bytes(k);
+  const int cb = chunk_record_bytes(mode, k);
   NGL_DISPATCH(mode, dtype, [&] {
     encode_kernel<M, T><<<grid, kThreads, 0, stream>>>(reinterpret_cast<const T*>(g), pred, ef_in, ef_out, n, nblk,
-                                                      k, rec, qp, out);
+                                                      nchunks, k, rec, cb, qp, out);
   });
   return cudaGetLastError();
 }
@@ -620,10 +632,12 @@ cudaError_t launch_encode(const void* g, const float* pred, const float* ef_in, 
 cudaError_t launch_reduce(const ReduceSrcs& srcs, int world, void* out, float* pred, int64_t n, int k,
                           const FParams& fp, int mode, int dtype, int grid, cudaStream_t stream) {
   const int nblk = (int)((n + kBlock - 1) / kBlock);
+  const int nchunks = (nblk + kChunkBlocks - 1) / kChunkBlocks;
   const int rec = topk_record_bytes(k);
+  const int cb = chunk_record_bytes(mode, k);
   NGL_DISPATCH(mode, dtype, [&] {
-    reduce_kernel<M, T><<<grid, kThreads, 0, stream>>>(srcs, world, reinterpret_cast<T*>(out), pred, n, nblk, k,
-                                                      rec, fp);
+    reduce_kernel<M, T><<<grid, kThreads, 0, stream>>>(srcs, world, reinterpret_cast<T*>(out), pred, n, nblk,
+                                                      nchunks, k, rec, cb, fp);
   });
   return cudaGetLastError();
 }

@@ -140,17 +140,16 @@ PYBIND11_MODULE(_host, m) {
   });
   m.def("lammps_generate_synthetic", [](size_t p, size_t s) { return to_np(lammps_generate_synthetic(p, s)); });
 
-  // Product format oracle
+  // Product format oracle (chunked wire payloads)
+  m.def("product_wire_bytes", &product_wire_bytes);
   m.def("product_encode", [](carr<float> g, py::object pred, py::object e_in, int bits, bool stochastic, bool ef,
                              uint64_t seed, uint32_t rank, uint32_t bucket, uint64_t step) {
     const size_t n = g.size();
-    const size_t nblk = (n + 255) / 256;
     carr<float> pr = pred.is_none() ? carr<float>() : pred.cast<carr<float>>();
     carr<float> ei = e_in.is_none() ? carr<float>() : e_in.cast<carr<float>>();
     if (!pred.is_none() && (size_t)pr.size() != n) throw std::runtime_error("pred size mismatch");
     if (!e_in.is_none() && (size_t)ei.size() != n) throw std::runtime_error("e size mismatch");
-    std::vector<float> scales(nblk);
-    std::vector<uint8_t> codes(nblk * (bits == 4 ? 128 : 256));
+    std::vector<uint8_t> wire(product_wire_bytes(n, bits == 4 ? 0 : 1, 0));
     std::vector<float> e_out(ef ? n : 0);
     ProductParams p;
     p.bits = bits;
@@ -161,38 +160,25 @@ PYBIND11_MODULE(_host, m) {
     p.bucket = bucket;
     p.step = step;
     product_encode(ptr(g), pred.is_none() ? nullptr : ptr(pr), e_in.is_none() ? nullptr : ptr(ei), n, p,
-                   scales.data(), codes.data(), ef ? e_out.data() : nullptr);
-    return py::make_tuple(to_np(std::move(scales)), to_np(std::move(codes)), to_np(std::move(e_out)));
+                   wire.data(), ef ? e_out.data() : nullptr);
+    return py::make_tuple(to_np(std::move(wire)), to_np(std::move(e_out)));
   });
-  m.def("product_reduce", [](std::vector<carr<float>> scales, std::vector<carr<uint8_t>> codes, size_t n, int bits,
-                             py::object pred, float inv_world) {
-    const int W = (int)scales.size();
-    std::vector<const float*> sp(W);
-    std::vector<const uint8_t*> cp(W);
-    for (int r = 0; r < W; ++r) {
-      sp[r] = ptr(scales[r]);
-      cp[r] = ptr(codes[r]);
-    }
-    carr<float> pr = pred.is_none() ? carr<float>() : pred.cast<carr<float>>();
-    std::vector<float> avg(n);
-    product_reduce(sp.data(), cp.data(), W, n, bits, pred.is_none() ? nullptr : ptr(pr), inv_world, avg.data());
-    return to_np(std::move(avg));
-  });
-  m.def("product_reduce_twoshot", [](std::vector<carr<float>> scales, std::vector<carr<uint8_t>> codes, size_t n,
-                                     int bits, py::object pred, float inv_world) {
-    const int W = (int)scales.size();
-    std::vector<const float*> sp(W);
-    std::vector<const uint8_t*> cp(W);
-    for (int r = 0; r < W; ++r) {
-      sp[r] = ptr(scales[r]);
-      cp[r] = ptr(codes[r]);
-    }
-    carr<float> pr = pred.is_none() ? carr<float>() : pred.cast<carr<float>>();
-    std::vector<float> avg(n);
-    product_reduce_twoshot(sp.data(), cp.data(), W, n, bits, pred.is_none() ? nullptr : ptr(pr), inv_world,
-                           avg.data());
-    return to_np(std::move(avg));
-  });
+  auto reduce_impl = [](bool twoshot) {
+    return [twoshot](std::vector<carr<uint8_t>> wires, size_t n, int bits, py::object pred, float inv_world) {
+      const int W = (int)wires.size();
+      std::vector<const uint8_t*> wp(W);
+      for (int r = 0; r < W; ++r) wp[r] = ptr(wires[r]);
+      carr<float> pr = pred.is_none() ? carr<float>() : pred.cast<carr<float>>();
+      std::vector<float> avg(n);
+      if (twoshot)
+        product_reduce_twoshot(wp.data(), W, n, bits, pred.is_none() ? nullptr : ptr(pr), inv_world, avg.data());
+      else
+        product_reduce(wp.data(), W, n, bits, pred.is_none() ? nullptr : ptr(pr), inv_world, avg.data());
+      return to_np(std::move(avg));
+    };
+  };
+  m.def("product_reduce", reduce_impl(false));
+  m.def("product_reduce_twoshot", reduce_impl(true));
   m.def("product_ema", [](carr<float> state, carr<float> avg, float beta, bool first) {
     std::vector<float> s(state.data(), state.data() + state.size());
     product_ema(s.data(), ptr(avg), s.size(), beta, first);
@@ -200,10 +186,9 @@ PYBIND11_MODULE(_host, m) {
   });
   m.def("product_topk_encode", [](carr<float> g, py::object pred, py::object e_in, int k, bool ef) {
     const size_t n = g.size();
-    const size_t nblk = (n + 255) / 256;
     carr<float> pr = pred.is_none() ? carr<float>() : pred.cast<carr<float>>();
     carr<float> ei = e_in.is_none() ? carr<float>() : e_in.cast<carr<float>>();
-    std::vector<uint8_t> rec(nblk * ngl::host::Bytes::size_type(((4 + 2 * k + 3) & ~3)));
+    std::vector<uint8_t> rec(product_wire_bytes(n, 2, k));
     std::vector<float> e_out(ef ? n : 0);
     product_topk_encode(ptr(g), pred.is_none() ? nullptr : ptr(pr), e_in.is_none() ? nullptr : ptr(ei), n, k, ef,
                         rec.data(), ef ? e_out.data() : nullptr);

@@ -148,19 +148,21 @@ struct ProductParams {
   uint32_t bucket = 0;
   uint64_t step = 0;
 };
-// Encode one rank's residual c = g - pred + e into per-256-block scales and
-// packed codes; writes the new error-feedback buffer when e_out != nullptr.
+// Encode one rank's residual c = g - pred + e into the chunked wire payload
+// (product_wire_bytes bytes); writes the new error feedback when e_out is set.
+size_t product_wire_bytes(size_t n, int mode, int k);
 void product_encode(const float* g, const float* pred, const float* e_in, size_t n, const ProductParams& p,
-                    float* scales, uint8_t* codes, float* e_out);
-// Rank-ordered reduction of W payloads: avg = pred + (sum_r q_r s_r) / W and
-// the EMA predictor update.  `first` copies avg into the state.
-void product_reduce(const float* const* scales, const uint8_t* const* codes, int world, size_t n, int bits,
-                    const float* pred, float inv_world, float* avg_out);
-void product_reduce_twoshot(const float* const* scales, const uint8_t* const* codes, int world, size_t n, int bits,
-                            const float* pred, float inv_world, float* avg_out);
+                    uint8_t* wire, float* e_out);
+// Rank-ordered reduction of W payloads: avg = pred + (sum_r q_r s_r) / W.
+void product_reduce(const uint8_t* const* wires, int world, size_t n, int bits, const float* pred, float inv_world,
+                    float* avg_out);
+// Two-shot: the mean residual re-encoded as INT8 per block, then decoded.
+void product_reduce_twoshot(const uint8_t* const* wires, int world, size_t n, int bits, const float* pred,
+                            float inv_world, float* avg_out);
+// EMA predictor update; `first` copies avg into the state.
 void product_ema(float* state, const float* avg, size_t n, float beta, bool first);
-// Per-256-block top-k: encode fixed-size records (scale, ascending indices,
-// int8 values); decode-sum in rank order.
+// Per-256-block top-k: fixed-size records (scale, ascending indices, int8
+// values), 8 per chunk; decode-sum in rank order.
 void product_topk_encode(const float* g, const float* pred, const float* e_in, size_t n, int k, bool ef,
                          uint8_t* records, float* e_out);
 void product_topk_reduce(const uint8_t* const* records, int world, size_t n, int k, const float* pred,

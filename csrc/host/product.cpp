@@ -10,13 +10,32 @@
 namespace ngl {
 namespace host {
 
+namespace {
+inline size_t nchunks_of(size_t n) { return ((n + kBlock - 1) / kBlock + kChunkBlocks - 1) / kChunkBlocks; }
+// Block b of a dense chunked payload: scale and code pointers.
+inline float* dense_scale(uint8_t* wire, size_t b, size_t cr) {
+  return reinterpret_cast<float*>(wire + (b / kChunkBlocks) * cr) + (b % kChunkBlocks);
+}
+inline uint8_t* dense_codes(uint8_t* wire, size_t b, size_t cr, size_t bpb) {
+  return wire + (b / kChunkBlocks) * cr + 4 * kChunkBlocks + (b % kChunkBlocks) * bpb;
+}
+inline float dense_scale_c(const uint8_t* wire, size_t b, size_t cr) {
+  float s;
+  std::memcpy(&s, wire + (b / kChunkBlocks) * cr + 4 * (b % kChunkBlocks), 4);
+  return s;
+}
+}  // namespace
+
+size_t product_wire_bytes(size_t n, int mode, int k) { return nchunks_of(n) * (size_t)chunk_record_bytes(mode, k); }
+
 void product_encode(const float* g, const float* pred, const float* e_in, size_t n, const ProductParams& p,
-                    float* scales, uint8_t* codes, float* e_out) {
+                    uint8_t* wire, float* e_out) {
   const int32_t qmax = p.bits == 4 ? 7 : 127;
   const float qmaxf = (float)qmax;
   const size_t nblk = (n + kBlock - 1) / kBlock;
   const size_t bpb = p.bits == 4 ? kInt4BlockBytes : kInt8BlockBytes;
-  std::memset(codes, 0, nblk * bpb);
+  const size_t cr = chunk_record_bytes(p.bits == 4 ? 0 : 1, 0);
+  std::memset(wire, 0, nchunks_of(n) * cr);
   float c[kBlock];
   int32_t q[kBlock];
   for (size_t b = 0; b < nblk; ++b) {
@@ -35,7 +54,7 @@ void product_encode(const float* g, const float* pred, const float* e_in, size_t
     }
     const float s = product_scale(absmax, qmaxf);
     const float inv = product_inv(s);
-    scales[b] = s;
+    *dense_scale(wire, b, cr) = s;
     for (size_t i = 0; i < kBlock; i += 4) {
       U32x4 r = {0, 0, 0, 0};
       if (p.stochastic) r = product_noise4(p.seed, p.rank, p.bucket, p.step, (uint32_t)((base + i) / 4));
@@ -50,7 +69,7 @@ void product_encode(const float* g, const float* pred, const float* e_in, size_t
         if (p.error_feedback && e_out) e_out[base + k] = NGL_FSUB(c[k], product_deq(q[k], s));
       }
     }
-    uint8_t* out = codes + b * bpb;
+    uint8_t* out = dense_codes(wire, b, cr, bpb);
     if (p.bits == 4) {
       for (size_t j = 0; j < kInt4BlockBytes; ++j) out[j] = (uint8_t)((nib(q[2 * j]) << 4) | nib(q[2 * j + 1]));
     } else {
@@ -59,14 +78,15 @@ void product_encode(const float* g, const float* pred, const float* e_in, size_t
   }
 }
 
-void product_reduce(const float* const* scales, const uint8_t* const* codes, int world, size_t n, int bits,
-                    const float* pred, float inv_world, float* avg_out) {
+void product_reduce(const uint8_t* const* wires, int world, size_t n, int bits, const float* pred, float inv_world,
+                    float* avg_out) {
   const size_t bpb = bits == 4 ? kInt4BlockBytes : kInt8BlockBytes;
+  const size_t cr = chunk_record_bytes(bits == 4 ? 0 : 1, 0);
   for (size_t i = 0; i < n; ++i) {
     const size_t b = i / kBlock, k = i % kBlock;
     float acc = 0.0f;
     for (int r = 0; r < world; ++r) {
-      const uint8_t* blk = codes[r] + b * bpb;
+      const uint8_t* blk = dense_codes(const_cast<uint8_t*>(wires[r]), b, cr, bpb);
       int32_t q;
       if (bits == 4) {
         uint32_t byte = blk[k / 2];
@@ -74,7 +94,7 @@ void product_reduce(const float* const* scales, const uint8_t* const* codes, int
       } else {
         q = (int8_t)blk[k];
       }
-      acc = product_accum(acc, q, scales[r][b]);
+      acc = product_accum(acc, q, dense_scale_c(wires[r], b, cr));
     }
     avg_out[i] = product_average(pred ? pred[i] : 0.0f, acc, inv_world);
   }
@@ -97,7 +117,7 @@ void product_topk_encode(const float* g, const float* pred, const float* e_in, s
                          uint8_t* records, float* e_out) {
   const size_t nblk = (n + kBlock - 1) / kBlock;
   const int rb = topk_record_bytes(k);
-  std::memset(records, 0, nblk * rb);
+  std::memset(records, 0, nchunks_of(n) * kChunkBlocks * rb);
   float c[kBlock];
   uint32_t mag[kBlock];
   for (size_t b = 0; b < nblk; ++b) {
@@ -171,9 +191,10 @@ void product_topk_reduce(const uint8_t* const* records, int world, size_t n, int
 
 // Two-shot: the chunk owner reduces, re-encodes the mean residual as INT8
 // with per-block scales (round to nearest), every rank decodes that.
-void product_reduce_twoshot(const float* const* scales, const uint8_t* const* codes, int world, size_t n, int bits,
-                            const float* pred, float inv_world, float* avg_out) {
+void product_reduce_twoshot(const uint8_t* const* wires, int world, size_t n, int bits, const float* pred,
+                            float inv_world, float* avg_out) {
   const size_t bpb = bits == 4 ? kInt4BlockBytes : kInt8BlockBytes;
+  const size_t cr = chunk_record_bytes(bits == 4 ? 0 : 1, 0);
   const size_t nblk = (n + kBlock - 1) / kBlock;
   float m[kBlock];
   for (size_t b = 0; b < nblk; ++b) {
@@ -184,7 +205,7 @@ void product_reduce_twoshot(const float* const* scales, const uint8_t* const* co
       float acc = 0.0f;
       if (k < len) {
         for (int r = 0; r < world; ++r) {
-          const uint8_t* blk = codes[r] + b * bpb;
+          const uint8_t* blk = dense_codes(const_cast<uint8_t*>(wires[r]), b, cr, bpb);
           int32_t q;
           if (bits == 4) {
             uint32_t byte = blk[k / 2];
@@ -192,7 +213,7 @@ void product_reduce_twoshot(const float* const* scales, const uint8_t* const* co
           } else {
             q = (int8_t)blk[k];
           }
-          acc = product_accum(acc, q, scales[r][b]);
+          acc = product_accum(acc, q, dense_scale_c(wires[r], b, cr));
         }
       }
       m[k] = NGL_FMUL(acc, inv_world);

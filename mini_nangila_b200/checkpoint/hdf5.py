@@ -1,0 +1,125 @@
+"""Chunked error-bounded checkpoint layout (nangila-checkpoint/src/lib.rs).
+
+``write_chunked_dataset`` splits a 1-D float array into ``chunk``-sized
+pieces (the last zero-padded), runs the LinearPredictor closed loop across
+chunks with the ErrorBounded INT16 quantizer (the codec string is only a
+label) and stores, under group ``dataset``:
+
+* ``blob``   u8[]                    concatenated payloads
+* ``offsets`` u64[num_chunks + 1]    payload boundaries in ``blob``
+* ``scales`` f32[num_chunks]
+* attrs ``total_len`` (u64), ``chunk`` (u64), ``codec`` (str), ``epsilon`` (f32)
+
+``read_compressed_1d`` reverses it.  With h5py installed the file is HDF5
+with exactly these names; without it the same arrays and attributes go into
+an ``.npz`` archive (keys ``<dataset>/blob`` ... and ``<dataset>/@attr``).
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from ..core.fixed_point import FixedPointBuffer
+from ..hpc import ErrorBoundedQuantizer, LinearPredictor
+
+try:  # optional dependency
+    import h5py  # type: ignore
+except ImportError:  # pragma: no cover - depends on the environment
+    h5py = None
+
+
+def _encode_chunks(data: np.ndarray, chunk: int, epsilon: float):
+    chunk = max(1, int(chunk))
+    total = data.size
+    nch = (total + chunk - 1) // chunk
+    pred = LinearPredictor()
+    q = ErrorBoundedQuantizer(epsilon)
+    blob, offsets, scales = bytearray(), [0], []
+    for c in range(nch):
+        buf = np.zeros(chunk, np.float32)
+        seg = data[c * chunk:(c + 1) * chunk]
+        buf[: seg.size] = seg
+        x = FixedPointBuffer.from_f32(buf)
+        p = pred.predict()
+        r = x.clone() if p.is_empty() else x.sub(p)
+        b, s = q.quantize(r)
+        scales.append(s)
+        d = q.dequantize(b, s)
+        pred.update(d if p.is_empty() else p.add(d))
+        blob += b
+        offsets.append(len(blob))
+    return np.frombuffer(bytes(blob), np.uint8), np.asarray(offsets, np.uint64), np.asarray(scales, np.float32)
+
+
+def _decode_chunks(blob, offsets, scales, total_len: int, epsilon: float) -> np.ndarray:
+    pred = LinearPredictor()
+    q = ErrorBoundedQuantizer(epsilon)
+    out = []
+    for c in range(len(scales)):
+        b = blob[int(offsets[c]):int(offsets[c + 1])]
+        p = pred.predict()
+        d = q.dequantize(b, float(scales[c]))
+        r = d if p.is_empty() else p.add(d)
+        pred.update(r)
+        out.append(r.to_f32())
+    v = np.concatenate(out) if out else np.zeros(0, np.float32)
+    return v[:total_len]
+
+
+def write_chunked_dataset(path: str, dataset: str, data, chunk: int, epsilon: float, codec: str) -> None:
+    data = np.ascontiguousarray(np.asarray(data, np.float32).reshape(-1))
+    blob, offsets, scales = _encode_chunks(data, chunk, epsilon)
+    attrs = {"total_len": np.uint64(data.size), "chunk": np.uint64(max(1, int(chunk))), "codec": codec,
+             "epsilon": np.float32(epsilon)}
+    if h5py is not None:
+        with h5py.File(path, "w") as f:
+            g = f.create_group(dataset)
+            g.create_dataset("blob", data=blob)
+            g.create_dataset("offsets", data=offsets)
+            g.create_dataset("scales", data=scales)
+            for k, v in attrs.items():
+                g.attrs[k] = v
+        return
+    arrays = {f"{dataset}/blob": blob, f"{dataset}/offsets": offsets, f"{dataset}/scales": scales}
+    arrays.update({f"{dataset}/@{k}": np.asarray(v) for k, v in attrs.items()})
+    with open(path, "wb") as fh:
+        np.savez(fh, **arrays)
+
+
+def read_compressed_1d(path: str, dataset: str) -> np.ndarray:
+    if h5py is not None:
+        with h5py.File(path, "r") as f:
+            g = f[dataset]
+            return _decode_chunks(g["blob"][()], g["offsets"][()], g["scales"][()], int(g.attrs["total_len"]),
+                                  float(g.attrs["epsilon"]))
+    with np.load(path) as z:
+        return _decode_chunks(z[f"{dataset}/blob"], z[f"{dataset}/offsets"], z[f"{dataset}/scales"],
+                              int(z[f"{dataset}/@total_len"]), float(z[f"{dataset}/@epsilon"]))
+
+
+def write_dataset(path: str, dataset: str, data, epsilon: float, codec: str) -> None:
+    data = np.asarray(data, np.float32).reshape(-1)
+    if h5py is not None:
+        with h5py.File(path, "a") as f:
+            ds = f.create_dataset(dataset, data=data)
+            ds.attrs["epsilon"] = np.float32(epsilon)
+            ds.attrs["codec"] = codec
+        return
+    existing = {}
+    try:
+        with np.load(path) as z:
+            existing = {k: z[k] for k in z.files}
+    except (OSError, ValueError):
+        pass
+    existing[dataset] = data
+    existing[f"{dataset}@epsilon"] = np.float32(epsilon)
+    existing[f"{dataset}@codec"] = np.asarray(codec)
+    with open(path, "wb") as fh:
+        np.savez(fh, **existing)
+
+
+def read_dataset(path: str, dataset: str) -> np.ndarray:
+    if h5py is not None:
+        with h5py.File(path, "r") as f:
+            return f[dataset][()]
+    with np.load(path) as z:
+        return z[dataset]

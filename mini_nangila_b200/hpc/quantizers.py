@@ -1,0 +1,80 @@
+"""HPC-domain error-bounded codecs (nangila-hpc): all quantize with
+``q = round(x / 2eps)`` to INT16 (|err| <= eps while |q| fits), then:
+
+* ``ErrorBoundedQuantizer``: q as little-endian i16 (error_bounded.rs);
+* ``RunLengthQuantizer``: opcode stream, ``0x80+count-1`` for a run of up to
+  128 zeros, ``count-1`` followed by up to 128 i16 literals (rle.rs);
+* ``BlockSparseQuantizer``: ``[u32 n]`` then per 32-block ``[u32 mask]`` and an
+  i16 per non-zero (block_sparse.rs);
+* ``BlockSparseRleQuantizer``: ``[u32 n]`` then runs of zero-mask blocks
+  ``0x80|(count-1)`` or literal runs ``count-1`` + count x ``[mask][i16...]``
+  (block_sparse_rle.rs).
+
+Device buffers (``residual.data.is_cuda``) run the sm_100a codec kernels
+and produce the same bytes.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from .._ext import host
+from ..core.fixed_point import FixedPointBuffer
+from ..core.quantizer import as_u8, host_i32, to_bytes
+
+
+def _dev():
+    from ..ops import codecs
+
+    return codecs
+
+
+class _EBBase:
+    _name = ""
+
+    def __init__(self, epsilon: float):
+        self.epsilon = float(np.float32(epsilon))
+
+    def quantize(self, residual: FixedPointBuffer):
+        if residual.data.is_cuda:
+            return getattr(_dev(), f"{self._name}_quantize")(residual.data, self.epsilon)
+        b, s = getattr(host(), f"{self._name}_quantize")(host_i32(residual), self.epsilon)
+        return to_bytes(b), float(s)
+
+    def dequantize(self, compressed, scale: float, device=None) -> FixedPointBuffer:
+        b = as_u8(compressed)
+        if device is not None and str(device).startswith("cuda"):
+            import torch
+
+            return FixedPointBuffer(getattr(_dev(), f"{self._name}_dequantize")(torch.from_numpy(b).to(device),
+                                                                               float(scale)))
+        return FixedPointBuffer(getattr(host(), f"{self._name}_dequantize")(b, float(np.float32(scale))))
+
+
+class ErrorBoundedQuantizer(_EBBase):
+    _name = "eb"
+
+
+class RunLengthQuantizer(_EBBase):
+    _name = "rle"
+
+
+class BlockSparseQuantizer(_EBBase):
+    _name = "bs"
+    block_size = 32
+
+
+class BlockSparseRleQuantizer(_EBBase):
+    _name = "bsrle"
+    block_size = 32
+
+
+class QuantizerError(ValueError):
+    """``FallbackRequired`` exists in the reference but is never produced."""
+
+
+def rle_encode_i16(q) -> bytes:
+    return to_bytes(host().rle_encode_i16(np.ascontiguousarray(np.asarray(q, dtype=np.int16))))
+
+
+def rle_decode_i16(b) -> np.ndarray:
+    return host().rle_decode_i16(as_u8(b))

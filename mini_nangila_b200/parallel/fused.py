@@ -57,31 +57,39 @@ def topk_record_bytes(k: int) -> int:
     return (4 + 2 * k + 3) & ~3
 
 
-def dense_payload_bytes(n: int, bits: int) -> int:
-    nblk = (n + BLOCK - 1) // BLOCK
-    return ((nblk * 4 + 15) & ~15) + nblk * (128 if bits == 4 else 256)
+def chunk_record_bytes(mode: str, k: int = 0) -> int:
+    """Wire bytes of one chunk record (8 blocks of 256 elements)."""
+    if mode == "int4":
+        return 4 * CHUNK_BLOCKS + CHUNK_BLOCKS * 128
+    if mode == "int8":
+        return 4 * CHUNK_BLOCKS + CHUNK_BLOCKS * 256
+    return CHUNK_BLOCKS * topk_record_bytes(k)
 
 
-def topk_payload_bytes(n: int, k: int) -> int:
-    return ((n + BLOCK - 1) // BLOCK) * topk_record_bytes(k)
+def nchunks_of(n: int) -> int:
+    return ((n + BLOCK - 1) // BLOCK + CHUNK_BLOCKS - 1) // CHUNK_BLOCKS
 
 
 def payload_bytes(n: int, mode: str, k: int = 0) -> int:
-    if mode == "topk":
-        return topk_payload_bytes(n, k)
-    return dense_payload_bytes(n, 4 if mode == "int4" else 8)
+    """Wire bytes one rank sends per bucket of n elements."""
+    return nchunks_of(n) * chunk_record_bytes(mode, k)
+
+
+def dense_payload_bytes(n: int, bits: int) -> int:
+    return payload_bytes(n, "int4" if bits == 4 else "int8")
 
 
 def _align(x: int, a: int = 256) -> int:
     return (x + a - 1) // a * a
 
 
+MAX_COLS = 2048  # flag columns (max CTAs of one launch)
+
+
 @dataclass
 class Layout:
     max_numel: int
-    max_chunks: int
     flags_off: int
-    rflags_off: int
     inbox_off: int
     slot_bytes: int
     result_off: int
@@ -89,17 +97,14 @@ class Layout:
     total: int
 
 
-def make_layout(world: int, max_numel: int, topk_k: int) -> Layout:
-    nblk = (max_numel + BLOCK - 1) // BLOCK
-    max_chunks = max(1, (nblk + CHUNK_BLOCKS - 1) // CHUNK_BLOCKS)
-    slot = _align(max(dense_payload_bytes(max_numel, 8), topk_payload_bytes(max_numel, max(1, topk_k))))
-    result = _align(dense_payload_bytes(max_numel, 8))
+def make_layout(world: int, max_numel: int, topk_k: int, modes=("int4", "int8", "topk")) -> Layout:
+    slot = _align(max(payload_bytes(max_numel, m, max(1, topk_k)) for m in modes))
+    result = _align(payload_bytes(max_numel, "int8"))
     flags_off = 0
-    rflags_off = _align(flags_off + 2 * world * max_chunks * 8)
-    inbox_off = _align(rflags_off + 2 * max_chunks * 8)
+    inbox_off = _align(flags_off + 2 * 2 * world * MAX_COLS * 8)
     result_off = _align(inbox_off + 2 * world * slot)
     total = _align(result_off + 2 * result)
-    return Layout(max_numel, max_chunks, flags_off, rflags_off, inbox_off, slot, result_off, result, total)
+    return Layout(max_numel, flags_off, inbox_off, slot, result_off, result, total)
 
 
 class FusedAllReduce:
@@ -114,12 +119,16 @@ class FusedAllReduce:
         timeout_s: float = 10.0,
         max_ctas: int = 0,
         twoshot_min_bytes: int | None = None,
+        modes=("int4", "int8", "topk"),
     ):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         if self.world > 8:
             raise ValueError("the fused communicator spans one node (at most 8 ranks)")
+        # Largest segment one launch handles; longer buckets are split into
+        # segments of this many elements (a multiple of one chunk).
+        self.capacity = int(max_numel)
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.timeout_ns = int(timeout_s * 1e9)
         self.max_ctas = int(max_ctas)
@@ -131,17 +140,17 @@ class FusedAllReduce:
         self.twoshot_min_bytes = twoshot_min_bytes if twoshot_min_bytes is not None else self._default_twoshot()
         self.region = None
         if self.world > 1:
-            self.layout = make_layout(self.world, max_numel, topk_k)
+            self.layout = make_layout(self.world, max_numel, topk_k, modes)
             self.region = SymmetricRegion(self.layout.total, group=group, device=self.device)
             ptrs = self.region.ptrs
             L = self.layout
             self.comm = _cuda().FusedComm(
-                self.world, self.rank, ptrs, L.flags_off, L.rflags_off, L.inbox_off, L.slot_bytes,
-                L.result_off, L.result_bytes, L.max_chunks, self.status,
+                self.world, self.rank, ptrs, L.flags_off, L.inbox_off, L.slot_bytes, L.result_off, L.result_bytes,
+                self.status,
             )
         else:
             self.layout = None
-            self.comm = _cuda().FusedComm(1, 0, [], 0, 0, 0, 0, 0, 0, 0, self.status)
+            self.comm = _cuda().FusedComm(1, 0, [], 0, 0, 0, 0, 0, self.status)
 
     def _default_twoshot(self) -> int:
         # One-shot moves (W-1)*P bytes per rank, two-shot about 2*P*(W-1)/W
@@ -181,10 +190,28 @@ class FusedAllReduce:
         first: bool = False,
         tag: int | None = None,
     ) -> str:
-        """Average ``grad`` across ranks in place on the current stream."""
-        v = self.choose_variant(grad.numel(), mode, variant)
+        """Average ``grad`` across ranks in place on the current stream.
+
+        Buckets longer than ``capacity`` run as several launches over
+        segments; segment s of bucket b draws its noise from stream
+        ``b * 65536 + s``.
+        """
+        n = grad.numel()
+        if self.world > 1 and n > self.capacity:
+            seg = max(CHUNK_BLOCKS * BLOCK, self.capacity // (CHUNK_BLOCKS * BLOCK) * (CHUNK_BLOCKS * BLOCK))
+            v = ""
+            for si, s0 in enumerate(range(0, n, seg)):
+                s1 = min(n, s0 + seg)
+                v = self.allreduce_(
+                    grad[s0:s1], None if pred is None else pred[s0:s1], None if ef is None else ef[s0:s1],
+                    mode=mode, k=k, variant=variant, stochastic=stochastic, seed=seed,
+                    bucket=(bucket * 65536 + si) & 0xFFFFFFFF, step=step, beta=beta, first=first,
+                    tag=None if tag is None else (tag + si) & 0xFFFFFFFF,
+                )
+            return v
+        v = self.choose_variant(n, mode, variant)
         if tag is None:
-            tag = self.tag_for(grad.numel(), bucket)
+            tag = self.tag_for(n, bucket)
         self.comm.run(
             grad, pred, ef, MODES[mode], int(k), VARIANTS[v], bool(stochastic), int(seed) & 0x7FFFFFFFFFFFFFFF,
             int(bucket), int(step), float(beta), bool(first), self.max_ctas, self.timeout_ns, int(tag),

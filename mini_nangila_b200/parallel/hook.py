@@ -198,23 +198,20 @@ def _host_hook(hs: NangilaHookState, bucket):
     ef = st.ef.cpu().numpy() if st.ef is not None else None
     n = g.size
     if cfg.mode == "topk":
-        rec, e_out = h.product_topk_encode(g, pred, ef, cfg.k, cfg.error_feedback)
-        payload = torch.from_numpy(np.ascontiguousarray(rec))
+        wire, e_out = h.product_topk_encode(g, pred, ef, cfg.k, cfg.error_feedback)
     else:
         bits = 4 if cfg.mode == "int4" else 8
-        scales, codes, e_out = h.product_encode(g, pred, ef, bits, cfg.stochastic, cfg.error_feedback,
-                                                cfg.seed & 0x7FFFFFFFFFFFFFFF, rank, bidx, st.calls)
-        payload = torch.cat([torch.from_numpy(scales).view(torch.uint8), torch.from_numpy(codes)])
+        wire, e_out = h.product_encode(g, pred, ef, bits, cfg.stochastic, cfg.error_feedback,
+                                       cfg.seed & 0x7FFFFFFFFFFFFFFF, rank, bidx, st.calls)
+    payload = torch.from_numpy(np.ascontiguousarray(wire))
     gathered = [torch.empty_like(payload) for _ in range(world)]
     dist.all_gather(gathered, payload, group=hs.group)
     inv_world = np.float32(1.0) / np.float32(world)
+    wires = [x.numpy() for x in gathered]
     if cfg.mode == "topk":
-        avg = h.product_topk_reduce([x.numpy() for x in gathered], n, cfg.k, pred, float(inv_world))
+        avg = h.product_topk_reduce(wires, n, cfg.k, pred, float(inv_world))
     else:
-        nblk = (n + 255) // 256
-        sc = [x[: nblk * 4].view(torch.float32).numpy() for x in gathered]
-        cd = [x[nblk * 4:].numpy() for x in gathered]
-        avg = h.product_reduce(sc, cd, n, bits, pred, float(inv_world))
+        avg = h.product_reduce(wires, n, bits, pred, float(inv_world))
     if st.pred is not None:
         st.pred.copy_(torch.from_numpy(h.product_ema(st.pred.cpu().numpy(), avg, cfg.beta, first)))
     if st.ef is not None:
@@ -279,12 +276,11 @@ def register_nangila_hook(
         if dev.type != "cuda":
             raise RuntimeError("impl='fused' needs a CUDA model; use impl='host' on CPU")
         bucket_cap = int(getattr(model, "bucket_bytes_cap", 25 * 1024 * 1024))
-        max_numel = max([p.numel() for p in model.parameters()] + [bucket_cap // 4]) + 8192
-        # Buckets may concatenate several parameters above the cap; size for
-        # the cap plus the largest parameter.
-        max_numel = max_numel + max(p.numel() for p in model.parameters())
+        # A bucket holds up to the cap plus one parameter; longer buckets (DDP's
+        # first iteration reduces the whole model as one) run in segments.
+        max_numel = bucket_cap // 4 + max(p.numel() for p in model.parameters()) + 8192
         hs.comm = FusedAllReduce(max_numel, group=process_group, device=dev, topk_k=max(cfg.k, 1),
-                                 timeout_s=timeout_s, max_ctas=max_ctas)
+                                 timeout_s=timeout_s, max_ctas=max_ctas, modes=(cfg.mode,))
         hs.stream = torch.cuda.Stream(device=dev, priority=-1)
 
         def hook(_state, bucket):

@@ -40,16 +40,10 @@ def test_encode_matches_oracle(n, mode, dtype):
     out, ef_out = c.product_encode(g.to(dev), torch.from_numpy(pred).to(dev), torch.from_numpy(ef).to(dev),
                                    mcode, k, True, 777, 3, 5, 9)
     if mode == "topk":
-        rec, e_ref = h.product_topk_encode(gf, pred, ef, k, True)
-        assert bytes(out.cpu().numpy()) == bytes(rec)
+        wire, e_ref = h.product_topk_encode(gf, pred, ef, k, True)
     else:
-        bits = 4 if mode == "int4" else 8
-        sc, cd, e_ref = h.product_encode(gf, pred, ef, bits, True, True, 777, 3, 5, 9)
-        nblk = (n + 255) // 256
-        o = out.cpu().numpy()
-        assert np.array_equal(o[: nblk * 4].view(np.float32).view(np.uint32), sc.view(np.uint32))
-        off = (nblk * 4 + 15) & ~15
-        assert bytes(o[off:]) == bytes(cd)
+        wire, e_ref = h.product_encode(gf, pred, ef, 4 if mode == "int4" else 8, True, True, 777, 3, 5, 9)
+    assert bytes(out.cpu().numpy()) == bytes(wire)
     assert np.array_equal(_bits(ef_out.cpu().numpy()), _bits(e_ref))
 
 
@@ -63,29 +57,22 @@ def test_reduce_matches_oracle(n, mode):
     bits = 8 if mode == "int8" else 4
     mcode = {"int4": 0, "int8": 1, "topk": 2}[mode]
     pred = _data(n, 50)
-    payloads_dev, sc_l, cd_l, rec_l = [], [], [], []
+    wires = []
     for r in range(W):
         g = _data(n, 10 + r)
         if mode == "topk":
-            rec, _ = h.product_topk_encode(g, pred, None, k, False)
-            rec_l.append(rec)
-            payloads_dev.append(torch.from_numpy(rec).to(dev))
+            wire, _ = h.product_topk_encode(g, pred, None, k, False)
         else:
-            sc, cd, _ = h.product_encode(g, pred, None, bits, True, False, 1, r, 0, 0)
-            sc_l.append(sc)
-            cd_l.append(cd)
-            nblk = (n + 255) // 256
-            buf = np.zeros(((nblk * 4 + 15) & ~15) + cd.size, np.uint8)
-            buf[: nblk * 4] = sc.view(np.uint8)
-            buf[((nblk * 4 + 15) & ~15):] = cd
-            payloads_dev.append(torch.from_numpy(buf).to(dev))
+            wire, _ = h.product_encode(g, pred, None, bits, True, False, 1, r, 0, 0)
+        wires.append(wire)
+    payloads_dev = [torch.from_numpy(w).to(dev) for w in wires]
     inv = float(np.float32(1.0) / np.float32(W))
     state = torch.from_numpy(pred.copy()).to(dev)
     avg = c.product_reduce(payloads_dev, n, mcode, k, state, 0.9, False, inv, torch.float32)
     if mode == "topk":
-        ref = h.product_topk_reduce(rec_l, n, k, pred, inv)
+        ref = h.product_topk_reduce(wires, n, k, pred, inv)
     else:
-        ref = h.product_reduce(sc_l, cd_l, n, bits, pred, inv)
+        ref = h.product_reduce(wires, n, bits, pred, inv)
     assert np.array_equal(_bits(avg.cpu().numpy()), _bits(ref))
     ema = h.product_ema(pred, ref, 0.9, False)
     assert np.array_equal(_bits(state.cpu().numpy()), _bits(ema))
@@ -112,8 +99,8 @@ def test_fused_single_rank_matches_oracle(mode, n):
             rec, e_new = h.product_topk_encode(g, pred, ef, k, True)
             avg = h.product_topk_reduce([rec], n, k, pred, 1.0)
         else:
-            sc, cd, e_new = h.product_encode(g, pred, ef, bits, True, True, 42, 0, 2, step)
-            avg = h.product_reduce([sc], [cd], n, bits, pred, 1.0)
+            wire, e_new = h.product_encode(g, pred, ef, bits, True, True, 42, 0, 2, step)
+            avg = h.product_reduce([wire], n, bits, pred, 1.0)
         pred = h.product_ema(pred, avg, 0.9, step == 0)
         ef = e_new
         assert np.array_equal(_bits(gd.cpu().numpy()), _bits(avg)), f"avg mismatch at step {step}"
@@ -124,9 +111,8 @@ def test_fused_single_rank_matches_oracle(mode, n):
 
 def _two_rank_emulation(n, mode, k, bad_tag=False, deliver=True, timeout_s=0.2):
     """Run rank 0 of a 2-rank one-shot all-reduce on one GPU with rank 1's
-    payload and flags pre-delivered into rank 0's region."""
-    from mini_nangila_b200.parallel.fused import (MODES, VARIANTS, FusedAllReduce, make_layout,
-                                                  payload_bytes)
+    payload and column flags pre-delivered into rank 0's region."""
+    from mini_nangila_b200.parallel.fused import MAX_COLS, MODES, VARIANTS, FusedAllReduce, make_layout
 
     h, c = _ext()
     dev = torch.device("cuda")
@@ -134,25 +120,26 @@ def _two_rank_emulation(n, mode, k, bad_tag=False, deliver=True, timeout_s=0.2):
     reg0 = torch.zeros(L.total, dtype=torch.uint8, device=dev)
     reg1 = torch.zeros(L.total, dtype=torch.uint8, device=dev)
     status = torch.zeros(4, dtype=torch.int32, device=dev)
-    comm = c.FusedComm(2, 0, [reg0.data_ptr(), reg1.data_ptr()], L.flags_off, L.rflags_off, L.inbox_off,
-                       L.slot_bytes, L.result_off, L.result_bytes, L.max_chunks, status)
+    comm = c.FusedComm(2, 0, [reg0.data_ptr(), reg1.data_ptr()], L.flags_off, L.inbox_off, L.slot_bytes,
+                       L.result_off, L.result_bytes, status)
     epoch = comm.epoch + 1
     parity = epoch & 1
     tag = FusedAllReduce.tag_for(n, 4)
     g0, g1 = _data(n, 1), _data(n, 2)
     bits = 8 if mode == "int8" else 4
     mcode = MODES[mode]
+    grid = c.fused_grid(n, mcode, False, VARIANTS["oneshot"], 0, 0)
     if deliver:
         p1, _ = c.product_encode(torch.from_numpy(g1).to(dev), None, None, mcode, k, True, 99, 1, 4, 7)
         slot = L.inbox_off + (parity * 2 + 1) * L.slot_bytes
         reg0[slot: slot + p1.numel()] = p1
-        nchunks = ((n + 255) // 256 + 7) // 8
         flags = reg0[L.flags_off:].view(torch.int64)
-        val = ((tag ^ (1 if bad_tag else 0)) << 32) | epoch
+        ftag = (tag ^ ((grid * 0x9E3779B1) & 0xFFFFFFFF)) ^ (1 if bad_tag else 0)
+        val = (ftag << 32) | epoch
         if val >= 1 << 63:
             val -= 1 << 64
-        base = (parity * 2 + 1) * L.max_chunks
-        flags[base: base + nchunks] = val
+        base = ((parity * 2 + 0) * 2 + 1) * MAX_COLS  # kind payload, src 1
+        flags[base: base + grid] = val
     torch.cuda.synchronize()
     gd = torch.from_numpy(g0).to(dev)
     comm.run(gd, None, None, mcode, k, VARIANTS["oneshot"], True, 99, 4, 7, 0.9, True, 0, int(timeout_s * 1e9), tag)
@@ -164,9 +151,9 @@ def _two_rank_emulation(n, mode, k, bad_tag=False, deliver=True, timeout_s=0.2):
         r1, _ = h.product_topk_encode(g1, None, None, k, False)
         ref = h.product_topk_reduce([r0, r1], n, k, None, inv)
     else:
-        s0, c0, _ = h.product_encode(g0, None, None, bits, True, False, 99, 0, 4, 7)
-        s1, c1, _ = h.product_encode(g1, None, None, bits, True, False, 99, 1, 4, 7)
-        ref = h.product_reduce([s0, s1], [c0, c1], n, bits, None, inv)
+        w0, _ = h.product_encode(g0, None, None, bits, True, False, 99, 0, 4, 7)
+        w1, _ = h.product_encode(g1, None, None, bits, True, False, 99, 1, 4, 7)
+        ref = h.product_reduce([w0, w1], n, bits, None, inv)
     return st, gd.cpu().numpy(), ref
 
 
