@@ -1,0 +1,151 @@
+"""DDP comm hooks on CPU gloo process groups (world 2): the host
+implementation of the product format gives bit-identical averages and
+predictor states on every rank and matches the oracle; the compat hook
+reproduces the reference's algorithm; a rank that fails is detected by the
+others through the process-group timeout (no GPU involved)."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _init(rank, world, port, timeout_s=60):
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=timeout_s))
+    return dist
+
+
+def _train_worker(rank, world, port, impl, mode, outdir):
+    dist = _init(rank, world, port)
+    try:
+        from mini_nangila_b200.models import GPT2, GPT2Config
+        from mini_nangila_b200.train import DDPTrainer
+
+        torch.manual_seed(0)
+        cfg = GPT2Config.tiny()
+        kw = dict(use_momentum=True, bits=8 if mode == "int8" else 4,
+                  topk_percent=0.1 if mode == "topk" else 0.0, seed=5)
+        if impl == "host":
+            kw["error_feedback"] = True
+        tr = DDPTrainer(GPT2(cfg), hook=impl, hook_kwargs=kw, device=torch.device("cpu"), bucket_cap_mb=0.05)
+        g = torch.Generator().manual_seed(100 + rank)
+        losses = []
+        for _ in range(3):
+            t = torch.randint(0, cfg.vocab_size, (2, 17), generator=g)
+            losses.append(float(tr.step(t[:, :-1], t[:, 1:])))
+        params = torch.cat([p.detach().reshape(-1) for p in tr.model.parameters()])
+        hs = tr.hook_state
+        preds = [st.pred.clone() for _, st in sorted(hs.buckets.items())] if impl == "host" else \
+            [v.clone() for _, v in sorted(hs.compat_states.items())]
+        torch.save({"params": params, "preds": preds, "losses": losses, "ratio": hs.compression_ratio()},
+                   os.path.join(outdir, f"r{rank}.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("impl,mode", [("host", "int4"), ("host", "int8"), ("host", "topk"), ("compat", "int4"),
+                                       ("compat", "topk")])
+def test_ddp_hook_ranks_stay_identical(impl, mode, tmp_path):
+    mp.start_processes(_train_worker, args=(2, _port(), impl, mode, str(tmp_path)), nprocs=2, join=True,
+                       start_method="spawn")
+    r0, r1 = torch.load(tmp_path / "r0.pt"), torch.load(tmp_path / "r1.pt")
+    # Identical averaged gradients -> identical parameters on both ranks.
+    assert torch.equal(r0["params"], r1["params"])
+    for a, b in zip(r0["preds"], r1["preds"]):
+        assert torch.equal(a, b)
+    assert r0["ratio"] > 3.0
+    assert all(np.isfinite(r0["losses"]))
+
+
+def _oracle_worker(rank, world, port, outdir):
+    dist = _init(rank, world, port)
+    try:
+        from mini_nangila_b200 import _ext
+        from mini_nangila_b200.parallel.hook import HookConfig, NangilaHookState, _host_hook
+
+        class Bucket:
+            def __init__(self, t):
+                self.t = t
+
+            def buffer(self):
+                return self.t
+
+            def index(self):
+                return 0
+
+            def parameters(self):
+                return []
+
+        hs = NangilaHookState(HookConfig(impl="host", use_momentum=True, seed=9))
+        n = 5000
+        gs = [np.random.default_rng(50 + r).standard_normal(n).astype(np.float32) * np.float32(1e-3)
+              for r in range(world)]
+        buf = torch.from_numpy(gs[rank].copy())
+        _host_hook(hs, Bucket(buf)).wait()
+        h = _ext.host()
+        wires = [h.product_encode(gs[r], np.zeros(n, np.float32), np.zeros(n, np.float32), 4, True, True, 9, r, 0,
+                                  1)[0] for r in range(world)]
+        ref = h.product_reduce(wires, n, 4, np.zeros(n, np.float32), float(np.float32(1) / np.float32(world)))
+        np.save(os.path.join(outdir, f"o{rank}.npy"), np.stack([buf.numpy(), ref]))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_host_hook_matches_oracle(tmp_path):
+    mp.start_processes(_oracle_worker, args=(2, _port(), str(tmp_path)), nprocs=2, join=True, start_method="spawn")
+    for r in range(2):
+        got, ref = np.load(tmp_path / f"o{r}.npy")
+        assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+
+def _dying_worker(rank, world, port, outdir):
+    """Rank 1 raises between steps without joining the next collective; rank 0
+    must get an error from its next collective (short process-group timeout)
+    instead of hanging."""
+    import time
+
+    dist = _init(rank, world, port, timeout_s=5)
+    if rank == 1:
+        dist.barrier()
+        raise SystemExit(3)
+    dist.barrier()
+    t0 = time.time()
+    err = ""
+    try:
+        x = torch.ones(4)
+        dist.all_reduce(x)
+    except Exception as e:  # noqa: BLE001
+        err = type(e).__name__
+    with open(os.path.join(outdir, "rank0.txt"), "w") as fh:
+        fh.write(f"{err}:{time.time() - t0:.1f}")
+
+
+def test_dead_rank_detected_by_timeout(tmp_path):
+    ctx = mp.get_context("spawn")
+    port = _port()
+    ps = [ctx.Process(target=_dying_worker, args=(r, 2, port, str(tmp_path))) for r in range(2)]
+    for p in ps:
+        p.start()
+    for p in ps:
+        p.join(60)
+    for p in ps:
+        if p.is_alive():
+            p.kill()
+    txt = (tmp_path / "rank0.txt").read_text()
+    err, dt = txt.split(":")
+    assert err != "" and float(dt) < 30.0
