@@ -3,10 +3,12 @@
 
 void register_fused(pybind11::module& m);
 void register_symm(pybind11::module& m);
+void register_codecs(pybind11::module& m);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sm_100a kernels: fused compressed all-reduce, codecs, symmetric memory";
   m.attr("ARCH") = "sm_100a";
   register_fused(m);
   register_symm(m);
+  register_codecs(m);
 }

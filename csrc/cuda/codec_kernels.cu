@@ -1,0 +1,920 @@
+// sm_100a codec kernels: Q8.23 math, the fused HPC closed-loop step, the
+// reference's byte formats (error-bounded INT16, BlockSparse,
+// BlockSparse+RLE, element RLE, stochastic INT4/INT8, top-k) on the device.
+//
+// Reference hot loops restated here (all scalar Rust loops in the reference):
+//   nangila-math/src/fixed_point.rs:34-60, ops.rs:6-49        -> q823_* kernels
+//   nangila-hpc/src/error_bounded.rs:294-333, linear.rs:26-57  -> hpc_step, eb_*
+//   nangila-hpc/src/block_sparse.rs:21-92                      -> bs_encode + walker
+//   nangila-hpc/src/block_sparse_rle.rs:137-242                -> bsrle_encode + walker
+//   nangila-hpc/src/rle.rs:500-579                             -> rle_encode + walker
+//   nangila-core/src/unified_quantizer.rs:171-375              -> stochastic_*, topk_*
+//
+// Variable-length encoders compute every item's output offset with a
+// single-pass decoupled look-back scan across tiles (tile status words in
+// scratch, dynamic tile ids from an atomic counter); every spin on a
+// predecessor tile is bounded and reports through the status word.
+#include "codecs.h"
+#include "ngl_cuda.cuh"
+
+namespace ngl {
+namespace codec {
+
+using dev::kFull;
+using dev::max64;
+using dev::min64;
+
+constexpr int kThreads = 256;
+constexpr uint64_t kSpinLimitNs = 2000000000ull;  // 2 s per look-back wait
+
+__device__ __forceinline__ int64_t gtid() { return (int64_t)blockIdx.x * blockDim.x + threadIdx.x; }
+__device__ __forceinline__ int64_t gstride() { return (int64_t)gridDim.x * blockDim.x; }
+
+inline int grid_for(int64_t n, int per_thread = 4) {
+  int64_t g = (n + (int64_t)kThreads * per_thread - 1) / ((int64_t)kThreads * per_thread);
+  if (g < 1) g = 1;
+  if (g > 148 * 16) g = 148 * 16;
+  return (int)g;
+}
+
+// ================================================================ Q8.23 (K2)
+__global__ void k_from_f32(const float* __restrict__ x, int32_t* __restrict__ q, int64_t n) {
+  for (int64_t i = gtid(); i < n; i += gstride()) q[i] = q823_from_f32(x[i]);
+}
+__global__ void k_to_f32(const int32_t* __restrict__ q, float* __restrict__ x, int64_t n) {
+  for (int64_t i = gtid(); i < n; i += gstride()) x[i] = q823_to_f32(q[i]);
+}
+__global__ void k_addsub(const int32_t* __restrict__ a, const int32_t* __restrict__ b, int32_t* __restrict__ o,
+                         int64_t n, int sub) {
+  for (int64_t i = gtid(); i < n; i += gstride()) o[i] = sub ? sat_sub_i32(a[i], b[i]) : sat_add_i32(a[i], b[i]);
+}
+__global__ void k_mul_scalar(const int32_t* __restrict__ a, int32_t* __restrict__ o, int64_t n, int64_t sf) {
+  for (int64_t i = gtid(); i < n; i += gstride()) o[i] = q823_mul_fixed(a[i], sf);
+}
+
+cudaError_t from_f32_dev(const float* x, int32_t* q, int64_t n, cudaStream_t s) {
+  if (n > 0) k_from_f32<<<grid_for(n), kThreads, 0, s>>>(x, q, n);
+  return cudaGetLastError();
+}
+cudaError_t to_f32_dev(const int32_t* q, float* x, int64_t n, cudaStream_t s) {
+  if (n > 0) k_to_f32<<<grid_for(n), kThreads, 0, s>>>(q, x, n);
+  return cudaGetLastError();
+}
+cudaError_t q823_addsub(const int32_t* a, const int32_t* b, int32_t* out, int64_t n, bool sub, cudaStream_t s) {
+  if (n > 0) k_addsub<<<grid_for(n), kThreads, 0, s>>>(a, b, out, n, sub ? 1 : 0);
+  return cudaGetLastError();
+}
+cudaError_t q823_mul_scalar(const int32_t* a, int32_t* out, int64_t n, float scalar, cudaStream_t s) {
+  // (scalar * 2^23) as i64 computed on the host with the same f32 multiply.
+  const int64_t sf = q823_scalar_fixed(scalar);
+  if (n > 0) k_mul_scalar<<<grid_for(n), kThreads, 0, s>>>(a, out, n, sf);
+  return cudaGetLastError();
+}
+
+// ======================================================= error-bounded (K3)
+__global__ void k_eb_encode(const int32_t* __restrict__ r, int16_t* __restrict__ c, int64_t n, float scale) {
+  for (int64_t i = gtid(); i < n; i += gstride()) c[i] = eb_code(q823_to_f32(r[i]), scale);
+}
+__global__ void k_eb_decode(const int16_t* __restrict__ c, int32_t* __restrict__ o, int64_t n, float scale) {
+  for (int64_t i = gtid(); i < n; i += gstride()) o[i] = q823_from_f32(NGL_FMUL((float)c[i], scale));
+}
+
+// One closed-loop step for a snapshot: predict, residual, code, reconstruct,
+// track the max error.  Four elements per thread with 16-byte accesses.
+// `vec` is set by the launcher only when x, st, stm1, recon are 16-byte and
+// codes 8-byte aligned; otherwise every access is scalar.
+__global__ void k_hpc_step(const float* __restrict__ x, const int32_t* __restrict__ st,
+                           const int32_t* __restrict__ stm1, int hist, float scale, int16_t* __restrict__ codes,
+                           int32_t* __restrict__ recon, uint32_t* __restrict__ maxerr, int64_t n, int vec) {
+  float emax = 0.0f;
+  const int64_t n4 = n / 4;
+  for (int64_t v = gtid(); v < n4 + (n % 4 ? 1 : 0); v += gstride()) {
+    const int64_t i0 = v * 4;
+    const bool full = vec && i0 + 4 <= n;
+    float xs[4];
+    int32_t s0[4] = {0, 0, 0, 0}, s1[4] = {0, 0, 0, 0};
+    if (full) {
+      const float4 xv = *reinterpret_cast<const float4*>(x + i0);
+      xs[0] = xv.x; xs[1] = xv.y; xs[2] = xv.z; xs[3] = xv.w;
+      if (hist >= 1) {
+        const int4 a = *reinterpret_cast<const int4*>(st + i0);
+        s0[0] = a.x; s0[1] = a.y; s0[2] = a.z; s0[3] = a.w;
+      }
+      if (hist >= 2) {
+        const int4 b = *reinterpret_cast<const int4*>(stm1 + i0);
+        s1[0] = b.x; s1[1] = b.y; s1[2] = b.z; s1[3] = b.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        xs[j] = (i0 + j < n) ? x[i0 + j] : 0.0f;
+        if (hist >= 1 && i0 + j < n) s0[j] = st[i0 + j];
+        if (hist >= 2 && i0 + j < n) s1[j] = stm1[i0 + j];
+      }
+    }
+    int16_t c[4];
+    int32_t rc[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int32_t xq = q823_from_f32(xs[j]);
+      int32_t pred = 0;
+      if (hist >= 2) pred = sat_add_i32(s0[j], sat_sub_i32(s0[j], s1[j]));
+      else if (hist == 1) pred = s0[j];
+      const int32_t r = hist >= 1 ? sat_sub_i32(xq, pred) : xq;
+      c[j] = eb_code(q823_to_f32(r), scale);
+      const int32_t d = q823_from_f32(NGL_FMUL((float)c[j], scale));
+      rc[j] = hist >= 1 ? sat_add_i32(pred, d) : d;
+      if (i0 + j < n) emax = fmaxf(emax, fabsf(NGL_FSUB(q823_to_f32(xq), q823_to_f32(rc[j]))));
+    }
+    if (full) {
+      *reinterpret_cast<int4*>(recon + i0) = make_int4(rc[0], rc[1], rc[2], rc[3]);
+      *reinterpret_cast<uint2*>(codes + i0) =
+          make_uint2(((uint32_t)(uint16_t)c[0]) | ((uint32_t)(uint16_t)c[1] << 16),
+                     ((uint32_t)(uint16_t)c[2]) | ((uint32_t)(uint16_t)c[3] << 16));
+    } else {
+      for (int j = 0; j < 4; ++j)
+        if (i0 + j < n) {
+          recon[i0 + j] = rc[j];
+          codes[i0 + j] = c[j];
+        }
+    }
+  }
+  const uint32_t m = __reduce_max_sync(kFull, __float_as_uint(emax));
+  if ((threadIdx.x & 31) == 0 && maxerr != nullptr) atomicMax(maxerr, m);
+}
+
+// Linear-predictor add-back over T snapshots: parallel over elements,
+// sequential over steps (the reference's chain: empty, s_t, 2 s_t - s_{t-1}).
+__global__ void k_linear_addback(int32_t* __restrict__ res, int64_t P, int64_t T) {
+  for (int64_t i = gtid(); i < P; i += gstride()) {
+    int32_t a = 0, b = 0;  // s_t, s_{t-1}
+    for (int64_t t = 0; t < T; ++t) {
+      const int32_t d = res[t * P + i];
+      int32_t rc;
+      if (t == 0) rc = d;
+      else if (t == 1) rc = sat_add_i32(a, d);
+      else rc = sat_add_i32(sat_add_i32(a, sat_sub_i32(a, b)), d);
+      res[t * P + i] = rc;
+      b = a;
+      a = rc;
+    }
+  }
+}
+
+cudaError_t eb_encode(const int32_t* r, int16_t* codes, int64_t n, float scale, cudaStream_t s) {
+  if (n > 0) k_eb_encode<<<grid_for(n), kThreads, 0, s>>>(r, codes, n, scale);
+  return cudaGetLastError();
+}
+cudaError_t eb_decode(const int16_t* codes, int32_t* out, int64_t n, float scale, cudaStream_t s) {
+  if (n > 0) k_eb_decode<<<grid_for(n), kThreads, 0, s>>>(codes, out, n, scale);
+  return cudaGetLastError();
+}
+cudaError_t hpc_step(const float* x, const int32_t* s_t, const int32_t* s_tm1, int hist, float scale, int16_t* codes,
+                     int32_t* recon, uint32_t* maxerr_bits, int64_t n, cudaStream_t s) {
+  auto a16 = [](const void* p) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  const int vec = a16(x) && a16(s_t) && a16(s_tm1) && a16(recon) && (reinterpret_cast<uintptr_t>(codes) & 7u) == 0;
+  if (n > 0)
+    k_hpc_step<<<grid_for(n, 4), kThreads, 0, s>>>(x, s_t, s_tm1, hist, scale, codes, recon, maxerr_bits, n, vec);
+  return cudaGetLastError();
+}
+cudaError_t linear_addback(int32_t* res, int64_t particles, int64_t steps, cudaStream_t s) {
+  if (particles > 0 && steps > 0) k_linear_addback<<<grid_for(particles, 1), kThreads, 0, s>>>(res, particles, steps);
+  return cudaGetLastError();
+}
+
+// ================================================ decoupled look-back scan
+// Status word: bits 63..62 state (1 = aggregate, 2 = inclusive prefix),
+// bits 61..0 value.  Warp 0 of the tile publishes and looks back over 32
+// predecessors at a time.
+constexpr uint64_t kStAgg = 1ull << 62, kStInc = 2ull << 62, kValMask = (1ull << 62) - 1;
+
+__device__ __forceinline__ void st_release_gpu(uint64_t* p, uint64_t v) {
+  asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_acquire_gpu(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+struct OpSum {
+  __device__ static uint64_t id() { return 0; }
+  __device__ static uint64_t op(uint64_t a, uint64_t b) { return a + b; }
+};
+struct OpMax {
+  __device__ static uint64_t id() { return 0; }
+  __device__ static uint64_t op(uint64_t a, uint64_t b) { return a > b ? a : b; }
+};
+
+template <class Op>
+__device__ __forceinline__ uint64_t warp_reduce_op(uint64_t v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = Op::op(v, __shfl_xor_sync(kFull, v, o));
+  return v;
+}
+
+// Called by every thread of the CTA; returns the exclusive prefix of this
+// tile (all threads).  On a timeout it records the status and returns the
+// identity (the caller's output is then invalid; status says so).
+template <class Op>
+__device__ uint64_t lookback(uint64_t* status_arr, int64_t tile, uint64_t agg, int* status, uint64_t* s_slot) {
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x < 32) {
+    uint64_t excl = Op::id();
+    if (tile == 0) {
+      if (lane == 0) st_release_gpu(&status_arr[0], kStInc | (agg & kValMask));
+    } else {
+      if (lane == 0) st_release_gpu(&status_arr[tile], kStAgg | (agg & kValMask));
+      int64_t base = tile - 1;
+      bool timed_out = false;
+      while (true) {
+        const int64_t idx = base - lane;
+        uint64_t s = idx >= 0 ? ld_acquire_gpu(&status_arr[idx]) : (kStInc | Op::id());
+        const uint64_t t0 = dev::globaltimer();
+        while (__any_sync(kFull, (s >> 62) == 0)) {  // uniform loop condition
+          if ((s >> 62) == 0) s = ld_acquire_gpu(&status_arr[idx]);
+          const bool late = dev::globaltimer() - t0 > kSpinLimitNs;
+          if (__any_sync(kFull, late)) {  // uniform exit
+            timed_out = true;
+            break;
+          }
+        }
+        if (timed_out) break;
+        const uint32_t inc = __ballot_sync(kFull, (s >> 62) == 2);
+        const int stop = inc ? (__ffs(inc) - 1) : 31;
+        uint64_t v = lane <= stop ? (s & kValMask) : Op::id();
+        excl = Op::op(excl, warp_reduce_op<Op>(v));
+        if (inc) break;
+        base -= 32;
+      }
+      if (timed_out) {
+        if (lane == 0) dev::set_status(status, dev::kBounds, (int)tile, -1);
+        excl = Op::id();
+      }
+      if (lane == 0) st_release_gpu(&status_arr[tile], kStInc | (Op::op(excl, agg) & kValMask));
+    }
+    if (lane == 0) *s_slot = excl;
+  }
+  __syncthreads();
+  const uint64_t r = *s_slot;
+  __syncthreads();
+  return r;
+}
+
+// Block-wide exclusive scan of one u64 per thread (256 threads).
+template <class Op>
+__device__ uint64_t block_excl_scan(uint64_t v, uint64_t* s_warp, uint64_t* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint64_t x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint64_t y = __shfl_up_sync(kFull, x, o);
+    if (lane >= o) x = Op::op(x, y);
+  }
+  if (lane == 31) s_warp[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    uint64_t w = lane < (kThreads / 32) ? s_warp[lane] : Op::id();
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint64_t y = __shfl_up_sync(kFull, w, o);
+      if (lane >= o) w = Op::op(w, y);
+    }
+    if (lane < (kThreads / 32)) s_warp[lane] = w;  // inclusive prefix of warps
+  }
+  __syncthreads();
+  const uint64_t wbase = warp ? s_warp[warp - 1] : Op::id();
+  const uint64_t excl_in_warp = __shfl_up_sync(kFull, x, 1);
+  const uint64_t r = Op::op(wbase, lane ? excl_in_warp : Op::id());
+  if (total) *total = s_warp[kThreads / 32 - 1];
+  __syncthreads();
+  return r;
+}
+
+int64_t pack_scratch_words(int64_t n) {
+  const int64_t nblk = (n + 31) / 32;
+  const int64_t tiles = (nblk + kPackTileBlocks - 1) / kPackTileBlocks;
+  return tiles + 2;  // status per tile, tile counter
+}
+int64_t run_scratch_words(int64_t items) {
+  const int64_t tiles = (items + kRunTileItems - 1) / kRunTileItems;
+  // two status arrays + tile counter + per-item offsets + per-item type bytes
+  return 2 * tiles + 2 + items + (items + 7) / 8;
+}
+
+// ==================================================== mask packers (K4, K8)
+struct SrcBS {  // BlockSparse from i16 codes: kept iff q != 0, value q
+  const int16_t* q;
+  static constexpr int kVBytes = 2;
+  __device__ __forceinline__ bool get(int64_t i, int32_t& v) const {
+    v = q[i];
+    return v != 0;
+  }
+};
+struct SrcTopK {  // top-k compat from Q8.23: kept iff |x| >= thr
+  const int32_t* r;
+  const float* thr;
+  const float* scale;
+  static constexpr int kVBytes = 1;
+  __device__ __forceinline__ bool get(int64_t i, int32_t& v) const {
+    const float x = q823_to_f32(r[i]);
+    const bool keep = fabsf(x) >= *thr;
+    float q = f_round(NGL_FDIV(x, *scale));
+    if (!is_nan(q)) q = fminf(fmaxf(q, -128.0f), 127.0f);
+    v = sat_f32_to_i8(q);
+    return keep;
+  }
+};
+
+__device__ __forceinline__ void put_u32_bytes(uint8_t* p, uint32_t v) {
+  p[0] = (uint8_t)v;
+  p[1] = (uint8_t)(v >> 8);
+  p[2] = (uint8_t)(v >> 16);
+  p[3] = (uint8_t)(v >> 24);
+}
+
+template <class Src>
+__global__ void __launch_bounds__(kThreads) k_mask_pack(Src src, int64_t n, uint8_t* __restrict__ out,
+                                                        uint64_t* scratch, uint64_t* total, int* status) {
+  __shared__ uint64_t s_warp[kThreads / 32];
+  __shared__ uint64_t s_slot;
+  __shared__ int64_t s_tile;
+  const int64_t nblk = (n + 31) / 32;
+  const int64_t ntiles = (nblk + kPackTileBlocks - 1) / kPackTileBlocks;
+  unsigned long long* ctr = reinterpret_cast<unsigned long long*>(scratch + ntiles);
+  if (threadIdx.x == 0) s_tile = (int64_t)atomicAdd(ctr, 1ull);
+  __syncthreads();
+  const int64_t tile = s_tile;
+  if (tile >= ntiles) return;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t blk0 = tile * kPackTileBlocks + (int64_t)warp * kPackBlocksPerWarp;
+  uint32_t masks[kPackBlocksPerWarp];
+  int32_t vals[kPackBlocksPerWarp];
+  uint64_t wsum = 0;
+#pragma unroll
+  for (int j = 0; j < kPackBlocksPerWarp; ++j) {
+    const int64_t i = (blk0 + j) * 32 + lane;
+    bool keep = false;
+    vals[j] = 0;
+    if (blk0 + j < nblk && i < n) keep = src.get(i, vals[j]);
+    masks[j] = __ballot_sync(kFull, keep);
+    if (blk0 + j < nblk) wsum += 4 + Src::kVBytes * __popc(masks[j]);
+  }
+  // tile aggregate and the warp's offset within the tile
+  uint64_t tile_agg;
+  const uint64_t wexcl = block_excl_scan<OpSum>(lane == 0 ? wsum : 0, s_warp, &tile_agg);
+  const uint64_t warp_base = __shfl_sync(kFull, wexcl, 0);
+  const uint64_t excl = lookback<OpSum>(scratch, tile, tile_agg, status, &s_slot);
+  if (tile == 0 && threadIdx.x == 0) put_u32_bytes(out, (uint32_t)n);
+  uint64_t off = 4 + excl + warp_base;
+  const uint32_t lt = (1u << lane) - 1u;
+#pragma unroll
+  for (int j = 0; j < kPackBlocksPerWarp; ++j) {
+    if (blk0 + j >= nblk) break;
+    const uint32_t m = masks[j];
+    if (lane == 0) put_u32_bytes(out + off, m);
+    if ((m >> lane) & 1u) {
+      const uint64_t pos = off + 4 + Src::kVBytes * __popc(m & lt);
+      if (Src::kVBytes == 2) {
+        out[pos] = (uint8_t)vals[j];
+        out[pos + 1] = (uint8_t)((uint32_t)vals[j] >> 8);
+      } else {
+        out[pos] = (uint8_t)vals[j];
+      }
+    }
+    off += 4 + Src::kVBytes * __popc(m);
+  }
+  if (tile == ntiles - 1 && threadIdx.x == 0) *total = 4 + excl + tile_agg;
+}
+
+template <class Src>
+cudaError_t launch_pack(const Src& src, int64_t n, uint8_t* out, uint64_t* scratch, uint64_t* total, int* status,
+                        cudaStream_t s) {
+  const int64_t words = pack_scratch_words(n);
+  cudaError_t e = cudaMemsetAsync(scratch, 0, words * sizeof(uint64_t), s);
+  if (e != cudaSuccess) return e;
+  const int64_t nblk = (n + 31) / 32;
+  const int64_t ntiles = (nblk + kPackTileBlocks - 1) / kPackTileBlocks;
+  if (ntiles == 0) {
+    // Empty input still writes the u32 header (n = 0).
+    e = cudaMemsetAsync(out, 0, 4, s);
+    if (e != cudaSuccess) return e;
+    const uint64_t four = 4;
+    return cudaMemcpyAsync(total, &four, sizeof(four), cudaMemcpyHostToDevice, s);
+  }
+  k_mask_pack<Src><<<(unsigned)ntiles, kThreads, 0, s>>>(src, n, out, scratch, total, status);
+  return cudaGetLastError();
+}
+
+cudaError_t bs_encode(const int16_t* q, int64_t n, uint8_t* out, uint64_t* scratch, uint64_t* total_bytes,
+                      int* status, cudaStream_t s) {
+  return launch_pack(SrcBS{q}, n, out, scratch, total_bytes, status, s);
+}
+cudaError_t topk_encode(const int32_t* r, int64_t n, const float* threshold, const float* scale, uint8_t* out,
+                        uint64_t* scratch, uint64_t* total_bytes, int* status, cudaStream_t s) {
+  return launch_pack(SrcTopK{r, threshold, scale}, n, out, scratch, total_bytes, status, s);
+}
+
+// ================================================= run-length encoders (K5, K6)
+// Items are 32-blocks (BlockSparse+RLE, item kept iff its mask != 0) or
+// single codes (RLE, kept iff code != 0).  A run starts at an item whose
+// kind differs from its predecessor, and every 128 items into a run; each
+// run head carries a one-byte opcode.  Pass 1 scans twice with look-back
+// (segment start by max-scan, byte offsets by sum-scan) and writes the item
+// payloads; pass 2 writes the opcodes (run length found by scanning ahead).
+template <bool BLOCKS>
+struct RunItems {
+  const int16_t* q;
+  int64_t n;
+  __device__ __forceinline__ int64_t count() const { return BLOCKS ? (n + 31) / 32 : n; }
+  __device__ __forceinline__ uint32_t mask(int64_t b) const {  // BLOCKS only
+    uint32_t m = 0;
+    const int64_t s0 = b * 32;
+    const int len = (int)min64(32, n - s0);
+    for (int i = 0; i < len; ++i) m |= (uint32_t)(q[s0 + i] != 0) << i;
+    return m;
+  }
+};
+
+template <bool BLOCKS>
+__global__ void __launch_bounds__(kThreads) k_run_pass1(RunItems<BLOCKS> it, uint8_t* __restrict__ out,
+                                                        uint64_t* scratch, uint64_t* total, int* status) {
+  constexpr int IPT = kRunTileItems / kThreads;  // 16 items per thread
+  __shared__ uint64_t s_warp[kThreads / 32];
+  __shared__ uint64_t s_slot;
+  __shared__ int64_t s_tile;
+  const int64_t nitems = it.count();
+  const int64_t ntiles = (nitems + kRunTileItems - 1) / kRunTileItems;
+  uint64_t* st_max = scratch;
+  uint64_t* st_sum = scratch + ntiles;
+  unsigned long long* ctr = reinterpret_cast<unsigned long long*>(scratch + 2 * ntiles);
+  int64_t* offs = reinterpret_cast<int64_t*>(scratch + 2 * ntiles + 2);
+  uint8_t* types = reinterpret_cast<uint8_t*>(scratch + 2 * ntiles + 2 + nitems);
+  if (threadIdx.x == 0) s_tile = (int64_t)atomicAdd(ctr, 1ull);
+  __syncthreads();
+  const int64_t tile = s_tile;
+  if (tile >= ntiles) return;
+  const int64_t i0 = tile * kRunTileItems + (int64_t)threadIdx.x * IPT;
+  uint32_t m[IPT];
+  bool nz[IPT];
+  bool prev_nz = false;
+  if (i0 > 0 && i0 - 1 < nitems) prev_nz = BLOCKS ? (it.mask(i0 - 1) != 0) : (it.q[i0 - 1] != 0);
+  // pass A: segment starts (max-scan of change positions)
+  uint64_t seg = 0;
+  bool any_change = false;
+#pragma unroll
+  for (int j = 0; j < IPT; ++j) {
+    const int64_t i = i0 + j;
+    m[j] = 0;
+    nz[j] = false;
+    if (i < nitems) {
+      if (BLOCKS) {
+        m[j] = it.mask(i);
+        nz[j] = m[j] != 0;
+      } else {
+        nz[j] = it.q[i] != 0;
+      }
+      const bool p = j == 0 ? prev_nz : nz[j - 1];
+      if (i == 0 || nz[j] != p) {
+        seg = (uint64_t)i;
+        any_change = true;
+      }
+    }
+  }
+  uint64_t tile_max;
+  const uint64_t thr_excl_max = block_excl_scan<OpMax>(any_change ? seg : 0, s_warp, &tile_max);
+  const uint64_t tile_excl_max = lookback<OpMax>(st_max, tile, tile_max, status, &s_slot);
+  // pass B: run heads and byte sizes
+  uint64_t run_start = OpMax::op(tile_excl_max, thr_excl_max);
+  uint64_t sizes[IPT];
+  bool head[IPT];
+  uint64_t tsum = 0;
+#pragma unroll
+  for (int j = 0; j < IPT; ++j) {
+    const int64_t i = i0 + j;
+    sizes[j] = 0;
+    head[j] = false;
+    if (i < nitems) {
+      const bool p = j == 0 ? prev_nz : nz[j - 1];
+      if (i == 0 || nz[j] != p) run_start = (uint64_t)i;
+      head[j] = (((uint64_t)i - run_start) % 128) == 0;
+      uint64_t sz = head[j] ? 1 : 0;
+      if (nz[j]) sz += BLOCKS ? (4 + 2 * (uint64_t)__popc(m[j])) : 2;
+      sizes[j] = sz;
+      tsum += sz;
+    }
+  }
+  uint64_t tile_sum;
+  const uint64_t thr_excl_sum = block_excl_scan<OpSum>(tsum, s_warp, &tile_sum);
+  const uint64_t tile_excl_sum = lookback<OpSum>(st_sum, tile, tile_sum, status, &s_slot);
+  const uint64_t hdr = BLOCKS ? 4 : 0;
+  if (BLOCKS && tile == 0 && threadIdx.x == 0) put_u32_bytes(out, (uint32_t)it.n);
+  uint64_t off = hdr + tile_excl_sum + thr_excl_sum;
+#pragma unroll
+  for (int j = 0; j < IPT; ++j) {
+    const int64_t i = i0 + j;
+    if (i >= nitems) break;
+    types[i] = (uint8_t)(nz[j] ? 1 : 0);
+    offs[i] = head[j] ? (int64_t)off : -1;
+    uint64_t p = off + (head[j] ? 1 : 0);
+    if (nz[j]) {
+      if (BLOCKS) {
+        put_u32_bytes(out + p, m[j]);
+        p += 4;
+        const int64_t s0 = i * 32;
+        for (int e = 0; e < 32; ++e)
+          if ((m[j] >> e) & 1u) {
+            const uint16_t v = (uint16_t)it.q[s0 + e];
+            out[p] = (uint8_t)v;
+            out[p + 1] = (uint8_t)(v >> 8);
+            p += 2;
+          }
+      } else {
+        const uint16_t v = (uint16_t)it.q[i];
+        out[p] = (uint8_t)v;
+        out[p + 1] = (uint8_t)(v >> 8);
+      }
+    }
+    off += sizes[j];
+  }
+  if (tile == ntiles - 1 && threadIdx.x == 0) *total = hdr + tile_excl_sum + tile_sum;
+}
+
+// Pass 2: opcode of every run head = kind bit | (run length - 1).
+__global__ void k_run_pass2(const uint64_t* scratch, int64_t nitems, uint8_t* __restrict__ out) {
+  const int64_t ntiles = (nitems + kRunTileItems - 1) / kRunTileItems;
+  const int64_t* offs = reinterpret_cast<const int64_t*>(scratch + 2 * ntiles + 2);
+  const uint8_t* types = reinterpret_cast<const uint8_t*>(scratch + 2 * ntiles + 2 + nitems);
+  for (int64_t i = gtid(); i < nitems; i += gstride()) {
+    const int64_t o = offs[i];
+    if (o < 0) continue;
+    const uint8_t t = types[i];
+    int count = 1;
+    while (count < 128 && i + count < nitems && types[i + count] == t) ++count;
+    out[o] = t ? (uint8_t)(count - 1) : (uint8_t)(0x80 | (count - 1));
+  }
+}
+
+template <bool BLOCKS>
+cudaError_t launch_run(const int16_t* q, int64_t n, uint8_t* out, uint64_t* scratch, uint64_t* total, int* status,
+                       cudaStream_t s) {
+  const int64_t nitems = BLOCKS ? (n + 31) / 32 : n;
+  const int64_t ntiles = (nitems + kRunTileItems - 1) / kRunTileItems;
+  cudaError_t e = cudaMemsetAsync(scratch, 0, (2 * ntiles + 2) * sizeof(uint64_t), s);
+  if (e != cudaSuccess) return e;
+  if (ntiles == 0) {
+    uint64_t hdr = BLOCKS ? 4 : 0;
+    if (BLOCKS) {
+      e = cudaMemsetAsync(out, 0, 4, s);
+      if (e != cudaSuccess) return e;
+    }
+    return cudaMemcpyAsync(total, &hdr, sizeof(hdr), cudaMemcpyHostToDevice, s);
+  }
+  k_run_pass1<BLOCKS><<<(unsigned)ntiles, kThreads, 0, s>>>(RunItems<BLOCKS>{q, n}, out, scratch, total, status);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  k_run_pass2<<<grid_for(nitems, 1), kThreads, 0, s>>>(scratch, nitems, out);
+  return cudaGetLastError();
+}
+
+cudaError_t bsrle_encode(const int16_t* q, int64_t n, uint8_t* out, uint64_t* scratch, uint64_t* total_bytes,
+                         int* status, cudaStream_t s) {
+  return launch_run<true>(q, n, out, scratch, total_bytes, status, s);
+}
+cudaError_t rle_encode(const int16_t* q, int64_t n, uint8_t* out, uint64_t* scratch, uint64_t* total_bytes,
+                       int* status, cudaStream_t s) {
+  return launch_run<false>(q, n, out, scratch, total_bytes, status, s);
+}
+
+// ============================================================ stream decode
+// Walk: one thread per stream reproduces the reference decoder's control
+// flow and records, per decoded 32-block or RLE opcode, a descriptor
+// (out offset | length << 48, input offset + 1 or 0 for zeros).
+__device__ __forceinline__ uint32_t rd_u32(const uint8_t* p) {
+  return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
+}
+
+// Position after reading `cnt` values of `vb` bytes from `vals` where only
+// whole values inside the stream are consumed (the reference decoder pushes
+// 0 for the rest without advancing).
+__device__ __forceinline__ int64_t advance_values(int64_t vals, int64_t len, int cnt, int vb) {
+  const int64_t room = len > vals ? (len - vals) / vb : 0;
+  return vals + (int64_t)vb * min64((int64_t)cnt, room);
+}
+
+__global__ void k_walk(int kind, const uint8_t* __restrict__ data, const int64_t* __restrict__ soff,
+                       int nstreams, int64_t out_cap, int64_t* __restrict__ out_len, int64_t* __restrict__ table,
+                       int64_t table_cap, int* status) {
+  const int64_t sidx = gtid();
+  if (sidx >= nstreams) return;
+  const uint8_t* b = data + soff[sidx];
+  const int64_t len = soff[sidx + 1] - soff[sidx];
+  int64_t* row = table + sidx * (2 * table_cap + 2);
+  int64_t* tab = row + 2;
+  int64_t nent = 0, out = 0;
+  bool overflow = false;
+  auto emit = [&](int64_t o, int64_t l, int64_t in_plus1) {
+    if (nent >= table_cap) {
+      overflow = true;
+      return;
+    }
+    tab[2 * nent] = o | (l << 48);
+    tab[2 * nent + 1] = in_plus1;
+    ++nent;
+  };
+  if (kind == 3) {  // element RLE: no header
+    int64_t ptr = 0;
+    while (ptr < len && !overflow) {
+      const uint8_t op = b[ptr++];
+      if (op >= 128) {
+        const int64_t c = (int64_t)op - 128 + 1;
+        emit(out, c, 0);
+        out += c;
+      } else {
+        const int64_t c = (int64_t)op + 1;
+        const int64_t avail = min64(c, (len - ptr) / 2);
+        if (avail > 0) emit(out, avail, ptr + 1);
+        ptr += 2 * avail;
+        out += avail;
+      }
+    }
+    out_len[sidx] = out;
+  } else if (len < 4) {
+    out_len[sidx] = 0;
+  } else {
+    const int64_t n = rd_u32(b);
+    const int64_t nblk = (n + 31) / 32;
+    const int vb = kind == 1 ? 1 : 2;
+    int64_t ptr = 4;
+    if (kind == 0 || kind == 1) {
+      for (int64_t blk = 0; blk < nblk && !overflow; ++blk) {
+        if (ptr + 4 > len) break;
+        const uint32_t m = rd_u32(b + ptr);
+        const int64_t bl = blk == nblk - 1 ? n - blk * 32 : 32;
+        emit(out, bl, ptr + 1);
+        out += bl;
+        // Values that run past the end decode as 0 and do not advance.
+        ptr = advance_values(ptr + 4, len, __popc(m & (bl >= 32 ? 0xffffffffu : ((1u << bl) - 1u))), vb);
+      }
+      out_len[sidx] = kind == 1 ? n : min64(out, n);  // top-k pads to n; BlockSparse truncates
+    } else {  // BlockSparse+RLE
+      int64_t blk = 0;
+      while (blk < nblk && ptr < len && !overflow) {
+        const uint8_t op = b[ptr++];
+        if (op & 0x80) {
+          const int64_t c = (int64_t)(op & 0x7f) + 1;
+          for (int64_t k = 0; k < c && !overflow; ++k) {
+            const int64_t bl = (blk + k == nblk - 1) ? n - (blk + k) * 32 : 32;
+            if (out < n) emit(out, bl, 0);
+            out += bl;
+          }
+          blk += c;
+        } else {
+          const int64_t c = (int64_t)op + 1;
+          for (int64_t k = 0; k < c && !overflow; ++k) {
+            if (ptr + 4 > len) break;
+            const uint32_t m = rd_u32(b + ptr);
+            const int64_t bl = (blk == nblk - 1) ? n - blk * 32 : 32;
+            if (out < n) emit(out, bl, ptr + 1);
+            out += bl;
+            ptr = advance_values(ptr + 4, len, __popc(m & (bl >= 32 ? 0xffffffffu : ((1u << bl) - 1u))), 2);
+            blk += 1;
+          }
+        }
+      }
+      out_len[sidx] = min64(out, n);
+    }
+  }
+  if (overflow || out_len[sidx] > out_cap) dev::set_status(status, dev::kBounds, (int)sidx, (int)nent);
+  row[0] = nent;
+}
+
+// Expansion: one warp per descriptor; lanes write elements.
+__global__ void k_expand(int kind, const uint8_t* __restrict__ data, const int64_t* __restrict__ soff,
+                         const float* __restrict__ scales, int nstreams, int32_t* __restrict__ out, int64_t out_cap,
+                         const int64_t* __restrict__ out_len, const int64_t* __restrict__ table, int64_t table_cap) {
+  const int lane = threadIdx.x & 31;
+  const int64_t wid = gtid() >> 5, nw = gstride() >> 5;
+  const int64_t total = (int64_t)nstreams * table_cap;
+  for (int64_t e = wid; e < total; e += nw) {
+    const int64_t sidx = e / table_cap, ent = e % table_cap;
+    const int64_t* row = table + sidx * (2 * table_cap + 2);
+    if (ent >= row[0]) continue;  // past this stream's last descriptor
+    const int64_t* tab = row + 2;
+    const int64_t w0 = tab[2 * ent];
+    const int64_t o = w0 & ((1ll << 48) - 1), l = w0 >> 48, in1 = tab[2 * ent + 1];
+    const uint8_t* b = data + soff[sidx];
+    const int64_t len = soff[sidx + 1] - soff[sidx];
+    const float sc = scales[sidx];
+    const int64_t lim = min64(out_len[sidx], out_cap);
+    int32_t* dst = out + sidx * out_cap;
+    if (kind == 3) {
+      for (int64_t j = lane; j < l; j += 32) {
+        if (o + j >= lim) break;
+        int32_t v = 0;
+        if (in1) {
+          const int64_t p = in1 - 1 + 2 * j;
+          const int16_t c = (int16_t)((uint16_t)b[p] | ((uint16_t)b[p + 1] << 8));
+          v = q823_from_f32(NGL_FMUL((float)c, sc));
+        }
+        dst[o + j] = v;
+      }
+    } else {
+      if (lane < l && o + lane < lim) {
+        int32_t v = 0;
+        if (in1) {
+          const int64_t mo = in1 - 1;
+          const uint32_t m = rd_u32(b + mo);
+          if ((m >> lane) & 1u) {
+            const int vb = kind == 1 ? 1 : 2;
+            const int64_t p = mo + 4 + (int64_t)vb * __popc(m & ((1u << lane) - 1u));
+            if (kind == 1) {
+              if (p < len) v = q823_from_f32(NGL_FMUL((float)(int8_t)b[p], sc));
+            } else if (p + 2 <= len) {
+              const int16_t c = (int16_t)((uint16_t)b[p] | ((uint16_t)b[p + 1] << 8));
+              v = q823_from_f32(NGL_FMUL((float)c, sc));
+            }
+          }
+        }
+        dst[o + lane] = v;
+      }
+    }
+  }
+}
+
+// Top-k pads the decoded stream with zeros up to n (the walk reports n).
+__global__ void k_zero_fill(int32_t* out, int64_t out_cap, const int64_t* out_len, int nstreams) {
+  for (int64_t i = gtid(); i < (int64_t)nstreams * out_cap; i += gstride()) out[i] = 0;
+}
+
+cudaError_t stream_decode(int kind, const uint8_t* data, const int64_t* stream_off, const float* scales, int nstreams,
+                          int32_t* out, int64_t out_cap, int64_t* out_len, int64_t* table, int64_t table_cap,
+                          int* status, cudaStream_t s) {
+  if (nstreams <= 0) return cudaSuccess;
+  if (kind == 1) {
+    k_zero_fill<<<grid_for((int64_t)nstreams * out_cap), kThreads, 0, s>>>(out, out_cap, out_len, nstreams);
+  }
+  k_walk<<<(nstreams + 63) / 64, 64, 0, s>>>(kind, data, stream_off, nstreams, out_cap, out_len, table, table_cap,
+                                            status);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  const int64_t warps = (int64_t)nstreams * table_cap;
+  int64_t g = (warps * 32 + kThreads - 1) / kThreads;
+  if (g > 148 * 32) g = 148 * 32;
+  if (g < 1) g = 1;
+  k_expand<<<(unsigned)g, kThreads, 0, s>>>(kind, data, stream_off, scales, nstreams, out, out_cap, out_len, table,
+                                           table_cap);
+  return cudaGetLastError();
+}
+
+// ===================================================== stochastic compat (K7)
+__global__ void k_absmax(const int32_t* __restrict__ r, int64_t n, uint32_t* max_bits) {
+  float m = 0.0f;
+  for (int64_t i = gtid(); i < n; i += gstride()) m = fmaxf(m, fabsf(q823_to_f32(r[i])));
+  const uint32_t w = __reduce_max_sync(kFull, __float_as_uint(m));
+  if ((threadIdx.x & 31) == 0) atomicMax(max_bits, w);
+}
+
+__device__ __forceinline__ float compat_scale(float max_val, int bits) {
+  if (!(max_val > 1e-9f)) return 1.0f;
+  const int levels = (bits >= 1 && bits < 31) ? ((1 << bits) - 1) : 255;
+  return NGL_FDIV(max_val, NGL_FDIV((float)levels, 2.0f));
+}
+
+__global__ void k_stochastic_encode(const int32_t* __restrict__ r, int64_t n, int bits, uint64_t seed,
+                                    uint64_t counter, const uint32_t* max_bits, float* scale_out,
+                                    uint8_t* __restrict__ out) {
+  const float scale = compat_scale(__uint_as_float(*max_bits), bits);
+  if (gtid() == 0) *scale_out = scale;
+  if (bits == 4) {
+    const int64_t nb = (n + 1) / 2;
+    for (int64_t j = gtid(); j < nb; j += gstride()) {
+      uint8_t byte = 0;
+      for (int k = 0; k < 2; ++k) {
+        const int64_t i = 2 * j + k;
+        if (i >= n) break;
+        int32_t q = compat_stochastic_round(NGL_FDIV(q823_to_f32(r[i]), scale), seed, counter + (uint64_t)i);
+        q = q < -8 ? -8 : (q > 7 ? 7 : q);
+        const uint8_t nb4 = (uint8_t)((int8_t)q & 0x0F);
+        byte |= k == 0 ? (uint8_t)(nb4 << 4) : nb4;
+      }
+      out[j] = byte;
+    }
+  } else if (bits == 8) {
+    for (int64_t i = gtid(); i < n; i += gstride()) {
+      int32_t q = compat_stochastic_round(NGL_FDIV(q823_to_f32(r[i]), scale), seed, counter + (uint64_t)i);
+      q = q < -128 ? -128 : (q > 127 ? 127 : q);
+      out[i] = (uint8_t)(int8_t)q;
+    }
+  } else {
+    for (int64_t i = gtid(); i < n; i += gstride()) {
+      float q = f_round(NGL_FDIV(q823_to_f32(r[i]), scale));
+      if (!is_nan(q)) q = fminf(fmaxf(q, -128.0f), 127.0f);
+      out[i] = (uint8_t)sat_f32_to_i8(q);
+    }
+  }
+}
+
+__global__ void k_stochastic_decode(const uint8_t* __restrict__ b, int64_t nbytes, int bits, float scale,
+                                    int32_t* __restrict__ out) {
+  for (int64_t i = gtid(); i < nbytes; i += gstride()) {
+    if (bits == 4) {
+      const int32_t hi = ((int32_t)((uint32_t)b[i] << 24)) >> 28;
+      const int32_t lo = ((int32_t)((uint32_t)b[i] << 28)) >> 28;
+      out[2 * i] = q823_from_f32(NGL_FMUL((float)hi, scale));
+      out[2 * i + 1] = q823_from_f32(NGL_FMUL((float)lo, scale));
+    } else {
+      out[i] = q823_from_f32(NGL_FMUL((float)(int8_t)b[i], scale));
+    }
+  }
+}
+
+cudaError_t absmax_f32_of_fixed(const int32_t* r, int64_t n, uint32_t* max_bits, cudaStream_t s) {
+  cudaError_t e = cudaMemsetAsync(max_bits, 0, sizeof(uint32_t), s);
+  if (e != cudaSuccess) return e;
+  if (n > 0) k_absmax<<<grid_for(n), kThreads, 0, s>>>(r, n, max_bits);
+  return cudaGetLastError();
+}
+cudaError_t stochastic_encode(const int32_t* r, int64_t n, int bits, uint64_t seed, uint64_t counter,
+                              const uint32_t* max_bits, float* scale_out, uint8_t* out, cudaStream_t s) {
+  k_stochastic_encode<<<grid_for(n > 0 ? n : 1), kThreads, 0, s>>>(r, n, bits, seed, counter, max_bits, scale_out,
+                                                                   out);
+  return cudaGetLastError();
+}
+cudaError_t stochastic_decode(const uint8_t* b, int64_t nbytes, int bits, float scale, int32_t* out,
+                              cudaStream_t s) {
+  if (nbytes > 0) k_stochastic_decode<<<grid_for(nbytes), kThreads, 0, s>>>(b, nbytes, bits, scale, out);
+  return cudaGetLastError();
+}
+
+// ============================================ top-k radix-select threshold (K8)
+// Pass p histograms digit p (MSB first) of the |x| bit patterns that match
+// the prefix selected by passes 0..p-1; every CTA re-derives that prefix
+// from the previous histograms (256 bins each), so no host round trip.
+__device__ void select_prefix(const uint32_t* hist, int passes, int64_t target, uint32_t* prefix_out,
+                              int64_t* target_out) {
+  uint32_t prefix = 0;
+  for (int p = 0; p < passes; ++p) {
+    const uint32_t* h = hist + p * 256;
+    int64_t acc = 0;
+    int d = 255;
+    for (; d > 0; --d) {
+      if (acc + (int64_t)h[d] >= target) break;
+      acc += h[d];
+    }
+    target -= acc;
+    prefix = (prefix << 8) | (uint32_t)d;
+  }
+  *prefix_out = prefix;
+  *target_out = target;
+}
+
+__global__ void k_radix_hist(const int32_t* __restrict__ r, int64_t n, int pass, int64_t keep,
+                             uint32_t* __restrict__ hist) {
+  __shared__ uint32_t sh[256];
+  __shared__ uint32_t s_prefix;
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) sh[i] = 0;
+  if (threadIdx.x == 0) {
+    int64_t t;
+    select_prefix(hist, pass, keep, &s_prefix, &t);
+  }
+  __syncthreads();
+  const uint32_t prefix = s_prefix;
+  const int shift = 24 - 8 * pass;
+  for (int64_t i = gtid(); i < n; i += gstride()) {
+    const uint32_t u = __float_as_uint(fabsf(q823_to_f32(r[i])));
+    if (pass == 0 || (u >> (shift + 8)) == prefix) atomicAdd(&sh[(u >> shift) & 0xffu], 1u);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < 256; i += blockDim.x)
+    if (sh[i]) atomicAdd(&hist[pass * 256 + i], sh[i]);
+}
+
+__global__ void k_radix_final(const uint32_t* hist, int64_t keep, const uint32_t* max_bits, float* thr,
+                              float* scale) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  if (keep == 0) {
+    *thr = 1e-9f;
+  } else {
+    uint32_t prefix;
+    int64_t t;
+    select_prefix(hist, 4, keep, &prefix, &t);
+    *thr = fmaxf(__uint_as_float(prefix), 1e-9f);
+  }
+  const float mx = __uint_as_float(*max_bits);
+  *scale = mx > 1e-9f ? NGL_FDIV(mx, 127.0f) : 1.0f;
+}
+
+cudaError_t topk_threshold(const int32_t* r, int64_t n, int64_t keep, uint32_t* hist, const uint32_t* max_bits,
+                           float* threshold, float* scale, cudaStream_t s) {
+  cudaError_t e = cudaMemsetAsync(hist, 0, 4 * 256 * sizeof(uint32_t), s);
+  if (e != cudaSuccess) return e;
+  if (keep > n) keep = n;
+  if (keep > 0)
+    for (int p = 0; p < 4; ++p) k_radix_hist<<<grid_for(n), kThreads, 0, s>>>(r, n, p, keep, hist);
+  k_radix_final<<<1, 32, 0, s>>>(hist, keep, max_bits, threshold, scale);
+  return cudaGetLastError();
+}
+
+}  // namespace codec
+}  // namespace ngl

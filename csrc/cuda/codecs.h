@@ -1,0 +1,88 @@
+// Launch API of the sm_100a codec kernels (csrc/cuda/codec_kernels.cu):
+// Q8.23 elementwise math, the fused HPC closed-loop step, the error-bounded,
+// BlockSparse, BlockSparse+RLE and RLE encoders/decoders, the reference's
+// stochastic INT4/INT8 codec and its top-k codec with a radix-select
+// threshold.  Every byte stream is identical to the host library's.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ngl {
+namespace codec {
+
+constexpr int kPackThreads = 256;
+constexpr int kPackBlocksPerWarp = 16;                            // 32-element blocks per warp per tile
+constexpr int kPackTileBlocks = (kPackThreads / 32) * kPackBlocksPerWarp;  // 128 blocks = 4096 elements
+constexpr int kRunTileItems = 4096;                               // items per tile of the run-length encoders
+
+// Scratch words needed by the look-back encoders for n elements.
+int64_t pack_scratch_words(int64_t n);
+int64_t run_scratch_words(int64_t items);
+
+// ---- Q8.23 (K2) ----
+cudaError_t from_f32_dev(const float* x, int32_t* q, int64_t n, cudaStream_t s);
+cudaError_t to_f32_dev(const int32_t* q, float* x, int64_t n, cudaStream_t s);
+cudaError_t q823_addsub(const int32_t* a, const int32_t* b, int32_t* out, int64_t n, bool sub, cudaStream_t s);
+cudaError_t q823_mul_scalar(const int32_t* a, int32_t* out, int64_t n, float scalar, cudaStream_t s);
+
+// ---- Error-bounded INT16 (K3) ----
+// codes[i] = round(to_f32(r[i]) / scale) clamped to i16.
+cudaError_t eb_encode(const int32_t* r, int16_t* codes, int64_t n, float scale, cudaStream_t s);
+// out[i] = from_f32(codes[i] * scale)
+cudaError_t eb_decode(const int16_t* codes, int32_t* out, int64_t n, float scale, cudaStream_t s);
+// Fused closed-loop step of the LinearPredictor + EB codec for one snapshot:
+// x -> Q8.23; pred = hist>=2 ? s_t + (s_t - s_tm1) : hist==1 ? s_t : none;
+// r = x - pred; codes = EB(r); recon = pred + from_f32(codes * scale);
+// maxerr (float bits, atomicMax) = max |to_f32(x) - to_f32(recon)|.
+cudaError_t hpc_step(const float* x, const int32_t* s_t, const int32_t* s_tm1, int hist, float scale, int16_t* codes,
+                     int32_t* recon, uint32_t* maxerr_bits, int64_t n, cudaStream_t s);
+// Linear predictor add-back over T decoded residual snapshots (in place):
+// recon_t = pred_t + res_t with the predictor's history chain.
+cudaError_t linear_addback(int32_t* res, int64_t particles, int64_t steps, cudaStream_t s);
+
+// ---- Mask packers (BlockSparse, top-k compat) with decoupled look-back ----
+// BlockSparse from i16 codes: [u32 n] then per 32-block [u32 mask][i16 per
+// set bit].  Top-k compat from Q8.23 residuals: [u32 n] then per 32-block
+// [u32 mask][i8 per kept], kept iff |x| >= *threshold, value
+// round(x / *scale) clamped to i8.
+// scratch: pack_scratch_words(n) u64 words; total_bytes: one u64.
+cudaError_t bs_encode(const int16_t* q, int64_t n, uint8_t* out, uint64_t* scratch, uint64_t* total_bytes,
+                      int* status, cudaStream_t s);
+cudaError_t topk_encode(const int32_t* r, int64_t n, const float* threshold, const float* scale, uint8_t* out,
+                        uint64_t* scratch, uint64_t* total_bytes, int* status, cudaStream_t s);
+
+// ---- Run-length encoders from i16 codes ----
+// BlockSparse+RLE ([u32 n], opcode runs over 32-blocks) and element RLE
+// (opcode runs over codes, no header).  scratch: run_scratch_words(items).
+cudaError_t bsrle_encode(const int16_t* q, int64_t n, uint8_t* out, uint64_t* scratch, uint64_t* total_bytes,
+                         int* status, cudaStream_t s);
+cudaError_t rle_encode(const int16_t* q, int64_t n, uint8_t* out, uint64_t* scratch, uint64_t* total_bytes,
+                       int* status, cudaStream_t s);
+
+// ---- Stream decoders: header walk (one thread per stream) + parallel expansion ----
+// kind: 0 = BlockSparse (i16), 1 = top-k compat (i8), 2 = BlockSparse+RLE, 3 = RLE.
+// Stream i is data[stream_off[i] .. stream_off[i+1]) with scale scales[i];
+// it decodes into out[i * out_cap ...] (Q8.23) and out_len[i] receives the
+// decoded length the reference's decoder produces (status kBounds when that
+// exceeds out_cap, or a stream needs more than table_cap descriptors).
+// table: nstreams * (2 * table_cap + 2) int64 words (count + descriptors).
+cudaError_t stream_decode(int kind, const uint8_t* data, const int64_t* stream_off, const float* scales, int nstreams,
+                          int32_t* out, int64_t out_cap, int64_t* out_len, int64_t* table, int64_t table_cap,
+                          int* status, cudaStream_t s);
+
+// ---- Reference stochastic INT4/INT8 codec (K7) ----
+cudaError_t absmax_f32_of_fixed(const int32_t* r, int64_t n, uint32_t* max_bits, cudaStream_t s);
+cudaError_t stochastic_encode(const int32_t* r, int64_t n, int bits, uint64_t seed, uint64_t counter,
+                              const uint32_t* max_bits, float* scale_out, uint8_t* out, cudaStream_t s);
+cudaError_t stochastic_decode(const uint8_t* b, int64_t nbytes, int bits, float scale, int32_t* out,
+                              cudaStream_t s);
+
+// ---- Top-k compat threshold by radix select (K8) ----
+// Finds the value at ascending rank (n - keep) of |to_f32(r)| with four 8-bit
+// radix passes; writes max(value, 1e-9) to *threshold (1e-9 when keep == 0)
+// and max|x|/127 (or 1) to *scale.  hist: 4 x 256 u32 + 4 words scratch.
+cudaError_t topk_threshold(const int32_t* r, int64_t n, int64_t keep, uint32_t* hist, const uint32_t* max_bits,
+                           float* threshold, float* scale, cudaStream_t s);
+
+}  // namespace codec
+}  // namespace ngl

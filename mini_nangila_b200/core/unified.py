@@ -116,7 +116,8 @@ class UnifiedQuantizer:
         c = _dev_codecs()
         if isinstance(m, Stochastic):
             b, s = c.stochastic_quantize(residual.data, int(m.bits), int(m.seed), self._counter)
-            self._counter += residual.len()
+            if int(m.bits) in (4, 8):  # other widths round deterministically (no PRNG draws)
+                self._counter += residual.len()
             return b, s
         if isinstance(m, ErrorBounded):
             return c.eb_quantize(residual.data, float(np.float32(m.epsilon)))

@@ -1,0 +1,123 @@
+"""sm_100a codec kernels vs the C++ host library: identical bytes and
+identical decoded Q8.23 values for every reference format."""
+import numpy as np
+import pytest
+import torch
+
+from mini_nangila_b200 import _ext
+from mini_nangila_b200.checkpoint import lammps, nzcp
+from mini_nangila_b200.core import FixedPointBuffer, QuantizationMode, UnifiedQuantizer
+from mini_nangila_b200.hpc import BlockSparseQuantizer, BlockSparseRleQuantizer, ErrorBoundedQuantizer, \
+    RunLengthQuantizer
+from mini_nangila_b200.ops import codecs, trajectory
+
+pytestmark = pytest.mark.gpu
+
+SIZES = [0, 1, 31, 32, 33, 255, 256, 257, 4095, 4096, 4097, 100003]
+
+
+def _resid(n, seed, sparsity=0.7, scale=0.01):
+    g = np.random.default_rng(seed)
+    x = (g.standard_normal(n) * scale).astype(np.float32)
+    x[g.random(n) < sparsity] = 0.0
+    return FixedPointBuffer.from_f32(x)
+
+
+def _host_bytes(b):
+    return b if isinstance(b, bytes) else b.tobytes()
+
+
+@pytest.mark.parametrize("n", SIZES)
+def test_q823_ops(n):
+    g = np.random.default_rng(n)
+    x = (g.standard_normal(n) * 50).astype(np.float32)
+    x[: min(n, 3)] = [1e30, -1e30, np.nan][: min(n, 3)]
+    h = FixedPointBuffer.from_f32(x)
+    d = FixedPointBuffer.from_f32(torch.from_numpy(x).cuda())
+    assert np.array_equal(d.numpy(), h.numpy())
+    assert np.array_equal(d.to_f32().cpu().numpy().view(np.uint32), h.to_f32().view(np.uint32))
+    y = FixedPointBuffer.from_f32((g.standard_normal(n) * 50).astype(np.float32))
+    assert np.array_equal(d.add(y.cuda()).numpy(), h.add(y).numpy())
+    assert np.array_equal(d.sub(y.cuda()).numpy(), h.sub(y).numpy())
+    for s in (0.9, np.float32(1.0) - np.float32(0.9), -1.5, 0.5):
+        assert np.array_equal(d.mul_scalar(s).numpy(), h.mul_scalar(s).numpy())
+
+
+@pytest.mark.parametrize("n", SIZES)
+@pytest.mark.parametrize("cls", [ErrorBoundedQuantizer, BlockSparseQuantizer, BlockSparseRleQuantizer,
+                                 RunLengthQuantizer])
+@pytest.mark.parametrize("sparsity", [0.0, 0.7, 0.99])
+def test_eb_family_bytes_and_decode(n, cls, sparsity):
+    q = cls(1e-3)
+    r = _resid(n, 11, sparsity)
+    hb, hs = q.quantize(r)
+    db, ds = q.quantize(r.cuda())
+    assert ds == hs
+    assert db.cpu().numpy().tobytes() == _host_bytes(hb)
+    hr = q.dequantize(hb, hs)
+    dr = q.dequantize(hb, hs, device="cuda")
+    assert np.array_equal(dr.numpy(), hr.numpy())
+
+
+@pytest.mark.parametrize("cls", [BlockSparseQuantizer, BlockSparseRleQuantizer, RunLengthQuantizer])
+def test_truncated_streams_decode_like_host(cls):
+    q = cls(1e-3)
+    r = _resid(3000, 5, 0.5)
+    hb, hs = q.quantize(r)
+    for cut in (1, 3, 4, 5, 7, 40, len(hb) // 2, len(hb) - 1):
+        b = hb[:cut]
+        assert np.array_equal(q.dequantize(b, hs, device="cuda").numpy(), q.dequantize(b, hs).numpy()), cut
+
+
+def test_long_zero_runs():
+    x = np.zeros(200000, np.float32)
+    x[::50000] = 1.0
+    r = FixedPointBuffer.from_f32(x)
+    for cls in (BlockSparseRleQuantizer, RunLengthQuantizer):
+        q = cls(1e-3)
+        hb, hs = q.quantize(r)
+        db, _ = q.quantize(r.cuda())
+        assert db.cpu().numpy().tobytes() == hb
+
+
+@pytest.mark.parametrize("n", [1, 2, 3, 31, 1000, 65537])
+@pytest.mark.parametrize("bits", [4, 8, 3])
+def test_stochastic_compat(n, bits):
+    r = _resid(n, 3, 0.2, 1.0)
+    hq = UnifiedQuantizer(QuantizationMode.Stochastic(seed=2**63 + 5, bits=bits))
+    dq = UnifiedQuantizer(QuantizationMode.Stochastic(seed=2**63 + 5, bits=bits))
+    for _ in range(2):  # counter persists across calls
+        hb, hs = hq.quantize(r)
+        db, ds = dq.quantize(r.cuda())
+        assert ds == hs and db.cpu().numpy().tobytes() == hb
+    assert hq.counter == dq.counter
+    assert np.array_equal(dq.dequantize(hb, hs, device="cuda").numpy(), hq.dequantize(hb, hs).numpy())
+
+
+@pytest.mark.parametrize("n", [1, 7, 32, 100, 1000, 65537, 300000])
+@pytest.mark.parametrize("k", [0.0, 0.001, 0.05, 0.1, 0.25, 1.0, 1.5])
+def test_topk_compat(n, k):
+    g = np.random.default_rng(n)
+    x = (g.standard_normal(n)).astype(np.float32)
+    x[g.random(n) < 0.3] = 0.25  # ties
+    r = FixedPointBuffer.from_f32(x)
+    q = UnifiedQuantizer(QuantizationMode.TopK(k))
+    hb, hs = q.quantize(r)
+    db, ds = q.quantize(r.cuda())
+    assert ds == hs
+    assert db.cpu().numpy().tobytes() == hb
+    assert np.array_equal(q.dequantize(hb, hs, device="cuda").numpy(), q.dequantize(hb, hs).numpy())
+
+
+@pytest.mark.parametrize("codec", ["eb", "rle", "bs", "bsrle"])
+def test_nz_pipeline_device_matches_host(codec):
+    P, T = 30001, 7
+    data = lammps.generate_synthetic(P, T)
+    hb, hst = nzcp.compress(data, P, T, codec, 1e-3)
+    db, dst = trajectory.compress(torch.from_numpy(data).cuda().view(T, P), codec, 1e-3)
+    assert db == hb
+    assert dst["total_comp"] == hst["total_comp"]
+    assert abs(dst["max_abs_err"] - hst["max_abs_err"]) == 0.0
+    host_vals = nzcp.decompress(hb)
+    dev_vals = trajectory.decompress(hb).cpu().numpy().reshape(-1)
+    assert np.array_equal(dev_vals.view(np.uint32), host_vals.view(np.uint32))
