@@ -1,0 +1,176 @@
+"""Time one sm_100a kernel on a synthetic input (single GPU).
+
+    python -m mini_nangila_b200.apps.kernel_bench --op fused_oneshot --n 67108864
+
+Ops: fused_single (INT4, world 1), fused_oneshot (rank 0 of a 2-rank one-shot
+all-reduce with the peer's payload and flags pre-delivered into local memory,
+so the exchange kernel runs in full on one GPU), fused_topk_single,
+fused_topk_oneshot, hpc_step, bs_encode, bsrle_encode, rle_encode,
+bs_decode, stochastic_encode, topk_encode.
+
+Inputs are larger than the 126 MB L2 for the default n.  Each timed launch is
+bracketed by CUDA events on the launching stream after warm-up; the figure
+reported is the median.  Algorithmic bytes / time is compared with the
+measured HBM copy bandwidth of MEASURED_PEAKS.json.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+def hbm_peak() -> tuple[float, str]:
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
+            return float(json.load(fh)["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def _time(fn, iters, warmup, setup=None):
+    for _ in range(warmup):
+        if setup:
+            setup()
+        fn()
+    torch.cuda.synchronize()
+    out = []
+    for _ in range(iters):
+        if setup:
+            setup()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        e.synchronize()
+        out.append(s.elapsed_time(e))
+    return statistics.median(out)
+
+
+def _emulated_oneshot(n, mode, k):
+    """Rank 0 of a 2-rank one-shot launch; the peer's record and column flags
+    are written into rank 0's region before every call."""
+    from mini_nangila_b200 import _ext
+    from mini_nangila_b200.parallel.fused import MAX_COLS, MODES, VARIANTS, FusedAllReduce, make_layout
+
+    c = _ext.cuda()
+    dev = torch.device("cuda")
+    L = make_layout(2, n, k, (mode,))
+    reg0 = torch.zeros(L.total, dtype=torch.uint8, device=dev)
+    reg1 = torch.zeros(L.total, dtype=torch.uint8, device=dev)
+    status = torch.zeros(4, dtype=torch.int32, device=dev)
+    comm = c.FusedComm(2, 0, [reg0.data_ptr(), reg1.data_ptr()], L.flags_off, L.inbox_off, L.slot_bytes,
+                       L.result_off, L.result_bytes, status)
+    mcode = MODES[mode]
+    grid = c.fused_grid(n, mcode, False, VARIANTS["oneshot"], 0, 0)
+    tag = FusedAllReduce.tag_for(n, 0)
+    g1 = torch.randn(n, device=dev) * 1e-3
+    p1, _ = c.product_encode(g1, None, None, mcode, k, True, 3, 1, 0, 0)
+    g = torch.randn(n, device=dev) * 1e-3
+    pred = torch.zeros(n, device=dev)
+    ef = torch.zeros(n, device=dev)
+    flags = reg0[L.flags_off:].view(torch.int64)
+    ftag = tag ^ ((grid * 0x9E3779B1) & 0xFFFFFFFF)
+    for par in (0, 1):
+        slot = L.inbox_off + (par * 2 + 1) * L.slot_bytes
+        reg0[slot: slot + p1.numel()] = p1
+
+    def setup():
+        epoch = comm.epoch + 1
+        par = epoch & 1
+        val = (ftag << 32) | epoch
+        if val >= 1 << 63:
+            val -= 1 << 64
+        base = ((par * 2 + 0) * 2 + 1) * MAX_COLS
+        flags[base: base + grid] = val
+
+    def run():
+        comm.run(g, pred, ef, mcode, k, VARIANTS["oneshot"], True, 3, 0, 1, 0.9, False, 0, int(5e9), tag)
+
+    wire = p1.numel()
+    # g, pred, ef read; ef, g, pred written; own record written twice (self + "peer"),
+    # two records read.
+    algo = 24 * n + 4 * wire
+    return setup, run, algo, status
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--op", required=True)
+    ap.add_argument("--n", type=int, default=64 << 20)
+    ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--k", type=int, default=13, help="top-k kept per 256-block")
+    args = ap.parse_args()
+    torch.cuda.set_device(0)
+    from mini_nangila_b200 import _ext
+    from mini_nangila_b200.parallel.fused import FusedAllReduce, payload_bytes
+
+    c = _ext.cuda()
+    n, dev = args.n, torch.device("cuda")
+    setup, status = None, None
+    if args.op in ("fused_single", "fused_topk_single"):
+        mode = "topk" if "topk" in args.op else "int4"
+        comm = FusedAllReduce(n, device=dev)
+        g = torch.randn(n, device=dev) * 1e-3
+        pred = torch.zeros(n, device=dev)
+        ef = torch.zeros(n, device=dev)
+        run = lambda: comm.allreduce_(g, pred, ef, mode=mode, k=args.k, step=1)  # noqa: E731
+        algo = 24 * n
+        status = comm.status
+    elif args.op in ("fused_oneshot", "fused_topk_oneshot"):
+        mode = "topk" if "topk" in args.op else "int4"
+        setup, run, algo, status = _emulated_oneshot(n, mode, args.k)
+    elif args.op == "hpc_step":
+        x = torch.rand(n, device=dev) * 100
+        st = c.q823_from_f32(x)
+        stm1 = c.q823_from_f32(x * 0.999)
+        codes = torch.empty(n, dtype=torch.int16, device=dev)
+        recon = torch.empty(n, dtype=torch.int32, device=dev)
+        mx = torch.zeros(1, dtype=torch.int32, device=dev)
+        run = lambda: c.hpc_step(x, st, stm1, 2, 2e-3, codes, recon, mx)  # noqa: E731
+        algo = 4 * n * 3 + 2 * n + 4 * n
+    elif args.op in ("bs_encode", "bsrle_encode", "rle_encode"):
+        kind = {"bs_encode": 0, "bsrle_encode": 2, "rle_encode": 3}[args.op]
+        g = np.random.default_rng(0)
+        q = torch.from_numpy((g.standard_normal(n) * 50).astype(np.int16)).to(dev)
+        q[torch.rand(n, device=dev) < 0.7] = 0
+        out_len = c.pack_codes(q, kind).numel()
+        run = lambda: c.pack_codes(q, kind)  # noqa: E731
+        algo = 2 * n + out_len
+    elif args.op == "bs_decode":
+        q = (torch.randn(n, device=dev) * 50).to(torch.int16)
+        q[torch.rand(n, device=dev) < 0.7] = 0
+        b = c.pack_codes(q, 0)
+        off = torch.tensor([0, b.numel()], dtype=torch.int64, device=dev)
+        sc = torch.tensor([2e-3], device=dev)
+        run = lambda: c.decode_streams(b, off, sc, 0, n, (n + 31) // 32)  # noqa: E731
+        algo = b.numel() + 4 * n
+    elif args.op == "stochastic_encode":
+        r = c.q823_from_f32(torch.randn(n, device=dev))
+        run = lambda: c.stochastic_quantize(r, 4, 42, 0)  # noqa: E731
+        algo = 2 * 4 * n + n // 2
+    elif args.op == "topk_encode":
+        r = c.q823_from_f32(torch.randn(n, device=dev))
+        run = lambda: c.topk_quantize(r, 0.05)  # noqa: E731
+        algo = 6 * 4 * n + n // 10
+    else:
+        raise SystemExit(f"unknown op {args.op}")
+    ms = _time(run, args.iters, args.warmup, setup)
+    torch.cuda.synchronize()
+    if status is not None and int(status[0]) != 0:
+        raise SystemExit(f"kernel reported status {status.tolist()}")
+    peak, src = hbm_peak()
+    gbs = algo / (ms * 1e6)
+    print(json.dumps({"op": args.op, "n": n, "ms": ms, "algo_bytes": algo, "GBps": gbs,
+                      f"frac_of_{src}_hbm": gbs / peak, "hbm_peak_gbs": peak}), flush=True)
+
+
+if __name__ == "__main__":
+    main()
