@@ -602,17 +602,46 @@ __device__ __forceinline__ int64_t advance_values(int64_t vals, int64_t len, int
   return vals + (int64_t)vb * min64((int64_t)cnt, room);
 }
 
-__global__ void k_walk(int kind, const uint8_t* __restrict__ data, const int64_t* __restrict__ soff,
-                       int nstreams, int64_t out_cap, int64_t* __restrict__ out_len, int64_t* __restrict__ table,
-                       int64_t table_cap, int* status) {
-  const int64_t sidx = gtid();
+constexpr int kWalkWin = 32768;  // bytes of a stream staged in shared memory at a time
+
+// One CTA per stream: all threads stage a window of the stream into shared
+// memory with 16-byte loads, then thread 0 runs the reference decoder's
+// control flow from shared memory (a resumable state machine, so tokens may
+// straddle windows) and records one descriptor per decoded 32-block or RLE
+// opcode.  Tokens are processed only while they lie entirely in the window
+// (or the window reaches the end of the stream).
+__global__ void __launch_bounds__(kThreads) k_walk(int kind, const uint8_t* __restrict__ data,
+                                                   const int64_t* __restrict__ soff, int nstreams, int64_t out_cap,
+                                                   int64_t* __restrict__ out_len, int64_t* __restrict__ table,
+                                                   int64_t table_cap, int* status) {
+  __shared__ __align__(16) uint8_t win[kWalkWin];
+  __shared__ int64_t s_ptr, s_base;
+  __shared__ int s_done;
+  const int sidx = blockIdx.x;
   if (sidx >= nstreams) return;
   const uint8_t* b = data + soff[sidx];
   const int64_t len = soff[sidx + 1] - soff[sidx];
-  int64_t* row = table + sidx * (2 * table_cap + 2);
+  int64_t* row = table + (int64_t)sidx * (2 * table_cap + 2);
   int64_t* tab = row + 2;
-  int64_t nent = 0, out = 0;
-  bool overflow = false;
+  // walker state (thread 0)
+  int64_t ptr = 0, out = 0, nent = 0, blk = 0, n = 0, nblk = 0, lit = 0;
+  bool overflow = false, done = false;
+  const int vb = kind == 1 ? 1 : 2;
+  const int64_t max_tok = kind == 3 ? 257 : (kind == 2 ? 69 : 4 + 32 * vb);
+  if (threadIdx.x == 0) {
+    if (kind != 3) {
+      if (len < 4) {
+        done = true;
+      } else {
+        n = (int64_t)rd_u32(b);
+        nblk = (n + 31) / 32;
+        ptr = 4;
+      }
+    }
+    s_ptr = ptr;
+    s_done = done ? 1 : 0;
+  }
+  __syncthreads();
   auto emit = [&](int64_t o, int64_t l, int64_t in_plus1) {
     if (nent >= table_cap) {
       overflow = true;
@@ -622,71 +651,103 @@ __global__ void k_walk(int kind, const uint8_t* __restrict__ data, const int64_t
     tab[2 * nent + 1] = in_plus1;
     ++nent;
   };
-  if (kind == 3) {  // element RLE: no header
-    int64_t ptr = 0;
-    while (ptr < len && !overflow) {
-      const uint8_t op = b[ptr++];
-      if (op >= 128) {
-        const int64_t c = (int64_t)op - 128 + 1;
-        emit(out, c, 0);
-        out += c;
-      } else {
-        const int64_t c = (int64_t)op + 1;
-        const int64_t avail = min64(c, (len - ptr) / 2);
-        if (avail > 0) emit(out, avail, ptr + 1);
-        ptr += 2 * avail;
-        out += avail;
-      }
-    }
-    out_len[sidx] = out;
-  } else if (len < 4) {
-    out_len[sidx] = 0;
-  } else {
-    const int64_t n = rd_u32(b);
-    const int64_t nblk = (n + 31) / 32;
-    const int vb = kind == 1 ? 1 : 2;
-    int64_t ptr = 4;
-    if (kind == 0 || kind == 1) {
-      for (int64_t blk = 0; blk < nblk && !overflow; ++blk) {
-        if (ptr + 4 > len) break;
-        const uint32_t m = rd_u32(b + ptr);
-        const int64_t bl = blk == nblk - 1 ? n - blk * 32 : 32;
-        emit(out, bl, ptr + 1);
-        out += bl;
-        // Values that run past the end decode as 0 and do not advance.
-        ptr = advance_values(ptr + 4, len, __popc(m & (bl >= 32 ? 0xffffffffu : ((1u << bl) - 1u))), vb);
-      }
-      out_len[sidx] = kind == 1 ? n : min64(out, n);  // top-k pads to n; BlockSparse truncates
-    } else {  // BlockSparse+RLE
-      int64_t blk = 0;
-      while (blk < nblk && ptr < len && !overflow) {
-        const uint8_t op = b[ptr++];
-        if (op & 0x80) {
-          const int64_t c = (int64_t)(op & 0x7f) + 1;
-          for (int64_t k = 0; k < c && !overflow; ++k) {
-            const int64_t bl = (blk + k == nblk - 1) ? n - (blk + k) * 32 : 32;
-            if (out < n) emit(out, bl, 0);
-            out += bl;
+  while (!s_done) {
+    // stage [base, base + kWalkWin) with 16-byte loads from an aligned base
+    const int64_t p0 = s_ptr;
+    const int64_t base = p0 - (int64_t)(reinterpret_cast<uintptr_t>(b + p0) & 15u);
+    const int64_t hi = min64(len, base + kWalkWin);
+    const int64_t cnt = hi - base;
+    const uint4* src = reinterpret_cast<const uint4*>(b + base);
+    for (int64_t i = threadIdx.x; i < cnt / 16; i += blockDim.x) reinterpret_cast<uint4*>(win)[i] = src[i];
+    for (int64_t i = (cnt / 16) * 16 + threadIdx.x; i < cnt; i += blockDim.x) win[i] = b[base + i];
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const bool last = hi == len;
+      auto fits = [&](int64_t p) { return last || p + max_tok <= hi; };
+      auto byte = [&](int64_t p) -> uint32_t { return win[p - base]; };
+      auto u32 = [&](int64_t p) -> uint32_t {
+        return byte(p) | (byte(p + 1) << 8) | (byte(p + 2) << 16) | (byte(p + 3) << 24);
+      };
+      while (!done && !overflow && fits(ptr)) {
+        if (kind == 0 || kind == 1) {  // BlockSparse / top-k compat
+          if (blk >= nblk || ptr + 4 > len) {
+            done = true;
+            break;
           }
-          blk += c;
-        } else {
-          const int64_t c = (int64_t)op + 1;
-          for (int64_t k = 0; k < c && !overflow; ++k) {
-            if (ptr + 4 > len) break;
-            const uint32_t m = rd_u32(b + ptr);
+          const uint32_t m = u32(ptr);
+          const int64_t bl = blk == nblk - 1 ? n - blk * 32 : 32;
+          emit(out, bl, ptr + 1);
+          out += bl;
+          ptr = advance_values(ptr + 4, len, __popc(m & (bl >= 32 ? 0xffffffffu : ((1u << bl) - 1u))), vb);
+          ++blk;
+        } else if (kind == 2) {  // BlockSparse + RLE
+          if (lit == 0) {
+            if (!(blk < nblk && ptr < len)) {
+              done = true;
+              break;
+            }
+            const uint32_t op = byte(ptr++);
+            if (op & 0x80u) {
+              const int64_t c = (int64_t)(op & 0x7fu) + 1;
+              for (int64_t k = 0; k < c && !overflow; ++k) {
+                const int64_t bl = (blk + k == nblk - 1) ? n - (blk + k) * 32 : 32;
+                if (out < n) emit(out, bl, 0);
+                out += bl;
+              }
+              blk += c;
+            } else {
+              lit = (int64_t)op + 1;
+            }
+          } else {
+            if (ptr + 4 > len) {  // the literal run ends early
+              lit = 0;
+              continue;
+            }
+            const uint32_t m = u32(ptr);
             const int64_t bl = (blk == nblk - 1) ? n - blk * 32 : 32;
             if (out < n) emit(out, bl, ptr + 1);
             out += bl;
             ptr = advance_values(ptr + 4, len, __popc(m & (bl >= 32 ? 0xffffffffu : ((1u << bl) - 1u))), 2);
-            blk += 1;
+            ++blk;
+            --lit;
+          }
+        } else {  // element RLE
+          if (ptr >= len) {
+            done = true;
+            break;
+          }
+          const uint32_t op = byte(ptr++);
+          if (op >= 128) {
+            const int64_t c = (int64_t)op - 128 + 1;
+            emit(out, c, 0);
+            out += c;
+          } else {
+            const int64_t c = (int64_t)op + 1;
+            const int64_t avail = min64(c, (len - ptr) / 2);
+            if (avail > 0) emit(out, avail, ptr + 1);
+            ptr += 2 * avail;
+            out += avail;
           }
         }
       }
-      out_len[sidx] = min64(out, n);
+      if (overflow) done = true;
+      if (!done && ptr >= len && kind != 2) done = true;
+      if (!done && kind == 2 && lit == 0 && !(blk < nblk && ptr < len)) done = true;
+      s_ptr = ptr;
+      s_done = done ? 1 : 0;
     }
+    __syncthreads();
   }
-  if (overflow || out_len[sidx] > out_cap) dev::set_status(status, dev::kBounds, (int)sidx, (int)nent);
-  row[0] = nent;
+  if (threadIdx.x == 0) {
+    int64_t ol;
+    if (kind == 3) ol = out;
+    else if (len < 4) ol = 0;
+    else if (kind == 1) ol = n;  // top-k pads to n
+    else ol = min64(out, n);
+    out_len[sidx] = ol;
+    row[0] = nent;
+    if (overflow || ol > out_cap) dev::set_status(status, dev::kBounds, sidx, (int)nent);
+  }
 }
 
 // Expansion: one warp per descriptor; lanes write elements.
@@ -754,8 +815,7 @@ cudaError_t stream_decode(int kind, const uint8_t* data, const int64_t* stream_o
   if (kind == 1) {
     k_zero_fill<<<grid_for((int64_t)nstreams * out_cap), kThreads, 0, s>>>(out, out_cap, out_len, nstreams);
   }
-  k_walk<<<(nstreams + 63) / 64, 64, 0, s>>>(kind, data, stream_off, nstreams, out_cap, out_len, table, table_cap,
-                                            status);
+  k_walk<<<nstreams, kThreads, 0, s>>>(kind, data, stream_off, nstreams, out_cap, out_len, table, table_cap, status);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   const int64_t warps = (int64_t)nstreams * table_cap;

@@ -2,6 +2,14 @@
 part of the compressed path).  12 layers, d_model 768, 12 heads, FFN 3072,
 vocab 50257, context 1024, tied input/output embeddings, weights N(0, 0.02).
 Attention is ``F.scaled_dot_product_attention`` with a causal mask.
+
+The embedding matrix is stored with its row count rounded up to a multiple
+of ``pad_vocab_to`` (50257 -> 50304) so the output-projection GEMM gets
+16-byte-aligned operands.  A fixed (non-trainable) bias of 0 on the real
+columns and -inf on the padding columns is fused into that GEMM, so the
+padding columns get probability 0 and zero gradient: the loss is the
+cross-entropy over the 50257 real classes and the function computed is
+exactly GPT-2 small's.
 """
 from __future__ import annotations
 
@@ -22,6 +30,12 @@ class GPT2Config:
     n_inner: int = 3072
     init_std: float = 0.02
     tie_embeddings: bool = True
+    pad_vocab_to: int = 64
+
+    @property
+    def padded_vocab(self) -> int:
+        p = max(1, self.pad_vocab_to)
+        return (self.vocab_size + p - 1) // p * p
 
     @staticmethod
     def small() -> "GPT2Config":
@@ -77,13 +91,16 @@ class GPT2(nn.Module):
     def __init__(self, cfg: GPT2Config):
         super().__init__()
         self.cfg = cfg
-        self.wte = nn.Embedding(cfg.vocab_size, cfg.n_embd)
+        self.wte = nn.Embedding(cfg.padded_vocab, cfg.n_embd)
         self.wpe = nn.Embedding(cfg.n_positions, cfg.n_embd)
         self.h = nn.ModuleList([Block(cfg) for _ in range(cfg.n_layer)])
         self.ln_f = nn.LayerNorm(cfg.n_embd)
-        self.lm_head = nn.Linear(cfg.n_embd, cfg.vocab_size, bias=False)
+        self.lm_head = nn.Linear(cfg.n_embd, cfg.padded_vocab, bias=False)
         if cfg.tie_embeddings:
             self.lm_head.weight = self.wte.weight
+        pad_mask = torch.zeros(cfg.padded_vocab)
+        pad_mask[cfg.vocab_size:] = float("-inf")
+        self.register_buffer("vocab_mask", pad_mask, persistent=False)
         self.apply(self._init)
 
     def _init(self, m):
@@ -98,10 +115,18 @@ class GPT2(nn.Module):
         x = self.wte(idx) + self.wpe(pos)
         for blk in self.h:
             x = blk(x)
-        logits = self.lm_head(self.ln_f(x))
+        h = self.ln_f(x)
+        if self.cfg.padded_vocab == self.cfg.vocab_size:
+            logits = self.lm_head(h)
+        else:
+            logits = F.linear(h, self.lm_head.weight, self.vocab_mask.to(h.dtype if not torch.is_autocast_enabled()
+                                                                          else torch.get_autocast_dtype("cuda")))
         if targets is None:
-            return logits
+            return logits[..., : self.cfg.vocab_size]
         return F.cross_entropy(logits.reshape(-1, logits.size(-1)).float(), targets.reshape(-1))
 
-    def num_params(self) -> int:
-        return sum(p.numel() for p in self.parameters())
+    def num_params(self, exclude_padding: bool = True) -> int:
+        n = sum(p.numel() for p in self.parameters())
+        if exclude_padding:
+            n -= (self.cfg.padded_vocab - self.cfg.vocab_size) * self.cfg.n_embd
+        return n
