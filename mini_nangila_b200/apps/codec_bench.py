@@ -1,0 +1,123 @@
+"""GPU error-bounded trajectory codec benchmark (1 GPU).
+
+    python -m mini_nangila_b200.apps.codec_bench [--atoms 1000000] [--steps 100] [--epsilon 1e-3]
+
+Synthetic LAMMPS-style trajectory: positions uniform in a 100^3 box, each
+step adds an N(0, 0.01^2) displacement per coordinate; fp32 x/y/z of every
+atom form one snapshot (3 * atoms values).  The codec sees unwrapped
+coordinates (LAMMPS xu/yu/zu): with periodic wrap a boundary crossing is a
+~100-unit residual, beyond INT16 range at eps 1e-3 (32767 * 2 eps = 65.5) in
+the reference's format, which has no escape code; ``--wrapped`` runs the
+wrapped positions and reports how many codes clamp.  ``--fields vel`` adds an
+N(0, 1) velocity stream.
+
+For EB, EB+BlockSparse and EB+BlockSparse+RLE it reports device encode and
+decode GB/s (raw fp32 bytes / CUDA-event time of the device pipeline: the
+closed loop of every step and the packers; all step payloads decoded and the
+predictor add-back chain), the compression ratio, the max error, byte
+identity with the C++ host library on the first steps, and the host
+library's single-thread MB/s on the same data as the CPU baseline.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import time
+
+import numpy as np
+import torch
+
+from ..checkpoint import nzcp
+from ..ops import trajectory
+
+
+def make_positions(atoms, steps, sigma, box, seed, wrapped, device):
+    g = torch.Generator(device=device).manual_seed(seed)
+    x = torch.empty(steps, 3 * atoms, device=device)
+    x[0] = torch.rand(3 * atoms, device=device, generator=g) * box
+    for t in range(1, steps):
+        x[t] = x[t - 1] + torch.randn(3 * atoms, device=device, generator=g) * sigma
+    if wrapped:
+        x = torch.remainder(x, box)
+    return x
+
+
+def run_codec(x, codec, eps, verify_steps, cpu_steps):
+    dev = x.device
+    T, P = x.shape
+    raw = T * P * 4
+    torch.cuda.synchronize()
+    payload, lens, maxerr, st = trajectory.encode_steps(x, codec, eps)  # warm-up
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    payload, lens, maxerr, st = trajectory.encode_steps(x, codec, eps)
+    e.record()
+    e.synchronize()
+    enc_ms = s.elapsed_time(e)
+    lens_h = lens.cpu().numpy()
+    assert int(st[0]) == 0, st.tolist()
+    comp = int(lens_h.sum()) + 8 * T + 14
+    # decode all steps on the device from the packed payloads
+    offs = np.zeros(T + 1, np.int64)
+    offs[1:] = np.cumsum(lens_h)
+    host = payload.cpu().numpy()
+    data = torch.from_numpy(np.concatenate([host[t, : lens_h[t]] for t in range(T)])).to(dev)
+    offs_d = torch.from_numpy(offs).to(dev)
+    scale = float(np.float32(2.0) * np.float32(eps))
+    sc = torch.full((T,), scale, dtype=torch.float32, device=dev)
+    from .._ext import cuda
+
+    cid = nzcp.CODECS[codec]
+    cuda().nz_decode_steps(data, offs_d, sc, cid, P)  # warm-up
+    torch.cuda.synchronize()
+    s.record()
+    vals = cuda().nz_decode_steps(data, offs_d, sc, cid, P)
+    e.record()
+    e.synchronize()
+    dec_ms = s.elapsed_time(e)
+    # decoded values vs the original snapshots
+    dec_err = float((vals.view(T, P) - x).abs().max())
+    # byte identity and CPU baseline on a prefix of the steps
+    xs = x[:verify_steps].contiguous().cpu().numpy()
+    hb, hstats = nzcp.compress(xs.reshape(-1), P, verify_steps, codec, eps)
+    db, _ = trajectory.compress(x[:verify_steps].contiguous(), codec, eps)
+    xc = x[:cpu_steps].contiguous().cpu().numpy().reshape(-1)
+    t0 = time.perf_counter()
+    nzcp.compress(xc, P, cpu_steps, codec, eps)
+    cpu_s = time.perf_counter() - t0
+    return {
+        "codec": codec, "encode_GBps": raw / (enc_ms * 1e6), "decode_GBps": raw / (dec_ms * 1e6),
+        "encode_ms": enc_ms, "decode_ms": dec_ms, "ratio": raw / comp, "max_abs_err": float(maxerr.item()),
+        "decode_max_abs_err": dec_err, "bytes_identical_to_host_on_first_steps": db == hb,
+        "cpu_single_thread_MBps": cpu_steps * P * 4 / cpu_s / 1e6,
+    }
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--atoms", type=int, default=1_000_000)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--epsilon", type=float, default=1e-3)
+    ap.add_argument("--sigma", type=float, default=0.01)
+    ap.add_argument("--box", type=float, default=100.0)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--wrapped", action="store_true")
+    ap.add_argument("--codecs", default="eb,bs,bsrle")
+    ap.add_argument("--verify-steps", type=int, default=3)
+    ap.add_argument("--cpu-steps", type=int, default=3)
+    a = ap.parse_args(argv)
+    dev = torch.device("cuda", 0)
+    x = make_positions(a.atoms, a.steps, a.sigma, a.box, a.seed, a.wrapped, dev)
+    rows = []
+    for codec in a.codecs.split(","):
+        r = run_codec(x, codec, a.epsilon, a.verify_steps, a.cpu_steps)
+        r.update(atoms=a.atoms, steps=a.steps, epsilon=a.epsilon, wrapped=a.wrapped,
+                 raw_GB=a.steps * 3 * a.atoms * 4 / 1e9)
+        rows.append(r)
+        print(json.dumps(r), flush=True)
+    return rows
+
+
+if __name__ == "__main__":
+    main()
