@@ -257,44 +257,44 @@ std::vector<torch::Tensor> nz_encode_steps(torch::Tensor x, int64_t codec, doubl
   const int64_t cap = codec == 1 ? 2 * P : codec == 2 ? 3 * P + 1 : codec == 3 ? 4 + nblk * 68 : 4 + nblk * 69;
   const int64_t capA = (std::max<int64_t>(cap, 4) + 15) / 16 * 16;
   auto opt = x.options();
-  auto payload = torch::empty({T, capA}, opt.dtype(torch::kUInt8));
-  auto lens = torch::zeros({T}, opt.dtype(torch::kInt64));
-  const int64_t Ppad = (P + 3) / 4 * 4;  // keep every state row 16-byte aligned
-  auto bufs = torch::empty({3, Ppad}, opt.dtype(torch::kInt32));
-  auto codes = torch::empty({P}, opt.dtype(torch::kInt16));
   auto maxerr = torch::zeros({1}, opt.dtype(torch::kInt32));
-  const int64_t words = codec == 3 ? pack_scratch_words(P) : codec == 4 ? run_scratch_words(nblk) : run_scratch_words(P);
-  auto scratch = torch::empty({std::max<int64_t>(words, 1)}, opt.dtype(torch::kInt64));
   auto st = status_tensor(x);
   cudaStream_t s = cur();
-  int32_t* b[3] = {bufs[0].data_ptr<int32_t>(), bufs[1].data_ptr<int32_t>(), bufs[2].data_ptr<int32_t>()};
-  int si = 0, stm1i = 1, ri = 2;
+  // Closed loop of every element over all steps in one kernel.  EB payloads
+  // are the codes themselves (row t of [T, P] i16 = 2P bytes); the packers
+  // encode every step's codes.
+  auto all_codes = torch::empty({T, P}, opt.dtype(torch::kInt16));
+  ck(hpc_encode_all(x.data_ptr<float>(), all_codes.data_ptr<int16_t>(),
+                    reinterpret_cast<uint32_t*>(maxerr.data_ptr<int32_t>()), P, T, scale, s),
+     "hpc_encode_all");
+  auto mx = maxerr.view(torch::kFloat32);
+  if (codec == 1) {
+    auto lens = torch::full({T}, 2 * P, opt.dtype(torch::kInt64));
+    return {all_codes.view(torch::kUInt8).view({T, 2 * P}), lens, mx, st};
+  }
+  auto payload = torch::empty({T, capA}, opt.dtype(torch::kUInt8));
+  auto lens = torch::zeros({T}, opt.dtype(torch::kInt64));
+  auto* lp = reinterpret_cast<uint64_t*>(lens.data_ptr<int64_t>());
+  if (codec == 3) {
+    // All steps in one launch (tile ranges and look-back status per step).
+    auto scratch = torch::empty({pack_scratch_words(P, T)}, opt.dtype(torch::kInt64));
+    ck(bs_encode_batch(all_codes.data_ptr<int16_t>(), P, (int)T, payload.data_ptr<uint8_t>(), capA,
+                       reinterpret_cast<uint64_t*>(scratch.data_ptr<int64_t>()), lp, st.data_ptr<int>(), s),
+       "bs_encode_batch");
+    return {payload, lens, mx, st};
+  }
+  const int64_t words = codec == 4 ? run_scratch_words(nblk) : run_scratch_words(P);
+  auto scratch = torch::empty({std::max<int64_t>(words, 1)}, opt.dtype(torch::kInt64));
   auto* sp = reinterpret_cast<uint64_t*>(scratch.data_ptr<int64_t>());
   for (int64_t t = 0; t < T; ++t) {
-    const int hist = (int)std::min<int64_t>(t, 2);
-    ck(hpc_step(x[t].data_ptr<float>(), b[si], b[stm1i], hist, scale, codes.data_ptr<int16_t>(), b[ri],
-                reinterpret_cast<uint32_t*>(maxerr.data_ptr<int32_t>()), P, s),
-       "hpc_step");
     uint8_t* out = payload[t].data_ptr<uint8_t>();
-    auto* tot = reinterpret_cast<uint64_t*>(lens.data_ptr<int64_t>() + t);
-    if (codec == 1) {
-      ck(cudaMemcpyAsync(out, codes.data_ptr<int16_t>(), 2 * P, cudaMemcpyDeviceToDevice, s), "copy codes");
-      const uint64_t l = 2 * P;
-      ck(cudaMemcpyAsync(tot, &l, sizeof(l), cudaMemcpyHostToDevice, s), "len");
-    } else if (codec == 2) {
-      ck(rle_encode(codes.data_ptr<int16_t>(), P, out, sp, tot, st.data_ptr<int>(), s), "rle_encode");
-    } else if (codec == 3) {
-      ck(bs_encode(codes.data_ptr<int16_t>(), P, out, sp, tot, st.data_ptr<int>(), s), "bs_encode");
+    const int16_t* q = all_codes[t].data_ptr<int16_t>();
+    if (codec == 2) {
+      ck(rle_encode(q, P, out, sp, lp + t, st.data_ptr<int>(), s), "rle_encode");
     } else {
-      ck(bsrle_encode(codes.data_ptr<int16_t>(), P, out, sp, tot, st.data_ptr<int>(), s), "bsrle_encode");
+      ck(bsrle_encode(q, P, out, sp, lp + t, st.data_ptr<int>(), s), "bsrle_encode");
     }
-    // shift the predictor history: s_{t-1} <- s_t, s_t <- recon
-    const int old_tm1 = stm1i;
-    stm1i = si;
-    si = ri;
-    ri = old_tm1;
   }
-  auto mx = maxerr.view(torch::kFloat32);
   return {payload, lens, mx, st};
 }
 
@@ -310,17 +310,30 @@ torch::Tensor nz_decode_steps(torch::Tensor data, torch::Tensor offsets, torch::
   auto opt = data.options();
   torch::Tensor res;
   if (codec == 1) {
-    res = torch::zeros({T, P}, opt.dtype(torch::kInt32));
+    // EB payloads: 2P bytes each (shorter, truncated ones decode to fewer
+    // values followed by zeros); gather them into [T, P] codes, then decode
+    // and add back in one kernel.
     auto offs_h = offsets.cpu();
-    auto sc_h = scales.cpu();
-    for (int64_t t = 0; t < T; ++t) {
-      const int64_t o0 = offs_h.data_ptr<int64_t>()[t], o1 = offs_h.data_ptr<int64_t>()[t + 1];
-      const int64_t n = std::min<int64_t>((o1 - o0) / 2, P);
-      TORCH_CHECK(o0 % 2 == 0, "EB step payloads must start at even offsets");
-      ck(eb_decode(reinterpret_cast<const int16_t*>(data.data_ptr<uint8_t>() + o0), res[t].data_ptr<int32_t>(), n,
-                   sc_h.data_ptr<float>()[t], cur()),
-         "eb_decode");
+    const int64_t* oh = offs_h.data_ptr<int64_t>();
+    bool dense = true;
+    for (int64_t t = 0; t < T && dense; ++t) dense = (oh[t + 1] - oh[t] == 2 * P) && (oh[t] % 2 == 0);
+    torch::Tensor codes;
+    if (dense && oh[0] == 0) {
+      codes = data.narrow(0, 0, 2 * P * T).view(torch::kInt16).view({T, P});
+    } else {
+      codes = torch::zeros({T, P}, opt.dtype(torch::kInt16));
+      for (int64_t t = 0; t < T; ++t) {
+        const int64_t nb = std::min<int64_t>((oh[t + 1] - oh[t]) / 2, P) * 2;
+        if (nb > 0)
+          ck(cudaMemcpyAsync(codes[t].data_ptr<int16_t>(), data.data_ptr<uint8_t>() + oh[t], nb,
+                             cudaMemcpyDeviceToDevice, cur()),
+             "gather codes");
+      }
     }
+    res = torch::empty({T, P}, opt.dtype(torch::kInt32));
+    ck(eb_decode_all(codes.data_ptr<int16_t>(), res.data_ptr<int32_t>(), P, T, scales.data_ptr<float>(), cur()),
+       "eb_decode_all");
+    return to_f32(res);
   } else {
     const int kind = codec == 2 ? 3 : codec == 3 ? 0 : 2;
     const int64_t nblk = (P + 31) / 32;

@@ -161,6 +161,95 @@ __global__ void k_linear_addback(int32_t* __restrict__ res, int64_t P, int64_t T
   }
 }
 
+// Whole-trajectory closed loop: thread owns 4 consecutive coordinates and
+// walks all T steps with the LinearPredictor history (s_t, s_{t-1}) in
+// registers; per element-step it reads the fp32 snapshot value and writes
+// the INT16 code.  Same arithmetic as k_hpc_step, step by step.
+__global__ void __launch_bounds__(kThreads) k_hpc_encode_all(const float* __restrict__ x, int16_t* __restrict__ codes,
+                                                             uint32_t* __restrict__ maxerr, int64_t P, int64_t T,
+                                                             float scale, int vec) {
+  float emax = 0.0f;
+  const int64_t nv = (P + 3) / 4;
+  for (int64_t v = gtid(); v < nv; v += gstride()) {
+    const int64_t i0 = v * 4;
+    const bool full = vec && i0 + 4 <= P;
+    int32_t a[4] = {0, 0, 0, 0}, b[4] = {0, 0, 0, 0};  // s_t, s_{t-1}
+    float4 nxt = full ? __ldcs(reinterpret_cast<const float4*>(x + i0)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int64_t t = 0; t < T; ++t) {
+      const float* xt = x + t * P;
+      float xs[4];
+      if (full) {
+        const float4 xv = nxt;  // prefetched one step ahead: two loads in flight
+        if (t + 1 < T) nxt = __ldcs(reinterpret_cast<const float4*>(xt + P + i0));
+        xs[0] = xv.x; xs[1] = xv.y; xs[2] = xv.z; xs[3] = xv.w;
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) xs[j] = (i0 + j < P) ? xt[i0 + j] : 0.0f;
+      }
+      int16_t c[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int32_t xq = q823_from_f32(xs[j]);
+        int32_t pred = 0;
+        if (t >= 2) pred = sat_add_i32(a[j], sat_sub_i32(a[j], b[j]));
+        else if (t == 1) pred = a[j];
+        const int32_t r = t >= 1 ? sat_sub_i32(xq, pred) : xq;
+        c[j] = eb_code(q823_to_f32(r), scale);
+        const int32_t d = q823_from_f32(NGL_FMUL((float)c[j], scale));
+        const int32_t rc = t >= 1 ? sat_add_i32(pred, d) : d;
+        if (i0 + j < P) emax = fmaxf(emax, fabsf(NGL_FSUB(q823_to_f32(xq), q823_to_f32(rc))));
+        b[j] = a[j];
+        a[j] = rc;
+      }
+      int16_t* ct = codes + t * P;
+      if (full) {
+        __stcs(reinterpret_cast<uint2*>(ct + i0),
+               make_uint2(((uint32_t)(uint16_t)c[0]) | ((uint32_t)(uint16_t)c[1] << 16),
+                          ((uint32_t)(uint16_t)c[2]) | ((uint32_t)(uint16_t)c[3] << 16)));
+      } else {
+        for (int j = 0; j < 4; ++j)
+          if (i0 + j < P) ct[i0 + j] = c[j];
+      }
+    }
+  }
+  const uint32_t m = __reduce_max_sync(kFull, __float_as_uint(emax));
+  if ((threadIdx.x & 31) == 0 && maxerr != nullptr) atomicMax(maxerr, m);
+}
+
+// Whole-trajectory EB decode + LinearPredictor add-back: codes [T, P] ->
+// Q8.23 reconstructions [T, P] (the chain kept in registers).
+__global__ void __launch_bounds__(kThreads) k_eb_decode_all(const int16_t* __restrict__ codes,
+                                                            int32_t* __restrict__ out, int64_t P, int64_t T,
+                                                            const float* __restrict__ scales) {
+  for (int64_t i = gtid(); i < P; i += gstride()) {
+    int32_t a = 0, b = 0;
+    for (int64_t t = 0; t < T; ++t) {
+      const int32_t d = q823_from_f32(NGL_FMUL((float)codes[t * P + i], scales[t]));
+      int32_t rc;
+      if (t == 0) rc = d;
+      else if (t == 1) rc = sat_add_i32(a, d);
+      else rc = sat_add_i32(sat_add_i32(a, sat_sub_i32(a, b)), d);
+      out[t * P + i] = rc;
+      b = a;
+      a = rc;
+    }
+  }
+}
+
+cudaError_t hpc_encode_all(const float* x, int16_t* codes, uint32_t* maxerr_bits, int64_t P, int64_t T, float scale,
+                           cudaStream_t s) {
+  const int vec = ((reinterpret_cast<uintptr_t>(x) & 15u) == 0) && ((reinterpret_cast<uintptr_t>(codes) & 7u) == 0) &&
+                  (P % 4 == 0);
+  if (P > 0 && T > 0)
+    k_hpc_encode_all<<<grid_for((P + 3) / 4, 1), kThreads, 0, s>>>(x, codes, maxerr_bits, P, T, scale, vec);
+  return cudaGetLastError();
+}
+cudaError_t eb_decode_all(const int16_t* codes, int32_t* out, int64_t P, int64_t T, const float* scales,
+                          cudaStream_t s) {
+  if (P > 0 && T > 0) k_eb_decode_all<<<grid_for(P, 1), kThreads, 0, s>>>(codes, out, P, T, scales);
+  return cudaGetLastError();
+}
+
 cudaError_t eb_encode(const int32_t* r, int16_t* codes, int64_t n, float scale, cudaStream_t s) {
   if (n > 0) k_eb_encode<<<grid_for(n), kThreads, 0, s>>>(r, codes, n, scale);
   return cudaGetLastError();
@@ -291,15 +380,16 @@ __device__ uint64_t block_excl_scan(uint64_t v, uint64_t* s_warp, uint64_t* tota
   return r;
 }
 
-int64_t pack_scratch_words(int64_t n) {
+int64_t pack_scratch_words(int64_t n, int64_t ns) {
   const int64_t nblk = (n + 31) / 32;
   const int64_t tiles = (nblk + kPackTileBlocks - 1) / kPackTileBlocks;
-  return tiles + 2;  // status per tile, tile counter
+  return tiles * ns + 2;  // status per tile of every stream, tile counter
 }
 int64_t run_scratch_words(int64_t items) {
   const int64_t tiles = (items + kRunTileItems - 1) / kRunTileItems;
-  // two status arrays + tile counter + per-item offsets + per-item type bytes
-  return 2 * tiles + 2 + items + (items + 7) / 8;
+  // two status arrays + tile counter + per-item offsets + per-item type
+  // bytes + per-item u32 masks (block items)
+  return 2 * tiles + 2 + items + (items + 7) / 8 + (items + 1) / 2;
 }
 
 // ==================================================== mask packers (K4, K8)
@@ -310,6 +400,7 @@ struct SrcBS {  // BlockSparse from i16 codes: kept iff q != 0, value q
     v = q[i];
     return v != 0;
   }
+  __device__ __forceinline__ SrcBS at(int64_t off) const { return SrcBS{q + off}; }
 };
 struct SrcTopK {  // top-k compat from Q8.23: kept iff |x| >= thr
   const int32_t* r;
@@ -324,6 +415,7 @@ struct SrcTopK {  // top-k compat from Q8.23: kept iff |x| >= thr
     v = sat_f32_to_i8(q);
     return keep;
   }
+  __device__ __forceinline__ SrcTopK at(int64_t off) const { return SrcTopK{r + off, thr, scale}; }
 };
 
 __device__ __forceinline__ void put_u32_bytes(uint8_t* p, uint32_t v) {
@@ -333,86 +425,108 @@ __device__ __forceinline__ void put_u32_bytes(uint8_t* p, uint32_t v) {
   p[3] = (uint8_t)(v >> 24);
 }
 
+// Batched over `ns` streams of n elements each (stream s: input src.at(s *
+// in_stride), output out + s * out_stride, length totals[s]); each stream
+// has its own tile-status range, tile ids are global.
 template <class Src>
-__global__ void __launch_bounds__(kThreads) k_mask_pack(Src src, int64_t n, uint8_t* __restrict__ out,
-                                                        uint64_t* scratch, uint64_t* total, int* status) {
+__global__ void __launch_bounds__(kThreads) k_mask_pack(Src src0, int64_t n, int ns, int64_t in_stride,
+                                                        uint8_t* __restrict__ out0, int64_t out_stride,
+                                                        uint64_t* scratch, uint64_t* totals, int* status) {
   __shared__ uint64_t s_warp[kThreads / 32];
   __shared__ uint64_t s_slot;
   __shared__ int64_t s_tile;
+  __shared__ uint32_t s_mask[kPackTileBlocks];
   const int64_t nblk = (n + 31) / 32;
-  const int64_t ntiles = (nblk + kPackTileBlocks - 1) / kPackTileBlocks;
-  unsigned long long* ctr = reinterpret_cast<unsigned long long*>(scratch + ntiles);
+  const int64_t tps = (nblk + kPackTileBlocks - 1) / kPackTileBlocks;
+  const int64_t ntiles_all = tps * ns;
+  unsigned long long* ctr = reinterpret_cast<unsigned long long*>(scratch + ntiles_all);
   if (threadIdx.x == 0) s_tile = (int64_t)atomicAdd(ctr, 1ull);
   __syncthreads();
-  const int64_t tile = s_tile;
-  if (tile >= ntiles) return;
+  const int64_t gtile = s_tile;
+  if (gtile >= ntiles_all) return;
+  const int64_t sidx = gtile / tps, tile = gtile % tps;
+  const Src src = src0.at(sidx * in_stride);
+  uint8_t* out = out0 + sidx * out_stride;
+  uint64_t* st = scratch + sidx * tps;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t blk0 = tile * kPackTileBlocks + (int64_t)warp * kPackBlocksPerWarp;
-  uint32_t masks[kPackBlocksPerWarp];
-  int32_t vals[kPackBlocksPerWarp];
+  // pass 1: masks (kept in shared memory) and this warp's byte count
   uint64_t wsum = 0;
-#pragma unroll
   for (int j = 0; j < kPackBlocksPerWarp; ++j) {
-    const int64_t i = (blk0 + j) * 32 + lane;
-    bool keep = false;
-    vals[j] = 0;
-    if (blk0 + j < nblk && i < n) keep = src.get(i, vals[j]);
-    masks[j] = __ballot_sync(kFull, keep);
-    if (blk0 + j < nblk) wsum += 4 + Src::kVBytes * __popc(masks[j]);
+    const int64_t blk = blk0 + j;
+    const int64_t i = blk * 32 + lane;
+    int32_t v = 0;
+    const bool keep = (blk < nblk && i < n) ? src.get(i, v) : false;
+    const uint32_t m = __ballot_sync(kFull, keep);
+    if (lane == 0) s_mask[warp * kPackBlocksPerWarp + j] = m;
+    if (blk < nblk) wsum += 4 + Src::kVBytes * __popc(m);
   }
-  // tile aggregate and the warp's offset within the tile
   uint64_t tile_agg;
   const uint64_t wexcl = block_excl_scan<OpSum>(lane == 0 ? wsum : 0, s_warp, &tile_agg);
   const uint64_t warp_base = __shfl_sync(kFull, wexcl, 0);
-  const uint64_t excl = lookback<OpSum>(scratch, tile, tile_agg, status, &s_slot);
+  const uint64_t excl = lookback<OpSum>(st, tile, tile_agg, status, &s_slot);
   if (tile == 0 && threadIdx.x == 0) put_u32_bytes(out, (uint32_t)n);
+  // pass 2: write masks and kept values (inputs re-read from L2)
   uint64_t off = 4 + excl + warp_base;
   const uint32_t lt = (1u << lane) - 1u;
-#pragma unroll
   for (int j = 0; j < kPackBlocksPerWarp; ++j) {
-    if (blk0 + j >= nblk) break;
-    const uint32_t m = masks[j];
+    const int64_t blk = blk0 + j;
+    if (blk >= nblk) break;
+    const uint32_t m = s_mask[warp * kPackBlocksPerWarp + j];
     if (lane == 0) put_u32_bytes(out + off, m);
     if ((m >> lane) & 1u) {
+      int32_t v = 0;
+      src.get(blk * 32 + lane, v);
       const uint64_t pos = off + 4 + Src::kVBytes * __popc(m & lt);
       if (Src::kVBytes == 2) {
-        out[pos] = (uint8_t)vals[j];
-        out[pos + 1] = (uint8_t)((uint32_t)vals[j] >> 8);
+        out[pos] = (uint8_t)v;
+        out[pos + 1] = (uint8_t)((uint32_t)v >> 8);
       } else {
-        out[pos] = (uint8_t)vals[j];
+        out[pos] = (uint8_t)v;
       }
     }
     off += 4 + Src::kVBytes * __popc(m);
   }
-  if (tile == ntiles - 1 && threadIdx.x == 0) *total = 4 + excl + tile_agg;
+  if (tile == tps - 1 && threadIdx.x == 0) totals[sidx] = 4 + excl + tile_agg;
+}
+
+__global__ void k_fill_u64(uint64_t* p, int64_t n, uint64_t v) {
+  for (int64_t i = gtid(); i < n; i += gstride()) p[i] = v;
 }
 
 template <class Src>
-cudaError_t launch_pack(const Src& src, int64_t n, uint8_t* out, uint64_t* scratch, uint64_t* total, int* status,
-                        cudaStream_t s) {
-  const int64_t words = pack_scratch_words(n);
-  cudaError_t e = cudaMemsetAsync(scratch, 0, words * sizeof(uint64_t), s);
-  if (e != cudaSuccess) return e;
+cudaError_t launch_pack(const Src& src, int64_t n, int ns, int64_t in_stride, uint8_t* out, int64_t out_stride,
+                        uint64_t* scratch, uint64_t* totals, int* status, cudaStream_t s) {
   const int64_t nblk = (n + 31) / 32;
-  const int64_t ntiles = (nblk + kPackTileBlocks - 1) / kPackTileBlocks;
-  if (ntiles == 0) {
-    // Empty input still writes the u32 header (n = 0).
-    e = cudaMemsetAsync(out, 0, 4, s);
-    if (e != cudaSuccess) return e;
-    const uint64_t four = 4;
-    return cudaMemcpyAsync(total, &four, sizeof(four), cudaMemcpyHostToDevice, s);
+  const int64_t tps = (nblk + kPackTileBlocks - 1) / kPackTileBlocks;
+  if (ns <= 0) return cudaSuccess;
+  cudaError_t e = cudaMemsetAsync(scratch, 0, (tps * ns + 2) * sizeof(uint64_t), s);
+  if (e != cudaSuccess) return e;
+  if (tps == 0) {
+    // Empty inputs still write the u32 header (n = 0).
+    for (int i = 0; i < ns; ++i) {
+      e = cudaMemsetAsync(out + (int64_t)i * out_stride, 0, 4, s);
+      if (e != cudaSuccess) return e;
+    }
+    k_fill_u64<<<1, 32, 0, s>>>(totals, ns, 4);
+    return cudaGetLastError();
   }
-  k_mask_pack<Src><<<(unsigned)ntiles, kThreads, 0, s>>>(src, n, out, scratch, total, status);
+  k_mask_pack<Src><<<(unsigned)(tps * ns), kThreads, 0, s>>>(src, n, ns, in_stride, out, out_stride, scratch, totals,
+                                                             status);
   return cudaGetLastError();
 }
 
 cudaError_t bs_encode(const int16_t* q, int64_t n, uint8_t* out, uint64_t* scratch, uint64_t* total_bytes,
                       int* status, cudaStream_t s) {
-  return launch_pack(SrcBS{q}, n, out, scratch, total_bytes, status, s);
+  return launch_pack(SrcBS{q}, n, 1, 0, out, 0, scratch, total_bytes, status, s);
+}
+cudaError_t bs_encode_batch(const int16_t* q, int64_t n, int ns, uint8_t* out, int64_t out_stride, uint64_t* scratch,
+                            uint64_t* totals, int* status, cudaStream_t s) {
+  return launch_pack(SrcBS{q}, n, ns, n, out, out_stride, scratch, totals, status, s);
 }
 cudaError_t topk_encode(const int32_t* r, int64_t n, const float* threshold, const float* scale, uint8_t* out,
                         uint64_t* scratch, uint64_t* total_bytes, int* status, cudaStream_t s) {
-  return launch_pack(SrcTopK{r, threshold, scale}, n, out, scratch, total_bytes, status, s);
+  return launch_pack(SrcTopK{r, threshold, scale}, n, 1, 0, out, 0, scratch, total_bytes, status, s);
 }
 
 // ================================================= run-length encoders (K5, K6)
@@ -426,15 +540,21 @@ template <bool BLOCKS>
 struct RunItems {
   const int16_t* q;
   int64_t n;
+  const uint32_t* masks;  // BLOCKS: per-block masks precomputed by k_block_masks
   __device__ __forceinline__ int64_t count() const { return BLOCKS ? (n + 31) / 32 : n; }
-  __device__ __forceinline__ uint32_t mask(int64_t b) const {  // BLOCKS only
-    uint32_t m = 0;
-    const int64_t s0 = b * 32;
-    const int len = (int)min64(32, n - s0);
-    for (int i = 0; i < len; ++i) m |= (uint32_t)(q[s0 + i] != 0) << i;
-    return m;
-  }
+  __device__ __forceinline__ uint32_t mask(int64_t b) const { return masks[b]; }
 };
+
+// One warp per 32-block: mask bit i = code i is non-zero (LSB first).
+__global__ void k_block_masks(const int16_t* __restrict__ q, int64_t n, uint32_t* __restrict__ masks) {
+  const int lane = threadIdx.x & 31;
+  const int64_t nblk = (n + 31) / 32;
+  for (int64_t b = gtid() >> 5; b < nblk; b += gstride() >> 5) {
+    const int64_t i = b * 32 + lane;
+    const uint32_t m = __ballot_sync(kFull, i < n && q[i] != 0);
+    if (lane == 0) masks[b] = m;
+  }
+}
 
 template <bool BLOCKS>
 __global__ void __launch_bounds__(kThreads) k_run_pass1(RunItems<BLOCKS> it, uint8_t* __restrict__ out,
@@ -570,7 +690,13 @@ cudaError_t launch_run(const int16_t* q, int64_t n, uint8_t* out, uint64_t* scra
     }
     return cudaMemcpyAsync(total, &hdr, sizeof(hdr), cudaMemcpyHostToDevice, s);
   }
-  k_run_pass1<BLOCKS><<<(unsigned)ntiles, kThreads, 0, s>>>(RunItems<BLOCKS>{q, n}, out, scratch, total, status);
+  uint32_t* masks = reinterpret_cast<uint32_t*>(scratch + 2 * ntiles + 2 + nitems + (nitems + 7) / 8);
+  if (BLOCKS) {
+    int64_t g = (nitems * 32 + kThreads - 1) / kThreads;
+    if (g > 148 * 32) g = 148 * 32;
+    k_block_masks<<<(unsigned)(g > 0 ? g : 1), kThreads, 0, s>>>(q, n, masks);
+  }
+  k_run_pass1<BLOCKS><<<(unsigned)ntiles, kThreads, 0, s>>>(RunItems<BLOCKS>{q, n, masks}, out, scratch, total, status);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   k_run_pass2<<<grid_for(nitems, 1), kThreads, 0, s>>>(scratch, nitems, out);
@@ -608,28 +734,30 @@ constexpr int kWalkWin = 32768;  // bytes of a stream staged in shared memory at
 // memory with 16-byte loads, then thread 0 runs the reference decoder's
 // control flow from shared memory (a resumable state machine, so tokens may
 // straddle windows) and records one descriptor per decoded 32-block or RLE
-// opcode.  Tokens are processed only while they lie entirely in the window
-// (or the window reaches the end of the stream).
-__global__ void __launch_bounds__(kThreads) k_walk(int kind, const uint8_t* __restrict__ data,
-                                                   const int64_t* __restrict__ soff, int nstreams, int64_t out_cap,
-                                                   int64_t* __restrict__ out_len, int64_t* __restrict__ table,
-                                                   int64_t table_cap, int* status) {
-  __shared__ __align__(16) uint8_t win[kWalkWin];
-  __shared__ int64_t s_ptr, s_base;
+// opcode (one 16-byte store each).  Tokens are processed only while they lie
+// entirely in the window (or the window reaches the end of the stream).
+template <int KIND>
+__global__ void __launch_bounds__(kThreads) k_walk(const uint8_t* __restrict__ data, const int64_t* __restrict__ soff,
+                                                   int nstreams, int64_t out_cap, int64_t* __restrict__ out_len,
+                                                   int64_t* __restrict__ table, int64_t table_cap, int* status) {
+  constexpr int VB = KIND == 1 ? 1 : 2;
+  constexpr int kMaxTok = KIND == 3 ? 257 : (KIND == 2 ? 69 : 4 + 32 * VB);
+  __shared__ __align__(16) uint32_t win32[kWalkWin / 4 + 4];
+  __shared__ int64_t s_ptr;
   __shared__ int s_done;
   const int sidx = blockIdx.x;
   if (sidx >= nstreams) return;
   const uint8_t* b = data + soff[sidx];
   const int64_t len = soff[sidx + 1] - soff[sidx];
   int64_t* row = table + (int64_t)sidx * (2 * table_cap + 2);
-  int64_t* tab = row + 2;
+  longlong2* tab = reinterpret_cast<longlong2*>(row + 2);
+  const uint8_t* win = reinterpret_cast<const uint8_t*>(win32);
   // walker state (thread 0)
-  int64_t ptr = 0, out = 0, nent = 0, blk = 0, n = 0, nblk = 0, lit = 0;
+  int64_t ptr = 0, out = 0, nent = 0, blk = 0, n = 0, nblk = 0;
+  int lit = 0;
   bool overflow = false, done = false;
-  const int vb = kind == 1 ? 1 : 2;
-  const int64_t max_tok = kind == 3 ? 257 : (kind == 2 ? 69 : 4 + 32 * vb);
   if (threadIdx.x == 0) {
-    if (kind != 3) {
+    if (KIND != 3) {
       if (len < 4) {
         done = true;
       } else {
@@ -642,51 +770,55 @@ __global__ void __launch_bounds__(kThreads) k_walk(int kind, const uint8_t* __re
     s_done = done ? 1 : 0;
   }
   __syncthreads();
-  auto emit = [&](int64_t o, int64_t l, int64_t in_plus1) {
-    if (nent >= table_cap) {
-      overflow = true;
-      return;
-    }
-    tab[2 * nent] = o | (l << 48);
-    tab[2 * nent + 1] = in_plus1;
-    ++nent;
-  };
   while (!s_done) {
-    // stage [base, base + kWalkWin) with 16-byte loads from an aligned base
     const int64_t p0 = s_ptr;
     const int64_t base = p0 - (int64_t)(reinterpret_cast<uintptr_t>(b + p0) & 15u);
     const int64_t hi = min64(len, base + kWalkWin);
-    const int64_t cnt = hi - base;
+    const int cnt = (int)(hi - base);
     const uint4* src = reinterpret_cast<const uint4*>(b + base);
-    for (int64_t i = threadIdx.x; i < cnt / 16; i += blockDim.x) reinterpret_cast<uint4*>(win)[i] = src[i];
-    for (int64_t i = (cnt / 16) * 16 + threadIdx.x; i < cnt; i += blockDim.x) win[i] = b[base + i];
+    for (int i = threadIdx.x; i < cnt / 16; i += blockDim.x) reinterpret_cast<uint4*>(win32)[i] = src[i];
+    for (int i = (cnt / 16) * 16 + threadIdx.x; i < cnt; i += blockDim.x)
+      reinterpret_cast<uint8_t*>(win32)[i] = b[base + i];
     __syncthreads();
     if (threadIdx.x == 0) {
       const bool last = hi == len;
-      auto fits = [&](int64_t p) { return last || p + max_tok <= hi; };
-      auto byte = [&](int64_t p) -> uint32_t { return win[p - base]; };
-      auto u32 = [&](int64_t p) -> uint32_t {
-        return byte(p) | (byte(p + 1) << 8) | (byte(p + 2) << 16) | (byte(p + 3) << 24);
+      const int lim = last ? cnt : cnt - kMaxTok;  // tokens must start at or before lim
+      int q = (int)(ptr - base);                    // window-relative position
+      const int qlen = (int)min64(len - base, (int64_t)1 << 30);
+      auto u32 = [&](int x) -> uint32_t {
+        const uint32_t w0 = win32[x >> 2], w1 = win32[(x >> 2) + 1];
+        return __funnelshift_r(w0, w1, (x & 3) * 8);
       };
-      while (!done && !overflow && fits(ptr)) {
-        if (kind == 0 || kind == 1) {  // BlockSparse / top-k compat
-          if (blk >= nblk || ptr + 4 > len) {
+      auto emit = [&](int64_t o, int64_t l, int64_t in_plus1) {
+        if (nent >= table_cap) {
+          overflow = true;
+          return;
+        }
+        tab[nent] = make_longlong2(o | (l << 48), in_plus1);
+        ++nent;
+      };
+      while (!done && !overflow && (q <= lim || last)) {
+        if (KIND == 0 || KIND == 1) {
+          if (blk >= nblk || q + 4 > qlen) {
             done = true;
             break;
           }
-          const uint32_t m = u32(ptr);
+          const uint32_t m = u32(q);
           const int64_t bl = blk == nblk - 1 ? n - blk * 32 : 32;
-          emit(out, bl, ptr + 1);
+          emit(out, bl, base + q + 1);
           out += bl;
-          ptr = advance_values(ptr + 4, len, __popc(m & (bl >= 32 ? 0xffffffffu : ((1u << bl) - 1u))), vb);
+          const int c = __popc(bl >= 32 ? m : (m & ((1u << bl) - 1u)));
+          const int vals = q + 4;
+          const int room = qlen > vals ? (qlen - vals) / VB : 0;
+          q = vals + VB * (c < room ? c : room);
           ++blk;
-        } else if (kind == 2) {  // BlockSparse + RLE
+        } else if (KIND == 2) {
           if (lit == 0) {
-            if (!(blk < nblk && ptr < len)) {
+            if (!(blk < nblk && q < qlen)) {
               done = true;
               break;
             }
-            const uint32_t op = byte(ptr++);
+            const uint32_t op = win[q++];
             if (op & 0x80u) {
               const int64_t c = (int64_t)(op & 0x7fu) + 1;
               for (int64_t k = 0; k < c && !overflow; ++k) {
@@ -696,43 +828,48 @@ __global__ void __launch_bounds__(kThreads) k_walk(int kind, const uint8_t* __re
               }
               blk += c;
             } else {
-              lit = (int64_t)op + 1;
+              lit = (int)op + 1;
             }
           } else {
-            if (ptr + 4 > len) {  // the literal run ends early
+            if (q + 4 > qlen) {  // the literal run ends early
               lit = 0;
               continue;
             }
-            const uint32_t m = u32(ptr);
+            const uint32_t m = u32(q);
             const int64_t bl = (blk == nblk - 1) ? n - blk * 32 : 32;
-            if (out < n) emit(out, bl, ptr + 1);
+            if (out < n) emit(out, bl, base + q + 1);
             out += bl;
-            ptr = advance_values(ptr + 4, len, __popc(m & (bl >= 32 ? 0xffffffffu : ((1u << bl) - 1u))), 2);
+            const int c = __popc(bl >= 32 ? m : (m & ((1u << bl) - 1u)));
+            const int vals = q + 4;
+            const int room = qlen > vals ? (qlen - vals) / 2 : 0;
+            q = vals + 2 * (c < room ? c : room);
             ++blk;
             --lit;
           }
         } else {  // element RLE
-          if (ptr >= len) {
+          if (q >= qlen) {
             done = true;
             break;
           }
-          const uint32_t op = byte(ptr++);
+          const uint32_t op = win[q++];
           if (op >= 128) {
             const int64_t c = (int64_t)op - 128 + 1;
             emit(out, c, 0);
             out += c;
           } else {
-            const int64_t c = (int64_t)op + 1;
-            const int64_t avail = min64(c, (len - ptr) / 2);
-            if (avail > 0) emit(out, avail, ptr + 1);
-            ptr += 2 * avail;
+            const int c = (int)op + 1;
+            const int room = (qlen - q) / 2;
+            const int avail = c < room ? c : room;
+            if (avail > 0) emit(out, avail, base + q + 1);
+            q += 2 * avail;
             out += avail;
           }
         }
       }
+      ptr = base + q;
       if (overflow) done = true;
-      if (!done && ptr >= len && kind != 2) done = true;
-      if (!done && kind == 2 && lit == 0 && !(blk < nblk && ptr < len)) done = true;
+      if (!done && KIND != 2 && ptr >= len) done = true;
+      if (!done && KIND == 2 && lit == 0 && !(blk < nblk && ptr < len)) done = true;
       s_ptr = ptr;
       s_done = done ? 1 : 0;
     }
@@ -740,9 +877,9 @@ __global__ void __launch_bounds__(kThreads) k_walk(int kind, const uint8_t* __re
   }
   if (threadIdx.x == 0) {
     int64_t ol;
-    if (kind == 3) ol = out;
+    if (KIND == 3) ol = out;
     else if (len < 4) ol = 0;
-    else if (kind == 1) ol = n;  // top-k pads to n
+    else if (KIND == 1) ol = n;  // top-k pads to n
     else ol = min64(out, n);
     out_len[sidx] = ol;
     row[0] = nent;
@@ -763,7 +900,7 @@ __global__ void k_expand(int kind, const uint8_t* __restrict__ data, const int64
     if (ent >= row[0]) continue;  // past this stream's last descriptor
     const int64_t* tab = row + 2;
     const int64_t w0 = tab[2 * ent];
-    const int64_t o = w0 & ((1ll << 48) - 1), l = w0 >> 48, in1 = tab[2 * ent + 1];
+    const int64_t o = w0 & ((1ll << 48) - 1), l = (int64_t)((uint64_t)w0 >> 48), in1 = tab[2 * ent + 1];
     const uint8_t* b = data + soff[sidx];
     const int64_t len = soff[sidx + 1] - soff[sidx];
     const float sc = scales[sidx];
@@ -815,7 +952,10 @@ cudaError_t stream_decode(int kind, const uint8_t* data, const int64_t* stream_o
   if (kind == 1) {
     k_zero_fill<<<grid_for((int64_t)nstreams * out_cap), kThreads, 0, s>>>(out, out_cap, out_len, nstreams);
   }
-  k_walk<<<nstreams, kThreads, 0, s>>>(kind, data, stream_off, nstreams, out_cap, out_len, table, table_cap, status);
+  if (kind == 0) k_walk<0><<<nstreams, kThreads, 0, s>>>(data, stream_off, nstreams, out_cap, out_len, table, table_cap, status);
+  else if (kind == 1) k_walk<1><<<nstreams, kThreads, 0, s>>>(data, stream_off, nstreams, out_cap, out_len, table, table_cap, status);
+  else if (kind == 2) k_walk<2><<<nstreams, kThreads, 0, s>>>(data, stream_off, nstreams, out_cap, out_len, table, table_cap, status);
+  else k_walk<3><<<nstreams, kThreads, 0, s>>>(data, stream_off, nstreams, out_cap, out_len, table, table_cap, status);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   const int64_t warps = (int64_t)nstreams * table_cap;

@@ -11,12 +11,12 @@ namespace ngl {
 namespace codec {
 
 constexpr int kPackThreads = 256;
-constexpr int kPackBlocksPerWarp = 16;                            // 32-element blocks per warp per tile
-constexpr int kPackTileBlocks = (kPackThreads / 32) * kPackBlocksPerWarp;  // 128 blocks = 4096 elements
+constexpr int kPackBlocksPerWarp = 64;                            // 32-element blocks per warp per tile
+constexpr int kPackTileBlocks = (kPackThreads / 32) * kPackBlocksPerWarp;  // 512 blocks = 16384 elements
 constexpr int kRunTileItems = 4096;                               // items per tile of the run-length encoders
 
 // Scratch words needed by the look-back encoders for n elements.
-int64_t pack_scratch_words(int64_t n);
+int64_t pack_scratch_words(int64_t n, int64_t nstreams = 1);
 int64_t run_scratch_words(int64_t items);
 
 // ---- Q8.23 (K2) ----
@@ -36,6 +36,14 @@ cudaError_t eb_decode(const int16_t* codes, int32_t* out, int64_t n, float scale
 // maxerr (float bits, atomicMax) = max |to_f32(x) - to_f32(recon)|.
 cudaError_t hpc_step(const float* x, const int32_t* s_t, const int32_t* s_tm1, int hist, float scale, int16_t* codes,
                      int32_t* recon, uint32_t* maxerr_bits, int64_t n, cudaStream_t s);
+// Whole trajectory at once (all T snapshots of P values): the closed loop
+// of every element runs its T steps with the predictor history in
+// registers; codes [T, P].  Identical codes to T calls of hpc_step.
+cudaError_t hpc_encode_all(const float* x, int16_t* codes, uint32_t* maxerr_bits, int64_t P, int64_t T, float scale,
+                           cudaStream_t s);
+// EB decode of codes [T, P] with the add-back chain -> Q8.23 values [T, P].
+cudaError_t eb_decode_all(const int16_t* codes, int32_t* out, int64_t P, int64_t T, const float* scales,
+                          cudaStream_t s);
 // Linear predictor add-back over T decoded residual snapshots (in place):
 // recon_t = pred_t + res_t with the predictor's history chain.
 cudaError_t linear_addback(int32_t* res, int64_t particles, int64_t steps, cudaStream_t s);
@@ -50,6 +58,11 @@ cudaError_t bs_encode(const int16_t* q, int64_t n, uint8_t* out, uint64_t* scrat
                       int* status, cudaStream_t s);
 cudaError_t topk_encode(const int32_t* r, int64_t n, const float* threshold, const float* scale, uint8_t* out,
                         uint64_t* scratch, uint64_t* total_bytes, int* status, cudaStream_t s);
+// BlockSparse over `ns` streams of n codes (stream i at q + i * n) in one
+// launch; stream i's bytes at out + i * out_stride, length totals[i].
+// scratch: pack_scratch_words(n, ns) words.
+cudaError_t bs_encode_batch(const int16_t* q, int64_t n, int ns, uint8_t* out, int64_t out_stride, uint64_t* scratch,
+                            uint64_t* totals, int* status, cudaStream_t s);
 
 // ---- Run-length encoders from i16 codes ----
 // BlockSparse+RLE ([u32 n], opcode runs over 32-blocks) and element RLE
