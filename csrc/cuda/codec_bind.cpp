@@ -283,17 +283,17 @@ std::vector<torch::Tensor> nz_encode_steps(torch::Tensor x, int64_t codec, doubl
        "bs_encode_batch");
     return {payload, lens, mx, st};
   }
-  const int64_t words = codec == 4 ? run_scratch_words(nblk) : run_scratch_words(P);
-  auto scratch = torch::empty({std::max<int64_t>(words, 1)}, opt.dtype(torch::kInt64));
+  const int64_t items = codec == 4 ? nblk : P;
+  auto scratch = torch::empty({run_scratch_words(items, T)}, opt.dtype(torch::kInt64));
   auto* sp = reinterpret_cast<uint64_t*>(scratch.data_ptr<int64_t>());
-  for (int64_t t = 0; t < T; ++t) {
-    uint8_t* out = payload[t].data_ptr<uint8_t>();
-    const int16_t* q = all_codes[t].data_ptr<int16_t>();
-    if (codec == 2) {
-      ck(rle_encode(q, P, out, sp, lp + t, st.data_ptr<int>(), s), "rle_encode");
-    } else {
-      ck(bsrle_encode(q, P, out, sp, lp + t, st.data_ptr<int>(), s), "bsrle_encode");
-    }
+  if (codec == 2) {
+    ck(rle_encode_batch(all_codes.data_ptr<int16_t>(), P, (int)T, payload.data_ptr<uint8_t>(), capA, sp, lp,
+                        st.data_ptr<int>(), s),
+       "rle_encode_batch");
+  } else {
+    ck(bsrle_encode_batch(all_codes.data_ptr<int16_t>(), P, (int)T, payload.data_ptr<uint8_t>(), capA, sp, lp,
+                          st.data_ptr<int>(), s),
+       "bsrle_encode_batch");
   }
   return {payload, lens, mx, st};
 }

@@ -385,12 +385,6 @@ int64_t pack_scratch_words(int64_t n, int64_t ns) {
   const int64_t tiles = (nblk + kPackTileBlocks - 1) / kPackTileBlocks;
   return tiles * ns + 2;  // status per tile of every stream, tile counter
 }
-int64_t run_scratch_words(int64_t items) {
-  const int64_t tiles = (items + kRunTileItems - 1) / kRunTileItems;
-  // two status arrays + tile counter + per-item offsets + per-item type
-  // bytes + per-item u32 masks (block items)
-  return 2 * tiles + 2 + items + (items + 7) / 8 + (items + 1) / 2;
-}
 
 // ==================================================== mask packers (K4, K8)
 struct SrcBS {  // BlockSparse from i16 codes: kept iff q != 0, value q
@@ -536,49 +530,71 @@ cudaError_t topk_encode(const int32_t* r, int64_t n, const float* threshold, con
 // run head carries a one-byte opcode.  Pass 1 scans twice with look-back
 // (segment start by max-scan, byte offsets by sum-scan) and writes the item
 // payloads; pass 2 writes the opcodes (run length found by scanning ahead).
-template <bool BLOCKS>
-struct RunItems {
-  const int16_t* q;
-  int64_t n;
-  const uint32_t* masks;  // BLOCKS: per-block masks precomputed by k_block_masks
-  __device__ __forceinline__ int64_t count() const { return BLOCKS ? (n + 31) / 32 : n; }
-  __device__ __forceinline__ uint32_t mask(int64_t b) const { return masks[b]; }
+//
+// Every launch encodes `ns` streams of n codes (stream s at q + s * n, its
+// bytes at out + s * out_stride, its length in totals[s]).  Scratch layout
+// (u64 words): [ns x (max status, sum status) per tile][tile counter, pad]
+// [ns x item head offsets][ns x item kinds (bytes)][ns x block masks (u32)].
+struct RunScratch {
+  int64_t nitems, tps;
+  int ns;
+  uint64_t* base;
+  __device__ __host__ uint64_t* st_max(int64_t s) const { return base + s * 2 * tps; }
+  __device__ __host__ uint64_t* st_sum(int64_t s) const { return base + s * 2 * tps + tps; }
+  __device__ __host__ unsigned long long* ctr() const {
+    return reinterpret_cast<unsigned long long*>(base + (int64_t)ns * 2 * tps);
+  }
+  __device__ __host__ int64_t* offs() const { return reinterpret_cast<int64_t*>(base + (int64_t)ns * 2 * tps + 2); }
+  __device__ __host__ uint8_t* types() const { return reinterpret_cast<uint8_t*>(offs() + (int64_t)ns * nitems); }
+  __device__ __host__ uint32_t* masks() const {
+    const int64_t tb = ((int64_t)ns * nitems + 7) / 8;  // u64 words of kinds
+    return reinterpret_cast<uint32_t*>(offs() + (int64_t)ns * nitems + tb);
+  }
 };
 
-// One warp per 32-block: mask bit i = code i is non-zero (LSB first).
-__global__ void k_block_masks(const int16_t* __restrict__ q, int64_t n, uint32_t* __restrict__ masks) {
+int64_t run_scratch_words(int64_t items, int64_t ns) {
+  const int64_t tiles = (items + kRunTileItems - 1) / kRunTileItems;
+  return 2 * tiles * ns + 2 + items * ns + (items * ns + 7) / 8 + (items * ns + 1) / 2;
+}
+
+// One warp per 32-block of every stream: mask bit i = code i is non-zero.
+__global__ void k_block_masks(const int16_t* __restrict__ q, int64_t n, int64_t nblk, int64_t total_blk,
+                              uint32_t* __restrict__ masks) {
   const int lane = threadIdx.x & 31;
-  const int64_t nblk = (n + 31) / 32;
-  for (int64_t b = gtid() >> 5; b < nblk; b += gstride() >> 5) {
-    const int64_t i = b * 32 + lane;
-    const uint32_t m = __ballot_sync(kFull, i < n && q[i] != 0);
+  for (int64_t b = gtid() >> 5; b < total_blk; b += gstride() >> 5) {
+    const int64_t sidx = b / nblk, lb = b - sidx * nblk;
+    const int64_t e = lb * 32 + lane;
+    const uint32_t m = __ballot_sync(kFull, e < n && q[sidx * n + e] != 0);
     if (lane == 0) masks[b] = m;
   }
 }
 
 template <bool BLOCKS>
-__global__ void __launch_bounds__(kThreads) k_run_pass1(RunItems<BLOCKS> it, uint8_t* __restrict__ out,
-                                                        uint64_t* scratch, uint64_t* total, int* status) {
+__global__ void __launch_bounds__(kThreads) k_run_pass1(const int16_t* __restrict__ q0, int64_t n, RunScratch sc,
+                                                        uint8_t* __restrict__ out0, int64_t out_stride,
+                                                        uint64_t* totals, int* status) {
   constexpr int IPT = kRunTileItems / kThreads;  // 16 items per thread
   __shared__ uint64_t s_warp[kThreads / 32];
   __shared__ uint64_t s_slot;
   __shared__ int64_t s_tile;
-  const int64_t nitems = it.count();
-  const int64_t ntiles = (nitems + kRunTileItems - 1) / kRunTileItems;
-  uint64_t* st_max = scratch;
-  uint64_t* st_sum = scratch + ntiles;
-  unsigned long long* ctr = reinterpret_cast<unsigned long long*>(scratch + 2 * ntiles);
-  int64_t* offs = reinterpret_cast<int64_t*>(scratch + 2 * ntiles + 2);
-  uint8_t* types = reinterpret_cast<uint8_t*>(scratch + 2 * ntiles + 2 + nitems);
-  if (threadIdx.x == 0) s_tile = (int64_t)atomicAdd(ctr, 1ull);
+  __shared__ uint32_t s_rel[BLOCKS ? kRunTileItems : 1];  // payload offset in the tile (~0u: none)
+  __shared__ uint32_t s_m[BLOCKS ? kRunTileItems : 1];
+  const int64_t nitems = sc.nitems, tps = sc.tps;
+  if (threadIdx.x == 0) s_tile = (int64_t)atomicAdd(sc.ctr(), 1ull);
   __syncthreads();
-  const int64_t tile = s_tile;
-  if (tile >= ntiles) return;
+  const int64_t gtile = s_tile;
+  if (gtile >= tps * sc.ns) return;
+  const int64_t sidx = gtile / tps, tile = gtile - sidx * tps;
+  const int16_t* q = q0 + sidx * n;
+  uint8_t* out = out0 + sidx * out_stride;
+  int64_t* offs = sc.offs() + sidx * nitems;
+  uint8_t* types = sc.types() + sidx * nitems;
+  const uint32_t* masks = sc.masks() + sidx * nitems;
   const int64_t i0 = tile * kRunTileItems + (int64_t)threadIdx.x * IPT;
   uint32_t m[IPT];
   bool nz[IPT];
   bool prev_nz = false;
-  if (i0 > 0 && i0 - 1 < nitems) prev_nz = BLOCKS ? (it.mask(i0 - 1) != 0) : (it.q[i0 - 1] != 0);
+  if (i0 > 0 && i0 - 1 < nitems) prev_nz = BLOCKS ? (masks[i0 - 1] != 0) : (q[i0 - 1] != 0);
   // pass A: segment starts (max-scan of change positions)
   uint64_t seg = 0;
   bool any_change = false;
@@ -589,10 +605,10 @@ __global__ void __launch_bounds__(kThreads) k_run_pass1(RunItems<BLOCKS> it, uin
     nz[j] = false;
     if (i < nitems) {
       if (BLOCKS) {
-        m[j] = it.mask(i);
+        m[j] = masks[i];
         nz[j] = m[j] != 0;
       } else {
-        nz[j] = it.q[i] != 0;
+        nz[j] = q[i] != 0;
       }
       const bool p = j == 0 ? prev_nz : nz[j - 1];
       if (i == 0 || nz[j] != p) {
@@ -603,7 +619,7 @@ __global__ void __launch_bounds__(kThreads) k_run_pass1(RunItems<BLOCKS> it, uin
   }
   uint64_t tile_max;
   const uint64_t thr_excl_max = block_excl_scan<OpMax>(any_change ? seg : 0, s_warp, &tile_max);
-  const uint64_t tile_excl_max = lookback<OpMax>(st_max, tile, tile_max, status, &s_slot);
+  const uint64_t tile_excl_max = lookback<OpMax>(sc.st_max(sidx), tile, tile_max, status, &s_slot);
   // pass B: run heads and byte sizes
   uint64_t run_start = OpMax::op(tile_excl_max, thr_excl_max);
   uint64_t sizes[IPT];
@@ -626,90 +642,120 @@ __global__ void __launch_bounds__(kThreads) k_run_pass1(RunItems<BLOCKS> it, uin
   }
   uint64_t tile_sum;
   const uint64_t thr_excl_sum = block_excl_scan<OpSum>(tsum, s_warp, &tile_sum);
-  const uint64_t tile_excl_sum = lookback<OpSum>(st_sum, tile, tile_sum, status, &s_slot);
+  const uint64_t tile_excl_sum = lookback<OpSum>(sc.st_sum(sidx), tile, tile_sum, status, &s_slot);
   const uint64_t hdr = BLOCKS ? 4 : 0;
-  if (BLOCKS && tile == 0 && threadIdx.x == 0) put_u32_bytes(out, (uint32_t)it.n);
-  uint64_t off = hdr + tile_excl_sum + thr_excl_sum;
+  if (BLOCKS && tile == 0 && threadIdx.x == 0) put_u32_bytes(out, (uint32_t)n);
+  const uint64_t tbase = hdr + tile_excl_sum;
+  uint64_t rel = thr_excl_sum;
 #pragma unroll
   for (int j = 0; j < IPT; ++j) {
     const int64_t i = i0 + j;
-    if (i >= nitems) break;
-    types[i] = (uint8_t)(nz[j] ? 1 : 0);
-    offs[i] = head[j] ? (int64_t)off : -1;
-    uint64_t p = off + (head[j] ? 1 : 0);
-    if (nz[j]) {
+    if (i < nitems) {
+      types[i] = (uint8_t)(nz[j] ? 1 : 0);
+      offs[i] = head[j] ? (int64_t)(tbase + rel) : -1;
+      const uint64_t p = rel + (head[j] ? 1 : 0);
       if (BLOCKS) {
-        put_u32_bytes(out + p, m[j]);
-        p += 4;
-        const int64_t s0 = i * 32;
-        for (int e = 0; e < 32; ++e)
-          if ((m[j] >> e) & 1u) {
-            const uint16_t v = (uint16_t)it.q[s0 + e];
-            out[p] = (uint8_t)v;
-            out[p + 1] = (uint8_t)(v >> 8);
-            p += 2;
-          }
-      } else {
-        const uint16_t v = (uint16_t)it.q[i];
-        out[p] = (uint8_t)v;
-        out[p + 1] = (uint8_t)(v >> 8);
+        s_rel[threadIdx.x * IPT + j] = nz[j] ? (uint32_t)p : ~0u;
+        s_m[threadIdx.x * IPT + j] = m[j];
+      } else if (nz[j]) {
+        const uint16_t v = (uint16_t)q[i];
+        out[tbase + p] = (uint8_t)v;
+        out[tbase + p + 1] = (uint8_t)(v >> 8);
+      }
+    } else if (BLOCKS) {
+      s_rel[threadIdx.x * IPT + j] = ~0u;
+    }
+    rel += sizes[j];
+  }
+  if (BLOCKS) {
+    // Payload of every kept block, one warp per block: lane e loads code e
+    // (coalesced) and stores it at its rank among the kept codes.
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t lt = (1u << lane) - 1u;
+    for (int j = warp; j < kRunTileItems; j += kThreads / 32) {
+      const uint32_t r = s_rel[j];
+      if (r == ~0u) continue;
+      const uint32_t mm = s_m[j];
+      const int64_t blk = tile * kRunTileItems + j;
+      uint8_t* dst = out + tbase + r;
+      if (lane == 0) put_u32_bytes(dst, mm);
+      if ((mm >> lane) & 1u) {
+        const uint16_t v = (uint16_t)q[blk * 32 + lane];
+        const uint32_t pos = 4 + 2 * __popc(mm & lt);
+        dst[pos] = (uint8_t)v;
+        dst[pos + 1] = (uint8_t)(v >> 8);
       }
     }
-    off += sizes[j];
   }
-  if (tile == ntiles - 1 && threadIdx.x == 0) *total = hdr + tile_excl_sum + tile_sum;
+  if (tile == tps - 1 && threadIdx.x == 0) totals[sidx] = hdr + tile_excl_sum + tile_sum;
 }
 
 // Pass 2: opcode of every run head = kind bit | (run length - 1).
-__global__ void k_run_pass2(const uint64_t* scratch, int64_t nitems, uint8_t* __restrict__ out) {
-  const int64_t ntiles = (nitems + kRunTileItems - 1) / kRunTileItems;
-  const int64_t* offs = reinterpret_cast<const int64_t*>(scratch + 2 * ntiles + 2);
-  const uint8_t* types = reinterpret_cast<const uint8_t*>(scratch + 2 * ntiles + 2 + nitems);
-  for (int64_t i = gtid(); i < nitems; i += gstride()) {
+__global__ void k_run_pass2(RunScratch sc, uint8_t* __restrict__ out0, int64_t out_stride) {
+  const int64_t nitems = sc.nitems, all = nitems * sc.ns;
+  const int64_t* offs = sc.offs();
+  const uint8_t* types = sc.types();
+  for (int64_t i = gtid(); i < all; i += gstride()) {
     const int64_t o = offs[i];
     if (o < 0) continue;
+    const int64_t sidx = i / nitems, li = i - sidx * nitems;
     const uint8_t t = types[i];
     int count = 1;
-    while (count < 128 && i + count < nitems && types[i + count] == t) ++count;
-    out[o] = t ? (uint8_t)(count - 1) : (uint8_t)(0x80 | (count - 1));
+    while (count < 128 && li + count < nitems && types[i + count] == t) ++count;
+    out0[sidx * out_stride + o] = t ? (uint8_t)(count - 1) : (uint8_t)(0x80 | (count - 1));
+  }
+}
+
+// Empty streams: header only (BlockSparse+RLE writes u32 n = 0).
+__global__ void k_run_empty(uint8_t* out0, int64_t out_stride, int ns, bool blocks, uint64_t* totals) {
+  for (int64_t i = gtid(); i < ns; i += gstride()) {
+    if (blocks) put_u32_bytes(out0 + i * out_stride, 0u);
+    totals[i] = blocks ? 4 : 0;
   }
 }
 
 template <bool BLOCKS>
-cudaError_t launch_run(const int16_t* q, int64_t n, uint8_t* out, uint64_t* scratch, uint64_t* total, int* status,
-                       cudaStream_t s) {
+cudaError_t launch_run(const int16_t* q, int64_t n, int ns, uint8_t* out, int64_t out_stride, uint64_t* scratch,
+                       uint64_t* totals, int* status, cudaStream_t s) {
+  if (ns <= 0) return cudaSuccess;
   const int64_t nitems = BLOCKS ? (n + 31) / 32 : n;
-  const int64_t ntiles = (nitems + kRunTileItems - 1) / kRunTileItems;
-  cudaError_t e = cudaMemsetAsync(scratch, 0, (2 * ntiles + 2) * sizeof(uint64_t), s);
+  const int64_t tps = (nitems + kRunTileItems - 1) / kRunTileItems;
+  if (tps == 0) {
+    k_run_empty<<<1, 128, 0, s>>>(out, out_stride, ns, BLOCKS, totals);
+    return cudaGetLastError();
+  }
+  RunScratch sc{nitems, tps, ns, scratch};
+  cudaError_t e = cudaMemsetAsync(scratch, 0, (2 * tps * ns + 2) * sizeof(uint64_t), s);
   if (e != cudaSuccess) return e;
-  if (ntiles == 0) {
-    uint64_t hdr = BLOCKS ? 4 : 0;
-    if (BLOCKS) {
-      e = cudaMemsetAsync(out, 0, 4, s);
-      if (e != cudaSuccess) return e;
-    }
-    return cudaMemcpyAsync(total, &hdr, sizeof(hdr), cudaMemcpyHostToDevice, s);
-  }
-  uint32_t* masks = reinterpret_cast<uint32_t*>(scratch + 2 * ntiles + 2 + nitems + (nitems + 7) / 8);
   if (BLOCKS) {
-    int64_t g = (nitems * 32 + kThreads - 1) / kThreads;
+    const int64_t total_blk = nitems * ns;
+    int64_t g = (total_blk * 32 + kThreads - 1) / kThreads;
     if (g > 148 * 32) g = 148 * 32;
-    k_block_masks<<<(unsigned)(g > 0 ? g : 1), kThreads, 0, s>>>(q, n, masks);
+    k_block_masks<<<(unsigned)g, kThreads, 0, s>>>(q, n, nitems, total_blk, sc.masks());
   }
-  k_run_pass1<BLOCKS><<<(unsigned)ntiles, kThreads, 0, s>>>(RunItems<BLOCKS>{q, n, masks}, out, scratch, total, status);
+  k_run_pass1<BLOCKS><<<(unsigned)(tps * ns), kThreads, 0, s>>>(q, n, sc, out, out_stride, totals, status);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  k_run_pass2<<<grid_for(nitems, 1), kThreads, 0, s>>>(scratch, nitems, out);
+  k_run_pass2<<<grid_for(nitems * ns, 1), kThreads, 0, s>>>(sc, out, out_stride);
   return cudaGetLastError();
 }
 
 cudaError_t bsrle_encode(const int16_t* q, int64_t n, uint8_t* out, uint64_t* scratch, uint64_t* total_bytes,
                          int* status, cudaStream_t s) {
-  return launch_run<true>(q, n, out, scratch, total_bytes, status, s);
+  return launch_run<true>(q, n, 1, out, 0, scratch, total_bytes, status, s);
 }
 cudaError_t rle_encode(const int16_t* q, int64_t n, uint8_t* out, uint64_t* scratch, uint64_t* total_bytes,
                        int* status, cudaStream_t s) {
-  return launch_run<false>(q, n, out, scratch, total_bytes, status, s);
+  return launch_run<false>(q, n, 1, out, 0, scratch, total_bytes, status, s);
+}
+cudaError_t bsrle_encode_batch(const int16_t* q, int64_t n, int ns, uint8_t* out, int64_t out_stride,
+                               uint64_t* scratch, uint64_t* totals, int* status, cudaStream_t s) {
+  return launch_run<true>(q, n, ns, out, out_stride, scratch, totals, status, s);
+}
+cudaError_t rle_encode_batch(const int16_t* q, int64_t n, int ns, uint8_t* out, int64_t out_stride,
+                             uint64_t* scratch, uint64_t* totals, int* status, cudaStream_t s) {
+  return launch_run<false>(q, n, ns, out, out_stride, scratch, totals, status, s);
 }
 
 // ============================================================ stream decode

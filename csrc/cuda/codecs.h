@@ -17,7 +17,7 @@ constexpr int kRunTileItems = 4096;                               // items per t
 
 // Scratch words needed by the look-back encoders for n elements.
 int64_t pack_scratch_words(int64_t n, int64_t nstreams = 1);
-int64_t run_scratch_words(int64_t items);
+int64_t run_scratch_words(int64_t items, int64_t nstreams = 1);
 
 // ---- Q8.23 (K2) ----
 cudaError_t from_f32_dev(const float* x, int32_t* q, int64_t n, cudaStream_t s);
@@ -71,6 +71,13 @@ cudaError_t bsrle_encode(const int16_t* q, int64_t n, uint8_t* out, uint64_t* sc
                          int* status, cudaStream_t s);
 cudaError_t rle_encode(const int16_t* q, int64_t n, uint8_t* out, uint64_t* scratch, uint64_t* total_bytes,
                        int* status, cudaStream_t s);
+// Both over `ns` streams of n codes in one launch sequence (stream i at
+// q + i * n, bytes at out + i * out_stride, length totals[i]); scratch:
+// run_scratch_words(items per stream, ns).
+cudaError_t bsrle_encode_batch(const int16_t* q, int64_t n, int ns, uint8_t* out, int64_t out_stride,
+                               uint64_t* scratch, uint64_t* totals, int* status, cudaStream_t s);
+cudaError_t rle_encode_batch(const int16_t* q, int64_t n, int ns, uint8_t* out, int64_t out_stride,
+                             uint64_t* scratch, uint64_t* totals, int* status, cudaStream_t s);
 
 // ---- Stream decoders: header walk (one thread per stream) + parallel expansion ----
 // kind: 0 = BlockSparse (i16), 1 = top-k compat (i8), 2 = BlockSparse+RLE, 3 = RLE.

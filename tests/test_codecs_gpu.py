@@ -110,11 +110,14 @@ def test_topk_compat(n, k):
 
 
 @pytest.mark.parametrize("codec", ["eb", "rle", "bs", "bsrle"])
-def test_nz_pipeline_device_matches_host(codec):
-    P, T = 30001, 7
+@pytest.mark.parametrize("P,T,eps", [(30001, 7, 1e-3), (300007, 3, 1e-3), (300007, 3, 0.05), (1, 3, 1e-3),
+                                     (33, 2, 1e-3), (131073, 2, 1e-2)])
+def test_nz_pipeline_device_matches_host(codec, P, T, eps):
+    # Multi-tile streams (BlockSparse tiles of 16384 codes, run tiles of 4096
+    # items), dense and sparse codes, and one- and two-block snapshots.
     data = lammps.generate_synthetic(P, T)
-    hb, hst = nzcp.compress(data, P, T, codec, 1e-3)
-    db, dst = trajectory.compress(torch.from_numpy(data).cuda().view(T, P), codec, 1e-3)
+    hb, hst = nzcp.compress(data, P, T, codec, eps)
+    db, dst = trajectory.compress(torch.from_numpy(data).cuda().view(T, P), codec, eps)
     assert db == hb
     assert dst["total_comp"] == hst["total_comp"]
     assert abs(dst["max_abs_err"] - hst["max_abs_err"]) == 0.0
