@@ -125,6 +125,13 @@ NGL_HD int chunk_record_bytes(int mode, int k) {
                    : kChunkBlocks * topk_record_bytes(k);
 }
 
+// Static topology drop at chunk granularity (all ranks agree): chunk c of
+// nchunks is a passenger iff (c * a + b) mod nchunks < ndrop, with a coprime
+// to nchunks so the map is a permutation and exactly ndrop chunks drop.
+NGL_HD bool topo_passenger(uint64_t c, uint64_t a, uint64_t b, int64_t ndrop, uint64_t nchunks) {
+  return ndrop > 0 && (int64_t)((c * a + b) % nchunks) < ndrop;
+}
+
 // Kept elements per 256-block for a keep fraction.
 inline int topk_per_block(double frac) {
   int k = (int)(frac * kBlock + 0.5);

@@ -18,6 +18,16 @@ constexpr int kMaxChunkRec = 8 * kTopkMaxRec;
 enum Mode : int { kInt4 = 0, kInt8 = 1, kTopK = 2 };
 enum FlagKind : int { kFlagPayload = 0, kFlagResult = 1 };
 
+// Static topology drop at chunk granularity: chunk c (of nchunks) is a
+// passenger iff (c * a + b) mod nchunks < ndrop.  Passengers are neither
+// encoded nor sent; they reconstruct to the prediction and keep their whole
+// residual in the error feedback.  ndrop = 0 disables it.
+struct Topo {
+  uint32_t a;
+  uint32_t b;
+  int ndrop;
+};
+
 struct QParams {
   uint64_t seed;
   uint64_t step;
@@ -26,6 +36,7 @@ struct QParams {
   int stochastic;
   int use_ef;
   int use_pred;
+  Topo topo;
 };
 struct FParams {
   float inv_world;
@@ -33,6 +44,7 @@ struct FParams {
   float omb;
   int first;
   int use_pred;
+  Topo topo;
 };
 
 // Symmetric region of every rank (same layout on all ranks):

@@ -39,6 +39,19 @@ int dtype_code(torch::ScalarType t) {
   TORCH_CHECK(false, "bucket dtype must be float32 or bfloat16");
   return -1;
 }
+Topo topo_of(const std::vector<int64_t>& t, int64_t nchunks) {
+  Topo r{1u, 0u, 0};
+  if (t.empty()) return r;
+  TORCH_CHECK(t.size() == 3, "topology must be (a, b, ndrop)");
+  TORCH_CHECK(t[0] > 0 && t[1] >= 0 && t[2] >= 0 && t[2] < std::max<int64_t>(nchunks, 1) &&
+                  (nchunks == 0 || (t[0] < std::max<int64_t>(nchunks, 2) && t[1] < nchunks)),
+              "topology (a, b, ndrop) out of range for ", nchunks, " chunks");
+  r.a = (uint32_t)t[0];
+  r.b = (uint32_t)t[1];
+  r.ndrop = (int)t[2];
+  return r;
+}
+
 void check_launch(cudaError_t e, const char* what) {
   TORCH_CHECK(e == cudaSuccess, what, " launch failed: ", cudaGetErrorString(e));
 }
@@ -71,7 +84,7 @@ class FusedComm {
   // variant: 0 = auto-single (world 1), 1 = one-shot, 2 = two-shot.
   int64_t run(torch::Tensor grad, c10::optional<torch::Tensor> pred, c10::optional<torch::Tensor> ef, int64_t mode,
               int64_t k, int64_t variant, bool stochastic, int64_t seed, int64_t bucket, int64_t step, double beta,
-              bool first, int64_t max_ctas, int64_t timeout_ns, int64_t tag) {
+              bool first, int64_t max_ctas, int64_t timeout_ns, int64_t tag, std::vector<int64_t> topo) {
     check_dev(grad, "bucket");
     const int64_t n = grad.numel();
     FusedParams P = base_;
@@ -123,6 +136,8 @@ class FusedComm {
     P.f.omb = 1.0f - (float)beta;
     P.f.first = first ? 1 : 0;
     P.f.use_pred = P.pred != nullptr;
+    P.q.topo = topo_of(topo, P.nchunks);
+    P.f.topo = P.q.topo;
     P.timeout_ns = (uint64_t)timeout_ns;
     if (P.nblk == 0) return epoch_;
     const c10::cuda::CUDAGuard guard(grad.device());
@@ -147,7 +162,7 @@ class FusedComm {
 std::vector<torch::Tensor> product_encode_cuda(torch::Tensor g, c10::optional<torch::Tensor> pred,
                                                c10::optional<torch::Tensor> ef, int64_t mode, int64_t k,
                                                bool stochastic, int64_t seed, int64_t rank, int64_t bucket,
-                                               int64_t step) {
+                                               int64_t step, std::vector<int64_t> topo) {
   check_dev(g, "g");
   const int64_t n = g.numel();
   const int nblk = (int)((n + 255) / 256);
@@ -163,6 +178,7 @@ std::vector<torch::Tensor> product_encode_cuda(torch::Tensor g, c10::optional<to
   qp.stochastic = stochastic;
   qp.use_ef = ef.has_value();
   qp.use_pred = pred.has_value();
+  qp.topo = topo_of(topo, nchunks_of(n));
   if (pred.has_value()) check_dev(*pred, "pred");
   if (ef.has_value()) check_dev(*ef, "ef");
   if (nblk == 0) return {out, ef_out};
@@ -181,7 +197,7 @@ std::vector<torch::Tensor> product_encode_cuda(torch::Tensor g, c10::optional<to
 // in place when given and returns the averaged bucket.
 torch::Tensor product_reduce_cuda(std::vector<torch::Tensor> payloads, int64_t n, int64_t mode, int64_t k,
                                   c10::optional<torch::Tensor> pred, double beta, bool first, double inv_world,
-                                  torch::ScalarType out_dtype) {
+                                  torch::ScalarType out_dtype, std::vector<int64_t> topo) {
   TORCH_CHECK(!payloads.empty() && (int)payloads.size() <= kMaxWorld, "1..8 payloads");
   ReduceSrcs s;
   std::memset(&s, 0, sizeof(s));
@@ -198,6 +214,7 @@ torch::Tensor product_reduce_cuda(std::vector<torch::Tensor> payloads, int64_t n
   fp.omb = 1.0f - (float)beta;
   fp.first = first;
   fp.use_pred = pred.has_value();
+  fp.topo = topo_of(topo, nchunks_of(n));
   if (pred.has_value()) check_dev(*pred, "pred");
   const c10::cuda::CUDAGuard guard(payloads[0].device());
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
@@ -215,10 +232,19 @@ void register_fused(pybind11::module& m) {
   pybind11::class_<FusedComm>(m, "FusedComm")
       .def(pybind11::init<int64_t, int64_t, std::vector<int64_t>, int64_t, int64_t, int64_t, int64_t, int64_t,
                           torch::Tensor>())
-      .def("run", &FusedComm::run)
+      .def("run", &FusedComm::run, pybind11::arg("grad"), pybind11::arg("pred"), pybind11::arg("ef"),
+           pybind11::arg("mode"), pybind11::arg("k"), pybind11::arg("variant"), pybind11::arg("stochastic"),
+           pybind11::arg("seed"), pybind11::arg("bucket"), pybind11::arg("step"), pybind11::arg("beta"),
+           pybind11::arg("first"), pybind11::arg("max_ctas"), pybind11::arg("timeout_ns"), pybind11::arg("tag"),
+           pybind11::arg("topo") = std::vector<int64_t>{})
       .def_property("epoch", &FusedComm::epoch, &FusedComm::set_epoch);
-  m.def("product_encode", &product_encode_cuda);
-  m.def("product_reduce", &product_reduce_cuda);
+  m.def("product_encode", &product_encode_cuda, pybind11::arg("g"), pybind11::arg("pred"), pybind11::arg("ef"),
+        pybind11::arg("mode"), pybind11::arg("k"), pybind11::arg("stochastic"), pybind11::arg("seed"),
+        pybind11::arg("rank"), pybind11::arg("bucket"), pybind11::arg("step"),
+        pybind11::arg("topo") = std::vector<int64_t>{});
+  m.def("product_reduce", &product_reduce_cuda, pybind11::arg("payloads"), pybind11::arg("n"), pybind11::arg("mode"),
+        pybind11::arg("k"), pybind11::arg("pred"), pybind11::arg("beta"), pybind11::arg("first"),
+        pybind11::arg("inv_world"), pybind11::arg("out_dtype"), pybind11::arg("topo") = std::vector<int64_t>{});
   m.def("payload_bytes", &payload_bytes);
   m.def("fused_grid", [](int64_t n, int64_t mode, bool bf16, int64_t variant, int64_t cap, int64_t device) {
     const int nchunks = (int)nchunks_of(n);

@@ -38,6 +38,11 @@ namespace dev {
 
 __device__ __forceinline__ int64_t align16(int64_t x) { return (x + 15) & ~int64_t(15); }
 
+__device__ __forceinline__ bool passenger(const Topo& t, int c, int nchunks) {
+  return topo_passenger((uint64_t)c, t.a, t.b, t.ndrop, (uint64_t)nchunks);
+}
+
+
 // ------------------------------------------------------------ warp encoders
 // Residual c = g - pred + e of the lane's 8 consecutive elements of a block.
 template <typename T>
@@ -56,6 +61,16 @@ __device__ __forceinline__ int load_residual(const T* g, const float* pred, cons
     c[j] = (j < valid) ? product_residual(gv[j], p, e) : 0.0f;
   }
   return valid;
+}
+
+// Passenger block: the whole residual goes to the error feedback.
+template <typename T>
+__device__ __forceinline__ void passenger_block(const T* g, const float* pred, float* ef, int64_t n, int blk, int lane,
+                                                const QParams& qp) {
+  if (!qp.use_ef) return;
+  float cv[8];
+  const int valid = load_residual<T>(g, pred, ef, n, blk, lane, qp, cv);
+  store8<float>(ef, (int64_t)blk * kBlock + lane * 8, valid, true, cv);
 }
 
 __device__ __forceinline__ float block_absmax(const float (&c)[8]) {
@@ -257,9 +272,19 @@ __device__ __forceinline__ void topk_accum_global(const uint8_t* rec_g, uint8_t*
 // with __syncthreads).  Blocks past the end are written as empty blocks.
 template <int MODE, typename T>
 __device__ __forceinline__ void encode_chunk(const T* g, const float* pred, const float* ef, int64_t n, int nblk,
-                                             int k, int rec_bytes, const QParams& qp, int c, uint8_t* rec) {
+                                             int nchunks, int k, int rec_bytes, const QParams& qp, int c,
+                                             uint8_t* rec) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int blk = c * kChunkBlocks + warp;
+  if (passenger(qp.topo, c, nchunks)) {
+    // No record is sent for a passenger; the zero record (which decodes to
+    // zero) is staged for the single-GPU encode path.
+    if (blk < nblk) passenger_block<T>(g, pred, const_cast<float*>(ef), n, blk, lane, qp);
+    const int bytes = chunk_record_bytes(MODE, k);
+    for (int w = threadIdx.x; w < bytes / 4; w += blockDim.x) reinterpret_cast<uint32_t*>(rec)[w] = 0u;
+    __syncthreads();
+    return;
+  }
   if (MODE == kTopK) {
     uint8_t* r = rec + warp * rec_bytes;
     if (blk < nblk) {
@@ -293,15 +318,17 @@ __device__ __forceinline__ void copy_record(uint8_t* dst, const uint8_t* rec, in
 // Decode chunk c: accumulate the W records in rank order, finalize.
 template <int MODE, typename T, typename RecOf>
 __device__ __forceinline__ void decode_chunk(const RecOf& rec_of, int world, T* grad, float* pred, int64_t n, int nblk,
-                                             int k, int rec_bytes, const FParams& fp, int c, uint8_t* stage_smem,
-                                             float* acc_smem) {
+                                             int nchunks, int k, int rec_bytes, const FParams& fp, int c,
+                                             uint8_t* stage_smem, float* acc_smem) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int blk = c * kChunkBlocks + warp;
   if (blk >= nblk) return;
   float acc[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
-  if (MODE == kTopK) {
+  if (passenger(fp.topo, c, nchunks)) {
+    // nothing was sent: the passenger reconstructs to the prediction
+  } else if (MODE == kTopK) {
     float* a = acc_smem + warp * kBlock;
     uint8_t* stage = stage_smem + warp * kTopkMaxRec;
 #pragma unroll
@@ -412,7 +439,8 @@ __global__ void __launch_bounds__(kThreads) oneshot_kernel(FusedParams P) {
   const T* g = reinterpret_cast<const T*>(P.grad);
   // Phase 1: encode each owned chunk and push its record to every rank.
   for (int c = blockIdx.x; c < P.nchunks; c += gridDim.x) {
-    encode_chunk<MODE, T>(g, P.pred, P.ef, P.n, P.nblk, P.k, P.rec_bytes, P.q, c, rec);
+    encode_chunk<MODE, T>(g, P.pred, P.ef, P.n, P.nblk, P.nchunks, P.k, P.rec_bytes, P.q, c, rec);
+    if (passenger(P.q.topo, c, P.nchunks)) continue;
     for (int i = 0; i < P.world; ++i) {
       const int r = (P.rank + 1 + i) % P.world;  // self last
       copy_record(slot_rec(P, r, P.rank, c), rec, P.chunk_bytes);
@@ -425,8 +453,8 @@ __global__ void __launch_bounds__(kThreads) oneshot_kernel(FusedParams P) {
   auto rec_of = [&](int src) { return slot_rec(P, P.rank, src, 0); };
   for (int c = blockIdx.x; c < P.nchunks; c += gridDim.x) {
     auto rc = [&](int src) { return rec_of(src) + (int64_t)c * P.chunk_bytes; };
-    decode_chunk<MODE, T>(rc, P.world, reinterpret_cast<T*>(P.grad), P.pred, P.n, P.nblk, P.k, P.rec_bytes, P.f, c,
-                          stage, acc_smem);
+    decode_chunk<MODE, T>(rc, P.world, reinterpret_cast<T*>(P.grad), P.pred, P.n, P.nblk, P.nchunks, P.k,
+                          P.rec_bytes, P.f, c, stage, acc_smem);
   }
 }
 
@@ -442,7 +470,8 @@ __global__ void __launch_bounds__(kThreads) twoshot_kernel(FusedParams P) {
   {
     int i = 0;
     for (int c = blockIdx.x; c < P.nchunks; c += gridDim.x, ++i) {
-      encode_chunk<MODE, T>(g, P.pred, P.ef, P.n, P.nblk, P.k, P.rec_bytes, P.q, c, rec);
+      encode_chunk<MODE, T>(g, P.pred, P.ef, P.n, P.nblk, P.nchunks, P.k, P.rec_bytes, P.q, c, rec);
+      if (passenger(P.q.topo, c, P.nchunks)) continue;
       copy_record(slot_rec(P, i % P.world, P.rank, c), rec, P.chunk_bytes);
       __syncthreads();
     }
@@ -453,7 +482,7 @@ __global__ void __launch_bounds__(kThreads) twoshot_kernel(FusedParams P) {
   {
     int i = 0;
     for (int c = blockIdx.x; c < P.nchunks; c += gridDim.x, ++i) {
-      if (i % P.world != P.rank) continue;
+      if (i % P.world != P.rank || passenger(P.q.topo, c, P.nchunks)) continue;
       const int blk = c * kChunkBlocks + warp;
       float acc[8];
 #pragma unroll
@@ -491,7 +520,7 @@ __global__ void __launch_bounds__(kThreads) twoshot_kernel(FusedParams P) {
     float acc[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
-    accum_dense<8>(result_rec(P, P.rank, c), warp, lane, acc);
+    if (!passenger(P.f.topo, c, P.nchunks)) accum_dense<8>(result_rec(P, P.rank, c), warp, lane, acc);
     finalize<T>(reinterpret_cast<T*>(P.grad), P.pred, P.n, blk, lane, acc, f);
   }
 }
@@ -504,7 +533,11 @@ __global__ void __launch_bounds__(kThreads) single_kernel(FusedParams P) {
   for (int blk = blockIdx.x * kWarps + warp; blk < P.nblk; blk += gridDim.x * kWarps) {
     float c[8], acc[8];
     const int valid = load_residual<T>(reinterpret_cast<const T*>(P.grad), P.pred, P.ef, P.n, blk, lane, P.q, c);
-    if (MODE == kTopK) {
+    if (passenger(P.q.topo, blk / kChunkBlocks, P.nchunks)) {
+      if (P.q.use_ef) store8<float>(P.ef, (int64_t)blk * kBlock + lane * 8, valid, true, c);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+    } else if (MODE == kTopK) {
       TopkSel r = topk_select(c, valid, blk, lane, P.k, P.n, P.q, P.ef, rec_smem + warp * kTopkMaxRec, P.rec_bytes);
 #pragma unroll
       for (int j = 0; j < 8; ++j) acc[j] = ((r.selmask >> j) & 1u) ? product_accum(0.0f, r.q[j], r.s) : 0.0f;
@@ -539,7 +572,7 @@ __global__ void __launch_bounds__(kThreads) encode_kernel(const T* g, const floa
       for (int64_t i = e0 + threadIdx.x; i < e1; i += blockDim.x) ef_out[i] = ef_in[i];
       __syncthreads();
     }
-    encode_chunk<MODE, T>(g, pred, ef_out, n, nblk, k, rec_bytes, qp, c, rec);
+    encode_chunk<MODE, T>(g, pred, ef_out, n, nblk, nchunks, k, rec_bytes, qp, c, rec);
     copy_record(out + (int64_t)c * chunk_bytes, rec, chunk_bytes);
     __syncthreads();
   }
@@ -553,7 +586,7 @@ __global__ void __launch_bounds__(kThreads) reduce_kernel(ReduceSrcs srcs, int w
   __shared__ __align__(16) float acc_smem[Smem<MODE>::kAcc];
   for (int c = blockIdx.x; c < nchunks; c += gridDim.x) {
     auto rc = [&](int src) { return srcs.p[src] + (int64_t)c * chunk_bytes; };
-    decode_chunk<MODE, T>(rc, world, out, pred, n, nblk, k, rec_bytes, fp, c, stage, acc_smem);
+    decode_chunk<MODE, T>(rc, world, out, pred, n, nblk, nchunks, k, rec_bytes, fp, c, stage, acc_smem);
   }
 }
 

@@ -142,8 +142,12 @@ PYBIND11_MODULE(_host, m) {
 
   // Product format oracle (chunked wire payloads)
   m.def("product_wire_bytes", &product_wire_bytes);
+  m.def("product_topology", [](size_t nchunks, double drop, uint64_t seed, uint64_t stream) {
+    const TopoChunks t = product_topology(nchunks, drop, seed, stream);
+    return py::make_tuple(t.a, t.b, t.ndrop);
+  });
   m.def("product_encode", [](carr<float> g, py::object pred, py::object e_in, int bits, bool stochastic, bool ef,
-                             uint64_t seed, uint32_t rank, uint32_t bucket, uint64_t step) {
+                             uint64_t seed, uint32_t rank, uint32_t bucket, uint64_t step, py::tuple topo) {
     const size_t n = g.size();
     carr<float> pr = pred.is_none() ? carr<float>() : pred.cast<carr<float>>();
     carr<float> ei = e_in.is_none() ? carr<float>() : e_in.cast<carr<float>>();
@@ -159,10 +163,16 @@ PYBIND11_MODULE(_host, m) {
     p.rank = rank;
     p.bucket = bucket;
     p.step = step;
+    if (topo.size() == 3) {
+      p.topo_a = topo[0].cast<uint64_t>();
+      p.topo_b = topo[1].cast<uint64_t>();
+      p.topo_ndrop = topo[2].cast<int64_t>();
+    }
     product_encode(ptr(g), pred.is_none() ? nullptr : ptr(pr), e_in.is_none() ? nullptr : ptr(ei), n, p,
                    wire.data(), ef ? e_out.data() : nullptr);
     return py::make_tuple(to_np(std::move(wire)), to_np(std::move(e_out)));
-  });
+  }, py::arg("g"), py::arg("pred"), py::arg("e_in"), py::arg("bits"), py::arg("stochastic"), py::arg("ef"),
+     py::arg("seed"), py::arg("rank"), py::arg("bucket"), py::arg("step"), py::arg("topo") = py::tuple());
   auto reduce_impl = [](bool twoshot) {
     return [twoshot](std::vector<carr<uint8_t>> wires, size_t n, int bits, py::object pred, float inv_world) {
       const int W = (int)wires.size();
@@ -184,16 +194,22 @@ PYBIND11_MODULE(_host, m) {
     product_ema(s.data(), ptr(avg), s.size(), beta, first);
     return to_np(std::move(s));
   });
-  m.def("product_topk_encode", [](carr<float> g, py::object pred, py::object e_in, int k, bool ef) {
+  m.def("product_topk_encode", [](carr<float> g, py::object pred, py::object e_in, int k, bool ef, py::tuple topo) {
+    TopoChunks t;
+    if (topo.size() == 3) {
+      t.a = topo[0].cast<uint64_t>();
+      t.b = topo[1].cast<uint64_t>();
+      t.ndrop = topo[2].cast<int64_t>();
+    }
     const size_t n = g.size();
     carr<float> pr = pred.is_none() ? carr<float>() : pred.cast<carr<float>>();
     carr<float> ei = e_in.is_none() ? carr<float>() : e_in.cast<carr<float>>();
     std::vector<uint8_t> rec(product_wire_bytes(n, 2, k));
     std::vector<float> e_out(ef ? n : 0);
     product_topk_encode(ptr(g), pred.is_none() ? nullptr : ptr(pr), e_in.is_none() ? nullptr : ptr(ei), n, k, ef,
-                        rec.data(), ef ? e_out.data() : nullptr);
+                        rec.data(), ef ? e_out.data() : nullptr, t);
     return py::make_tuple(to_np(std::move(rec)), to_np(std::move(e_out)));
-  });
+  }, py::arg("g"), py::arg("pred"), py::arg("e_in"), py::arg("k"), py::arg("ef"), py::arg("topo") = py::tuple());
   m.def("product_topk_reduce", [](std::vector<carr<uint8_t>> recs, size_t n, int k, py::object pred, float inv_world) {
     const int W = (int)recs.size();
     std::vector<const uint8_t*> rp(W);

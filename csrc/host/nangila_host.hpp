@@ -147,7 +147,18 @@ struct ProductParams {
   uint32_t rank = 0;
   uint32_t bucket = 0;
   uint64_t step = 0;
+  // static topology drop (topo_passenger); ndrop = 0 keeps every chunk
+  uint64_t topo_a = 0, topo_b = 0;
+  int64_t topo_ndrop = 0;
 };
+// Topology drop parameters of a bucket of nchunks chunk records: exactly
+// nchunks - max(1, floor(nchunks * (1 - drop))) chunks become passengers,
+// spread by a keyed permutation of (seed, stream).
+struct TopoChunks {
+  uint64_t a = 1, b = 0;
+  int64_t ndrop = 0;
+};
+TopoChunks product_topology(size_t nchunks, double drop, uint64_t seed, uint64_t stream);
 // Encode one rank's residual c = g - pred + e into the chunked wire payload
 // (product_wire_bytes bytes); writes the new error feedback when e_out is set.
 size_t product_wire_bytes(size_t n, int mode, int k);
@@ -164,7 +175,7 @@ void product_ema(float* state, const float* avg, size_t n, float beta, bool firs
 // Per-256-block top-k: fixed-size records (scale, ascending indices, int8
 // values), 8 per chunk; decode-sum in rank order.
 void product_topk_encode(const float* g, const float* pred, const float* e_in, size_t n, int k, bool ef,
-                         uint8_t* records, float* e_out);
+                         uint8_t* records, float* e_out, const TopoChunks& topo = TopoChunks());
 void product_topk_reduce(const uint8_t* const* records, int world, size_t n, int k, const float* pred,
                          float inv_world, float* avg_out);
 

@@ -2,7 +2,9 @@
 // (csrc/cuda/fused_allreduce.cu).  Same per-element arithmetic
 // (csrc/common/ngl_product.h) in plain sequential loops.
 #include <algorithm>
+#include <cmath>
 #include <cstring>
+#include <numeric>
 
 #include "../common/ngl_product.h"
 #include "nangila_host.hpp"
@@ -28,6 +30,22 @@ inline float dense_scale_c(const uint8_t* wire, size_t b, size_t cr) {
 
 size_t product_wire_bytes(size_t n, int mode, int k) { return nchunks_of(n) * (size_t)chunk_record_bytes(mode, k); }
 
+TopoChunks product_topology(size_t nchunks, double drop, uint64_t seed, uint64_t stream) {
+  TopoChunks t;
+  if (nchunks == 0) return t;
+  drop = std::min(1.0, std::max(0.0, drop));
+  int64_t keep = (int64_t)std::floor((double)nchunks * (1.0 - drop));
+  keep = std::max<int64_t>(1, std::min<int64_t>(keep, (int64_t)nchunks));
+  t.ndrop = (int64_t)nchunks - keep;
+  const uint64_t h = fmix64(seed ^ (stream * 0x9E3779B97F4A7C15ull));
+  const uint64_t nc = (uint64_t)nchunks;
+  uint64_t a = nc > 1 ? 1 + h % (nc - 1) : 1;
+  while (std::gcd(a, nc) != 1) a = a + 1 < nc ? a + 1 : 1;
+  t.a = a;
+  t.b = fmix64(h ^ 0xD1B54A32D192ED03ull) % nc;
+  return t;
+}
+
 void product_encode(const float* g, const float* pred, const float* e_in, size_t n, const ProductParams& p,
                     uint8_t* wire, float* e_out) {
   const int32_t qmax = p.bits == 4 ? 7 : 127;
@@ -38,9 +56,17 @@ void product_encode(const float* g, const float* pred, const float* e_in, size_t
   std::memset(wire, 0, nchunks_of(n) * cr);
   float c[kBlock];
   int32_t q[kBlock];
+  const uint64_t nch = nchunks_of(n);
   for (size_t b = 0; b < nblk; ++b) {
     const size_t base = b * kBlock;
     const size_t len = std::min<size_t>(kBlock, n - base);
+    if (topo_passenger(b / kChunkBlocks, p.topo_a, p.topo_b, p.topo_ndrop, nch)) {
+      // passenger: zero record, the whole residual goes to the error feedback
+      if (p.error_feedback && e_out)
+        for (size_t i = 0; i < len; ++i)
+          e_out[base + i] = product_residual(g[base + i], pred ? pred[base + i] : 0.0f, e_in ? e_in[base + i] : 0.0f);
+      continue;
+    }
     float absmax = 0.0f;
     for (size_t i = 0; i < kBlock; ++i) {
       if (i < len) {
@@ -114,15 +140,22 @@ inline uint32_t fbits(float x) {
 }  // namespace
 
 void product_topk_encode(const float* g, const float* pred, const float* e_in, size_t n, int k, bool ef,
-                         uint8_t* records, float* e_out) {
+                         uint8_t* records, float* e_out, const TopoChunks& topo) {
   const size_t nblk = (n + kBlock - 1) / kBlock;
   const int rb = topk_record_bytes(k);
   std::memset(records, 0, nchunks_of(n) * kChunkBlocks * rb);
   float c[kBlock];
   uint32_t mag[kBlock];
+  const uint64_t nch = nchunks_of(n);
   for (size_t b = 0; b < nblk; ++b) {
     const size_t base = b * kBlock;
     const int len = (int)std::min<size_t>(kBlock, n - base);
+    if (topo_passenger(b / kChunkBlocks, topo.a, topo.b, topo.ndrop, nch)) {
+      if (ef && e_out)
+        for (int i = 0; i < len; ++i)
+          e_out[base + i] = product_residual(g[base + i], pred ? pred[base + i] : 0.0f, e_in ? e_in[base + i] : 0.0f);
+      continue;
+    }
     float absmax = 0.0f;
     for (int i = 0; i < len; ++i) {
       c[i] = product_residual(g[base + i], pred ? pred[base + i] : 0.0f, (ef && e_in) ? e_in[base + i] : 0.0f);

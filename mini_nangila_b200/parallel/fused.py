@@ -75,6 +75,34 @@ def payload_bytes(n: int, mode: str, k: int = 0) -> int:
     return nchunks_of(n) * chunk_record_bytes(mode, k)
 
 
+_TOPO_CACHE: dict = {}
+
+
+def topology(n: int, drop: float, seed: int, stream: int) -> tuple[int, int, int]:
+    """Chunk-granular static topology drop of a bucket of n elements:
+    (a, b, ndrop) such that chunk c is a passenger iff
+    (c * a + b) mod nchunks < ndrop.  Identical on every rank."""
+    if drop <= 0.0:
+        return (1, 0, 0)
+    key = (nchunks_of(n), float(drop), int(seed), int(stream))
+    t = _TOPO_CACHE.get(key)
+    if t is None:
+        from .._ext import host
+
+        t = tuple(int(x) for x in host().product_topology(key[0], key[1], key[2] & 0xFFFFFFFFFFFFFFFF,
+                                                          key[3] & 0xFFFFFFFFFFFFFFFF))
+        if len(_TOPO_CACHE) > 4096:
+            _TOPO_CACHE.clear()
+        _TOPO_CACHE[key] = t
+    return t
+
+
+def wire_bytes(n: int, mode: str, k: int = 0, drop: float = 0.0, seed: int = 0, stream: int = 0) -> int:
+    """Bytes one rank actually sends for a bucket (passenger chunks are not sent)."""
+    ndrop = topology(n, drop, seed, stream)[2]
+    return (nchunks_of(n) - ndrop) * chunk_record_bytes(mode, k)
+
+
 def dense_payload_bytes(n: int, bits: int) -> int:
     return payload_bytes(n, "int4" if bits == 4 else "int8")
 
@@ -189,12 +217,15 @@ class FusedAllReduce:
         beta: float = 0.9,
         first: bool = False,
         tag: int | None = None,
+        topo_drop: float = 0.0,
+        topo_seed: int = 0,
     ) -> str:
         """Average ``grad`` across ranks in place on the current stream.
 
         Buckets longer than ``capacity`` run as several launches over
         segments; segment s of bucket b draws its noise from stream
-        ``b * 65536 + s``.
+        ``b * 65536 + s``.  ``topo_drop`` > 0 makes that fraction of the
+        bucket's 2048-element chunks passengers (see ``topology``).
         """
         n = grad.numel()
         if self.world > 1 and n > self.capacity:
@@ -206,7 +237,8 @@ class FusedAllReduce:
                     grad[s0:s1], None if pred is None else pred[s0:s1], None if ef is None else ef[s0:s1],
                     mode=mode, k=k, variant=variant, stochastic=stochastic, seed=seed,
                     bucket=(bucket * 65536 + si) & 0xFFFFFFFF, step=step, beta=beta, first=first,
-                    tag=None if tag is None else (tag + si) & 0xFFFFFFFF,
+                    tag=None if tag is None else (tag + si) & 0xFFFFFFFF, topo_drop=topo_drop,
+                    topo_seed=topo_seed,
                 )
             return v
         v = self.choose_variant(n, mode, variant)
@@ -215,6 +247,7 @@ class FusedAllReduce:
         self.comm.run(
             grad, pred, ef, MODES[mode], int(k), VARIANTS[v], bool(stochastic), int(seed) & 0x7FFFFFFFFFFFFFFF,
             int(bucket), int(step), float(beta), bool(first), self.max_ctas, self.timeout_ns, int(tag),
+            list(topology(n, topo_drop, topo_seed, bucket)) if topo_drop > 0.0 else [],
         )
         self.launches += 1
         self._status_host.copy_(self.status, non_blocking=True)

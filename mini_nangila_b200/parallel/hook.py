@@ -15,6 +15,13 @@ hook (``python/nangila_ddp/comm_hook.py:47-60``) and adds:
 * ``error_feedback`` (fused/host; the reference has none), ``variant``
   (``auto|oneshot|twoshot``), ``timeout_s``, ``verbose``, ``max_ctas``.
 
+``topo_drop_percent`` (a fraction, as in the reference) selects passengers
+per bucket.  fused/host drop whole 2048-element chunks by a keyed
+permutation that every rank computes alike: passengers are neither encoded
+nor sent, reconstruct to the prediction, and (with error feedback) carry
+their residual to the next step.  The reference drops single elements with a
+seeded ``randperm`` (``comm_hook.py:149-174``); ``impl="compat"`` does that.
+
 The hook state object returned by ``register_nangila_hook`` exposes
 ``state_dict()/load_state_dict()`` (predictor and error-feedback buffers,
 call counters) so a resumed run continues bit-identically.
@@ -28,7 +35,7 @@ import numpy as np
 import torch
 import torch.distributed as dist
 
-from .fused import FusedAllReduce, payload_bytes, topk_per_block
+from .fused import FusedAllReduce, topk_per_block, topology, wire_bytes
 
 
 @dataclass
@@ -171,10 +178,11 @@ def _fused_hook(hs: NangilaHookState, bucket):
         hs.last_variant = hs.comm.allreduce_(
             buf, st.pred, st.ef, mode=cfg.mode, k=cfg.k, variant=cfg.variant, stochastic=cfg.stochastic,
             seed=cfg.seed, bucket=bidx, step=st.calls, beta=cfg.beta, first=first,
+            topo_drop=cfg.topo_drop_percent, topo_seed=cfg.topo_seed,
         )
         fut = torch.futures.Future(devices=[buf.device])
         fut.set_result(buf)
-    comp = payload_bytes(buf.numel(), cfg.mode, cfg.k)
+    comp = wire_bytes(buf.numel(), cfg.mode, cfg.k, cfg.topo_drop_percent, cfg.topo_seed, bidx)
     hs.raw_bytes += buf.numel() * 4
     hs.comp_bytes += comp
     _log(hs, bidx, buf.numel(), comp)
@@ -197,12 +205,13 @@ def _host_hook(hs: NangilaHookState, bucket):
     pred = st.pred.cpu().numpy() if st.pred is not None else None
     ef = st.ef.cpu().numpy() if st.ef is not None else None
     n = g.size
+    topo = topology(n, cfg.topo_drop_percent, cfg.topo_seed, bidx)
     if cfg.mode == "topk":
-        wire, e_out = h.product_topk_encode(g, pred, ef, cfg.k, cfg.error_feedback)
+        wire, e_out = h.product_topk_encode(g, pred, ef, cfg.k, cfg.error_feedback, topo)
     else:
         bits = 4 if cfg.mode == "int4" else 8
         wire, e_out = h.product_encode(g, pred, ef, bits, cfg.stochastic, cfg.error_feedback,
-                                       cfg.seed & 0x7FFFFFFFFFFFFFFF, rank, bidx, st.calls)
+                                       cfg.seed & 0x7FFFFFFFFFFFFFFF, rank, bidx, st.calls, topo)
     payload = torch.from_numpy(np.ascontiguousarray(wire))
     gathered = [torch.empty_like(payload) for _ in range(world)]
     dist.all_gather(gathered, payload, group=hs.group)
@@ -217,7 +226,7 @@ def _host_hook(hs: NangilaHookState, bucket):
     if st.ef is not None:
         st.ef.copy_(torch.from_numpy(e_out))
     buf.copy_(torch.from_numpy(avg).to(buf.dtype))
-    comp = payload.numel()
+    comp = wire_bytes(n, cfg.mode, cfg.k, cfg.topo_drop_percent, cfg.topo_seed, bidx)
     hs.raw_bytes += n * 4
     hs.comp_bytes += comp
     _log(hs, bidx, n, comp)
@@ -266,8 +275,6 @@ def register_nangila_hook(
         hs = NangilaHookState(cfg, process_group)
         model.register_comm_hook(state=None, hook=make_compat_hook(hs))
         return hs
-    if topo_drop_percent > 0.0:
-        raise NotImplementedError("static topology drop is provided by impl='compat'")
     cfg = HookConfig(beta, bits, stochastic, use_fp16_transport, seed, metrics_path, use_momentum, topk_percent,
                      topo_drop_percent, topo_seed, impl, True if error_feedback is None else bool(error_feedback),
                      variant, timeout_s, verbose, max_ctas)

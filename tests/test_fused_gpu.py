@@ -28,8 +28,12 @@ def _bits(a):
 @pytest.mark.parametrize("n", SIZES)
 @pytest.mark.parametrize("mode", ["int4", "int8", "topk"])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_encode_matches_oracle(n, mode, dtype):
+@pytest.mark.parametrize("drop", [0.0, 0.4])
+def test_encode_matches_oracle(n, mode, dtype, drop):
+    from mini_nangila_b200.parallel.fused import topology
+
     h, c = _ext()
+    topo = topology(n, drop, 11, 5)
     g = torch.from_numpy(_data(n, 1)).to(dtype)
     gf = g.float().numpy()
     pred = _data(n, 2)
@@ -38,11 +42,11 @@ def test_encode_matches_oracle(n, mode, dtype):
     mcode = {"int4": 0, "int8": 1, "topk": 2}[mode]
     k = 13
     out, ef_out = c.product_encode(g.to(dev), torch.from_numpy(pred).to(dev), torch.from_numpy(ef).to(dev),
-                                   mcode, k, True, 777, 3, 5, 9)
+                                   mcode, k, True, 777, 3, 5, 9, list(topo) if drop else [])
     if mode == "topk":
-        wire, e_ref = h.product_topk_encode(gf, pred, ef, k, True)
+        wire, e_ref = h.product_topk_encode(gf, pred, ef, k, True, topo)
     else:
-        wire, e_ref = h.product_encode(gf, pred, ef, 4 if mode == "int4" else 8, True, True, 777, 3, 5, 9)
+        wire, e_ref = h.product_encode(gf, pred, ef, 4 if mode == "int4" else 8, True, True, 777, 3, 5, 9, topo)
     assert bytes(out.cpu().numpy()) == bytes(wire)
     assert np.array_equal(_bits(ef_out.cpu().numpy()), _bits(e_ref))
 
@@ -80,8 +84,9 @@ def test_reduce_matches_oracle(n, mode):
 
 @pytest.mark.parametrize("mode", ["int4", "int8", "topk"])
 @pytest.mark.parametrize("n", [1000, 65536 + 3])
-def test_fused_single_rank_matches_oracle(mode, n):
-    from mini_nangila_b200.parallel.fused import FusedAllReduce
+@pytest.mark.parametrize("drop", [0.0, 0.3])
+def test_fused_single_rank_matches_oracle(mode, n, drop):
+    from mini_nangila_b200.parallel.fused import FusedAllReduce, topology
 
     h, _ = _ext()
     dev = torch.device("cuda")
@@ -94,12 +99,14 @@ def test_fused_single_rank_matches_oracle(mode, n):
     for step in range(3):
         g = _data(n, 100 + step)
         gd = torch.from_numpy(g).to(dev)
-        comm.allreduce_(gd, pred_d, ef_d, mode=mode, k=k, seed=42, bucket=2, step=step, beta=0.9, first=(step == 0))
+        comm.allreduce_(gd, pred_d, ef_d, mode=mode, k=k, seed=42, bucket=2, step=step, beta=0.9, first=(step == 0),
+                        topo_drop=drop, topo_seed=17)
+        topo = topology(n, drop, 17, 2)
         if mode == "topk":
-            rec, e_new = h.product_topk_encode(g, pred, ef, k, True)
+            rec, e_new = h.product_topk_encode(g, pred, ef, k, True, topo)
             avg = h.product_topk_reduce([rec], n, k, pred, 1.0)
         else:
-            wire, e_new = h.product_encode(g, pred, ef, bits, True, True, 42, 0, 2, step)
+            wire, e_new = h.product_encode(g, pred, ef, bits, True, True, 42, 0, 2, step, topo)
             avg = h.product_reduce([wire], n, bits, pred, 1.0)
         pred = h.product_ema(pred, avg, 0.9, step == 0)
         ef = e_new
@@ -109,10 +116,13 @@ def test_fused_single_rank_matches_oracle(mode, n):
     comm.check()
 
 
-def _two_rank_emulation(n, mode, k, bad_tag=False, deliver=True, timeout_s=0.2):
+def _two_rank_emulation(n, mode, k, bad_tag=False, deliver=True, timeout_s=0.2, drop=0.0):
     """Run rank 0 of a 2-rank one-shot all-reduce on one GPU with rank 1's
     payload and column flags pre-delivered into rank 0's region."""
-    from mini_nangila_b200.parallel.fused import MAX_COLS, MODES, VARIANTS, FusedAllReduce, make_layout
+    from mini_nangila_b200.parallel.fused import MAX_COLS, MODES, VARIANTS, FusedAllReduce, make_layout, topology
+
+    topo = topology(n, drop, 3, 4)
+    tl = list(topo) if drop else []
 
     h, c = _ext()
     dev = torch.device("cuda")
@@ -130,7 +140,7 @@ def _two_rank_emulation(n, mode, k, bad_tag=False, deliver=True, timeout_s=0.2):
     mcode = MODES[mode]
     grid = c.fused_grid(n, mcode, False, VARIANTS["oneshot"], 0, 0)
     if deliver:
-        p1, _ = c.product_encode(torch.from_numpy(g1).to(dev), None, None, mcode, k, True, 99, 1, 4, 7)
+        p1, _ = c.product_encode(torch.from_numpy(g1).to(dev), None, None, mcode, k, True, 99, 1, 4, 7, tl)
         slot = L.inbox_off + (parity * 2 + 1) * L.slot_bytes
         reg0[slot: slot + p1.numel()] = p1
         flags = reg0[L.flags_off:].view(torch.int64)
@@ -142,24 +152,26 @@ def _two_rank_emulation(n, mode, k, bad_tag=False, deliver=True, timeout_s=0.2):
         flags[base: base + grid] = val
     torch.cuda.synchronize()
     gd = torch.from_numpy(g0).to(dev)
-    comm.run(gd, None, None, mcode, k, VARIANTS["oneshot"], True, 99, 4, 7, 0.9, True, 0, int(timeout_s * 1e9), tag)
+    comm.run(gd, None, None, mcode, k, VARIANTS["oneshot"], True, 99, 4, 7, 0.9, True, 0, int(timeout_s * 1e9), tag,
+             tl)
     torch.cuda.synchronize()
     st = status.cpu().tolist()
     inv = float(np.float32(0.5))
     if mode == "topk":
-        r0, _ = h.product_topk_encode(g0, None, None, k, False)
-        r1, _ = h.product_topk_encode(g1, None, None, k, False)
+        r0, _ = h.product_topk_encode(g0, None, None, k, False, topo)
+        r1, _ = h.product_topk_encode(g1, None, None, k, False, topo)
         ref = h.product_topk_reduce([r0, r1], n, k, None, inv)
     else:
-        w0, _ = h.product_encode(g0, None, None, bits, True, False, 99, 0, 4, 7)
-        w1, _ = h.product_encode(g1, None, None, bits, True, False, 99, 1, 4, 7)
+        w0, _ = h.product_encode(g0, None, None, bits, True, False, 99, 0, 4, 7, topo)
+        w1, _ = h.product_encode(g1, None, None, bits, True, False, 99, 1, 4, 7, topo)
         ref = h.product_reduce([w0, w1], n, bits, None, inv)
     return st, gd.cpu().numpy(), ref
 
 
 @pytest.mark.parametrize("mode", ["int4", "int8", "topk"])
-def test_oneshot_kernel_with_predelivered_peer(mode):
-    st, out, ref = _two_rank_emulation(50000, mode, 13)
+@pytest.mark.parametrize("drop", [0.0, 0.5])
+def test_oneshot_kernel_with_predelivered_peer(mode, drop):
+    st, out, ref = _two_rank_emulation(50000, mode, 13, drop=drop)
     assert st[0] == 0, st
     assert np.array_equal(_bits(out), _bits(ref))
 

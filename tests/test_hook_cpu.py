@@ -38,8 +38,10 @@ def _train_worker(rank, world, port, impl, mode, outdir):
 
         torch.manual_seed(0)
         cfg = GPT2Config.tiny()
+        topo = mode.endswith("+topo")
+        mode = mode.split("+")[0]
         kw = dict(use_momentum=True, bits=8 if mode == "int8" else 4,
-                  topk_percent=0.1 if mode == "topk" else 0.0, seed=5)
+                  topk_percent=0.1 if mode == "topk" else 0.0, seed=5, topo_drop_percent=0.3 if topo else 0.0)
         if impl == "host":
             kw["error_feedback"] = True
         tr = DDPTrainer(GPT2(cfg), hook=impl, hook_kwargs=kw, device=torch.device("cpu"), bucket_cap_mb=0.05)
@@ -58,8 +60,9 @@ def _train_worker(rank, world, port, impl, mode, outdir):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("impl,mode", [("host", "int4"), ("host", "int8"), ("host", "topk"), ("compat", "int4"),
-                                       ("compat", "topk")])
+@pytest.mark.parametrize("impl,mode", [("host", "int4"), ("host", "int8"), ("host", "topk"), ("host", "int4+topo"),
+                                       ("host", "topk+topo"), ("compat", "int4"), ("compat", "topk"),
+                                       ("compat", "int4+topo")])
 def test_ddp_hook_ranks_stay_identical(impl, mode, tmp_path):
     mp.start_processes(_train_worker, args=(2, _port(), impl, mode, str(tmp_path)), nprocs=2, join=True,
                        start_method="spawn")

@@ -38,14 +38,15 @@ def _worker(rank, world, port, cases, errfile):
                             device_id=dev)
     try:
         from mini_nangila_b200 import _ext
-        from mini_nangila_b200.parallel.fused import FusedAllReduce
+        from mini_nangila_b200.parallel.fused import FusedAllReduce, topology
 
         h = _ext.host()
         nmax = max(c[0] for c in cases)
         comm = FusedAllReduce(nmax, device=dev, topk_k=26, timeout_s=20.0)
         inv = float(np.float32(1.0) / np.float32(world))
-        for (n, mode, variant) in cases:
+        for (n, mode, variant, drop) in cases:
             k = 26
+            topo = topology(n, drop, 8, 3)
             bits = 8 if mode == "int8" else 4
             pred = _data(n, 5)
             efs = [_data(n, 900 + r, 1e-4) for r in range(world)]
@@ -55,12 +56,12 @@ def _worker(rank, world, port, cases, errfile):
                 gs = [_data(n, 100 * step + r) for r in range(world)]
                 gd = torch.from_numpy(gs[rank].copy()).to(dev)
                 comm.allreduce_(gd, pred_d, ef_d, mode=mode, k=k, variant=variant, seed=11, bucket=3, step=step,
-                                beta=0.9, first=(step == 0))
+                                beta=0.9, first=(step == 0), topo_drop=drop, topo_seed=8)
                 if mode == "topk":
-                    encs = [h.product_topk_encode(gs[r], pred, efs[r], k, True) for r in range(world)]
+                    encs = [h.product_topk_encode(gs[r], pred, efs[r], k, True, topo) for r in range(world)]
                     avg = h.product_topk_reduce([e[0] for e in encs], n, k, pred, inv)
                 else:
-                    encs = [h.product_encode(gs[r], pred, efs[r], bits, True, True, 11, r, 3, step)
+                    encs = [h.product_encode(gs[r], pred, efs[r], bits, True, True, 11, r, 3, step, topo)
                             for r in range(world)]
                     fn = h.product_reduce_twoshot if variant == "twoshot" else h.product_reduce
                     avg = fn([e[0] for e in encs], n, bits, pred, inv)
@@ -92,7 +93,9 @@ def test_fused_allreduce_matches_oracle_across_ranks(world, tmp_path):
     for n in (1000, 70001):
         for mode in ("int4", "int8", "topk"):
             for variant in (("oneshot", "twoshot") if mode != "topk" else ("oneshot",)):
-                cases.append((n, mode, variant))
+                cases.append((n, mode, variant, 0.0))
+                if n > 1000:
+                    cases.append((n, mode, variant, 0.3))
     err = str(tmp_path / "err.txt")
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     mp.start_processes(_worker, args=(world, _port(), cases, err), nprocs=world, join=True, start_method="spawn")
