@@ -4,6 +4,7 @@
 void register_fused(pybind11::module& m);
 void register_symm(pybind11::module& m);
 void register_codecs(pybind11::module& m);
+void register_synth(pybind11::module& m);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sm_100a kernels: fused compressed all-reduce, codecs, symmetric memory";
@@ -11,4 +12,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   register_fused(m);
   register_symm(m);
   register_codecs(m);
+  register_synth(m);
 }

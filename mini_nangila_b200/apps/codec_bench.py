@@ -2,8 +2,9 @@
 
     python -m mini_nangila_b200.apps.codec_bench [--atoms 1000000] [--steps 100] [--epsilon 1e-3]
 
-Synthetic LAMMPS-style trajectory: positions uniform in a 100^3 box
-centred on the origin ([-50, 50)^3), each step adds an N(0, 0.01^2)
+Synthetic LAMMPS-style trajectory from the device generator (Philox +
+Box-Muller, ``csrc/cuda/synth_kernels.cu``): positions uniform in a 100^3
+box centred on the origin ([-50, 50)^3), each step adds an N(0, 0.01^2)
 displacement per coordinate; fp32 x/y/z of every atom form one snapshot
 (3 * atoms values).  The first snapshot has no prediction, so its codes are
 the coordinates themselves: a box reaching 100 would exceed the INT16 code
@@ -11,8 +12,7 @@ range at eps 1e-3 (+-65.5) in the reference's format.  The codec sees unwrapped
 coordinates (LAMMPS xu/yu/zu): with periodic wrap a boundary crossing is a
 ~100-unit residual, beyond INT16 range at eps 1e-3 (32767 * 2 eps = 65.5) in
 the reference's format, which has no escape code; ``--wrapped`` runs the
-wrapped positions and reports how many codes clamp.  ``--fields vel`` adds an
-N(0, 1) velocity stream.
+wrapped positions (the max error then shows the clamping).
 
 For EB, EB+BlockSparse and EB+BlockSparse+RLE it reports device encode and
 decode GB/s (raw fp32 bytes / CUDA-event time of the device pipeline: the
@@ -35,14 +35,13 @@ from ..ops import trajectory
 
 
 def make_positions(atoms, steps, sigma, box, seed, wrapped, device):
-    g = torch.Generator(device=device).manual_seed(seed)
-    x = torch.empty(steps, 3 * atoms, device=device)
-    x[0] = (torch.rand(3 * atoms, device=device, generator=g) - 0.5) * box
-    for t in range(1, steps):
-        x[t] = x[t - 1] + torch.randn(3 * atoms, device=device, generator=g) * sigma
-    if wrapped:
-        x = torch.remainder(x + box / 2, box) - box / 2
-    return x
+    """[steps, 3 * atoms] positions from the device Brownian generator
+    (Philox + Box-Muller), uniform start in [-box/2, box/2)."""
+    from .._ext import cuda
+
+    dev = torch.device(device)
+    return cuda().synth_brownian(3 * atoms, steps, seed=seed, sigma=sigma, box=box, lo=-box / 2, periodic=wrapped,
+                                 device=dev.index if dev.index is not None else torch.cuda.current_device())
 
 
 def _median_ms(fn, warmup=2, iters=5):

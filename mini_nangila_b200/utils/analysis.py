@@ -1,0 +1,193 @@
+"""Log analysis for training, DDP-hook, HPC and twin runs.
+
+Readers for the CSV/text layouts the apps write (the same layouts as the
+reference's: ``train_log.csv`` rows ``ts,step,loss,...``
+(python/nangila_ddp/train_nano.py:147-181), hook metrics rows of
+``key,value`` pairs (comm_hook.py:307-319) or the older ``step,<n>,...``
+prefix (python/nangila_ddp/plot_metrics.py:6-21), HPC bench lines
+``step N ratio R ... max_err E`` (python/snippets/plot_hpc_logs.py:6-17),
+twin metric CSVs with the tick first and the ratio last
+(python/snippets/plot_rotor_net.py:6-19)), numeric summaries of each, and
+optional PNG plots when matplotlib is importable (it is optional: every
+summary works without it).  ``entropy_reduction`` restates the reference's
+entropy illustration (python/snippets/entropy_plot.py:5-33) as numbers: the
+histogram entropy of a signal and of its EMA-prediction residual.
+"""
+from __future__ import annotations
+
+import csv
+import math
+import re
+
+import numpy as np
+
+
+# ------------------------------------------------------------------ readers
+def load_train_log(path: str):
+    ts, step, loss = [], [], []
+    with open(path) as fh:
+        for row in csv.reader(fh):
+            if not row or row[0] == "ts":
+                continue
+            try:
+                ts.append(float(row[0]))
+                step.append(int(row[1]))
+                loss.append(float(row[2]))
+            except (ValueError, IndexError):
+                continue
+    return np.array(ts), np.array(step, dtype=np.int64), np.array(loss)
+
+
+def load_hook_metrics(path: str):
+    """Rows of ``key,value`` pairs -> dict of arrays (ts, ratio, ...); rows
+    with the older ``step,<n>,...,ratio,<r>`` prefix are read too."""
+    cols: dict[str, list[float]] = {}
+    with open(path) as fh:
+        for line in fh:
+            parts = line.strip().split(",")
+            if len(parts) < 2 or parts[0] not in ("ts", "step"):
+                continue
+            kv = {parts[i]: parts[i + 1] for i in range(0, len(parts) - 1, 2)}
+            if parts[0] == "step" and "ratio" not in kv:
+                kv["ratio"] = parts[-1]
+            for key, v in kv.items():
+                try:
+                    cols.setdefault(key, []).append(float(v))
+                except ValueError:
+                    continue
+    return {k: np.array(v) for k, v in cols.items()}
+
+
+_HPC_RE = re.compile(r"step\s+(\d+)\s+ratio\s+([0-9.eE+-]+).+max_err\s+([0-9.eE+-]+)", re.IGNORECASE)
+
+
+def parse_hpc_log(path: str):
+    steps, ratios, errs = [], [], []
+    with open(path) as fh:
+        for line in fh:
+            m = _HPC_RE.search(line)
+            if m:
+                steps.append(int(m.group(1)))
+                ratios.append(float(m.group(2)))
+                errs.append(float(m.group(3)))
+    return np.array(steps, dtype=np.int64), np.array(ratios), np.array(errs)
+
+
+def load_tick_ratio_csv(path: str):
+    ticks, ratios = [], []
+    with open(path) as fh:
+        rd = csv.reader(fh)
+        next(rd, None)
+        for row in rd:
+            try:
+                ticks.append(int(row[0]))
+                ratios.append(float(row[-1]))
+            except (ValueError, IndexError):
+                continue
+    return np.array(ticks, dtype=np.int64), np.array(ratios)
+
+
+# ---------------------------------------------------------------- summaries
+def _stats(x: np.ndarray) -> dict:
+    if x.size == 0:
+        return {"n": 0}
+    return {"n": int(x.size), "first": float(x[0]), "last": float(x[-1]), "min": float(x.min()),
+            "max": float(x.max()), "median": float(np.median(x)), "mean": float(x.mean())}
+
+
+def summarize_training(train_csv: str, metrics_csv: str | None = None) -> dict:
+    ts, step, loss = load_train_log(train_csv)
+    out = {"loss": _stats(loss), "steps": int(step.size)}
+    if ts.size > 1:
+        out["seconds"] = float(ts[-1] - ts[0])
+    if metrics_csv:
+        m = load_hook_metrics(metrics_csv)
+        out["ratio"] = _stats(m.get("ratio", np.array([])))
+        if "res_mean_abs" in m:
+            r = m["res_mean_abs"]
+            out["res_mean_abs"] = _stats(r[np.isfinite(r)])
+    return out
+
+
+def summarize_hpc(path: str) -> dict:
+    steps, ratios, errs = parse_hpc_log(path)
+    return {"steps": int(steps.size), "ratio": _stats(ratios), "max_err": _stats(errs)}
+
+
+def summarize_ticks(path: str) -> dict:
+    t, r = load_tick_ratio_csv(path)
+    return {"ticks": int(t.size), "ratio": _stats(r)}
+
+
+def histogram_entropy(x: np.ndarray, bins: int = 100) -> float:
+    """Shannon entropy (bits) of a ``bins``-bin histogram of x."""
+    h, _ = np.histogram(np.asarray(x, np.float64), bins=bins)
+    p = h[h > 0] / h.sum()
+    return float(-(p * np.log2(p)).sum())
+
+
+def ema_residual(x: np.ndarray, beta: float = 0.9) -> np.ndarray:
+    """r_i = x_i - m_{i-1} with m = beta * m + (1 - beta) * x (m_{-1} = 0)."""
+    x = np.asarray(x, np.float32)
+    pred = np.empty_like(x)
+    m = np.float32(0.0)
+    b, omb = np.float32(beta), np.float32(1.0) - np.float32(beta)
+    for i, v in enumerate(x):
+        pred[i] = m
+        m = b * m + omb * v
+    return x - pred
+
+
+def entropy_reduction(x: np.ndarray | None = None, beta: float = 0.9, bins: int = 100) -> dict:
+    if x is None:
+        t = np.arange(100000)
+        x = (np.sin(t * 0.01) + 0.1 * np.sin(t * 0.05)
+             + 0.01 * np.random.default_rng(0).standard_normal(t.size)).astype(np.float32)
+    r = ema_residual(x, beta)
+    return {"signal_entropy_bits": histogram_entropy(x, bins), "residual_entropy_bits": histogram_entropy(r, bins),
+            "signal_std": float(np.std(x)), "residual_std": float(np.std(r)),
+            "std_reduction": float(np.std(x) / max(np.std(r), 1e-30))}
+
+
+# -------------------------------------------------------------------- plots
+def _plt():
+    try:
+        import matplotlib
+
+        matplotlib.use("Agg")
+        import matplotlib.pyplot as plt
+    except ImportError as e:  # optional dependency
+        raise RuntimeError("plots need matplotlib, which is not installed; the summaries do not") from e
+    return plt
+
+
+def plot_training(train_csv: str, metrics_csv: str, out: str = "train_and_compression.png") -> str:
+    plt = _plt()
+    ts, _, loss = load_train_log(train_csv)
+    m = load_hook_metrics(metrics_csv)
+    d_ts, ratio = m.get("ts", np.array([])), m.get("ratio", np.array([]))
+    t0 = min(ts.min() if ts.size else math.inf, d_ts.min() if d_ts.size else math.inf)
+    fig, ax1 = plt.subplots(figsize=(9, 4))
+    ax1.plot(ts - t0, loss, color="tab:blue")
+    ax1.set_xlabel("time (s)")
+    ax1.set_ylabel("loss")
+    ax2 = ax1.twinx()
+    ax2.plot(d_ts - t0, ratio, ".", alpha=0.3, color="tab:orange")
+    ax2.set_ylabel("compression ratio")
+    fig.tight_layout()
+    fig.savefig(out)
+    plt.close(fig)
+    return out
+
+
+def plot_series(x, y, xlabel: str, ylabel: str, out: str) -> str:
+    plt = _plt()
+    fig = plt.figure(figsize=(8, 4))
+    plt.plot(x, y, "-o", alpha=0.7)
+    plt.xlabel(xlabel)
+    plt.ylabel(ylabel)
+    plt.grid(True, alpha=0.3)
+    fig.tight_layout()
+    fig.savefig(out)
+    plt.close(fig)
+    return out

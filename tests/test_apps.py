@@ -110,3 +110,46 @@ def test_train_nano_two_cpu_ranks(tmp_path):
     assert rows[0] == "ts,step,loss,lr,tokens_per_sec,step_ms" and len(rows) == 4
     m = (tmp_path / "m.csv").read_text().splitlines()
     assert m and m[0].startswith("ts,") and ",ratio," in m[0]
+
+
+def test_determinism_hash_app():
+    from mini_nangila_b200.apps import determinism_hash
+
+    assert determinism_hash.main([]) == "c18cd836f0cb712247e0ace683d710b8550f3e3f40a6a2998252df59498aab56"
+
+
+def test_analyze_app(tmp_path):
+    from mini_nangila_b200.apps import analyze
+
+    tr = tmp_path / "train_log.csv"
+    tr.write_text("ts,step,loss,tokens_per_s\n100.0,0,4.2,1000\n101.0,1,3.9,1100\n102.0,2,3.5,1200\n")
+    mt = tmp_path / "ddp_metrics.csv"
+    mt.write_text("ts,100.5,hook_idx,1,bucket_elems,10,raw_bytes,40,comp_bytes,5,ratio,8.0,res_mean_abs,1e-3\n"
+                  "ts,101.5,hook_idx,2,bucket_elems,10,raw_bytes,40,comp_bytes,4,ratio,10.0,res_mean_abs,2e-3\n"
+                  "step,3,bucket_elems,10,raw_bytes,40,comp_bytes,4,ratio,10.0\n")
+    out = analyze.main(["train", str(tr), str(mt)])
+    assert out["loss"]["first"] == 4.2 and out["loss"]["last"] == 3.5 and out["seconds"] == 2.0
+    assert out["ratio"]["n"] == 3 and out["ratio"]["max"] == 10.0
+    hp = tmp_path / "hpc.log"
+    hp.write_text("step 0 ratio 2.00 raw 400 max_err 0.0009\nnoise\nstep 1 ratio 2.5 raw 400 max_err 0.001\n")
+    out = analyze.main(["hpc", str(hp)])
+    assert out["steps"] == 2 and out["ratio"]["median"] == 2.25
+    tw = tmp_path / "client.csv"
+    tw.write_text("tick,raw,comp,ratio\n0,24,16,1.5\n1,24,12,2.0\n")
+    out = analyze.main(["twin", str(tw)])
+    assert out["client"]["ratio"]["mean"] == 1.75
+    out = analyze.main(["entropy"])
+    assert out["std_reduction"] > 2.0
+
+
+def test_analyze_reads_checkpoint(tmp_path):
+    import numpy as np
+
+    from mini_nangila_b200.apps import analyze
+    from mini_nangila_b200.checkpoint import hdf5
+
+    x = np.linspace(-1, 1, 5000, dtype=np.float32)
+    p = str(tmp_path / "ck.h5")
+    hdf5.write_chunked_dataset(p, "w", x, 1024, 1e-3, "eb")
+    out = analyze.main(["checkpoint", p, "w"])
+    assert out["n"] == 5000 and abs(out["first"][0] + 1.0) <= 1e-3
