@@ -198,15 +198,19 @@ __device__ __forceinline__ TopkSel topk_select(const float (&c)[8], int valid, i
   uint32_t m[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) m[j] = __float_as_uint(fabsf(c[j]));
-  // Largest T with |{j : m_j >= T}| >= keff, one bit at a time (MSB first).
+  // Largest T with |{j : m_j >= T}| >= keff, one bit at a time (MSB first;
+  // bit 31 of |x| is clear).  Once exactly keff elements are >= T the kept
+  // set is {m >= T} whatever the lower bits, so the search stops there (the
+  // tie handling below then keeps all of them).
   uint32_t T = 0;
-  for (int bit = 31; bit >= 0; --bit) {
+  for (int bit = 30; bit >= 0; --bit) {
     const uint32_t cand = T | (1u << bit);
     int cnt = 0;
 #pragma unroll
     for (int j = 0; j < 8; ++j) cnt += (m[j] >= cand);
     cnt = (int)__reduce_add_sync(kFull, (unsigned)cnt);
     if (cnt >= keff) T = cand;
+    if (cnt == keff) break;
   }
   int gt = 0, eq = 0;
 #pragma unroll
