@@ -131,9 +131,15 @@ std::vector<torch::Tensor> decode_streams(torch::Tensor data, torch::Tensor stre
   auto out_len = torch::zeros({std::max<int64_t>(ns, 1)}, opt.dtype(torch::kInt64));
   auto table = torch::empty({std::max<int64_t>(ns * (2 * table_cap + 2), 1)}, opt.dtype(torch::kInt64));
   auto st = status_tensor(data);
+  torch::Tensor scratch;
+  uint64_t* sp = nullptr;
+  if (kind == 0 || kind == 1) {
+    scratch = torch::empty({bs_decode_scratch_words(data.numel(), ns)}, opt.dtype(torch::kInt64));
+    sp = reinterpret_cast<uint64_t*>(scratch.data_ptr<int64_t>());
+  }
   ck(stream_decode((int)kind, data.data_ptr<uint8_t>(), stream_off.data_ptr<int64_t>(), scales.data_ptr<float>(),
                    (int)ns, out.data_ptr<int32_t>(), out_cap, out_len.data_ptr<int64_t>(), table.data_ptr<int64_t>(),
-                   table_cap, st.data_ptr<int>(), cur()),
+                   table_cap, st.data_ptr<int>(), sp, data.numel(), cur()),
      "stream_decode");
   check_status(st, "stream_decode");
   return {out, out_len};

@@ -987,22 +987,266 @@ __global__ void k_expand(int kind, const uint8_t* __restrict__ data, const int64
 }
 
 // Top-k pads the decoded stream with zeros up to n (the walk reports n).
+// ------------------------------------- parallel BlockSparse-family decode
+// A BlockSparse (or top-k compat) stream is a chain of blocks [u32 mask]
+// [VB bytes per set bit]: each block's position depends on every earlier
+// mask, so a single thread walking it is latency bound.  Blocks are at most
+// kMaxBlk = 4 + 32 VB bytes, so the chain enters a window [start, start + W)
+// of the stream at one of kCand candidate offsets (even offsets for VB = 2,
+// where every position is even; every offset for VB = 1).
+//   A  one thread per (window, candidate) walks from the candidate to the
+//      window's end: exit offset into the next window and block count.
+//   B  one CTA per stream stages the candidate tables in shared memory and
+//      chains them from the stream start: true entry and first block index of
+//      every window.
+//   C  one thread per window re-walks from its true entry with the exact
+//      reference rules (last-block mask, truncated values, block limit) and
+//      writes the block descriptors; the expansion kernel then writes values.
+constexpr int64_t kBsWin = 16384;
+constexpr uint32_t kExitEnd = 255u;  // the stream ends inside the window
+
+template <int VB>
+struct BsGeom {
+  static constexpr int kMaxBlk = 4 + 32 * VB;
+  static constexpr int kStep = VB == 2 ? 2 : 1;
+  static constexpr int kCand = kMaxBlk / kStep;  // 34 or 36
+};
+
+__device__ __forceinline__ uint32_t rd_u32_bytes(const uint8_t* p) {
+  return (uint32_t)__ldg(p) | ((uint32_t)__ldg(p + 1) << 8) | ((uint32_t)__ldg(p + 2) << 16) |
+         ((uint32_t)__ldg(p + 3) << 24);
+}
+
+// Window ranges: win_off[s] = first window of stream s (prefix over streams
+// of ceil((len_s - 4) / W)), win_off[ns] = total.
+__global__ void k_bs_win_offsets(const int64_t* __restrict__ soff, int ns, int64_t max_windows,
+                                 int64_t* __restrict__ win_off, int* status) {
+  if (blockIdx.x != 0 || threadIdx.x != 0) return;
+  int64_t acc = 0;
+  for (int i = 0; i < ns; ++i) {
+    win_off[i] = acc;
+    const int64_t len = soff[i + 1] - soff[i];
+    acc += len > 4 ? (len - 4 + kBsWin - 1) / kBsWin : 0;
+  }
+  win_off[ns] = acc;
+  // streams that overlap or lie outside `data` can need more windows than
+  // the scratch holds: report instead of decoding part of them
+  if (acc > max_windows) dev::set_status(status, dev::kBounds, -1, (int)min64(acc, 0x7fffffff));
+}
+
+__device__ __forceinline__ int stream_of_window(const int64_t* win_off, int ns, int64_t w) {
+  int lo = 0, hi = ns - 1;  // last s with win_off[s] <= w
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (win_off[mid] <= w) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
+}
+
+template <int VB>
+__global__ void __launch_bounds__(kThreads) k_bs_spec(const uint8_t* __restrict__ data, const int64_t* __restrict__ soff,
+                                                      int ns, const int64_t* __restrict__ win_off,
+                                                      int64_t max_windows, uint32_t* __restrict__ spec) {
+  using G = BsGeom<VB>;
+  const int64_t total = min64(win_off[ns], max_windows) * G::kCand;
+  for (int64_t t = gtid(); t < total; t += gstride()) {
+    const int64_t gw = t / G::kCand;
+    const int cand = (int)(t - gw * G::kCand);
+    const int s = stream_of_window(win_off, ns, gw);
+    const int64_t w = gw - win_off[s];
+    const uint8_t* b = data + soff[s];
+    const int64_t len = soff[s + 1] - soff[s];
+    const int64_t start = 4 + w * kBsWin, end = start + kBsWin;
+    int64_t q = start + (int64_t)cand * G::kStep;
+    uint32_t cnt = 0, exit = kExitEnd;
+    while (true) {
+      if (q >= end) {
+        exit = (uint32_t)(q - end);
+        break;
+      }
+      if (q + 4 > len) break;  // the stream ends here
+      const int c = __popc(rd_u32_bytes(b + q));
+      q = advance_values(q + 4, len, c, VB);
+      ++cnt;
+    }
+    spec[t] = exit | (cnt << 8);
+  }
+}
+
+// One CTA per stream: chain the windows.  entry[w] = true first block
+// position in window w (-1: inactive), base[w] = its block index.
+template <int VB>
+__global__ void __launch_bounds__(kThreads) k_bs_chain(const uint8_t* __restrict__ data, const int64_t* __restrict__ soff,
+                                                       int ns, const int64_t* __restrict__ win_off,
+                                                       int64_t max_windows, const uint32_t* __restrict__ spec,
+                                                       int64_t* __restrict__ entry, int64_t* __restrict__ base) {
+  using G = BsGeom<VB>;
+  constexpr int kChunk = 96;  // windows staged per round
+  __shared__ uint32_t tab[kChunk * G::kCand];
+  __shared__ int64_t s_e, s_base;
+  __shared__ int s_stop;
+  const int s = blockIdx.x;
+  if (s >= ns) return;
+  const int64_t w0 = win_off[s];
+  const int64_t nw = min64(win_off[s + 1], max_windows) - min64(w0, max_windows);
+  const int64_t len = soff[s + 1] - soff[s];
+  if (threadIdx.x == 0) {
+    const uint8_t* b = data + soff[s];
+    int64_t nblk = 0;
+    if (len >= 4) nblk = ((int64_t)rd_u32_bytes(b) + 31) / 32;
+    s_e = 4;
+    s_base = 0;
+    s_stop = (len < 4 || nblk == 0) ? 1 : 0;
+  }
+  __syncthreads();
+  for (int64_t c0 = 0; c0 < nw; c0 += kChunk) {
+    const int nc = (int)min64(kChunk, nw - c0);
+    if (!s_stop)
+      for (int i = threadIdx.x; i < nc * G::kCand; i += blockDim.x) tab[i] = spec[(w0 + c0) * G::kCand + i];
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int64_t e = s_e, bs = s_base;
+      bool stop = s_stop != 0;
+      for (int i = 0; i < nc; ++i) {
+        const int64_t w = c0 + i;
+        if (stop) {
+          entry[w0 + w] = -1;
+          continue;
+        }
+        const int64_t start = 4 + w * kBsWin;
+        entry[w0 + w] = e;
+        base[w0 + w] = bs;
+        const uint32_t f = tab[i * G::kCand + (int)((e - start) / G::kStep)];
+        const uint32_t ex = f & 0xffu;
+        if (ex == kExitEnd) {
+          stop = true;  // the chain ends inside this window
+          continue;
+        }
+        bs += f >> 8;
+        e = start + kBsWin + ex;
+      }
+      s_e = e;
+      s_base = bs;
+      s_stop = stop ? 1 : 0;
+    }
+    __syncthreads();
+  }
+}
+
+// One thread per window: exact walk from the true entry, descriptors by
+// block index; row[0] of the stream = decoded block count (atomicMax of the
+// block index each window reached, capped at the header's block count).
+template <int VB>
+__global__ void __launch_bounds__(kThreads) k_bs_emit(const uint8_t* __restrict__ data, const int64_t* __restrict__ soff,
+                                                      int ns, const int64_t* __restrict__ win_off,
+                                                      int64_t max_windows, const int64_t* __restrict__ entry,
+                                                      const int64_t* __restrict__ base, int64_t* __restrict__ table,
+                                                      int64_t table_cap, int* status) {
+  const int64_t total = min64(win_off[ns], max_windows);
+  for (int64_t gw = gtid(); gw < total; gw += gstride()) {
+    int64_t q = entry[gw];
+    if (q < 0) continue;
+    const int s = stream_of_window(win_off, ns, gw);
+    const int64_t w = gw - win_off[s];
+    const uint8_t* b = data + soff[s];
+    const int64_t len = soff[s + 1] - soff[s];
+    const int64_t n = (int64_t)rd_u32_bytes(b);
+    const int64_t nblk = (n + 31) / 32;
+    const int64_t end = 4 + (w + 1) * kBsWin;
+    int64_t* row = table + (int64_t)s * (2 * table_cap + 2);
+    longlong2* tab = reinterpret_cast<longlong2*>(row + 2);
+    int64_t blk = base[gw];
+    while (q < end && blk < nblk && q + 4 <= len) {
+      if (blk >= table_cap) {
+        dev::set_status(status, dev::kBounds, s, (int)blk);
+        break;
+      }
+      const uint32_t m = rd_u32_bytes(b + q);
+      const int64_t bl = blk == nblk - 1 ? n - blk * 32 : 32;
+      tab[blk] = make_longlong2((blk * 32) | (bl << 48), q + 1);
+      const int c = __popc(bl >= 32 ? m : (m & ((1u << bl) - 1u)));
+      q = advance_values(q + 4, len, c, VB);
+      ++blk;
+    }
+    // A window entered after the last block carries a speculative base >=
+    // nblk: the chain decoded all nblk blocks.
+    atomicMax(reinterpret_cast<unsigned long long*>(row), (unsigned long long)min64(blk, nblk));
+  }
+}
+
+// Decoded length per stream: BlockSparse min(blocks * 32, n), top-k n.
+__global__ void k_bs_len(const uint8_t* __restrict__ data, const int64_t* __restrict__ soff, int ns, int kind,
+                         const int64_t* __restrict__ table, int64_t table_cap, int64_t out_cap,
+                         int64_t* __restrict__ out_len, int* status) {
+  for (int64_t s = gtid(); s < ns; s += gstride()) {
+    const int64_t len = soff[s + 1] - soff[s];
+    int64_t ol = 0;
+    if (len >= 4) {
+      const int64_t n = (int64_t)rd_u32_bytes(data + soff[s]);
+      const int64_t blocks = table[s * (2 * table_cap + 2)];
+      ol = kind == 1 ? n : min64(blocks * 32, n);
+    }
+    out_len[s] = ol;
+    if (ol > out_cap) dev::set_status(status, dev::kBounds, (int)s, -1);
+  }
+}
+
+int64_t bs_decode_scratch_words(int64_t total_bytes, int64_t nstreams) {
+  const int64_t wins = total_bytes / kBsWin + 2 * nstreams + 1;
+  // win_off (ns + 1), entry + base (2 per window), candidate tables (u32)
+  return (nstreams + 1) + 2 * wins + (wins * 36 + 1) / 2;
+}
+
+template <int VB>
+cudaError_t launch_bs_parallel(int kind, const uint8_t* data, const int64_t* soff, int ns, int64_t out_cap,
+                               int64_t* out_len, int64_t* table, int64_t table_cap, int* status, uint64_t* scratch,
+                               int64_t total_bytes, cudaStream_t s) {
+  using G = BsGeom<VB>;
+  const int64_t max_w = total_bytes / kBsWin + 2 * (int64_t)ns + 1;
+  int64_t* win_off = reinterpret_cast<int64_t*>(scratch);
+  int64_t* entry = win_off + ns + 1;
+  int64_t* base = entry + max_w;
+  uint32_t* spec = reinterpret_cast<uint32_t*>(base + max_w);
+  // row[0] of every stream starts at 0 (atomicMax of block counts)
+  cudaError_t e = cudaMemset2DAsync(table, (size_t)(2 * table_cap + 2) * sizeof(int64_t), 0, sizeof(int64_t),
+                                    (size_t)ns, s);
+  if (e != cudaSuccess) return e;
+  k_bs_win_offsets<<<1, 32, 0, s>>>(soff, ns, max_w, win_off, status);
+  const int64_t cand = max_w * G::kCand;
+  int64_t g = (cand + kThreads - 1) / kThreads;
+  if (g > 148 * 16) g = 148 * 16;
+  k_bs_spec<VB><<<(unsigned)(g > 0 ? g : 1), kThreads, 0, s>>>(data, soff, ns, win_off, max_w, spec);
+  k_bs_chain<VB><<<ns, kThreads, 0, s>>>(data, soff, ns, win_off, max_w, spec, entry, base);
+  int64_t g2 = (max_w + kThreads - 1) / kThreads;
+  if (g2 > 148 * 8) g2 = 148 * 8;
+  k_bs_emit<VB><<<(unsigned)(g2 > 0 ? g2 : 1), kThreads, 0, s>>>(data, soff, ns, win_off, max_w, entry, base, table,
+                                                                 table_cap, status);
+  k_bs_len<<<(unsigned)((ns + kThreads - 1) / kThreads), kThreads, 0, s>>>(data, soff, ns, kind, table, table_cap,
+                                                                          out_cap, out_len, status);
+  return cudaGetLastError();
+}
+
 __global__ void k_zero_fill(int32_t* out, int64_t out_cap, const int64_t* out_len, int nstreams) {
   for (int64_t i = gtid(); i < (int64_t)nstreams * out_cap; i += gstride()) out[i] = 0;
 }
 
 cudaError_t stream_decode(int kind, const uint8_t* data, const int64_t* stream_off, const float* scales, int nstreams,
                           int32_t* out, int64_t out_cap, int64_t* out_len, int64_t* table, int64_t table_cap,
-                          int* status, cudaStream_t s) {
+                          int* status, uint64_t* scratch, int64_t total_bytes, cudaStream_t s) {
   if (nstreams <= 0) return cudaSuccess;
   if (kind == 1) {
     k_zero_fill<<<grid_for((int64_t)nstreams * out_cap), kThreads, 0, s>>>(out, out_cap, out_len, nstreams);
   }
-  if (kind == 0) k_walk<0><<<nstreams, kThreads, 0, s>>>(data, stream_off, nstreams, out_cap, out_len, table, table_cap, status);
+  cudaError_t e = cudaSuccess;
+  if (kind == 0 && scratch) e = launch_bs_parallel<2>(kind, data, stream_off, nstreams, out_cap, out_len, table, table_cap, status, scratch, total_bytes, s);
+  else if (kind == 1 && scratch) e = launch_bs_parallel<1>(kind, data, stream_off, nstreams, out_cap, out_len, table, table_cap, status, scratch, total_bytes, s);
+  else if (kind == 0) k_walk<0><<<nstreams, kThreads, 0, s>>>(data, stream_off, nstreams, out_cap, out_len, table, table_cap, status);
   else if (kind == 1) k_walk<1><<<nstreams, kThreads, 0, s>>>(data, stream_off, nstreams, out_cap, out_len, table, table_cap, status);
   else if (kind == 2) k_walk<2><<<nstreams, kThreads, 0, s>>>(data, stream_off, nstreams, out_cap, out_len, table, table_cap, status);
   else k_walk<3><<<nstreams, kThreads, 0, s>>>(data, stream_off, nstreams, out_cap, out_len, table, table_cap, status);
-  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   const int64_t warps = (int64_t)nstreams * table_cap;
   int64_t g = (warps * 32 + kThreads - 1) / kThreads;

@@ -79,16 +79,20 @@ cudaError_t bsrle_encode_batch(const int16_t* q, int64_t n, int ns, uint8_t* out
 cudaError_t rle_encode_batch(const int16_t* q, int64_t n, int ns, uint8_t* out, int64_t out_stride,
                              uint64_t* scratch, uint64_t* totals, int* status, cudaStream_t s);
 
-// ---- Stream decoders: header walk (one thread per stream) + parallel expansion ----
+// ---- Stream decoders: header walk + parallel expansion ----
 // kind: 0 = BlockSparse (i16), 1 = top-k compat (i8), 2 = BlockSparse+RLE, 3 = RLE.
 // Stream i is data[stream_off[i] .. stream_off[i+1]) with scale scales[i];
 // it decodes into out[i * out_cap ...] (Q8.23) and out_len[i] receives the
 // decoded length the reference's decoder produces (status kBounds when that
 // exceeds out_cap, or a stream needs more than table_cap descriptors).
 // table: nstreams * (2 * table_cap + 2) int64 words (count + descriptors).
+// scratch (kinds 0 and 1): bs_decode_scratch_words(total_bytes, nstreams)
+// u64 words, total_bytes = data bytes covered by all streams; with scratch
+// those kinds decode window-parallel, without it by the one-thread walk.
+int64_t bs_decode_scratch_words(int64_t total_bytes, int64_t nstreams);
 cudaError_t stream_decode(int kind, const uint8_t* data, const int64_t* stream_off, const float* scales, int nstreams,
                           int32_t* out, int64_t out_cap, int64_t* out_len, int64_t* table, int64_t table_cap,
-                          int* status, cudaStream_t s);
+                          int* status, uint64_t* scratch, int64_t total_bytes, cudaStream_t s);
 
 // ---- Reference stochastic INT4/INT8 codec (K7) ----
 cudaError_t absmax_f32_of_fixed(const int32_t* r, int64_t n, uint32_t* max_bits, cudaStream_t s);

@@ -69,6 +69,37 @@ def test_truncated_streams_decode_like_host(cls):
         assert np.array_equal(q.dequantize(b, hs, device="cuda").numpy(), q.dequantize(b, hs).numpy()), cut
 
 
+@pytest.mark.parametrize("sparsity", [0.0, 0.5, 0.99])
+def test_truncated_multiwindow_blocksparse(sparsity):
+    # Streams longer than the 16 KB decode windows, cut at and around window
+    # boundaries and inside blocks: the window-parallel decoder must follow
+    # the reference's tolerant decode exactly.
+    q = BlockSparseQuantizer(1e-3)
+    r = _resid(120001, 9, sparsity)
+    hb, hs = q.quantize(r)
+    W = 16384
+    cuts = {len(hb), len(hb) - 1, len(hb) - 3, len(hb) // 3}
+    for k in (1, 2, 3):
+        for d in (-5, -4, -2, -1, 0, 1, 2, 3, 4, 5, 37):
+            c = 4 + k * W + d
+            if 0 < c <= len(hb):
+                cuts.add(c)
+    for cut in sorted(cuts):
+        b = hb[:cut]
+        assert np.array_equal(q.dequantize(b, hs, device="cuda").numpy(), q.dequantize(b, hs).numpy()), cut
+
+
+def test_topk_compat_truncated_multiwindow():
+    g = np.random.default_rng(3)
+    x = g.standard_normal(400000).astype(np.float32)
+    r = FixedPointBuffer.from_f32(x)
+    q = UnifiedQuantizer(QuantizationMode.TopK(0.5))
+    hb, hs = q.quantize(r)
+    for cut in (len(hb), len(hb) - 1, 4 + 16384 + 1, 4 + 2 * 16384 - 2, len(hb) // 2 + 1):
+        b = hb[:cut]
+        assert np.array_equal(q.dequantize(b, hs, device="cuda").numpy(), q.dequantize(b, hs).numpy()), cut
+
+
 def test_long_zero_runs():
     x = np.zeros(200000, np.float32)
     x[::50000] = 1.0
