@@ -51,6 +51,8 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
     ap.add_argument("--max-ctas", type=int, default=0)
+    ap.add_argument("--momentum", choices=["auto", "on", "off"], default="auto",
+                    help="EMA predictor in the hook (auto: on for int4/int8, off for top-k, which uses error feedback)")
     return ap.parse_args()
 
 
@@ -160,13 +162,18 @@ def main():
             model = model.to(torch.bfloat16)
         hk = None
         if args.hook in ("fused", "compat"):
-            hk = dict(beta=0.9, bits=8 if args.mode == "int8" else 4, stochastic=True, use_momentum=True,
+            momentum = args.momentum == "on" or (args.momentum == "auto" and args.mode != "topk")
+            hk = dict(beta=0.9, bits=8 if args.mode == "int8" else 4, stochastic=True, use_momentum=momentum,
                       topk_percent=args.topk if args.mode == "topk" else 0.0, seed=12345,
                       error_feedback=True, variant=args.variant, max_ctas=args.max_ctas)
         trainer = DDPTrainer(model, lr=6e-4, hook=args.hook, hook_kwargs=hk, bucket_cap_mb=25.0,
                              autocast_dtype=torch.bfloat16 if args.model == "gpt2" else None, device=device)
         step_fn = trainer.step
         hook_name = {"fused": f"fused-{args.mode}", "nccl": "nccl-fp32-allreduce", "compat": f"compat-{args.mode}"}[args.hook]
+        if args.hook != "nccl":
+            hook_name += ("-ema" if momentum else "") + "-ef"
+            if args.mode == "topk":
+                hook_name += f"-keep{args.topk:g}"
 
     batches = make_batches(vocab, mb, seq, 4, 1000 + rank, device)
     with quiet:

@@ -91,6 +91,9 @@ int fused_grid(int nchunks, int mode, int dtype, int variant, int cap, int devic
 cudaError_t launch_fused(const FusedParams& P, int mode, int dtype, int variant, int grid, cudaStream_t stream);
 cudaError_t launch_encode(const void* g, const float* pred, const float* ef_in, float* ef_out, int64_t n, int k,
                           const QParams& qp, uint8_t* out, int mode, int dtype, int grid, cudaStream_t stream);
+// Check of the shared-memory prefetch pipeline: dst = src through it.
+cudaError_t launch_pipe_copy(const float* src, float* dst, int64_t n, int grid, int vec, int* status,
+                             cudaStream_t stream);
 cudaError_t launch_reduce(const ReduceSrcs& srcs, int world, void* out, float* pred, int64_t n, int k,
                           const FParams& fp, int mode, int dtype, int grid, cudaStream_t stream);
 

@@ -246,6 +246,16 @@ void register_fused(pybind11::module& m) {
         pybind11::arg("k"), pybind11::arg("pred"), pybind11::arg("beta"), pybind11::arg("first"),
         pybind11::arg("inv_world"), pybind11::arg("out_dtype"), pybind11::arg("topo") = std::vector<int64_t>{});
   m.def("payload_bytes", &payload_bytes);
+  m.def("pipe_copy", [](torch::Tensor src, int64_t grid, torch::Tensor status, bool vec) {
+    check_dev(src, "src");
+    TORCH_CHECK(src.scalar_type() == torch::kFloat32, "src must be float32");
+    auto dst = torch::empty_like(src);
+    const c10::cuda::CUDAGuard guard(src.device());
+    check_launch(launch_pipe_copy(src.data_ptr<float>(), dst.data_ptr<float>(), src.numel(), (int)grid, vec ? 1 : 0,
+                                  status.data_ptr<int>(), at::cuda::getCurrentCUDAStream()),
+                 "pipe_copy");
+    return dst;
+  });
   m.def("fused_grid", [](int64_t n, int64_t mode, bool bf16, int64_t variant, int64_t cap, int64_t device) {
     const int nchunks = (int)nchunks_of(n);
     return fused_grid(nchunks, (int)mode, bf16 ? kBF16 : kF32, (int)variant, (int)cap, (int)device);

@@ -44,16 +44,28 @@ __device__ __forceinline__ bool passenger(const Topo& t, int c, int nchunks) {
 
 
 // ------------------------------------------------------------ warp encoders
+constexpr int kChunkElems = kChunkBlocks * kBlock;  // 2048
+
+// Where a chunk's inputs are read: global memory (roff = 0) or a shared-
+// memory copy of chunk c (pointers to the copy, roff = c * kChunkElems).
+template <typename T>
+struct ChunkSrc {
+  const T* g;
+  const float* pred;
+  const float* ef;
+  int64_t roff;
+};
+
 // Residual c = g - pred + e of the lane's 8 consecutive elements of a block.
 template <typename T>
-__device__ __forceinline__ int load_residual(const T* g, const float* pred, const float* ef, int64_t n, int blk,
-                                             int lane, const QParams& qp, float (&c)[8]) {
+__device__ __forceinline__ int load_residual(const ChunkSrc<T>& s, int64_t n, int blk, int lane, const QParams& qp,
+                                             float (&c)[8]) {
   const int64_t e0 = (int64_t)blk * kBlock + lane * 8;
   const int valid = (int)min64(8, max64(0, n - e0));
   float gv[8], pv[8], ev[8];
-  load8<T>(g, e0, valid, true, gv);
-  if (qp.use_pred) load8<float>(pred, e0, valid, true, pv);
-  if (qp.use_ef) load8<float>(ef, e0, valid, true, ev);
+  load8<T>(s.g, e0 - s.roff, valid, true, gv);
+  if (qp.use_pred) load8<float>(s.pred, e0 - s.roff, valid, true, pv);
+  if (qp.use_ef) load8<float>(s.ef, e0 - s.roff, valid, true, ev);
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     const float p = qp.use_pred ? pv[j] : 0.0f;
@@ -63,15 +75,78 @@ __device__ __forceinline__ int load_residual(const T* g, const float* pred, cons
   return valid;
 }
 
-// Passenger block: the whole residual goes to the error feedback.
+// Passenger block: the whole residual goes to the error feedback (ef_w).
 template <typename T>
-__device__ __forceinline__ void passenger_block(const T* g, const float* pred, float* ef, int64_t n, int blk, int lane,
+__device__ __forceinline__ void passenger_block(const ChunkSrc<T>& s, float* ef_w, int64_t n, int blk, int lane,
                                                 const QParams& qp) {
   if (!qp.use_ef) return;
   float cv[8];
-  const int valid = load_residual<T>(g, pred, ef, n, blk, lane, qp, cv);
-  store8<float>(ef, (int64_t)blk * kBlock + lane * 8, valid, true, cv);
+  const int valid = load_residual<T>(s, n, blk, lane, qp, cv);
+  store8<float>(ef_w, (int64_t)blk * kBlock + lane * 8, valid, true, cv);
 }
+
+// Double-buffered prefetch of whole chunks (g, pred, ef slices) into dynamic
+// shared memory with bulk copies completing on an mbarrier per buffer, so
+// the loads of the next owned chunk overlap the current chunk's encode.  A
+// partial last chunk is read from global memory instead.  Thread 0 issues;
+// every thread waits (bounded) on the buffer's mbarrier phase.
+template <typename T>
+struct ChunkPipe {
+  static constexpr int kG = kChunkElems * (int)sizeof(T);
+  static constexpr int kBuf = kG + 2 * kChunkElems * 4;
+  static constexpr int kBytes = 2 * kBuf;  // dynamic shared memory
+  uint64_t* mbar;                          // 2 mbarriers (static shared)
+  uint8_t* buf;
+  uint32_t phase = 0;    // bit b: parity of buffer b's next completion
+  uint32_t pending = 0;  // bit b: a copy into buffer b is in flight
+
+  __device__ static bool full(int64_t n, int c) { return (int64_t)(c + 1) * kChunkElems <= n; }
+  // All threads, once, before the first issue.
+  __device__ void init() {
+    if (threadIdx.x == 0) {
+      mbar_init(&mbar[0], 1);
+      mbar_init(&mbar[1], 1);
+      fence_mbar_init();
+    }
+    __syncthreads();
+  }
+  // All threads (uniform); thread 0 issues the copies of chunk c into buffer b.
+  __device__ void issue(const T* g, const float* pred, const float* ef, int c, int b) {
+    if (threadIdx.x == 0) {
+      uint8_t* d = buf + b * kBuf;
+      const int64_t e0 = (int64_t)c * kChunkElems;
+      const uint32_t bytes = kG + (pred ? kChunkElems * 4 : 0) + (ef ? kChunkElems * 4 : 0);
+      fence_proxy_async_smem();  // earlier generic reads of this buffer before the async writes
+      mbar_expect_tx(&mbar[b], bytes);
+      bulk_g2s(d, g + e0, kG, &mbar[b]);
+      if (pred) bulk_g2s(d + kG, pred + e0, kChunkElems * 4, &mbar[b]);
+      if (ef) bulk_g2s(d + kG + kChunkElems * 4, ef + e0, kChunkElems * 4, &mbar[b]);
+    }
+    pending |= 1u << b;
+  }
+  // All threads: wait for buffer b; false (uniform) after limit_ns.
+  __device__ bool wait(int b, uint64_t limit_ns) {
+    const bool ok = mbar_wait(&mbar[b], (phase >> b) & 1u, limit_ns);
+    phase ^= 1u << b;
+    pending &= ~(1u << b);
+    return __syncthreads_or(!ok) == 0;
+  }
+  // Pointers into buffer b holding chunk c.  Callers pass the result
+  // straight to the chunk routine, one call per branch: a source variable
+  // merged from this and the global source kept the global base pointer
+  // with the buffer's offset (measured on sm_100a), so none is formed.
+  __device__ ChunkSrc<T> buffer_source(int b, int c) const {
+    const uint8_t* d = buf + b * kBuf;
+    return ChunkSrc<T>{reinterpret_cast<const T*>(d), reinterpret_cast<const float*>(d + kG),
+                       reinterpret_cast<const float*>(d + kG + kChunkElems * 4), (int64_t)c * kChunkElems};
+  }
+  // Before leaving early: let copies still in flight land (bounded).
+  __device__ void drain(uint64_t limit_ns) {
+    for (int b = 0; b < 2; ++b)
+      if ((pending >> b) & 1u) mbar_wait(&mbar[b], (phase >> b) & 1u, limit_ns);
+    pending = 0;
+  }
+};
 
 __device__ __forceinline__ float block_absmax(const float (&c)[8]) {
   float m = 0.0f;
@@ -275,15 +350,14 @@ __device__ __forceinline__ void topk_accum_global(const uint8_t* rec_g, uint8_t*
 // Encode chunk c into the shared-memory record `rec` (all threads; ends
 // with __syncthreads).  Blocks past the end are written as empty blocks.
 template <int MODE, typename T>
-__device__ __forceinline__ void encode_chunk(const T* g, const float* pred, const float* ef, int64_t n, int nblk,
-                                             int nchunks, int k, int rec_bytes, const QParams& qp, int c,
-                                             uint8_t* rec) {
+__device__ __forceinline__ void encode_chunk(const ChunkSrc<T>& src, float* ef_w, int64_t n, int nblk, int nchunks,
+                                             int k, int rec_bytes, const QParams& qp, int c, uint8_t* rec) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int blk = c * kChunkBlocks + warp;
   if (passenger(qp.topo, c, nchunks)) {
     // No record is sent for a passenger; the zero record (which decodes to
     // zero) is staged for the single-GPU encode path.
-    if (blk < nblk) passenger_block<T>(g, pred, const_cast<float*>(ef), n, blk, lane, qp);
+    if (blk < nblk) passenger_block<T>(src, ef_w, n, blk, lane, qp);
     const int bytes = chunk_record_bytes(MODE, k);
     for (int w = threadIdx.x; w < bytes / 4; w += blockDim.x) reinterpret_cast<uint32_t*>(rec)[w] = 0u;
     __syncthreads();
@@ -293,8 +367,8 @@ __device__ __forceinline__ void encode_chunk(const T* g, const float* pred, cons
     uint8_t* r = rec + warp * rec_bytes;
     if (blk < nblk) {
       float cv[8];
-      const int valid = load_residual<T>(g, pred, ef, n, blk, lane, qp, cv);
-      topk_select(cv, valid, blk, lane, k, n, qp, const_cast<float*>(ef), r, rec_bytes);
+      const int valid = load_residual<T>(src, n, blk, lane, qp, cv);
+      topk_select(cv, valid, blk, lane, k, n, qp, ef_w, r, rec_bytes);
     } else {
       for (int w = lane; w < rec_bytes / 4; w += 32) reinterpret_cast<uint32_t*>(r)[w] = 0u;
     }
@@ -305,8 +379,8 @@ __device__ __forceinline__ void encode_chunk(const T* g, const float* pred, cons
     if (blk < nblk) {
       float cv[8];
       int32_t q[8];
-      const int valid = load_residual<T>(g, pred, ef, n, blk, lane, qp, cv);
-      s = encode_dense<BITS>(cv, valid, blk, lane, qp, const_cast<float*>(ef), w, q);
+      const int valid = load_residual<T>(src, n, blk, lane, qp, cv);
+      s = encode_dense<BITS>(cv, valid, blk, lane, qp, ef_w, w, q);
     }
     put_dense<BITS>(rec, warp, lane, s, w);
   }
@@ -433,6 +507,20 @@ struct Smem {
   static constexpr int kAcc = MODE == kTopK ? kWarps * kBlock : 4;
 };
 
+// Phase-1 loop shared by the exchange kernels: encode every owned chunk
+// (direct loads: measured faster here than the prefetch pipeline, since the
+// exchange phases want the occupancy its buffers would take) and hand the
+// staged record to `send`.
+template <int MODE, typename T, typename Send>
+__device__ __forceinline__ void encode_owned(const FusedParams& P, uint8_t* rec, Send&& send) {
+  const ChunkSrc<T> gsrc{reinterpret_cast<const T*>(P.grad), P.pred, P.ef, 0};
+  int it = 0;
+  for (int c = blockIdx.x; c < P.nchunks; c += gridDim.x, ++it) {
+    encode_chunk<MODE, T>(gsrc, P.ef, P.n, P.nblk, P.nchunks, P.k, P.rec_bytes, P.q, c, rec);
+    send(c, it);
+  }
+}
+
 template <int MODE, typename T>
 __global__ void __launch_bounds__(kThreads) oneshot_kernel(FusedParams P) {
   __shared__ int s_abort;
@@ -440,17 +528,16 @@ __global__ void __launch_bounds__(kThreads) oneshot_kernel(FusedParams P) {
   __shared__ __align__(16) uint8_t stage[Smem<MODE>::kStage];
   __shared__ __align__(16) float acc_smem[Smem<MODE>::kAcc];
   if (threadIdx.x == 0) s_abort = 0;
-  const T* g = reinterpret_cast<const T*>(P.grad);
   // Phase 1: encode each owned chunk and push its record to every rank.
-  for (int c = blockIdx.x; c < P.nchunks; c += gridDim.x) {
-    encode_chunk<MODE, T>(g, P.pred, P.ef, P.n, P.nblk, P.nchunks, P.k, P.rec_bytes, P.q, c, rec);
-    if (passenger(P.q.topo, c, P.nchunks)) continue;
-    for (int i = 0; i < P.world; ++i) {
-      const int r = (P.rank + 1 + i) % P.world;  // self last
-      copy_record(slot_rec(P, r, P.rank, c), rec, P.chunk_bytes);
+  encode_owned<MODE, T>(P, rec, [&](int c, int) {
+    if (!passenger(P.q.topo, c, P.nchunks)) {
+      for (int i = 0; i < P.world; ++i) {
+        const int r = (P.rank + 1 + i) % P.world;  // self last
+        copy_record(slot_rec(P, r, P.rank, c), rec, P.chunk_bytes);
+      }
     }
     __syncthreads();
-  }
+  });
   signal_column(P, kFlagPayload);
   // Phase 2: wait for the peers' records of this column, reduce.
   if (!wait_column(P, kFlagPayload, &s_abort)) return;
@@ -469,17 +556,11 @@ __global__ void __launch_bounds__(kThreads) twoshot_kernel(FusedParams P) {
   __shared__ __align__(16) uint8_t rec[2080];
   if (threadIdx.x == 0) s_abort = 0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const T* g = reinterpret_cast<const T*>(P.grad);
   // Phase A: chunk i of this column goes to its owner rank i mod W.
-  {
-    int i = 0;
-    for (int c = blockIdx.x; c < P.nchunks; c += gridDim.x, ++i) {
-      encode_chunk<MODE, T>(g, P.pred, P.ef, P.n, P.nblk, P.nchunks, P.k, P.rec_bytes, P.q, c, rec);
-      if (passenger(P.q.topo, c, P.nchunks)) continue;
-      copy_record(slot_rec(P, i % P.world, P.rank, c), rec, P.chunk_bytes);
-      __syncthreads();
-    }
-  }
+  encode_owned<MODE, T>(P, rec, [&](int c, int i) {
+    if (!passenger(P.q.topo, c, P.nchunks)) copy_record(slot_rec(P, i % P.world, P.rank, c), rec, P.chunk_bytes);
+    __syncthreads();
+  });
   signal_column(P, kFlagPayload);
   if (!wait_column(P, kFlagPayload, &s_abort)) return;
   // Phase B: reduce owned chunks, re-encode the mean residual as INT8.
@@ -529,31 +610,74 @@ __global__ void __launch_bounds__(kThreads) twoshot_kernel(FusedParams P) {
   }
 }
 
-// Single rank: encode + decode in registers (no exchange).
+// One chunk of the single-rank kernel: encode + decode in registers.
+template <int MODE, typename T>
+__device__ __forceinline__ void single_chunk(const FusedParams& P, const ChunkSrc<T>& in, int ch, uint8_t* rec_smem) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int blk = ch * kChunkBlocks + warp;
+  if (blk >= P.nblk) return;
+  float c[8], acc[8];
+  const int valid = load_residual<T>(in, P.n, blk, lane, P.q, c);
+  if (passenger(P.q.topo, ch, P.nchunks)) {
+    if (P.q.use_ef) store8<float>(P.ef, (int64_t)blk * kBlock + lane * 8, valid, true, c);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+  } else if (MODE == kTopK) {
+    TopkSel r = topk_select(c, valid, blk, lane, P.k, P.n, P.q, P.ef, rec_smem + warp * kTopkMaxRec, P.rec_bytes);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = ((r.selmask >> j) & 1u) ? product_accum(0.0f, r.q[j], r.s) : 0.0f;
+  } else {
+    constexpr int BITS = MODE == kInt4 ? 4 : 8;
+    uint32_t w[2];
+    int32_t q[8];
+    const float s = encode_dense<BITS>(c, valid, blk, lane, P.q, P.ef, w, q);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = product_accum(0.0f, q[j], s);
+  }
+  finalize<T>(reinterpret_cast<T*>(P.grad), P.pred, P.n, blk, lane, acc, P.f);
+}
+
+// Single rank: encode + decode in registers (no exchange); inputs of whole
+// chunks through the prefetch pipeline.
+// Which kernels read their inputs through the prefetch pipeline (measured
+// per kernel on B200, 64M-element buckets): the dense single-rank kernel
+// gains; the exchange kernels and top-k, which need their occupancy, lose.
+template <int MODE, bool kExchange>
+inline constexpr bool kPrefetch = !kExchange && MODE != kTopK;
+
 template <int MODE, typename T>
 __global__ void __launch_bounds__(kThreads) single_kernel(FusedParams P) {
   __shared__ __align__(16) uint8_t rec_smem[MODE == kTopK ? kWarps * kTopkMaxRec : 16];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int blk = blockIdx.x * kWarps + warp; blk < P.nblk; blk += gridDim.x * kWarps) {
-    float c[8], acc[8];
-    const int valid = load_residual<T>(reinterpret_cast<const T*>(P.grad), P.pred, P.ef, P.n, blk, lane, P.q, c);
-    if (passenger(P.q.topo, blk / kChunkBlocks, P.nchunks)) {
-      if (P.q.use_ef) store8<float>(P.ef, (int64_t)blk * kBlock + lane * 8, valid, true, c);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
-    } else if (MODE == kTopK) {
-      TopkSel r = topk_select(c, valid, blk, lane, P.k, P.n, P.q, P.ef, rec_smem + warp * kTopkMaxRec, P.rec_bytes);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) acc[j] = ((r.selmask >> j) & 1u) ? product_accum(0.0f, r.q[j], r.s) : 0.0f;
+  __shared__ __align__(8) uint64_t mbar[2];
+  extern __shared__ __align__(128) uint8_t dsm[];
+  const T* g = reinterpret_cast<const T*>(P.grad);
+  const ChunkSrc<T> gsrc{g, P.pred, P.ef, 0};
+  const float* pp = P.q.use_pred ? P.pred : nullptr;
+  const float* pe = P.q.use_ef ? P.ef : nullptr;
+  if constexpr (!kPrefetch<MODE, false>) {
+    for (int ch = blockIdx.x; ch < P.nchunks; ch += gridDim.x) single_chunk<MODE, T>(P, gsrc, ch, rec_smem);
+    return;
+  }
+  ChunkPipe<T> pipe{mbar, dsm};
+  pipe.init();
+  const int c0 = blockIdx.x;
+  if (c0 < P.nchunks && ChunkPipe<T>::full(P.n, c0)) pipe.issue(g, pp, pe, c0, 0);
+  int it = 0;
+  for (int ch = c0; ch < P.nchunks; ch += gridDim.x, ++it) {
+    const int b = it & 1;
+    const int cn = ch + gridDim.x;
+    if (cn < P.nchunks && ChunkPipe<T>::full(P.n, cn)) pipe.issue(g, pp, pe, cn, b ^ 1);
+    if (ChunkPipe<T>::full(P.n, ch)) {
+      if (!pipe.wait(b, P.timeout_ns)) {
+        if (threadIdx.x == 0) set_status(P.status, kTimeoutCopy, ch, 0);
+        pipe.drain(P.timeout_ns);
+        return;
+      }
+      single_chunk<MODE, T>(P, pipe.buffer_source(b, ch), ch, rec_smem);
     } else {
-      constexpr int BITS = MODE == kInt4 ? 4 : 8;
-      uint32_t w[2];
-      int32_t q[8];
-      const float s = encode_dense<BITS>(c, valid, blk, lane, P.q, P.ef, w, q);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) acc[j] = product_accum(0.0f, q[j], s);
+      single_chunk<MODE, T>(P, gsrc, ch, rec_smem);
     }
-    finalize<T>(reinterpret_cast<T*>(P.grad), P.pred, P.n, blk, lane, acc, P.f);
+    __syncthreads();  // buffer b is reused two iterations on
   }
 }
 
@@ -576,7 +700,7 @@ __global__ void __launch_bounds__(kThreads) encode_kernel(const T* g, const floa
       for (int64_t i = e0 + threadIdx.x; i < e1; i += blockDim.x) ef_out[i] = ef_in[i];
       __syncthreads();
     }
-    encode_chunk<MODE, T>(g, pred, ef_out, n, nblk, nchunks, k, rec_bytes, qp, c, rec);
+    encode_chunk<MODE, T>(ChunkSrc<T>{g, pred, ef_out, 0}, ef_out, n, nblk, nchunks, k, rec_bytes, qp, c, rec);
     copy_record(out + (int64_t)c * chunk_bytes, rec, chunk_bytes);
     __syncthreads();
   }
@@ -610,6 +734,86 @@ __global__ void __launch_bounds__(kThreads) reduce_kernel(ReduceSrcs srcs, int w
     }                                                                             \
   }()
 
+// Dynamic shared memory of the prefetch pipeline; set on first use of each
+// kernel instance (above the 48 KB default).
+template <auto Kernel>
+int prepare_dsmem(int bytes) {
+  static bool done = false;  // one flag per kernel instance
+  if (!done) {
+    cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    done = true;
+  }
+  return bytes;
+}
+
+// ------------------------------------------------ prefetch pipeline check
+// Every whole chunk of src goes through the ChunkPipe buffers (g slice only)
+// and is written back to dst; the partial tail is copied directly.
+__global__ void __launch_bounds__(kThreads) pipe_copy_kernel(const float* src, float* dst, int64_t n, int nchunks,
+                                                             int vec, int* status) {
+  __shared__ __align__(8) uint64_t mbar[2];
+  extern __shared__ __align__(128) uint8_t dsm[];
+  ChunkPipe<float> pipe{mbar, dsm};
+  pipe.init();
+  const int c0 = blockIdx.x;
+  if (c0 < nchunks && ChunkPipe<float>::full(n, c0)) pipe.issue(src, nullptr, nullptr, c0, 0);
+  int it = 0;
+  for (int c = c0; c < nchunks; c += gridDim.x, ++it) {
+    const int b = it & 1;
+    const int cn = c + gridDim.x;
+    if (cn < nchunks && ChunkPipe<float>::full(n, cn)) pipe.issue(src, nullptr, nullptr, cn, b ^ 1);
+    const int64_t e0 = (int64_t)c * kChunkElems;
+    if (ChunkPipe<float>::full(n, c)) {
+      if (!pipe.wait(b, 1000000000ull)) {
+        if (threadIdx.x == 0) set_status(status, kTimeoutCopy, c, 0);
+        pipe.drain(1000000000ull);
+        return;
+      }
+      const ChunkSrc<float> s = pipe.buffer_source(b, c);
+      if (vec) {  // the encoders' read path: 8 elements per lane, vector loads
+        float v[8];
+        const int64_t l0 = (int64_t)threadIdx.x * 8;
+        load8<float>(s.g, e0 + l0 - s.roff, 8, true, v);
+        store8<float>(dst, e0 + l0, 8, true, v);
+      } else {
+        for (int i = threadIdx.x; i < kChunkElems; i += blockDim.x) dst[e0 + i] = s.g[e0 + i - s.roff];
+      }
+    } else {
+      for (int64_t i = e0 + threadIdx.x; i < n; i += blockDim.x) dst[i] = src[i];
+    }
+    __syncthreads();
+  }
+}
+
+cudaError_t launch_pipe_copy(const float* src, float* dst, int64_t n, int grid, int vec, int* status,
+                             cudaStream_t stream) {
+  const int nchunks = (int)((n + kChunkElems - 1) / kChunkElems);
+  if (nchunks == 0) return cudaSuccess;
+  const int dyn = prepare_dsmem<pipe_copy_kernel>(ChunkPipe<float>::kBytes);
+  pipe_copy_kernel<<<grid, kThreads, dyn, stream>>>(src, dst, n, nchunks, vec, status);
+  return cudaGetLastError();
+}
+
+// Dynamic shared memory of a kernel: the pipeline buffers when it prefetches.
+template <int M, typename T, bool kExchange>
+constexpr int dsmem_of() {
+  return kPrefetch<M, kExchange> ? ChunkPipe<T>::kBytes : 0;
+}
+
+// Two-shot exists for the dense modes only; these wrappers keep the top-k
+// instance from being referenced (discarded branches inside a template).
+template <int M, typename T>
+int twoshot_occupancy() {
+  int v = 1;
+  if constexpr (M != kTopK)
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, twoshot_kernel<M, T>, kThreads, dsmem_of<M, T, true>());
+  return v;
+}
+template <int M, typename T>
+void twoshot_launch(const FusedParams& P, int grid, cudaStream_t stream) {
+  if constexpr (M != kTopK) twoshot_kernel<M, T><<<grid, kThreads, dsmem_of<M, T, true>(), stream>>>(P);
+}
+
 int fused_grid(int nchunks, int mode, int dtype, int variant, int cap, int device) {
   static int occ_cache[3][2][3] = {};
   static int sms = 0;
@@ -619,11 +823,12 @@ int fused_grid(int nchunks, int mode, int dtype, int variant, int cap, int devic
     int v = 1;
     NGL_DISPATCH(mode, dtype, [&] {
       if (variant == kVariantTwoShot) {
-        if constexpr (M != kTopK) cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, twoshot_kernel<M, T>, kThreads, 0);
+        v = twoshot_occupancy<M, T>();
       } else if (variant == kVariantOneShot) {
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, oneshot_kernel<M, T>, kThreads, 0);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, oneshot_kernel<M, T>, kThreads, dsmem_of<M, T, true>());
       } else {
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, single_kernel<M, T>, kThreads, 0);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, single_kernel<M, T>, kThreads,
+                                                      prepare_dsmem<single_kernel<M, T>>(dsmem_of<M, T, false>()));
       }
     });
     occ = v > 0 ? v : 1;
@@ -642,13 +847,14 @@ int fused_grid(int nchunks, int mode, int dtype, int variant, int cap, int devic
 
 cudaError_t launch_fused(const FusedParams& P, int mode, int dtype, int variant, int grid, cudaStream_t stream) {
   if (variant == kVariantSingle) {
-    NGL_DISPATCH(mode, dtype, [&] { single_kernel<M, T><<<grid, kThreads, 0, stream>>>(P); });
-  } else if (variant == kVariantTwoShot) {
     NGL_DISPATCH(mode, dtype, [&] {
-      if constexpr (M != kTopK) twoshot_kernel<M, T><<<grid, kThreads, 0, stream>>>(P);
+      const int dyn = prepare_dsmem<single_kernel<M, T>>(dsmem_of<M, T, false>());
+      single_kernel<M, T><<<grid, kThreads, dyn, stream>>>(P);
     });
+  } else if (variant == kVariantTwoShot) {
+    NGL_DISPATCH(mode, dtype, [&] { twoshot_launch<M, T>(P, grid, stream); });
   } else {
-    NGL_DISPATCH(mode, dtype, [&] { oneshot_kernel<M, T><<<grid, kThreads, 0, stream>>>(P); });
+    NGL_DISPATCH(mode, dtype, [&] { oneshot_kernel<M, T><<<grid, kThreads, dsmem_of<M, T, true>(), stream>>>(P); });
   }
   return cudaGetLastError();
 }

@@ -22,6 +22,7 @@ enum Status : int {
   kTimeoutResult = 2,    // a two-shot result flag never arrived
   kBadHeader = 3,        // payload header did not match (n / epoch)
   kBounds = 4,           // bounds check failed (NGL_BOUNDS_CHECK builds)
+  kTimeoutCopy = 5,      // a bulk copy into shared memory never completed
 };
 
 __device__ __forceinline__ uint64_t globaltimer() {
@@ -132,6 +133,41 @@ struct Vec8<__nv_bfloat16> {
 
 // Load 8 elements starting at element `e0` of which `valid` (0..8) are in
 // range; out-of-range lanes read 0.  `vec_ok` selects the vector path.
+// ---- bulk copies global -> shared with an mbarrier (no tensor map, no multicast)
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void mbar_init(uint64_t* m, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(m)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* m, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(m)), "r"(bytes) : "memory");
+}
+// src, dst 16-byte aligned, bytes a multiple of 16; src is this GPU's memory.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* m) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(m))
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* m, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(m)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for phase `parity` of an mbarrier: false after limit_ns.
+__device__ __forceinline__ bool mbar_wait(uint64_t* m, uint32_t parity, uint64_t limit_ns) {
+  if (mbar_try_wait(m, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try_wait(m, parity))
+    if (globaltimer() - t0 > limit_ns) return false;
+  return true;
+}
+
 template <typename T>
 __device__ __forceinline__ void load8(const T* base, int64_t e0, int valid, bool vec_ok, float (&v)[8]) {
   if (valid == 8 && vec_ok) {

@@ -39,6 +39,7 @@ STATUS_NAMES = {
     0: "ok",
     1: "timeout waiting for a peer's payload",
     2: "timeout waiting for a two-shot result",
+    5: "timeout of a bulk copy into shared memory",
     3: "payload tag mismatch (ranks disagree on bucket size or order)",
     4: "bounds check",
 }

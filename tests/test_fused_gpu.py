@@ -188,3 +188,16 @@ def test_wait_times_out_and_reports_status():
 def test_bad_tag_is_reported():
     st, _, _ = _two_rank_emulation(5000, "int4", 13, bad_tag=True)
     assert st[0] == 3, st
+
+
+@pytest.mark.parametrize("n", [2048, 4096, 65539, 1 << 20])
+@pytest.mark.parametrize("grid", [1, 3, 33, 148])
+@pytest.mark.parametrize("vec", [False, True])
+def test_prefetch_pipeline_copies_every_chunk(n, grid, vec):
+    _, c = _ext()
+    src = torch.randn(n, device="cuda")
+    status = torch.zeros(4, dtype=torch.int32, device="cuda")
+    dst = c.pipe_copy(src, grid, status, vec)
+    torch.cuda.synchronize()
+    assert status.tolist()[0] == 0
+    assert torch.equal(dst, src)
