@@ -6,7 +6,9 @@ Ops: fused_single (INT4, world 1), fused_oneshot (rank 0 of a 2-rank one-shot
 all-reduce with the peer's payload and flags pre-delivered into local memory,
 so the exchange kernel runs in full on one GPU), fused_topk_single,
 fused_topk_oneshot, hpc_step, bs_encode, bsrle_encode, rle_encode,
-bs_decode, stochastic_encode, topk_encode.
+bs_decode, stochastic_encode, topk_encode, nz_encode_eb / nz_encode_bs /
+nz_encode_bsrle (whole-trajectory device .nz encode, --steps snapshots of
+n / steps values), synth_brownian (device trajectory generator).
 
 Inputs are larger than the 126 MB L2 for the default n.  Each timed launch is
 bracketed by CUDA events on the launching stream after warm-up; the figure
@@ -107,6 +109,7 @@ def main():
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--k", type=int, default=13, help="top-k kept per 256-block")
+    ap.add_argument("--steps", type=int, default=100, help="snapshots for the trajectory ops")
     args = ap.parse_args()
     torch.cuda.set_device(0)
     from mini_nangila_b200 import _ext
@@ -152,6 +155,21 @@ def main():
         sc = torch.tensor([2e-3], device=dev)
         run = lambda: c.decode_streams(b, off, sc, 0, n, (n + 31) // 32)  # noqa: E731
         algo = b.numel() + 4 * n
+    elif args.op in ("nz_encode_eb", "nz_encode_bs", "nz_encode_bsrle"):
+        # Whole-trajectory device .nz encode: T steps of P values (Brownian
+        # positions from the device generator), closed loop + packer.
+        from ..ops import trajectory
+
+        codec = args.op.split("_")[-1]
+        T = args.steps
+        P = max(1, n // T)
+        x = c.synth_brownian(P, T, seed=1, sigma=0.01, box=100.0, lo=-50.0, periodic=False)
+        run = lambda: trajectory.encode_steps(x, codec, 1e-3)  # noqa: E731
+        algo = 4 * T * P + 2 * T * P
+    elif args.op == "synth_brownian":
+        T = args.steps
+        run = lambda: c.synth_brownian(max(1, n // T), T, seed=1)  # noqa: E731
+        algo = 4 * (n // T) * T
     elif args.op == "stochastic_encode":
         r = c.q823_from_f32(torch.randn(n, device=dev))
         run = lambda: c.stochastic_quantize(r, 4, 42, 0)  # noqa: E731
