@@ -528,6 +528,11 @@ __global__ void __launch_bounds__(kThreads) oneshot_kernel(FusedParams P) {
   __shared__ __align__(16) uint8_t stage[Smem<MODE>::kStage];
   __shared__ __align__(16) float acc_smem[Smem<MODE>::kAcc];
   if (threadIdx.x == 0) s_abort = 0;
+  // Debug builds: every record of this launch fits its inbox slot, and every
+  // rank's region is mapped.
+  NGL_BOUNDS_UNIFORM((int64_t)P.nchunks * P.chunk_bytes <= P.slot_bytes && P.world <= kMaxWorld, P.status,
+                     P.nchunks, P.chunk_bytes);
+  for (int r = 0; r < P.world; ++r) NGL_BOUNDS_UNIFORM(P.sym[r] != nullptr, P.status, -2, r);
   // Phase 1: encode each owned chunk and push its record to every rank.
   encode_owned<MODE, T>(P, rec, [&](int c, int) {
     if (!passenger(P.q.topo, c, P.nchunks)) {
@@ -556,6 +561,10 @@ __global__ void __launch_bounds__(kThreads) twoshot_kernel(FusedParams P) {
   __shared__ __align__(16) uint8_t rec[2080];
   if (threadIdx.x == 0) s_abort = 0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  NGL_BOUNDS_UNIFORM((int64_t)P.nchunks * P.chunk_bytes <= P.slot_bytes &&
+                         (int64_t)P.nchunks * chunk_record_bytes(kInt8, 0) <= P.result_bytes && P.world <= kMaxWorld,
+                     P.status, P.nchunks, P.chunk_bytes);
+  for (int r = 0; r < P.world; ++r) NGL_BOUNDS_UNIFORM(P.sym[r] != nullptr, P.status, -2, r);
   // Phase A: chunk i of this column goes to its owner rank i mod W.
   encode_owned<MODE, T>(P, rec, [&](int c, int i) {
     if (!passenger(P.q.topo, c, P.nchunks)) copy_record(slot_rec(P, i % P.world, P.rank, c), rec, P.chunk_bytes);

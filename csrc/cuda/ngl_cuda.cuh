@@ -133,6 +133,25 @@ struct Vec8<__nv_bfloat16> {
 
 // Load 8 elements starting at element `e0` of which `valid` (0..8) are in
 // range; out-of-range lanes read 0.  `vec_ok` selects the vector path.
+// ---- bounds-checked debug builds (-DNGL_BOUNDS_CHECK)
+// NGL_BOUNDS_UNIFORM(cond, status, a, b): when cond fails, record kBounds
+// with (a, b) in the status word and leave the kernel.  Only for conditions
+// that are uniform across the CTA at that point (no thread may be left
+// waiting at a barrier).  Compiled out in release builds.
+#ifdef NGL_BOUNDS_CHECK
+#define NGL_BOUNDS_UNIFORM(cond, status, a, b)                           \
+  do {                                                                   \
+    if (!(cond)) {                                                       \
+      if (threadIdx.x == 0) ::ngl::dev::set_status((status), ::ngl::dev::kBounds, (a), (b)); \
+      return;                                                            \
+    }                                                                    \
+  } while (0)
+#else
+#define NGL_BOUNDS_UNIFORM(cond, status, a, b) \
+  do {                                         \
+  } while (0)
+#endif
+
 // ---- bulk copies global -> shared with an mbarrier (no tensor map, no multicast)
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 __device__ __forceinline__ void mbar_init(uint64_t* m, uint32_t count) {

@@ -13,7 +13,8 @@ hook (``python/nangila_ddp/comm_hook.py:47-60``) and adds:
   ``floor(x + U - 0.5)`` rounding, hi/lo nibbles, LSB-first top-k mask,
   static randperm topology) with torch ops.
 * ``error_feedback`` (fused/host; the reference has none), ``variant``
-  (``auto|oneshot|twoshot``), ``timeout_s``, ``verbose``, ``max_ctas``.
+  (``auto|oneshot|twoshot``, or ``nccl`` for the uncompressed averaged
+  all-reduce behind the same API), ``timeout_s``, ``verbose``, ``max_ctas``.
 
 ``topo_drop_percent`` (a fraction, as in the reference) selects passengers
 per bucket.  fused/host drop whole 2048-element chunks by a keyed
@@ -28,14 +29,17 @@ call counters) so a resumed run continues bit-identically.
 """
 from __future__ import annotations
 
+import os
 import time
+import zlib
 from dataclasses import dataclass, field
 
 import numpy as np
 import torch
 import torch.distributed as dist
 
-from .fused import FusedAllReduce, topk_per_block, topology, wire_bytes
+from ..utils.nvtx import nvtx_range
+from .fused import CommError, FusedAllReduce, topk_per_block, topology, wire_bytes
 
 
 @dataclass
@@ -174,7 +178,7 @@ def _fused_hook(hs: NangilaHookState, bucket):
     hs.calls += 1
     cur = torch.cuda.current_stream(buf.device)
     hs.stream.wait_stream(cur)
-    with torch.cuda.stream(hs.stream):
+    with torch.cuda.stream(hs.stream), nvtx_range(f"nangila/bucket{bidx}/{buf.numel()}"):
         hs.last_variant = hs.comm.allreduce_(
             buf, st.pred, st.ef, mode=cfg.mode, k=cfg.k, variant=cfg.variant, stochastic=cfg.stochastic,
             seed=cfg.seed, bucket=bidx, step=st.calls, beta=cfg.beta, first=first,
@@ -190,6 +194,47 @@ def _fused_hook(hs: NangilaHookState, bucket):
 
 
 # ------------------------------------------------------- host (CPU, gloo)
+_MAGIC = 0x504C474E  # "NGLP"
+
+
+def _fault(rank: int, call: int) -> str | None:
+    """Host-side fault injection for tests: NGL_FAULT="<kind>:<rank>:<call>"
+    with kind corrupt (flip a payload byte after its checksum) or mismatch
+    (announce another bucket) applies to that rank's hook call."""
+    spec = os.environ.get("NGL_FAULT", "")
+    if not spec:
+        return None
+    kind, r, c = (spec.split(":") + ["", "", ""])[:3]
+    return kind if (r == str(rank) and c == str(call)) else None
+
+
+def _frame(wire: np.ndarray, n: int, step: int, bucket: int, fault: str | None) -> torch.Tensor:
+    """Payload = [magic, n lo, n hi, step, bucket, crc32(wire)] (u32) + wire."""
+    w = np.ascontiguousarray(wire, dtype=np.uint8)
+    crc = zlib.crc32(w.tobytes()) & 0xFFFFFFFF
+    hdr = np.array([_MAGIC, n & 0xFFFFFFFF, n >> 32, step & 0xFFFFFFFF, bucket & 0xFFFFFFFF, crc], dtype=np.uint32)
+    if fault == "corrupt" and w.size:
+        w = w.copy()
+        w[w.size // 2] ^= 0xFF
+    elif fault == "mismatch":
+        hdr[4] ^= 1
+    return torch.from_numpy(np.concatenate([hdr.view(np.uint8), w]))
+
+
+def _unframe(x: torch.Tensor, src: int, n: int, step: int, bucket: int) -> np.ndarray:
+    b = x.numpy()
+    hdr = b[:24].view(np.uint32)
+    w = b[24:]
+    if hdr[0] != _MAGIC or (int(hdr[1]) | (int(hdr[2]) << 32)) != n:
+        raise CommError(f"rank {src}: bad payload header (magic/length) for bucket {bucket}")
+    if int(hdr[3]) != (step & 0xFFFFFFFF) or int(hdr[4]) != (bucket & 0xFFFFFFFF):
+        raise CommError(f"rank {src}: payload of bucket {int(hdr[4])} step {int(hdr[3])}, expected bucket {bucket} "
+                        f"step {step} (ranks disagree on bucket order)")
+    if (zlib.crc32(w.tobytes()) & 0xFFFFFFFF) != int(hdr[5]):
+        raise CommError(f"rank {src}: payload checksum mismatch in bucket {bucket} step {step}")
+    return w
+
+
 def _host_hook(hs: NangilaHookState, bucket):
     from .._ext import host
 
@@ -212,11 +257,13 @@ def _host_hook(hs: NangilaHookState, bucket):
         bits = 4 if cfg.mode == "int4" else 8
         wire, e_out = h.product_encode(g, pred, ef, bits, cfg.stochastic, cfg.error_feedback,
                                        cfg.seed & 0x7FFFFFFFFFFFFFFF, rank, bidx, st.calls, topo)
-    payload = torch.from_numpy(np.ascontiguousarray(wire))
+    payload = _frame(wire, n, st.calls, bidx, _fault(rank, hs.calls))
     gathered = [torch.empty_like(payload) for _ in range(world)]
     dist.all_gather(gathered, payload, group=hs.group)
     inv_world = np.float32(1.0) / np.float32(world)
-    wires = [x.numpy() for x in gathered]
+    # every rank checks every payload after the same collective, so all of
+    # them raise together on a corrupt or mismatched one
+    wires = [_unframe(x, r, n, st.calls, bidx) for r, x in enumerate(gathered)]
     if cfg.mode == "topk":
         avg = h.product_topk_reduce(wires, n, cfg.k, pred, float(inv_world))
     else:
@@ -233,6 +280,20 @@ def _host_hook(hs: NangilaHookState, bucket):
     fut = torch.futures.Future()
     fut.set_result(buf)
     return fut
+
+
+# ------------------------------------------------ uncompressed (baseline)
+def _nccl_hook(hs: NangilaHookState, bucket):
+    """Plain averaged all-reduce of the bucket (the stock DDP path), behind
+    the same API and metrics for A/B runs."""
+    buf = bucket.buffer()
+    world = dist.get_world_size(hs.group)
+    hs.calls += 1
+    hs.raw_bytes += buf.numel() * buf.element_size()
+    hs.comp_bytes += buf.numel() * buf.element_size()
+    with nvtx_range(f"nccl/bucket{bucket.index()}"):
+        fut = dist.all_reduce(buf.div_(world), group=hs.group, async_op=True).get_future()
+    return fut.then(lambda f: f.value()[0])
 
 
 def register_nangila_hook(
@@ -267,6 +328,8 @@ def register_nangila_hook(
     dev = next(model.parameters()).device
     if impl is None:
         impl = "fused" if dev.type == "cuda" else "host"
+    if variant == "nccl":  # uncompressed all-reduce through the same hook API
+        impl = "nccl"
     if impl == "compat":
         from .compat_hook import make_compat_hook
 
@@ -295,6 +358,9 @@ def register_nangila_hook(
     elif impl == "host":
         def hook(_state, bucket):
             return _host_hook(hs, bucket)
+    elif impl == "nccl":
+        def hook(_state, bucket):
+            return _nccl_hook(hs, bucket)
     else:
         raise ValueError(f"unknown impl {impl!r}")
     model.register_comm_hook(state=None, hook=hook)

@@ -21,6 +21,8 @@ import os
 from datetime import timedelta
 
 import torch
+
+from .utils.nvtx import nvtx_range
 import torch.distributed as dist
 from torch.nn.parallel import DistributedDataParallel as DDP
 
@@ -90,14 +92,17 @@ class DDPTrainer:
         return self.ddp.module
 
     def step(self, x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
-        if self.autocast_dtype is not None:
-            with torch.autocast(self.device.type, dtype=self.autocast_dtype):
+        with nvtx_range("forward"):
+            if self.autocast_dtype is not None:
+                with torch.autocast(self.device.type, dtype=self.autocast_dtype):
+                    loss = self.ddp(x, y)
+            else:
                 loss = self.ddp(x, y)
-        else:
-            loss = self.ddp(x, y)
         self.opt.zero_grad(set_to_none=False)
-        loss.backward()
-        self.opt.step()
+        with nvtx_range("backward"):
+            loss.backward()
+        with nvtx_range("optimizer"):
+            self.opt.step()
         return loss.detach()
 
     def step_host(self, x_host: torch.Tensor, y_host: torch.Tensor) -> float:

@@ -28,6 +28,9 @@ NVCC_FLAGS = [
     "-Xptxas", "-v",
     "-DNGL_DEVICE_BUILD",
 ]
+# Bounds-checked debug build: NGL_BOUNDS_CHECK=1 python setup.py build_ext --inplace
+if os.environ.get("NGL_BOUNDS_CHECK", "0") == "1":
+    NVCC_FLAGS.append("-DNGL_BOUNDS_CHECK")
 
 ext_modules = [
     Extension(

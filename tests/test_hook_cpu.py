@@ -152,3 +152,74 @@ def test_dead_rank_detected_by_timeout(tmp_path):
     txt = (tmp_path / "rank0.txt").read_text()
     err, dt = txt.split(":")
     assert err != "" and float(dt) < 30.0
+
+
+def _fault_worker(rank, world, port, outdir, spec):
+    os.environ["NGL_FAULT"] = spec
+    dist = _init(rank, world, port)
+    try:
+        from mini_nangila_b200.models import GPT2, GPT2Config
+        from mini_nangila_b200.parallel.fused import CommError
+        from mini_nangila_b200.train import DDPTrainer
+
+        torch.manual_seed(0)
+        cfg = GPT2Config.tiny()
+        tr = DDPTrainer(GPT2(cfg), hook="host", hook_kwargs=dict(use_momentum=True, seed=5),
+                        device=torch.device("cpu"), bucket_cap_mb=0.05)
+        g = torch.Generator().manual_seed(100 + rank)
+        msg = "none"
+        try:
+            for _ in range(3):
+                t = torch.randint(0, cfg.vocab_size, (2, 17), generator=g)
+                tr.step(t[:, :-1], t[:, 1:])
+        except CommError as e:
+            msg = str(e)
+        except RuntimeError as e:  # DDP wraps exceptions raised inside the hook
+            msg = str(e) if "rank 1" in str(e) else "other: " + str(e)[:200]
+        (open(os.path.join(outdir, f"f{rank}.txt"), "w")).write(msg)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("kind,needle", [("corrupt", "checksum"), ("mismatch", "disagree")])
+def test_injected_payload_fault_is_detected_on_every_rank(kind, needle, tmp_path):
+    """A rank's payload is corrupted (or claims another bucket) on its 3rd
+    hook call: every rank detects it from the checksummed header and raises,
+    naming the rank; none proceeds with a wrong average."""
+    mp.start_processes(_fault_worker, args=(2, _port(), str(tmp_path), f"{kind}:1:3"), nprocs=2, join=True,
+                       start_method="spawn")
+    for r in range(2):
+        msg = (tmp_path / f"f{r}.txt").read_text()
+        assert "rank 1" in msg and needle in msg, msg
+
+
+def _plain_worker(rank, world, port, outdir):
+    dist = _init(rank, world, port)
+    try:
+        from mini_nangila_b200.models import GPT2, GPT2Config
+        from mini_nangila_b200.train import DDPTrainer
+
+        res = {}
+        for variant in ("nccl", None):
+            torch.manual_seed(0)
+            cfg = GPT2Config.tiny()
+            kw = dict(variant="nccl") if variant else None
+            tr = DDPTrainer(GPT2(cfg), hook="fused" if variant else "nccl", hook_kwargs=kw,
+                            device=torch.device("cpu"), bucket_cap_mb=0.05)
+            g = torch.Generator().manual_seed(100 + rank)
+            for _ in range(2):
+                t = torch.randint(0, cfg.vocab_size, (2, 17), generator=g)
+                tr.step(t[:, :-1], t[:, 1:])
+            res[str(variant)] = torch.cat([p.detach().reshape(-1) for p in tr.model.parameters()])
+        torch.save(res, os.path.join(outdir, f"p{rank}.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_nccl_variant_is_the_plain_allreduce(tmp_path):
+    """variant="nccl" routes buckets through the uncompressed averaged
+    all-reduce: parameters match stock DDP on every rank."""
+    mp.start_processes(_plain_worker, args=(2, _port(), str(tmp_path)), nprocs=2, join=True, start_method="spawn")
+    p0, p1 = torch.load(tmp_path / "p0.pt"), torch.load(tmp_path / "p1.pt")
+    assert torch.equal(p0["nccl"], p1["nccl"])
+    assert torch.allclose(p0["nccl"], p0["None"], atol=1e-6)
