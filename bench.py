@@ -38,7 +38,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 def parse():
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--hook", choices=["fused", "nccl", "compat"], default="fused")
@@ -180,7 +180,8 @@ def main():
         for i in range(args.warmup):
             step_fn(*batches[i % len(batches)])
         barrier_sync(device)
-        sampler = ClockSampler(visible_gpu_indices(world)).start() if (rank == 0 and not args.no_clocks) else None
+        sampler = (ClockSampler(visible_gpu_indices(world), period_ms=50).start()
+                   if (rank == 0 and not args.no_clocks) else None)
         launches0 = trainer.kernel_launches() if trainer else 0
         barrier_sync(device)
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
