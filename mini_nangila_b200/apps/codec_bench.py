@@ -6,7 +6,8 @@ Synthetic LAMMPS-style trajectory from the device generator (Philox +
 Box-Muller, ``csrc/cuda/synth_kernels.cu``): positions uniform in a 100^3
 box centred on the origin ([-50, 50)^3), each step adds an N(0, 0.01^2)
 displacement per coordinate; fp32 x/y/z of every atom form one snapshot
-(3 * atoms values).  The first snapshot has no prediction, so its codes are
+(3 * atoms values).  ``--fields pos,vel`` adds the velocity field, N(0, 1)
+per coordinate and step, and reports both fields and their total.  The first snapshot has no prediction, so its codes are
 the coordinates themselves: a box reaching 100 would exceed the INT16 code
 range at eps 1e-3 (+-65.5) in the reference's format.  The codec sees unwrapped
 coordinates (LAMMPS xu/yu/zu): with periodic wrap a boundary crossing is a
@@ -42,6 +43,16 @@ def make_positions(atoms, steps, sigma, box, seed, wrapped, device):
     dev = torch.device(device)
     return cuda().synth_brownian(3 * atoms, steps, seed=seed, sigma=sigma, box=box, lo=-box / 2, periodic=wrapped,
                                  device=dev.index if dev.index is not None else torch.cuda.current_device())
+
+
+def make_velocities(atoms, steps, seed, device):
+    """[steps, 3 * atoms] N(0, 1) velocities, independent per step (the device
+    AR(1) generator with rho 0)."""
+    from .._ext import cuda
+
+    dev = torch.device(device)
+    return cuda().synth_ar1(3 * atoms, steps, seed=seed + 1, rho=0.0, sigma=1.0, sigma0=1.0, sparse_frac=0.0,
+                            sparse_scale=1.0, device=dev.index if dev.index is not None else torch.cuda.current_device())
 
 
 def _median_ms(fn, warmup=2, iters=5):
@@ -115,16 +126,37 @@ def main(argv=None):
     ap.add_argument("--codecs", default="eb,bs,bsrle")
     ap.add_argument("--verify-steps", type=int, default=3)
     ap.add_argument("--cpu-steps", type=int, default=3)
+    ap.add_argument("--fields", default="pos,vel", help="pos (positions), vel (N(0,1) velocities)")
     a = ap.parse_args(argv)
     dev = torch.device("cuda", 0)
-    x = make_positions(a.atoms, a.steps, a.sigma, a.box, a.seed, a.wrapped, dev)
     rows = []
+    for field in a.fields.split(","):
+        if field == "pos":
+            x = make_positions(a.atoms, a.steps, a.sigma, a.box, a.seed, a.wrapped, dev)
+        elif field == "vel":
+            x = make_velocities(a.atoms, a.steps, a.seed, dev)
+        else:
+            raise SystemExit(f"unknown field {field}")
+        for codec in a.codecs.split(","):
+            r = run_codec(x, codec, a.epsilon, a.verify_steps, a.cpu_steps)
+            r.update(field=field, atoms=a.atoms, steps=a.steps, epsilon=a.epsilon, wrapped=a.wrapped,
+                     raw_GB=a.steps * 3 * a.atoms * 4 / 1e9)
+            rows.append(r)
+            print(json.dumps(r), flush=True)
+        del x
+    # both fields together, as one 1M-atom x 100-step dump of positions + velocities
     for codec in a.codecs.split(","):
-        r = run_codec(x, codec, a.epsilon, a.verify_steps, a.cpu_steps)
-        r.update(atoms=a.atoms, steps=a.steps, epsilon=a.epsilon, wrapped=a.wrapped,
-                 raw_GB=a.steps * 3 * a.atoms * 4 / 1e9)
-        rows.append(r)
-        print(json.dumps(r), flush=True)
+        rs = [r for r in rows if r["codec"] == codec]
+        if len(rs) > 1:
+            raw = sum(r["raw_GB"] for r in rs)
+            enc = sum(r["encode_ms"] for r in rs)
+            dec = sum(r["decode_ms"] for r in rs)
+            comp = sum(r["raw_GB"] / r["ratio"] for r in rs)
+            tot = {"codec": codec, "field": "+".join(r["field"] for r in rs), "raw_GB": raw,
+                   "encode_GBps": raw / (enc * 1e-3), "decode_GBps": raw / (dec * 1e-3), "ratio": raw / comp,
+                   "max_abs_err": max(r["max_abs_err"] for r in rs)}
+            rows.append(tot)
+            print(json.dumps(tot), flush=True)
     return rows
 
 
