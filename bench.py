@@ -255,6 +255,9 @@ def main():
         if hs is not None and hs.raw_bytes:
             out["compression_ratio"] = hs.compression_ratio()
             out["config"]["variant"] = hs.last_variant
+            if getattr(hs, "comm", None) is not None and hs.comm.world > 1:
+                out["config"]["twoshot_from_mb"] = (None if hs.comm.twoshot_min_bytes >= (1 << 60)
+                                                    else hs.comm.twoshot_min_bytes / 2 ** 20)
         if clocks is not None:
             out["clocks"] = clocks
         if e2e is not None:

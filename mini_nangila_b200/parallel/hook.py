@@ -14,7 +14,9 @@ hook (``python/nangila_ddp/comm_hook.py:47-60``) and adds:
   static randperm topology) with torch ops.
 * ``error_feedback`` (fused/host; the reference has none), ``variant``
   (``auto|oneshot|twoshot``, or ``nccl`` for the uncompressed averaged
-  all-reduce behind the same API), ``timeout_s``, ``verbose``, ``max_ctas``.
+  all-reduce behind the same API), ``timeout_s``, ``verbose``, ``max_ctas``,
+  ``autotune`` (fused, more than 2 ranks: the first bucket times one-shot
+  against two-shot on this box and sets the size from which two-shot runs).
 
 ``topo_drop_percent`` (a fraction, as in the reference) selects passengers
 per bucket.  fused/host drop whole 2048-element chunks by a keyed
@@ -39,7 +41,7 @@ import torch
 import torch.distributed as dist
 
 from ..utils.nvtx import nvtx_range
-from .fused import CommError, FusedAllReduce, topk_per_block, topology, wire_bytes
+from .fused import CommError, FusedAllReduce, autotune_twoshot, topk_per_block, topology, wire_bytes
 
 
 @dataclass
@@ -176,6 +178,12 @@ def _fused_hook(hs: NangilaHookState, bucket):
     bidx = bucket.index()
     st, first = _get_state(hs, bidx, buf, _bucket_sig(bucket), cfg.use_momentum, cfg.error_feedback)
     hs.calls += 1
+    if getattr(hs, "autotune_pending", False):
+        # First bucket: time one-shot vs two-shot at bucket-like sizes on this
+        # box (every rank runs the same sequence; max over ranks decides).
+        hs.autotune_pending = False
+        with nvtx_range("nangila/autotune"):
+            autotune_twoshot(hs.comm, sizes_mb=(4, 16, 32, 64, 128, 256))
     cur = torch.cuda.current_stream(buf.device)
     hs.stream.wait_stream(cur)
     with torch.cuda.stream(hs.stream), nvtx_range(f"nangila/bucket{bidx}/{buf.numel()}"):
@@ -316,6 +324,7 @@ def register_nangila_hook(
     verbose: bool = False,
     max_ctas: int = 0,
     process_group=None,
+    autotune: bool = True,
 ) -> NangilaHookState:
     """Register a predictive-residual compression comm hook on a DDP model.
 
@@ -352,6 +361,7 @@ def register_nangila_hook(
         hs.comm = FusedAllReduce(max_numel, group=process_group, device=dev, topk_k=max(cfg.k, 1),
                                  timeout_s=timeout_s, max_ctas=max_ctas, modes=(cfg.mode,))
         hs.stream = torch.cuda.Stream(device=dev, priority=-1)
+        hs.autotune_pending = bool(autotune) and hs.comm.world > 2 and variant == "auto" and cfg.mode != "topk"
 
         def hook(_state, bucket):
             return _fused_hook(hs, bucket)
