@@ -8,7 +8,8 @@ with the reconstruction (closed loop) in Q8.23 either way.
 
 Defaults reproduce the reference example (sin gradients, global-scale
 stochastic INT4, BlockSparse checkpoints — ``--checkpoint-block-sparse`` is
-always on there).  ``--preset baseline`` runs the measured configuration:
+always on there).  ``--preset ar1-block-int4`` runs AR(1) gradients with
+block-scaled INT4 and EB checkpoints:
 10,000 elements, 50 steps, checkpoint every 10, AR(1) gradients
 g_t = 0.9 g_{t-1} + N(0, 1e-3^2) from seed 0 with g_0 ~ N(0, 1e-2^2) and 70 %
 of coordinates scaled by 0.01, momentum beta 0.9, stochastic INT4 with one
@@ -115,7 +116,7 @@ def run(num_steps=50, checkpoint_interval=10, gradient_size=10_000, epsilon=1e-3
 
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("--preset", choices=["reference", "baseline"], default="reference")
+    ap.add_argument("--preset", choices=["reference", "ar1-block-int4"], default="reference")
     ap.add_argument("--num-steps", type=int, default=50)
     ap.add_argument("--checkpoint-interval", type=int, default=10)
     ap.add_argument("--gradient-size", type=int, default=10_000)
@@ -126,7 +127,7 @@ def main(argv=None):
     ap.add_argument("--train-topk", type=float, default=0.0)
     ap.add_argument("--json", action="store_true")
     a = ap.parse_args(argv)
-    if a.preset == "baseline":
+    if a.preset == "ar1-block-int4":
         kw = dict(generator="ar1", train="block-int4", checkpoint_codec="eb")
     else:
         kw = dict(generator="sin", train="rust-int4", checkpoint_codec="bsrle" if a.checkpoint_bsrle else "bs")

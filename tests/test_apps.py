@@ -9,7 +9,7 @@ from mini_nangila_b200.apps import (checkpoint_demo, cpu_compression_bench, hpc_
                                     mode_switching, nano_gpt, rotor_twin, throughput_bench, topology_calibration)
 
 
-def test_mode_switching_baseline_deterministic():
+def test_mode_switching_ar1_block_int4_deterministic():
     a = mode_switching.run(generator="ar1", train="block-int4", checkpoint_codec="eb", verbose=False)
     b = mode_switching.run(generator="ar1", train="block-int4", checkpoint_codec="eb", verbose=False)
     assert a["determinism_hash"] == b["determinism_hash"]
