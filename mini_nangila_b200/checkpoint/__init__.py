@@ -1,6 +1,6 @@
-"""Checkpoint / trajectory I/O: the ``.nz`` container, LAMMPS dumps and the
-chunked error-bounded checkpoint layout (nangila-checkpoint)."""
-from . import hdf5, lammps, nzcp
+"""Checkpoint / trajectory I/O: the ``.nz`` container, LAMMPS dumps, the
+chunked error-bounded checkpoint layout (nangila-checkpoint) and
+error-bounded model / optimizer state checkpoints."""
+from . import hdf5, lammps, nzcp, tensor_ckpt
 
-__all__ = ["hdf5", "lammps", "nzcp"]
-from . import tensor_ckpt  # noqa: E402,F401  error-bounded model/optimizer checkpoints
+__all__ = ["hdf5", "lammps", "nzcp", "tensor_ckpt"]
