@@ -786,6 +786,7 @@ __device__ __forceinline__ int64_t advance_values(int64_t vals, int64_t len, int
 
 constexpr int kWalkWin = 32768;  // bytes of a stream staged in shared memory at a time
 
+// BlockSparse (fallback without scratch), top-k compat and element RLE.
 // One CTA per stream: all threads stage a window of the stream into shared
 // memory with 16-byte loads, then thread 0 runs the reference decoder's
 // control flow from shared memory (a resumable state machine, so tokens may
@@ -797,8 +798,10 @@ __global__ void __launch_bounds__(kThreads) k_walk(const uint8_t* __restrict__ d
                                                    int nstreams, int64_t out_cap, int64_t* __restrict__ out_len,
                                                    int64_t* __restrict__ table, int64_t table_cap, int* status) {
   constexpr int VB = KIND == 1 ? 1 : 2;
-  constexpr int kMaxTok = KIND == 3 ? 257 : (KIND == 2 ? 69 : 4 + 32 * VB);
-  __shared__ __align__(16) uint32_t win32[kWalkWin / 4 + 4];
+  constexpr int kMaxTok = KIND == 3 ? 257 : 4 + 32 * VB;
+  static_assert(KIND != 2, "BlockSparse+RLE streams use k_walk_bsrle");
+  constexpr int kWin = kWalkWin;
+  __shared__ __align__(16) uint32_t win32[kWin / 4 + 4];
   __shared__ int64_t s_ptr;
   __shared__ int s_done;
   const int sidx = blockIdx.x;
@@ -810,7 +813,6 @@ __global__ void __launch_bounds__(kThreads) k_walk(const uint8_t* __restrict__ d
   const uint8_t* win = reinterpret_cast<const uint8_t*>(win32);
   // walker state (thread 0)
   int64_t ptr = 0, out = 0, nent = 0, blk = 0, n = 0, nblk = 0;
-  int lit = 0;
   bool overflow = false, done = false;
   if (threadIdx.x == 0) {
     if (KIND != 3) {
@@ -829,7 +831,7 @@ __global__ void __launch_bounds__(kThreads) k_walk(const uint8_t* __restrict__ d
   while (!s_done) {
     const int64_t p0 = s_ptr;
     const int64_t base = p0 - (int64_t)(reinterpret_cast<uintptr_t>(b + p0) & 15u);
-    const int64_t hi = min64(len, base + kWalkWin);
+    const int64_t hi = min64(len, base + kWin);
     const int cnt = (int)(hi - base);
     const uint4* src = reinterpret_cast<const uint4*>(b + base);
     for (int i = threadIdx.x; i < cnt / 16; i += blockDim.x) reinterpret_cast<uint4*>(win32)[i] = src[i];
@@ -868,40 +870,6 @@ __global__ void __launch_bounds__(kThreads) k_walk(const uint8_t* __restrict__ d
           const int room = qlen > vals ? (qlen - vals) / VB : 0;
           q = vals + VB * (c < room ? c : room);
           ++blk;
-        } else if (KIND == 2) {
-          if (lit == 0) {
-            if (!(blk < nblk && q < qlen)) {
-              done = true;
-              break;
-            }
-            const uint32_t op = win[q++];
-            if (op & 0x80u) {
-              const int64_t c = (int64_t)(op & 0x7fu) + 1;
-              for (int64_t k = 0; k < c && !overflow; ++k) {
-                const int64_t bl = (blk + k == nblk - 1) ? n - (blk + k) * 32 : 32;
-                if (out < n) emit(out, bl, 0);
-                out += bl;
-              }
-              blk += c;
-            } else {
-              lit = (int)op + 1;
-            }
-          } else {
-            if (q + 4 > qlen) {  // the literal run ends early
-              lit = 0;
-              continue;
-            }
-            const uint32_t m = u32(q);
-            const int64_t bl = (blk == nblk - 1) ? n - blk * 32 : 32;
-            if (out < n) emit(out, bl, base + q + 1);
-            out += bl;
-            const int c = __popc(bl >= 32 ? m : (m & ((1u << bl) - 1u)));
-            const int vals = q + 4;
-            const int room = qlen > vals ? (qlen - vals) / 2 : 0;
-            q = vals + 2 * (c < room ? c : room);
-            ++blk;
-            --lit;
-          }
         } else {  // element RLE
           if (q >= qlen) {
             done = true;
@@ -909,9 +877,7 @@ __global__ void __launch_bounds__(kThreads) k_walk(const uint8_t* __restrict__ d
           }
           const uint32_t op = win[q++];
           if (op >= 128) {
-            const int64_t c = (int64_t)op - 128 + 1;
-            emit(out, c, 0);
-            out += c;
+            out += (int64_t)op - 128 + 1;  // zeros: the output is zero-filled already
           } else {
             const int c = (int)op + 1;
             const int room = (qlen - q) / 2;
@@ -924,8 +890,7 @@ __global__ void __launch_bounds__(kThreads) k_walk(const uint8_t* __restrict__ d
       }
       ptr = base + q;
       if (overflow) done = true;
-      if (!done && KIND != 2 && ptr >= len) done = true;
-      if (!done && KIND == 2 && lit == 0 && !(blk < nblk && ptr < len)) done = true;
+      if (!done && ptr >= len) done = true;
       s_ptr = ptr;
       s_done = done ? 1 : 0;
     }
@@ -940,6 +905,148 @@ __global__ void __launch_bounds__(kThreads) k_walk(const uint8_t* __restrict__ d
     out_len[sidx] = ol;
     row[0] = nent;
     if (overflow || ol > out_cap) dev::set_status(status, dev::kBounds, sidx, (int)nent);
+  }
+}
+
+// BlockSparse+RLE walk with warp specialisation.  Fixed windows: window k
+// is home to the tokens starting in [k W, (k+1) W) and is staged with kROV
+// more bytes, so every such token (at most 69 bytes) lies inside it.  While
+// thread 0 walks window k, warps 1..7 stage window k+1 into the other buffer
+// and fill its advance table (per byte position: 4 + 2 x the kept values of
+// a block starting there, clamped to the whole values left), so a literal
+// block costs the walker one byte load and an add.  Zero runs emit nothing
+// (the output is zero-filled).  Same descriptors, lengths and status as the
+// generic walker.
+constexpr int kRW = 8192;
+constexpr int kROV = 96;
+constexpr int kRBuf = kRW + kROV + 32;
+
+__device__ __forceinline__ void bsrle_prep(const uint8_t* b, int64_t len, int k, uint32_t* win, uint8_t* adv,
+                                           int tid, int nthreads, bool all_threads) {
+  const int64_t start = (int64_t)k * kRW;
+  const int mis = (int)(reinterpret_cast<uintptr_t>(b + start) & 15u);
+  const int64_t base = start - mis;
+  const int64_t hi = min64(len, start + kRW + kROV);
+  const int cnt = (int)(hi - base);
+  const uint4* src = reinterpret_cast<const uint4*>(b + base);
+  for (int i = tid; i < cnt / 16; i += nthreads) reinterpret_cast<uint4*>(win)[i] = src[i];
+  for (int i = (cnt / 16) * 16 + tid; i < cnt; i += nthreads) reinterpret_cast<uint8_t*>(win)[i] = b[base + i];
+  if (all_threads) __syncthreads();
+  else asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
+  const int qlen = (int)min64(len - base, (int64_t)1 << 30);
+  for (int x = tid; x < cnt; x += nthreads) {
+    uint32_t a = 0;
+    if (x + 4 <= qlen) {
+      const uint32_t w0 = win[x >> 2], w1 = win[(x >> 2) + 1];
+      const int ad = 2 * __popc(__funnelshift_r(w0, w1, (x & 3) * 8)), rem = (qlen - (x + 4)) & ~1;
+      a = 4 + (ad < rem ? ad : rem);
+    }
+    adv[x] = (uint8_t)a;
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) k_walk_bsrle(const uint8_t* __restrict__ data,
+                                                         const int64_t* __restrict__ soff, int nstreams,
+                                                         int64_t out_cap, int64_t* __restrict__ out_len,
+                                                         int64_t* __restrict__ table, int64_t table_cap, int* status) {
+  __shared__ __align__(16) uint32_t win[2][kRBuf / 4 + 4];
+  __shared__ uint8_t adv[2][kRBuf];
+  __shared__ int s_done;
+  const int sidx = blockIdx.x;
+  if (sidx >= nstreams) return;
+  const uint8_t* b = data + soff[sidx];
+  const int64_t len = soff[sidx + 1] - soff[sidx];
+  int64_t* row = table + (int64_t)sidx * (2 * table_cap + 2);
+  longlong2* tab = reinterpret_cast<longlong2*>(row + 2);
+  const int64_t nwin = (len + kRW - 1) / kRW;
+  // walker state (thread 0)
+  int64_t ptr = 4, nent = 0, blk = 0, n = 0, nblk = 0;
+  int lit = 0;
+  bool done = false;
+  if (threadIdx.x == 0) {
+    if (len < 4) {
+      done = true;
+    } else {
+      n = (int64_t)rd_u32(b);
+      nblk = (n + 31) / 32;
+      if (nblk > table_cap) {  // one descriptor per literal block at most
+        dev::set_status(status, dev::kBounds, sidx, -1);
+        done = true;
+      }
+    }
+    s_done = done ? 1 : 0;
+  }
+  if (nwin > 0) bsrle_prep(b, len, 0, win[0], adv[0], threadIdx.x, blockDim.x, true);
+  __syncthreads();
+  for (int64_t k = 0; k < nwin && !s_done; ++k) {
+    const int cur = (int)(k & 1);
+    if (threadIdx.x >= 32) {
+      if (k + 1 < nwin) bsrle_prep(b, len, (int)(k + 1), win[cur ^ 1], adv[cur ^ 1], threadIdx.x - 32,
+                                   blockDim.x - 32, false);
+    } else if (threadIdx.x == 0) {
+      const int64_t start = k * kRW;
+      const int64_t base = start - (int64_t)(reinterpret_cast<uintptr_t>(b + start) & 15u);
+      const int64_t hi = min64(len, start + kRW + kROV);
+      const bool last = hi == len;
+      const int qlen = (int)min64(len - base, (int64_t)1 << 30);
+      const int home_end = (int)(start + kRW - base);  // tokens starting before it belong here
+      const uint8_t* wb = reinterpret_cast<const uint8_t*>(win[cur]);
+      const uint8_t* av = adv[cur];
+      int q = (int)(ptr - base);
+      while (!done && (last || q < home_end)) {
+        if (lit == 0) {
+          if (!(blk < nblk && q < qlen)) {
+            done = true;
+            break;
+          }
+          const uint32_t op = wb[q++];
+          if (op & 0x80u) blk += (int64_t)(op & 0x7fu) + 1;
+          else lit = (int)op + 1;
+          continue;
+        }
+        // full blocks before the last one, while a block fits (window, stream)
+        {
+          const int qstop = last ? qlen - 4 : home_end - 1;
+          const int kmax = (int)min64((int64_t)lit, nblk - 1 - blk);
+          longlong2* tp = tab + nent;
+          const int64_t d0 = (blk * 32) | (32ll << 48), in0 = base + 1;
+          int j = 0;
+          while (j < kmax && q <= qstop) {
+            tp[j] = make_longlong2(d0 + 32ll * j, in0 + q);
+            q += av[q];
+            ++j;
+          }
+          nent += j;
+          blk += j;
+          lit -= j;
+        }
+        if (lit == 0 || (!last && q >= home_end)) continue;
+        if (blk >= nblk) {  // later blocks add nothing
+          done = true;
+          break;
+        }
+        if (q + 4 > qlen) {  // the literal run ends early; an opcode may follow
+          lit = 0;
+          continue;
+        }
+        // the stream's last block (its mask is read by the expansion)
+        const int64_t l = n - blk * 32;
+        tab[nent++] = make_longlong2((blk * 32) | (l << 48), base + q + 1);
+        q += av[q];  // only decides when the walk ends: nothing follows the last block
+        ++blk;
+        --lit;
+      }
+      ptr = base + q;
+      if (!done && last) done = true;
+      s_done = done ? 1 : 0;
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    const int64_t ol = len < 4 ? 0 : min64(blk * 32, n);
+    out_len[sidx] = ol;
+    row[0] = nent;
+    if (ol > out_cap) dev::set_status(status, dev::kBounds, sidx, (int)nent);
   }
 }
 
@@ -1260,7 +1367,7 @@ cudaError_t stream_decode(int kind, const uint8_t* data, const int64_t* stream_o
   else if (kind == 1 && scratch) e = launch_bs_parallel<1>(kind, data, stream_off, nstreams, out_cap, out_len, table, table_cap, status, scratch, total_bytes, s);
   else if (kind == 0) k_walk<0><<<nstreams, kThreads, 0, s>>>(data, stream_off, nstreams, out_cap, out_len, table, table_cap, status);
   else if (kind == 1) k_walk<1><<<nstreams, kThreads, 0, s>>>(data, stream_off, nstreams, out_cap, out_len, table, table_cap, status);
-  else if (kind == 2) k_walk<2><<<nstreams, kThreads, 0, s>>>(data, stream_off, nstreams, out_cap, out_len, table, table_cap, status);
+  else if (kind == 2) k_walk_bsrle<<<nstreams, kThreads, 0, s>>>(data, stream_off, nstreams, out_cap, out_len, table, table_cap, status);
   else k_walk<3><<<nstreams, kThreads, 0, s>>>(data, stream_off, nstreams, out_cap, out_len, table, table_cap, status);
   if (e != cudaSuccess) return e;
   e = cudaGetLastError();

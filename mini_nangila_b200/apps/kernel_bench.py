@@ -6,7 +6,7 @@ Ops: fused_single (INT4, world 1), fused_oneshot (rank 0 of a 2-rank one-shot
 all-reduce with the peer's payload and flags pre-delivered into local memory,
 so the exchange kernel runs in full on one GPU), fused_topk_single,
 fused_topk_oneshot, hpc_step, bs_encode, bsrle_encode, rle_encode,
-bs_decode, stochastic_encode, topk_encode, nz_encode_eb / nz_encode_bs /
+bs_decode, bsrle_decode, stochastic_encode, topk_encode, nz_encode_eb / nz_encode_bs /
 nz_encode_bsrle (whole-trajectory device .nz encode, --steps snapshots of
 n / steps values), synth_brownian (device trajectory generator).
 
@@ -147,6 +147,14 @@ def main():
         out_len = c.pack_codes(q, kind).numel()
         run = lambda: c.pack_codes(q, kind)  # noqa: E731
         algo = 2 * n + out_len
+    elif args.op == "bsrle_decode":
+        q = (torch.randn(n, device=dev) * 50).to(torch.int16)
+        q[torch.rand(n, device=dev) < 0.3] = 0
+        b = c.pack_codes(q, 2)
+        off = torch.tensor([0, b.numel()], dtype=torch.int64, device=dev)
+        sc = torch.tensor([2e-3], device=dev)
+        run = lambda: c.decode_streams(b, off, sc, 2, n, (n + 31) // 32)  # noqa: E731
+        algo = b.numel() + 4 * n
     elif args.op == "bs_decode":
         q = (torch.randn(n, device=dev) * 50).to(torch.int16)
         q[torch.rand(n, device=dev) < 0.7] = 0
