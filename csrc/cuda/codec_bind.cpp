@@ -336,10 +336,12 @@ torch::Tensor nz_decode_steps(torch::Tensor data, torch::Tensor offsets, torch::
              "gather codes");
       }
     }
-    res = torch::empty({T, P}, opt.dtype(torch::kInt32));
-    ck(eb_decode_all(codes.data_ptr<int16_t>(), res.data_ptr<int32_t>(), P, T, scales.data_ptr<float>(), cur()),
+    // decode + add-back + fp32 conversion in one pass over [T, P]
+    auto outf = torch::empty({T, P}, opt.dtype(torch::kFloat32));
+    ck(eb_decode_all(codes.data_ptr<int16_t>(), nullptr, P, T, scales.data_ptr<float>(), cur(),
+                     outf.data_ptr<float>()),
        "eb_decode_all");
-    return to_f32(res);
+    return outf;
   } else {
     const int kind = codec == 2 ? 3 : codec == 3 ? 0 : 2;
     const int64_t nblk = (P + 31) / 32;
@@ -354,8 +356,10 @@ torch::Tensor nz_decode_steps(torch::Tensor data, torch::Tensor offsets, torch::
     auto r = decode_streams(data, offsets, scales, kind, P, tcap);
     res = r[0].view({T, P});
   }
-  ck(linear_addback(res.data_ptr<int32_t>(), P, T, cur()), "linear_addback");
-  return to_f32(res);
+  // add-back + fp32 conversion in one pass
+  auto outf = torch::empty({T, P}, opt.dtype(torch::kFloat32));
+  ck(linear_addback(res.data_ptr<int32_t>(), P, T, cur(), outf.data_ptr<float>()), "linear_addback");
+  return outf;
 }
 
 }  // namespace

@@ -145,7 +145,9 @@ __global__ void k_hpc_step(const float* __restrict__ x, const int32_t* __restric
 
 // Linear-predictor add-back over T snapshots: parallel over elements,
 // sequential over steps (the reference's chain: empty, s_t, 2 s_t - s_{t-1}).
-__global__ void k_linear_addback(int32_t* __restrict__ res, int64_t P, int64_t T) {
+// Add-back chain over T residual snapshots; writes the Q8.23 values in place
+// (f32out == nullptr) or their fp32 conversions to f32out (one pass fewer).
+__global__ void k_linear_addback(int32_t* __restrict__ res, float* __restrict__ f32out, int64_t P, int64_t T) {
   for (int64_t i = gtid(); i < P; i += gstride()) {
     int32_t a = 0, b = 0;  // s_t, s_{t-1}
     for (int64_t t = 0; t < T; ++t) {
@@ -154,7 +156,8 @@ __global__ void k_linear_addback(int32_t* __restrict__ res, int64_t P, int64_t T
       if (t == 0) rc = d;
       else if (t == 1) rc = sat_add_i32(a, d);
       else rc = sat_add_i32(sat_add_i32(a, sat_sub_i32(a, b)), d);
-      res[t * P + i] = rc;
+      if (f32out) __stcs(f32out + t * P + i, q823_to_f32(rc));
+      else res[t * P + i] = rc;
       b = a;
       a = rc;
     }
@@ -219,17 +222,18 @@ __global__ void __launch_bounds__(kThreads) k_hpc_encode_all(const float* __rest
 // Whole-trajectory EB decode + LinearPredictor add-back: codes [T, P] ->
 // Q8.23 reconstructions [T, P] (the chain kept in registers).
 __global__ void __launch_bounds__(kThreads) k_eb_decode_all(const int16_t* __restrict__ codes,
-                                                            int32_t* __restrict__ out, int64_t P, int64_t T,
-                                                            const float* __restrict__ scales) {
+                                                            int32_t* __restrict__ out, float* __restrict__ f32out,
+                                                            int64_t P, int64_t T, const float* __restrict__ scales) {
   for (int64_t i = gtid(); i < P; i += gstride()) {
     int32_t a = 0, b = 0;
     for (int64_t t = 0; t < T; ++t) {
-      const int32_t d = q823_from_f32(NGL_FMUL((float)codes[t * P + i], scales[t]));
+      const int32_t d = q823_from_f32(NGL_FMUL((float)__ldcs(codes + t * P + i), scales[t]));
       int32_t rc;
       if (t == 0) rc = d;
       else if (t == 1) rc = sat_add_i32(a, d);
       else rc = sat_add_i32(sat_add_i32(a, sat_sub_i32(a, b)), d);
-      out[t * P + i] = rc;
+      if (f32out) __stcs(f32out + t * P + i, q823_to_f32(rc));
+      else out[t * P + i] = rc;
       b = a;
       a = rc;
     }
@@ -245,8 +249,8 @@ cudaError_t hpc_encode_all(const float* x, int16_t* codes, uint32_t* maxerr_bits
   return cudaGetLastError();
 }
 cudaError_t eb_decode_all(const int16_t* codes, int32_t* out, int64_t P, int64_t T, const float* scales,
-                          cudaStream_t s) {
-  if (P > 0 && T > 0) k_eb_decode_all<<<grid_for(P, 1), kThreads, 0, s>>>(codes, out, P, T, scales);
+                          cudaStream_t s, float* f32out) {
+  if (P > 0 && T > 0) k_eb_decode_all<<<grid_for(P, 1), kThreads, 0, s>>>(codes, out, f32out, P, T, scales);
   return cudaGetLastError();
 }
 
@@ -266,8 +270,9 @@ cudaError_t hpc_step(const float* x, const int32_t* s_t, const int32_t* s_tm1, i
     k_hpc_step<<<grid_for(n, 4), kThreads, 0, s>>>(x, s_t, s_tm1, hist, scale, codes, recon, maxerr_bits, n, vec);
   return cudaGetLastError();
 }
-cudaError_t linear_addback(int32_t* res, int64_t particles, int64_t steps, cudaStream_t s) {
-  if (particles > 0 && steps > 0) k_linear_addback<<<grid_for(particles, 1), kThreads, 0, s>>>(res, particles, steps);
+cudaError_t linear_addback(int32_t* res, int64_t particles, int64_t steps, cudaStream_t s, float* f32out) {
+  if (particles > 0 && steps > 0)
+    k_linear_addback<<<grid_for(particles, 1), kThreads, 0, s>>>(res, f32out, particles, steps);
   return cudaGetLastError();
 }
 

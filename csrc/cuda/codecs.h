@@ -41,12 +41,14 @@ cudaError_t hpc_step(const float* x, const int32_t* s_t, const int32_t* s_tm1, i
 // registers; codes [T, P].  Identical codes to T calls of hpc_step.
 cudaError_t hpc_encode_all(const float* x, int16_t* codes, uint32_t* maxerr_bits, int64_t P, int64_t T, float scale,
                            cudaStream_t s);
-// EB decode of codes [T, P] with the add-back chain -> Q8.23 values [T, P].
+// EB decode of codes [T, P] with the add-back chain -> Q8.23 values [T, P]
+// in `out`, or (f32out != nullptr) their fp32 conversions in f32out.
 cudaError_t eb_decode_all(const int16_t* codes, int32_t* out, int64_t P, int64_t T, const float* scales,
-                          cudaStream_t s);
-// Linear predictor add-back over T decoded residual snapshots (in place):
-// recon_t = pred_t + res_t with the predictor's history chain.
-cudaError_t linear_addback(int32_t* res, int64_t particles, int64_t steps, cudaStream_t s);
+                          cudaStream_t s, float* f32out = nullptr);
+// Linear predictor add-back over T decoded residual snapshots:
+// recon_t = pred_t + res_t with the predictor's history chain, in place, or
+// (f32out != nullptr) as fp32 values in f32out.
+cudaError_t linear_addback(int32_t* res, int64_t particles, int64_t steps, cudaStream_t s, float* f32out = nullptr);
 
 // ---- Mask packers (BlockSparse, top-k compat) with decoupled look-back ----
 // BlockSparse from i16 codes: [u32 n] then per 32-block [u32 mask][i16 per
