@@ -1,7 +1,9 @@
 from .fused import CommError, FusedAllReduce, autotune_twoshot, payload_bytes, topk_per_block
 from .hook import HookConfig, NangilaHookState, register_nangila_hook
+from .monitor import RankMonitor
 
 __all__ = [
+    "RankMonitor",
     "CommError",
     "FusedAllReduce",
     "HookConfig",

@@ -176,6 +176,11 @@ def _fused_hook(hs: NangilaHookState, bucket):
     cfg = hs.config
     buf = bucket.buffer()
     bidx = bucket.index()
+    # A launch that gave up (a peer's flag never came, a tag mismatch) left
+    # its bucket unreduced; its status reaches the host asynchronously.
+    st_code = hs.comm.poll_status()
+    if st_code != 0:
+        hs.comm.check()  # synchronizes and raises CommError with the details
     st, first = _get_state(hs, bidx, buf, _bucket_sig(bucket), cfg.use_momentum, cfg.error_feedback)
     hs.calls += 1
     if getattr(hs, "autotune_pending", False):

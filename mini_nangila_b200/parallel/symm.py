@@ -46,3 +46,21 @@ class SymmetricRegion:
             dist.barrier(group=self.group)
         self._region.close()
         self._region = None
+
+    def unmap_peers(self) -> None:
+        """Local, no collective: stop addressing the peers' regions (a peer
+        is leaving or has left); this rank's own region stays allocated."""
+        if self._region is None:
+            return
+        torch.cuda.synchronize(self.device)
+        self._region.close_peers()
+
+    def free_local(self) -> None:
+        """Local, no collective: free this rank's region.  Only once every
+        peer has unmapped it (see RankMonitor)."""
+        if self._region is None:
+            return
+        torch.cuda.synchronize(self.device)
+        self._region.close_peers()
+        self._region.close()
+        self._region = None

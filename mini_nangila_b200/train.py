@@ -68,6 +68,7 @@ class DDPTrainer:
         autocast_dtype: torch.dtype | None = torch.bfloat16,
         device: torch.device | None = None,
         fused_optimizer: bool = True,
+        monitor: bool = False,
     ):
         self.device = device or (torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available()
                                  else torch.device("cpu"))
@@ -83,6 +84,13 @@ class DDPTrainer:
             self.hook_state = register_nangila_hook(self.ddp, **hk)
         elif hook != "nccl":
             raise ValueError(f"unknown hook {hook!r}")
+        self.steps_done = 0
+        self.monitor = None
+        if monitor:
+            from .parallel.monitor import RankMonitor
+
+            comm = getattr(self.hook_state, "comm", None) if self.hook_state is not None else None
+            self.monitor = RankMonitor(comms=[comm] if comm is not None else [])
         use_fused = fused_optimizer and self.device.type == "cuda"
         self.opt = torch.optim.AdamW(self.ddp.parameters(), lr=lr, fused=use_fused)
         self.autocast_dtype = autocast_dtype if self.device.type == "cuda" else None
@@ -92,6 +100,8 @@ class DDPTrainer:
         return self.ddp.module
 
     def step(self, x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
+        if self.monitor is not None:
+            self.monitor.check(self.steps_done)  # a peer that left is noticed before any launch
         with nvtx_range("forward"):
             if self.autocast_dtype is not None:
                 with torch.autocast(self.device.type, dtype=self.autocast_dtype):
@@ -103,6 +113,7 @@ class DDPTrainer:
             loss.backward()
         with nvtx_range("optimizer"):
             self.opt.step()
+        self.steps_done += 1
         return loss.detach()
 
     def step_host(self, x_host: torch.Tensor, y_host: torch.Tensor) -> float:

@@ -223,3 +223,61 @@ def test_nccl_variant_is_the_plain_allreduce(tmp_path):
     p0, p1 = torch.load(tmp_path / "p0.pt"), torch.load(tmp_path / "p1.pt")
     assert torch.equal(p0["nccl"], p1["nccl"])
     assert torch.allclose(p0["nccl"], p0["None"], atol=1e-6)
+
+
+def _leave_worker(rank, world, port, outdir, crash):
+    dist = _init(rank, world, port, timeout_s=30)
+    try:
+        from mini_nangila_b200.models import GPT2, GPT2Config
+        from mini_nangila_b200.parallel.fused import CommError
+        from mini_nangila_b200.train import DDPTrainer
+
+        torch.manual_seed(0)
+        cfg = GPT2Config.tiny()
+        tr = DDPTrainer(GPT2(cfg), hook="host", hook_kwargs=dict(use_momentum=True, seed=5),
+                        device=torch.device("cpu"), bucket_cap_mb=0.05, monitor=True)
+        tr.monitor.timeout_s = 5.0
+        g = torch.Generator().manual_seed(100 + rank)
+        msg = "none"
+        for step in range(3):
+            if rank == 1 and step == 1:
+                if crash:
+                    os._exit(0)  # no announcement: the others see silence
+                ok = tr.monitor.leave("test leave")
+                open(os.path.join(outdir, "f1.txt"), "w").write(f"left ack={ok}")
+                return
+            t = torch.randint(0, cfg.vocab_size, (2, 17), generator=g)
+            try:
+                tr.step(t[:, :-1], t[:, 1:])
+            except CommError as e:
+                msg = str(e)
+                break
+        open(os.path.join(outdir, f"f{rank}.txt"), "w").write(msg)
+    finally:
+        if not (crash and rank == 1):
+            dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("crash", [False, True])
+def test_rank_leaving_between_steps_is_noticed_before_the_next_launch(crash, tmp_path):
+    """A rank that leaves between steps announces it in the store (or crashes
+    and stays silent); the survivor raises CommError naming it before the
+    next step's collectives, instead of waiting in one."""
+    import time as _t
+
+    ctx = mp.get_context("spawn")
+    port = _port()
+    ps = [ctx.Process(target=_leave_worker, args=(r, 2, port, str(tmp_path), crash)) for r in range(2)]
+    t0 = _t.time()
+    for p in ps:
+        p.start()
+    for p in ps:
+        p.join(120)
+    for p in ps:
+        if p.is_alive():
+            p.kill()
+    msg = (tmp_path / "f0.txt").read_text()
+    assert "rank 1" in msg and ("left (test leave)" in msg if not crash else "silent" in msg), msg
+    if not crash:
+        assert (tmp_path / "f1.txt").read_text() == "left ack=True"
+    assert _t.time() - t0 < 100

@@ -100,3 +100,66 @@ def test_fused_allreduce_matches_oracle_across_ranks(world, tmp_path):
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     mp.start_processes(_worker, args=(world, _port(), cases, err), nprocs=world, join=True, start_method="spawn")
     assert not os.path.exists(err) or open(err).read() == ""
+
+
+def _leave_worker(rank, world, port, errfile, outdir):
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        from mini_nangila_b200.models import GPT2, GPT2Config
+        from mini_nangila_b200.parallel.fused import CommError
+        from mini_nangila_b200.train import DDPTrainer
+
+        torch.manual_seed(0)
+        cfg = GPT2Config.tiny()
+        tr = DDPTrainer(GPT2(cfg), hook="fused", hook_kwargs=dict(use_momentum=True, seed=5, timeout_s=5.0),
+                        device=dev, bucket_cap_mb=0.05, monitor=True)
+        tr.monitor.timeout_s = 10.0
+        g = torch.Generator().manual_seed(100 + rank)
+        msg = "none"
+        for step in range(3):
+            if rank == 1 and step == 2:
+                torch.cuda.synchronize()  # none of this rank's kernels in flight
+                ok = tr.monitor.leave("test leave")
+                open(os.path.join(outdir, "f1.txt"), "w").write(f"left ack={ok}")
+                return
+            t = torch.randint(0, cfg.vocab_size, (2, 17), generator=g).to(dev)
+            try:
+                tr.step(t[:, :-1], t[:, 1:])
+                torch.cuda.synchronize()
+            except CommError as e:
+                msg = str(e)
+                break
+        tr.hook_state.comm.check()  # no launch gave up
+        open(os.path.join(outdir, f"f{rank}.txt"), "w").write(msg)
+    except Exception as e:
+        with open(errfile, "a") as fh:
+            fh.write(f"{type(e).__name__}: {e}\n")
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+def test_rank_leaving_between_steps_fused(tmp_path):
+    """Two ranks with the fused hook: rank 1 leaves between steps; rank 0
+    notices in the store before launching, unmaps rank 1's region and
+    acknowledges, rank 1 then frees it.  NVLS is off; nothing waits on the
+    departed rank on the device."""
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    err = str(tmp_path / "err.txt")
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    mp.start_processes(_leave_worker, args=(2, _port(), err, str(tmp_path)), nprocs=2, join=True,
+                       start_method="spawn")
+    assert not os.path.exists(err) or open(err).read() == ""
+    assert "rank 1 left (test leave)" in (tmp_path / "f0.txt").read_text()
+    assert (tmp_path / "f1.txt").read_text() == "left ack=True"
