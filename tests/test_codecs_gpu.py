@@ -155,3 +155,27 @@ def test_nz_pipeline_device_matches_host(codec, P, T, eps):
     host_vals = nzcp.decompress(hb)
     dev_vals = trajectory.decompress(hb).cpu().numpy().reshape(-1)
     assert np.array_equal(dev_vals.view(np.uint32), host_vals.view(np.uint32))
+
+
+@pytest.mark.parametrize("eps", [1e-3, 5e-7, 0.05, 1.5, 3e-5, 1e-35])
+def test_eb_codes_match_host_at_near_ties(eps):
+    """Device EB codes equal the host library's on quotients placed at and
+    around half-integers (where round-half-away after the f32 division
+    decides), across the clamp boundary, and on random residuals."""
+    from mini_nangila_b200 import _ext
+
+    h, c = _ext.host(), _ext.cuda()
+    g = np.random.default_rng(int(eps * 1e9) % 1000)
+    s = float(np.float32(2.0) * np.float32(eps))
+    k = g.integers(-45000, 45000, 300000).astype(np.float64)
+    d = g.integers(-12, 13, k.size).astype(np.float64)
+    v = (k + 0.5) * s + d * 2.0 ** -23  # near-ties, a few Q8.23 steps apart
+    r_near = np.clip(np.round(v * 2.0 ** 23), -2 ** 31, 2 ** 31 - 1).astype(np.int32)
+    r_rand = g.integers(-2 ** 31, 2 ** 31 - 1, 300000, dtype=np.int64).astype(np.int32)
+    r_small = g.integers(-2 ** 16, 2 ** 16, 300000).astype(np.int32)
+    for r in (r_near, r_rand, r_small):
+        hb, _ = h.eb_quantize(r, float(np.float32(eps)))
+        host = np.frombuffer(bytes(hb), dtype="<i2")
+        dev = c.eb_codes(torch.from_numpy(r).cuda(), s).cpu().numpy()
+        bad = np.flatnonzero(host != dev)
+        assert bad.size == 0, (bad[:5], r[bad[:5]], host[bad[:5]], dev[bad[:5]])
