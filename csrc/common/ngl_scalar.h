@@ -110,25 +110,53 @@ NGL_HD int8_t sat_f32_to_i8(float x) {
 // FixedPointBuffer::from_f32 element (fixed_point.rs:34-53).
 NGL_HD int32_t q823_from_f32(float v) {
   float s = NGL_FMUL(v, kQScale);
+#if defined(__CUDA_ARCH__)
+  // roundf (half away from zero), then a saturating conversion: >= 2^31 ->
+  // INT32_MAX, <= -2^31 -> INT32_MIN, NaN -> 0, the same cases as below.
+  int32_t r;
+  asm("cvt.rzi.sat.s32.f32 %0, %1;" : "=r"(r) : "f"(roundf(s)));
+  return r;
+#else
   if (s >= 2147483648.0f) return INT32_MAX;   // i32::MAX as f32 == 2^31
   if (s <= -2147483648.0f) return INT32_MIN;
   if (is_nan(s)) return 0;
   return (int32_t)f_round(s);                 // half away from zero
+#endif
 }
-// FixedPointBuffer::to_f32 element (fixed_point.rs:56-60).
-NGL_HD float q823_to_f32(int32_t q) { return NGL_FDIV((float)q, kQScale); }
+// FixedPointBuffer::to_f32 element (fixed_point.rs:56-60): q / 2^23.  On the
+// device as q * 2^-23: a power-of-two scale of (float)q (0 or |.| >= 1) is
+// exact, so the product equals the quotient bit for bit.
+NGL_HD float q823_to_f32(int32_t q) {
+#if defined(__CUDA_ARCH__)
+  return __fmul_rn((float)q, 1.1920928955078125e-07f);
+#else
+  return NGL_FDIV((float)q, kQScale);
+#endif
+}
 
 NGL_HD int32_t sat_add_i32(int32_t a, int32_t b) {
+#if defined(__CUDA_ARCH__)
+  int32_t r;
+  asm("add.sat.s32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+#else
   int64_t s = (int64_t)a + (int64_t)b;
   if (s > INT32_MAX) return INT32_MAX;
   if (s < INT32_MIN) return INT32_MIN;
   return (int32_t)s;
+#endif
 }
 NGL_HD int32_t sat_sub_i32(int32_t a, int32_t b) {
+#if defined(__CUDA_ARCH__)
+  int32_t r;
+  asm("sub.sat.s32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+#else
   int64_t s = (int64_t)a - (int64_t)b;
   if (s > INT32_MAX) return INT32_MAX;
   if (s < INT32_MIN) return INT32_MIN;
   return (int32_t)s;
+#endif
 }
 // mul_scalar's fixed-point scalar: (s * 2^23) as i64 (ops.rs:38).
 NGL_HD int64_t q823_scalar_fixed(float s) { return sat_f32_to_i64(NGL_FMUL(s, kQScale)); }
