@@ -22,13 +22,20 @@
 //            residual as INT8 with per-block scales and pushes that record
 //            to every rank
 //   phase C  every rank decodes the owners' INT8 records
+// single rank (world 1)
+//   encode and decode in registers; whole chunks of the gradient, predictor
+//   and EF arrive in shared memory by cp.async.bulk on an mbarrier, one
+//   chunk ahead (dense modes)
+// Chunks chosen as topology passengers are neither encoded nor sent; they
+// reconstruct to the prediction and keep their residual as error feedback.
 //
 // The reference does this work as ~20 eager PyTorch ops, five NCCL
 // all_gathers and nine host syncs per bucket
 // (python/nangila_ddp/comm_hook.py:125-324).
 //
-// Every peer access is a plain global load/store through an IPC mapping:
-// there is no TMA and no multicast in this file.  Every wait is bounded and
+// Every peer access is a plain global load/store through an IPC mapping.
+// The only bulk copies (the single-rank prefetch) read this GPU's own
+// memory; nothing in this file multicasts.  Every wait is bounded and
 // reports through the status word instead of trapping.
 #include "fused.h"
 #include "ngl_cuda.cuh"
