@@ -113,7 +113,7 @@ def main():
     args = ap.parse_args()
     torch.cuda.set_device(0)
     from mini_nangila_b200 import _ext
-    from mini_nangila_b200.parallel.fused import FusedAllReduce, payload_bytes
+    from mini_nangila_b200.parallel.fused import FusedAllReduce
 
     c = _ext.cuda()
     n, dev = args.n, torch.device("cuda")

@@ -6,7 +6,6 @@ per ``ITEM: TIMESTEP`` block, locating the x/y/z columns by name.
 """
 from __future__ import annotations
 
-import math
 
 import numpy as np
 

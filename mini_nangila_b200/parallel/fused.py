@@ -21,7 +21,6 @@ reduction with eager ops and five ``all_gather`` calls.
 """
 from __future__ import annotations
 
-import math
 import zlib
 from dataclasses import dataclass
 

@@ -9,7 +9,7 @@ from mini_nangila_b200.checkpoint import lammps, nzcp
 from mini_nangila_b200.core import FixedPointBuffer, QuantizationMode, UnifiedQuantizer
 from mini_nangila_b200.hpc import BlockSparseQuantizer, BlockSparseRleQuantizer, ErrorBoundedQuantizer, \
     RunLengthQuantizer
-from mini_nangila_b200.ops import codecs, trajectory
+from mini_nangila_b200.ops import trajectory
 
 pytestmark = pytest.mark.gpu
 

@@ -3,7 +3,6 @@ counters and Box-Muller transform (float64 math; the device uses CUDA's
 float32 log/sqrt/sincospi, so values agree to float32 rounding)."""
 import numpy as np
 import pytest
-import torch
 
 pytestmark = pytest.mark.gpu
 

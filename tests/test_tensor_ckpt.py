@@ -2,7 +2,6 @@
 path is checked for identical bytes in test_tensor_ckpt_gpu)."""
 import io
 
-import numpy as np
 import pytest
 import torch
 
