@@ -123,6 +123,7 @@ def main():
     args = parse()
     from mini_nangila_b200.train import DDPTrainer, init_distributed
     from mini_nangila_b200.utils import ClockSampler, barrier_sync, max_over_ranks
+    from mini_nangila_b200.workloads import GPT2SmallDDP, Llama1BTopK
 
     rank, world, local = init_distributed("nccl", timeout_s=300)
     device = torch.device("cuda", local)
@@ -131,14 +132,16 @@ def main():
     if args.model == "gpt2":
         from mini_nangila_b200.models import GPT2, GPT2Config
 
+        w = GPT2SmallDDP()
         mcfg = GPT2Config.small()
-        vocab, mb, seq = mcfg.vocab_size, args.micro_batch or 8, args.seq or 1024
+        vocab, mb, seq = mcfg.vocab_size, args.micro_batch or w.micro_batch, args.seq or w.seq
         model_name = "gpt2-small-124M"
     else:
         from mini_nangila_b200.models import Llama, LlamaConfig
 
+        w = Llama1BTopK()
         mcfg = LlamaConfig.b1_1()
-        vocab, mb, seq = mcfg.vocab_size, args.micro_batch or 4, args.seq or 2048
+        vocab, mb, seq = mcfg.vocab_size, args.micro_batch or w.micro_batch, args.seq or w.seq
         model_name = "llama-1.1B"
 
     quiet = contextlib.redirect_stdout(open(os.devnull, "w")) if args.impl == "reference" else contextlib.nullcontext()
