@@ -204,12 +204,26 @@ def main():
             import time
 
             t0 = time.perf_counter()
-            for i in range(args.steps):
-                x, y = host_batches[i % len(host_batches)]
-                if trainer is not None:
-                    trainer.step_host(x, y)
-                else:
-                    float(step_fn(x.to(device, non_blocking=True), y.to(device, non_blocking=True)).item())
+            seq_batches = [host_batches[i % len(host_batches)] for i in range(args.steps)]
+            if trainer is not None:
+                # every step: pinned H2D copy of its batch and a D2H read of its
+                # loss, read one step late so the host does not wait in between
+                losses = trainer.train_steps(seq_batches)
+            else:
+                losses, pending = [], None
+                for x, y in seq_batches:
+                    loss = step_fn(x.to(device, non_blocking=True), y.to(device, non_blocking=True))
+                    out = torch.empty((), dtype=loss.dtype, pin_memory=True)
+                    out.copy_(loss, non_blocking=True)
+                    ev = torch.cuda.Event()
+                    ev.record()
+                    if pending is not None:
+                        pending[1].synchronize()
+                        losses.append(float(pending[0]))
+                    pending = (out, ev)
+                pending[1].synchronize()
+                losses.append(float(pending[0]))
+            assert len(losses) == args.steps
             barrier_sync(device)
             e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1000.0, device)
             xb, yb = host_batches[0]

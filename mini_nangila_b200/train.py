@@ -121,6 +121,41 @@ class DDPTrainer:
         y = y_host.to(self.device, non_blocking=True)
         return float(self.step(x, y).item())
 
+    def step_host_async(self, x_host: torch.Tensor, y_host: torch.Tensor):
+        """One step from pinned host tensors without waiting for it: the
+        batch is copied to the device, the step is queued, and its loss is
+        copied back into pinned host memory.  Returns ``(loss, event)``;
+        ``event.synchronize()`` then ``float(loss)`` reads it, typically
+        after the next step has been queued (``train_steps`` does this)."""
+        x = x_host.to(self.device, non_blocking=True)
+        y = y_host.to(self.device, non_blocking=True)
+        loss = self.step(x, y)
+        if self.device.type != "cuda":
+            return loss.detach().clone(), None
+        out = torch.empty((), dtype=loss.dtype, pin_memory=True)
+        out.copy_(loss, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        return out, ev
+
+    def train_steps(self, batches_host) -> list[float]:
+        """Run one step per (x, y) pinned host batch, reading every step's loss
+        one step late, so the host never waits for the step in flight."""
+        losses: list[float] = []
+        pending = None
+        for x_host, y_host in batches_host:
+            cur = self.step_host_async(x_host, y_host)
+            if pending is not None:
+                if pending[1] is not None:
+                    pending[1].synchronize()
+                losses.append(float(pending[0]))
+            pending = cur
+        if pending is not None:
+            if pending[1] is not None:
+                pending[1].synchronize()
+            losses.append(float(pending[0]))
+        return losses
+
     def kernel_launches(self) -> int:
         hs = self.hook_state
         if hs is not None and getattr(hs, "comm", None) is not None:
