@@ -150,8 +150,10 @@ __global__ void k_hpc_step(const float* __restrict__ x, const int32_t* __restric
 __global__ void k_linear_addback(int32_t* __restrict__ res, float* __restrict__ f32out, int64_t P, int64_t T) {
   for (int64_t i = gtid(); i < P; i += gstride()) {
     int32_t a = 0, b = 0;  // s_t, s_{t-1}
+    int32_t nxt = T > 0 ? res[i] : 0;
     for (int64_t t = 0; t < T; ++t) {
-      const int32_t d = res[t * P + i];
+      const int32_t d = nxt;  // loaded one step ahead
+      if (t + 1 < T) nxt = res[(t + 1) * P + i];
       int32_t rc;
       if (t == 0) rc = d;
       else if (t == 1) rc = sat_add_i32(a, d);
@@ -1055,7 +1057,8 @@ __global__ void __launch_bounds__(kThreads) k_walk_bsrle(const uint8_t* __restri
   }
 }
 
-// Expansion: one warp per descriptor; lanes write elements.
+// Expansion of element-RLE descriptors: one warp per descriptor; lanes write
+// elements.
 __global__ void k_expand(int kind, const uint8_t* __restrict__ data, const int64_t* __restrict__ soff,
                          const float* __restrict__ scales, int nstreams, int32_t* __restrict__ out, int64_t out_cap,
                          const int64_t* __restrict__ out_len, const int64_t* __restrict__ table, int64_t table_cap) {
@@ -1100,6 +1103,63 @@ __global__ void k_expand(int kind, const uint8_t* __restrict__ data, const int64
               const int16_t c = (int16_t)((uint16_t)b[p] | ((uint16_t)b[p + 1] << 8));
               v = q823_from_f32(NGL_FMUL((float)c, sc));
             }
+          }
+        }
+        dst[o + lane] = v;
+      }
+    }
+  }
+}
+
+// Block descriptors (BlockSparse, top-k compat, BlockSparse+RLE): one warp
+// per 32 consecutive descriptors of a stream.  Every lane first loads one
+// descriptor and its mask (32 independent loads in flight), then the warp
+// writes the 32 blocks in turn, coalesced, with each block's descriptor
+// broadcast by shuffle; the value loads of successive blocks pipeline.
+__global__ void __launch_bounds__(kThreads) k_expand_blocks(int kind, const uint8_t* __restrict__ data,
+                                                            const int64_t* __restrict__ soff,
+                                                            const float* __restrict__ scales, int nstreams,
+                                                            int32_t* __restrict__ out, int64_t out_cap,
+                                                            const int64_t* __restrict__ out_len,
+                                                            const int64_t* __restrict__ table, int64_t table_cap) {
+  const int lane = threadIdx.x & 31;
+  const int vb = kind == 1 ? 1 : 2;
+  const int64_t groups = (table_cap + 31) / 32;
+  const int64_t wid = gtid() >> 5, nw = gstride() >> 5;
+  const uint32_t lt = (1u << lane) - 1u;
+  for (int64_t gi = wid; gi < (int64_t)nstreams * groups; gi += nw) {
+    const int64_t sidx = gi / groups, g0 = (gi - sidx * groups) * 32;
+    const int64_t* row = table + sidx * (2 * table_cap + 2);
+    const int64_t count = row[0];
+    if (g0 >= count) continue;  // uniform across the warp
+    const int nd = (int)min64(32, count - g0);
+    const uint8_t* b = data + soff[sidx];
+    const int64_t len = soff[sidx + 1] - soff[sidx];
+    const float sc = scales[sidx];
+    const int64_t lim = min64(out_len[sidx], out_cap);
+    int32_t* dst = out + sidx * out_cap;
+    long long w0 = 0, in1 = 0;
+    uint32_t m = 0;
+    if (lane < nd) {
+      const longlong2 dd = reinterpret_cast<const longlong2*>(row + 2)[g0 + lane];
+      w0 = dd.x;
+      in1 = dd.y;
+      if (in1) m = rd_u32(b + in1 - 1);
+    }
+    for (int d = 0; d < nd; ++d) {
+      const long long wd = __shfl_sync(kFull, w0, d);
+      const long long id = __shfl_sync(kFull, in1, d);
+      const uint32_t md = __shfl_sync(kFull, m, d);
+      const int64_t o = wd & ((1ll << 48) - 1), l = (int64_t)((unsigned long long)wd >> 48);
+      if (lane < l && o + lane < lim) {
+        int32_t v = 0;
+        if (id && ((md >> lane) & 1u)) {
+          const int64_t p = id - 1 + 4 + (int64_t)vb * __popc(md & lt);
+          if (kind == 1) {
+            if (p < len) v = q823_from_f32(NGL_FMUL((float)(int8_t)b[p], sc));
+          } else if (p + 2 <= len) {
+            const int16_t c = (int16_t)((uint16_t)b[p] | ((uint16_t)b[p + 1] << 8));
+            v = q823_from_f32(NGL_FMUL((float)c, sc));
           }
         }
         dst[o + lane] = v;
@@ -1377,6 +1437,15 @@ cudaError_t stream_decode(int kind, const uint8_t* data, const int64_t* stream_o
   if (e != cudaSuccess) return e;
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
+  if (kind != 3) {  // block descriptors: 32 per warp
+    const int64_t warps = (int64_t)nstreams * ((table_cap + 31) / 32);
+    int64_t g = (warps * 32 + kThreads - 1) / kThreads;
+    if (g > 148 * 32) g = 148 * 32;
+    if (g < 1) g = 1;
+    k_expand_blocks<<<(unsigned)g, kThreads, 0, s>>>(kind, data, stream_off, scales, nstreams, out, out_cap, out_len,
+                                                     table, table_cap);
+    return cudaGetLastError();
+  }
   const int64_t warps = (int64_t)nstreams * table_cap;
   int64_t g = (warps * 32 + kThreads - 1) / kThreads;
   if (g > 148 * 32) g = 148 * 32;
