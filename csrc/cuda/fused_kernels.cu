@@ -263,6 +263,73 @@ __device__ __forceinline__ void finalize(T* grad, float* pred, int64_t n, int bl
 }
 
 // --------------------------------------------------------------- top-k warp
+// Warp sums of |{m >= c1}|, |{m >= c2}|, |{m >= c3}| over the block, as
+// three 10-bit fields of one word (each count is at most 256).
+__device__ __forceinline__ uint32_t count_ge3(const uint32_t (&m)[8], uint32_t c1, uint32_t c2, uint32_t c3) {
+  uint32_t l = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    l += (uint32_t)(m[j] >= c1) | ((uint32_t)(m[j] >= c2) << 10) | ((uint32_t)(m[j] >= c3) << 20);
+  return __reduce_add_sync(kFull, l);
+}
+
+// Selection threshold of one 256-block from the |c| bit patterns m (bit 31
+// clear, so the unsigned order is the order of |c|; NaN sorts above inf):
+// either the keff-th largest pattern, or a T with exactly keff patterns
+// >= T.  Both keep the same set as the host's bitwise search for the
+// largest T with |{m >= T}| >= keff, after the tie handling of the caller.
+//
+// Bracket search: lo always has |{m >= lo}| >= keff and hi has fewer.  The
+// first round tests three patterns half a binade, one and two binades
+// below the block maximum M together (three counts in one warp sum): the
+// kept fraction of a gradient block mostly lies there, so one round
+// narrows [0, M] to a quarter binade.  Later rounds split [lo, hi) in four
+// the same way, until hi = lo + 1 or exactly keff patterns are >= lo.
+// This takes about 4-6 dependent warp sums on gradient blocks instead of
+// the ~14 of a bit-at-a-time search.
+__device__ __forceinline__ uint32_t topk_threshold_bits(const uint32_t (&m)[8], int keff) {
+  if (keff <= 0) return 0xffffffffu;  // nothing is >= it: no element kept
+  uint32_t mx = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) mx = max(mx, m[j]);
+  const uint32_t M = __reduce_max_sync(kFull, mx);
+  uint32_t lo = 0, hi = M + 1;  // M <= 0x7fffffff
+  bool first = true;
+  while (hi - lo > 1) {
+    uint32_t c1, c2, c3;
+    if (first) {
+      c3 = M > (1u << 22) ? M - (1u << 22) : 0u;
+      c2 = M > (1u << 23) ? M - (1u << 23) : 0u;
+      c1 = M > (2u << 23) ? M - (2u << 23) : 0u;
+      first = false;
+    } else {
+      const uint32_t d = hi - lo;
+      c1 = lo + (d >> 2);
+      c2 = lo + (d >> 1);  // lo < c2 < hi: every round makes progress
+      c3 = hi - (d >> 2);
+    }
+    const uint32_t s = count_ge3(m, c1, c2, c3);
+    const int n1 = (int)(s & 1023u), n2 = (int)((s >> 10) & 1023u), n3 = (int)(s >> 20);
+    int nlo = -1;
+    if (n3 >= keff) {
+      lo = c3;
+      nlo = n3;
+    } else if (n2 >= keff) {
+      lo = c2;
+      hi = c3;
+      nlo = n2;
+    } else if (n1 >= keff) {
+      lo = c1;
+      hi = c2;
+      nlo = n1;
+    } else {
+      hi = c1;
+    }
+    if (nlo == keff) break;
+  }
+  return lo;
+}
+
 struct TopkSel {
   float s;
   uint32_t selmask;  // bit j: element j of this lane kept
@@ -280,20 +347,7 @@ __device__ __forceinline__ TopkSel topk_select(const float (&c)[8], int valid, i
   uint32_t m[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) m[j] = __float_as_uint(fabsf(c[j]));
-  // Largest T with |{j : m_j >= T}| >= keff, one bit at a time (MSB first;
-  // bit 31 of |x| is clear).  Once exactly keff elements are >= T the kept
-  // set is {m >= T} whatever the lower bits, so the search stops there (the
-  // tie handling below then keeps all of them).
-  uint32_t T = 0;
-  for (int bit = 30; bit >= 0; --bit) {
-    const uint32_t cand = T | (1u << bit);
-    int cnt = 0;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) cnt += (m[j] >= cand);
-    cnt = (int)__reduce_add_sync(kFull, (unsigned)cnt);
-    if (cnt >= keff) T = cand;
-    if (cnt == keff) break;
-  }
+  const uint32_t T = topk_threshold_bits(m, keff);
   int gt = 0, eq = 0;
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
