@@ -139,6 +139,26 @@ PYBIND11_MODULE(_host, m) {
     return to_np(std::move(f));
   });
   m.def("lammps_generate_synthetic", [](size_t p, size_t s) { return to_np(lammps_generate_synthetic(p, s)); });
+  m.def("lammps_read_dump", [](const std::string& path) {
+    std::vector<Floats> snaps;
+    {
+      py::gil_scoped_release nogil;
+      snaps = lammps_read_dump(path);
+    }
+    py::list out;
+    for (auto& v : snaps) out.append(to_np(std::move(v)));
+    return out;
+  });
+  m.def("lammps_read_dump_text", [](py::bytes text) {
+    const std::string t = text;
+    py::list out;
+    for (auto& v : lammps_read_dump_text(t.data(), t.size())) out.append(to_np(std::move(v)));
+    return out;
+  });
+  m.def("lammps_write_dump", [](const std::string& path, size_t atoms, size_t steps) {
+    py::gil_scoped_release nogil;
+    lammps_write_dump(path, atoms, steps);
+  });
 
   // Product format oracle (chunked wire payloads)
   m.def("product_wire_bytes", &product_wire_bytes);

@@ -138,6 +138,14 @@ Floats nz_decompress(const uint8_t* b, size_t n, bool add_back);
 // Synthetic LAMMPS-like generator of the reference (main.rs:311-322).
 Floats lammps_generate_synthetic(size_t particles, size_t steps);
 
+// LAMMPS ASCII dump I/O (main.rs:324-419): one flattened [x0, y0, z0, x1, ...]
+// snapshot per ITEM: TIMESTEP block; std::runtime_error with the reference's
+// messages on malformed input.  The writer emits the reference's synthetic
+// dump (cos/sin/cos(0.5) of phase 0.1 t + 0.001 i, six decimals).
+std::vector<Floats> lammps_read_dump(const std::string& path);
+std::vector<Floats> lammps_read_dump_text(const char* text, size_t size);
+void lammps_write_dump(const std::string& path, size_t atoms, size_t steps);
+
 // ---- Product wire format (fused GPU all-reduce oracle) ----
 struct ProductParams {
   int bits = 4;            // 4 or 8

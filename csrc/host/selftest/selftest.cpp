@@ -2,16 +2,18 @@
 // and UndefinedBehaviorSanitizer): every codec on random inputs (round trip
 // within its bound), every decoder on random garbage and on truncations of
 // valid streams (no out-of-bounds access, no undefined arithmetic), the NZCP
-// container, TopologyMask bincode (including malformed input), and the
-// product-format oracle.  Exit status 0 and "selftest ok" on success.
+// container, TopologyMask bincode (including malformed input), the LAMMPS
+// dump reader (valid, truncated and random text), and the product-format
+// oracle.  Exit status 0 and "selftest ok" on success.
 //
 //   g++ -std=c++17 -O1 -g -fsanitize=address,undefined -fno-sanitize-recover=all \
 //       -fno-omit-frame-pointer -Icsrc csrc/host/codecs.cpp csrc/host/pipeline.cpp \
-//       csrc/host/product.cpp csrc/host/selftest/selftest.cpp -o selftest && ./selftest
+//       csrc/host/product.cpp csrc/host/lammps_io.cpp csrc/host/selftest/selftest.cpp -o selftest && ./selftest
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
 #include <random>
+#include <string>
 
 #include "../nangila_host.hpp"
 
@@ -152,6 +154,33 @@ int main() {
       Bytes g = garbage((size_t)(rng() % 200));
       try {
         (void)TopologyMask::from_bytes(g.data(), g.size());
+      } catch (const std::exception&) {
+      }
+    }
+  }
+  // LAMMPS dump reader: a valid dump, every truncation of it, random text
+  {
+    std::string d;
+    for (int t = 0; t < 2; ++t) {
+      d += "ITEM: TIMESTEP\n" + std::to_string(t) + "\nITEM: NUMBER OF ATOMS\n3\nITEM: BOX BOUNDS xx yy zz\n";
+      d += "0 10\n0 10\n0 10\nITEM: ATOMS id type z y x\n";
+      d += "1 1 0.5 -1e-3 inf\n2 1 +2. .25 1e40\n3 1 nan 7 -0\n";
+    }
+    std::vector<Floats> snaps = lammps_read_dump_text(d.data(), d.size());
+    CHECK(snaps.size() == 2 && snaps[0].size() == 9 && snaps[0][2] == 0.5f && snaps[0][0] == INFINITY);
+    for (size_t cut = 0; cut < d.size(); ++cut) {
+      try {
+        (void)lammps_read_dump_text(d.data(), cut);
+      } catch (const std::exception&) {
+      }
+    }
+    const char alphabet[] = "ITEM: TIMESTEPNUMBEROFATOMSBXyz0123456789.e+-\n \t";
+    for (int t = 0; t < 300; ++t) {
+      std::string g = t % 2 ? d.substr(0, (size_t)(rng() % d.size())) : std::string();
+      const size_t extra = (size_t)(rng() % 400);
+      for (size_t i = 0; i < extra; ++i) g += alphabet[rng() % (sizeof(alphabet) - 1)];
+      try {
+        (void)lammps_read_dump_text(g.data(), g.size());
       } catch (const std::exception&) {
       }
     }

@@ -6,10 +6,12 @@
     python -m mini_nangila_b200.apps.analyze twin client_metrics.csv [server_metrics.csv] [--plot]
     python -m mini_nangila_b200.apps.analyze entropy
     python -m mini_nangila_b200.apps.analyze checkpoint ckpt.h5 dataset
+    python -m mini_nangila_b200.apps.analyze baselines baseline_comparison.csv [--plot]
 
 The reference's plotting snippets (python/snippets/*.py,
-python/nangila_ddp/plot_*.py) as one CLI: prints a JSON summary; ``--plot``
-also writes the PNGs when matplotlib is installed.
+python/nangila_ddp/plot_*.py, benchmarks/plot_baselines.py) as one CLI:
+prints a JSON summary; ``--plot`` also writes the PNGs when matplotlib is
+installed.
 """
 from __future__ import annotations
 
@@ -23,7 +25,7 @@ from ..utils import analysis as A
 
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("kind", choices=["train", "metrics", "hpc", "twin", "entropy", "checkpoint"])
+    ap.add_argument("kind", choices=["train", "metrics", "hpc", "twin", "entropy", "checkpoint", "baselines"])
     ap.add_argument("files", nargs="*")
     ap.add_argument("--plot", action="store_true")
     a = ap.parse_args(argv)
@@ -53,6 +55,10 @@ def main(argv=None):
             out["plot"] = A.plot_series(t, r, "tick", "compression ratio", "rotor_net_ratio.png")
     elif a.kind == "entropy":
         out.update(A.entropy_reduction())
+    elif a.kind == "baselines":
+        out.update(A.summarize_baselines(a.files[0]))
+        if a.plot:
+            out["plot"] = A.plot_baselines(a.files[0], a.files[0].replace(".csv", ".png"))
     else:
         from ..checkpoint import hdf5
 

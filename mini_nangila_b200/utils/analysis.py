@@ -7,7 +7,9 @@ reference's: ``train_log.csv`` rows ``ts,step,loss,...``
 prefix (python/nangila_ddp/plot_metrics.py:6-21), HPC bench lines
 ``step N ratio R ... max_err E`` (python/snippets/plot_hpc_logs.py:6-17),
 twin metric CSVs with the tick first and the ratio last
-(python/snippets/plot_rotor_net.py:6-19)), numeric summaries of each, and
+(python/snippets/plot_rotor_net.py:6-19), the compression-baseline CSV of
+``apps/baselines`` (benchmarks/plot_baselines.py:8-16)), numeric summaries
+of each, and
 optional PNG plots when matplotlib is importable (it is optional: every
 summary works without it).  ``entropy_reduction`` restates the reference's
 entropy illustration (python/snippets/entropy_plot.py:5-33) as numbers: the
@@ -87,6 +89,13 @@ def load_tick_ratio_csv(path: str):
     return np.array(ticks, dtype=np.int64), np.array(ratios)
 
 
+def load_baseline_rows(path: str) -> list[dict]:
+    """OK rows with a nonzero size of a ``baseline_comparison.csv``."""
+    with open(path, newline="") as fh:
+        return [r for r in csv.DictReader(fh)
+                if r.get("status") == "OK" and r.get("compressed_bytes") not in (None, "", "0")]
+
+
 # ---------------------------------------------------------------- summaries
 def _stats(x: np.ndarray) -> dict:
     if x.size == 0:
@@ -117,6 +126,23 @@ def summarize_hpc(path: str) -> dict:
 def summarize_ticks(path: str) -> dict:
     t, r = load_tick_ratio_csv(path)
     return {"ticks": int(t.size), "ratio": _stats(r)}
+
+
+def summarize_baselines(path: str) -> dict:
+    """Per epsilon (empty for the general-purpose compressors): each tool's
+    ratio and throughput, and the best ratio."""
+    groups: dict = {}
+    for r in load_baseline_rows(path):
+        groups.setdefault(r.get("epsilon") or "", []).append(
+            {"tool": r["tool"], "ratio": _float(r["ratio"]), "MBps": _float(r["throughput_MBps"])})
+    return {eps or "general": {"tools": rs, "best_ratio": max(x["ratio"] for x in rs)} for eps, rs in groups.items()}
+
+
+def _float(s, default: float = 0.0) -> float:
+    try:
+        return float(s)
+    except (TypeError, ValueError):
+        return default
 
 
 def histogram_entropy(x: np.ndarray, bins: int = 100) -> float:
@@ -187,6 +213,32 @@ def plot_series(x, y, xlabel: str, ylabel: str, out: str) -> str:
     plt.xlabel(xlabel)
     plt.ylabel(ylabel)
     plt.grid(True, alpha=0.3)
+    fig.tight_layout()
+    fig.savefig(out)
+    plt.close(fig)
+    return out
+
+
+def plot_baselines(csv_path: str, out: str = "baseline_comparison.png") -> str:
+    """Ratio bars and throughput line per epsilon group, one panel each."""
+    plt = _plt()
+    groups: dict = {}
+    for r in load_baseline_rows(csv_path):
+        groups.setdefault(r.get("epsilon") or "", []).append(r)
+    if not groups:
+        raise RuntimeError(f"no OK rows in {csv_path}")
+    fig, axes = plt.subplots(len(groups), 1, figsize=(9, 4 * len(groups)), squeeze=False)
+    for ax, (eps, rs) in zip(axes[:, 0], groups.items()):
+        x = range(len(rs))
+        ax.bar(x, [_float(r["ratio"]) for r in rs], color="tab:blue", alpha=0.7, label="ratio")
+        ax2 = ax.twinx()
+        ax2.plot(x, [_float(r["throughput_MBps"]) for r in rs], color="tab:orange", marker="o", label="throughput")
+        ax.set_xticks(list(x))
+        ax.set_xticklabels([r["tool"] for r in rs], rotation=20, ha="right")
+        ax.set_ylabel("ratio (raw/comp)")
+        ax2.set_ylabel("throughput (MB/s)")
+        ax.set_title(f"Baseline Comparison (epsilon={eps})" if eps else "Baseline Comparison")
+        ax.grid(True, axis="y", alpha=0.3)
     fig.tight_layout()
     fig.savefig(out)
     plt.close(fig)

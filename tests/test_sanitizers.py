@@ -15,7 +15,7 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 @pytest.mark.skipif(shutil.which("g++") is None, reason="needs g++")
 def test_host_library_clean_under_asan_ubsan(tmp_path):
     exe = str(tmp_path / "selftest")
-    src = [os.path.join(ROOT, "csrc", "host", f) for f in ("codecs.cpp", "pipeline.cpp", "product.cpp")]
+    src = [os.path.join(ROOT, "csrc", "host", f) for f in ("codecs.cpp", "pipeline.cpp", "product.cpp", "lammps_io.cpp")]
     src.append(os.path.join(ROOT, "csrc", "host", "selftest", "selftest.cpp"))
     cmd = ["g++", "-std=c++17", "-O1", "-g", "-fsanitize=address,undefined", "-fno-sanitize-recover=all",
            "-fno-omit-frame-pointer", "-I" + os.path.join(ROOT, "csrc"), *src, "-o", exe]
