@@ -118,6 +118,22 @@ def test_determinism_hash_app():
     assert determinism_hash.main([]) == "c18cd836f0cb712247e0ace683d710b8550f3e3f40a6a2998252df59498aab56"
 
 
+def test_verify_app_reproduces_the_reference_artifacts(tmp_path):
+    import json
+
+    from mini_nangila_b200.apps import verify
+
+    out = str(tmp_path / "verification")
+    checks = verify.main(["--out", out, "--skip-tests", "--quick"])
+    assert all(c["ok"] for c in checks.values())
+    assert checks["rotor"]["ratio"] == 1.5 and checks["rotor"]["rms_err"] == 0.02304  # reference: rotor.txt
+    assert checks["topology"]["mask_bytes"] == 124
+    for f in ("determinism_hash.txt", "ai_throughput.txt", "hpc_bench.txt", "topology.txt", "rotor.txt"):
+        assert os.path.getsize(os.path.join(out, f)) > 0
+    assert json.load(open(os.path.join(out, "checks.json"))) == json.loads(json.dumps(checks))
+    assert open(os.path.join(out, "determinism_hash.txt")).read().strip() == f"Q823_HASH {verify.REFERENCE_HASH}"
+
+
 def test_analyze_app(tmp_path):
     from mini_nangila_b200.apps import analyze
 
