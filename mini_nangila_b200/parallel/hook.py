@@ -31,6 +31,7 @@ call counters) so a resumed run continues bit-identically.
 """
 from __future__ import annotations
 
+import atexit
 import os
 import time
 import zlib
@@ -94,9 +95,27 @@ class NangilaHookState:
     comp_bytes: int = 0
     calls: int = 0
     last_variant: str = ""
+    # metrics lines whose res_mean_abs is still being computed on the
+    # device: (ts, hook_idx, numel, comp_bytes, pinned scalar, event)
+    pending_metrics: list = field(default_factory=list)
 
     def compression_ratio(self) -> float:
         return self.raw_bytes / max(1, self.comp_bytes)
+
+    def flush_metrics(self, wait: bool = True) -> int:
+        """Write the metrics lines whose device statistic has landed (all of
+        them with ``wait``, which waits for each one's event).  Returns the
+        number of lines written."""
+        lines = []
+        while self.pending_metrics:
+            ts, idx, numel, comp, val, ev = self.pending_metrics[0]
+            if not wait and not ev.query():
+                break
+            ev.synchronize()
+            self.pending_metrics.pop(0)
+            lines.append(_metrics_line(ts, idx, numel, comp, float(val)))
+        _append(self.config.metrics_path, lines)
+        return len(lines)
 
     def state_dict(self) -> dict:
         out = {"calls": self.calls, "buckets": {}}
@@ -150,25 +169,53 @@ def _get_state(hs: NangilaHookState, bidx: int, buf: torch.Tensor, sig: tuple, w
     return st, first
 
 
-def _log(hs: NangilaHookState, bidx: int, numel: int, comp: int, res_mean_abs: float = float("nan")) -> None:
+def _metrics_line(ts: float, idx: int, numel: int, comp: int, res_mean_abs: float) -> str:
+    # Same key,value layout as the reference's metrics CSV (comm_hook.py:307-319)
+    raw = numel * 4
+    return (f"ts,{ts:.6f},hook_idx,{idx},bucket_elems,{numel},raw_bytes,{raw},"
+            f"comp_bytes,{comp},ratio,{raw / max(comp, 1):.6f},res_mean_abs,{res_mean_abs:.6e}\n")
+
+
+def _append(path: str | None, lines: list[str]) -> None:
+    if not path or not lines:
+        return
+    try:
+        with open(path, "a") as fh:
+            fh.write("".join(lines))
+    except OSError:
+        pass
+
+
+def _wants_metrics(hs: NangilaHookState) -> bool:
+    cfg = hs.config
+    return bool(cfg.metrics_path) and (dist.get_rank(hs.group) if dist.is_initialized() else 0) == 0
+
+
+def _log(hs: NangilaHookState, bidx: int, numel: int, comp: int, res_mean_abs=float("nan")) -> None:
+    """One metrics line for this hook call (rank 0).  ``res_mean_abs`` is a
+    float, or a CUDA scalar still being computed: its line is queued with an
+    event and written once the value has landed, so logging adds no host
+    sync to the step."""
     cfg = hs.config
     rank = dist.get_rank(hs.group) if dist.is_initialized() else 0
     if rank != 0 or not (cfg.metrics_path or cfg.verbose):
         return
     raw = numel * 4
-    ratio = raw / max(comp, 1)
     if cfg.verbose:
         print(f"[nangila-b200-{cfg.mode}] bucket={numel} raw={raw/1e6:.3f}MB comp_local={comp/1e6:.3f}MB "
-              f"ratio={ratio:.2f}x pred_mode={'EMA' if cfg.use_momentum else 'none'} bits={cfg.bits}")
-    if cfg.metrics_path:
-        # Same key,value layout as the reference's metrics CSV (comm_hook.py:307-319)
-        line = (f"ts,{time.time():.6f},hook_idx,{hs.calls},bucket_elems,{numel},raw_bytes,{raw},"
-                f"comp_bytes,{comp},ratio,{ratio:.6f},res_mean_abs,{res_mean_abs:.6e}\n")
-        try:
-            with open(cfg.metrics_path, "a") as fh:
-                fh.write(line)
-        except OSError:
-            pass
+              f"ratio={raw / max(comp, 1):.2f}x pred_mode={'EMA' if cfg.use_momentum else 'none'} bits={cfg.bits}")
+    if not cfg.metrics_path:
+        return
+    if isinstance(res_mean_abs, torch.Tensor) and res_mean_abs.is_cuda:
+        val = torch.empty((), dtype=torch.float32, pin_memory=True)
+        val.copy_(res_mean_abs, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        hs.pending_metrics.append((time.time(), hs.calls, numel, comp, val, ev))
+        hs.flush_metrics(wait=False)
+        return
+    hs.flush_metrics(wait=True)  # keep the file in call order
+    _append(cfg.metrics_path, [_metrics_line(time.time(), hs.calls, numel, comp, float(res_mean_abs))])
 
 
 # --------------------------------------------------------------- fused (GPU)
@@ -192,6 +239,15 @@ def _fused_hook(hs: NangilaHookState, bucket):
     cur = torch.cuda.current_stream(buf.device)
     hs.stream.wait_stream(cur)
     with torch.cuda.stream(hs.stream), nvtx_range(f"nangila/bucket{bidx}/{buf.numel()}"):
+        # mean |g - pred| of this rank's bucket, the reference's res_mean_abs
+        # (comm_hook.py:146,178); computed only when it is logged
+        res = None
+        if _wants_metrics(hs):
+            # out of place: buf.float() of an fp32 bucket is the bucket itself
+            if st.pred is not None and not first:
+                res = (buf.float() - st.pred).abs_().mean()
+            else:
+                res = buf.float().abs().mean()
         hs.last_variant = hs.comm.allreduce_(
             buf, st.pred, st.ef, mode=cfg.mode, k=cfg.k, variant=cfg.variant, stochastic=cfg.stochastic,
             seed=cfg.seed, bucket=bidx, step=st.calls, beta=cfg.beta, first=first,
@@ -199,10 +255,10 @@ def _fused_hook(hs: NangilaHookState, bucket):
         )
         fut = torch.futures.Future(devices=[buf.device])
         fut.set_result(buf)
-    comp = wire_bytes(buf.numel(), cfg.mode, cfg.k, cfg.topo_drop_percent, cfg.topo_seed, bidx)
-    hs.raw_bytes += buf.numel() * 4
-    hs.comp_bytes += comp
-    _log(hs, bidx, buf.numel(), comp)
+        comp = wire_bytes(buf.numel(), cfg.mode, cfg.k, cfg.topo_drop_percent, cfg.topo_seed, bidx)
+        hs.raw_bytes += buf.numel() * 4
+        hs.comp_bytes += comp
+        _log(hs, bidx, buf.numel(), comp, res if res is not None else float("nan"))
     return fut
 
 
@@ -263,6 +319,12 @@ def _host_hook(hs: NangilaHookState, bucket):
     pred = st.pred.cpu().numpy() if st.pred is not None else None
     ef = st.ef.cpu().numpy() if st.ef is not None else None
     n = g.size
+    # mean |g - pred| (comm_hook.py:146,178), before g (a view of the bucket
+    # on CPU) is overwritten with the average
+    res = float("nan")
+    if _wants_metrics(hs):
+        r = g - pred if (pred is not None and not first) else g
+        res = float(np.abs(r, dtype=np.float64).mean()) if n else 0.0
     topo = topology(n, cfg.topo_drop_percent, cfg.topo_seed, bidx)
     if cfg.mode == "topk":
         wire, e_out = h.product_topk_encode(g, pred, ef, cfg.k, cfg.error_feedback, topo)
@@ -289,7 +351,7 @@ def _host_hook(hs: NangilaHookState, bucket):
     comp = wire_bytes(n, cfg.mode, cfg.k, cfg.topo_drop_percent, cfg.topo_seed, bidx)
     hs.raw_bytes += n * 4
     hs.comp_bytes += comp
-    _log(hs, bidx, n, comp)
+    _log(hs, bidx, n, comp, res)
     fut = torch.futures.Future()
     fut.set_result(buf)
     return fut
@@ -379,4 +441,13 @@ def register_nangila_hook(
     else:
         raise ValueError(f"unknown impl {impl!r}")
     model.register_comm_hook(state=None, hook=hook)
+    if cfg.metrics_path and impl == "fused":
+        atexit.register(_flush_at_exit, hs)
     return hs
+
+
+def _flush_at_exit(hs: NangilaHookState) -> None:
+    try:
+        hs.flush_metrics(wait=True)
+    except Exception:  # the CUDA context may already be unusable at exit
+        pass

@@ -116,6 +116,52 @@ def test_host_hook_matches_oracle(tmp_path):
         assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
 
 
+def _metrics_worker(rank, world, port, outdir):
+    dist = _init(rank, world, port)
+    try:
+        from mini_nangila_b200.parallel.hook import HookConfig, NangilaHookState, _host_hook
+
+        class Bucket:
+            def __init__(self, t):
+                self.t = t
+
+            def buffer(self):
+                return self.t
+
+            def index(self):
+                return 0
+
+            def parameters(self):
+                return []
+
+        path = os.path.join(outdir, "metrics.csv")
+        hs = NangilaHookState(HookConfig(impl="host", use_momentum=True, seed=9, metrics_path=path))
+        n = 3000
+        for call in range(2):
+            g = np.random.default_rng(10 * call + rank).standard_normal(n).astype(np.float32) * np.float32(1e-3)
+            pred = None if call == 0 else hs.buckets[0].pred.numpy().copy()
+            _host_hook(hs, Bucket(torch.from_numpy(g.copy()))).wait()
+            want = np.abs(g.astype(np.float64) if pred is None else (g - pred).astype(np.float64)).mean()
+            np.save(os.path.join(outdir, f"m{rank}_{call}.npy"), np.array([want]))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_host_hook_metrics_log_residual_mean_abs(tmp_path):
+    """rank 0 writes one reference-layout line per hook call with
+    res_mean_abs = mean |g - pred| of its own bucket (comm_hook.py:178)."""
+    mp.start_processes(_metrics_worker, args=(2, _port(), str(tmp_path)), nprocs=2, join=True, start_method="spawn")
+    lines = (tmp_path / "metrics.csv").read_text().splitlines()
+    assert len(lines) == 2  # rank 0 only
+    for call, line in enumerate(lines):
+        kv = line.split(",")
+        d = dict(zip(kv[0::2], kv[1::2]))
+        assert kv[0::2] == ["ts", "hook_idx", "bucket_elems", "raw_bytes", "comp_bytes", "ratio", "res_mean_abs"]
+        assert int(d["hook_idx"]) == call + 1 and int(d["bucket_elems"]) == 3000
+        want = float(np.load(tmp_path / f"m0_{call}.npy")[0])
+        assert float(d["res_mean_abs"]) == pytest.approx(want, rel=1e-5)
+
+
 def _dying_worker(rank, world, port, outdir):
     """Rank 1 raises between steps without joining the next collective; rank 0
     must get an error from its next collective (short process-group timeout)
