@@ -52,6 +52,9 @@ class _BucketState:
     pred: torch.Tensor | None
     ef: torch.Tensor | None
     calls: int = 0
+    # ((parameter index, offset, numel), ...) of the bucket's gradients when
+    # DDP names them; lets a state follow its parameters into another layout
+    layout: tuple | None = None
 
 
 @dataclass
@@ -98,6 +101,11 @@ class NangilaHookState:
     # metrics lines whose res_mean_abs is still being computed on the
     # device: (ts, hook_idx, numel, comp_bytes, pinned scalar, event)
     pending_metrics: list = field(default_factory=list)
+    # parameter data_ptr -> index in model.parameters()
+    param_index: dict = field(default_factory=dict)
+    # bucket states (a loaded state_dict, or the buckets DDP just replaced)
+    # that new buckets take their predictor / EF state from, per parameter
+    restore: dict | None = None
 
     def compression_ratio(self) -> float:
         return self.raw_bytes / max(1, self.comp_bytes)
@@ -118,6 +126,12 @@ class NangilaHookState:
         return len(lines)
 
     def state_dict(self) -> dict:
+        """Predictor and error-feedback state of every bucket (CPU copies),
+        call counters (the stochastic-rounding step keys) and the exchange
+        epoch.  With the same bucket layout a resumed run is bit-identical
+        to an uninterrupted one; with another layout (a new DDP instance
+        whose buckets differ), each parameter's state is carried over
+        through the saved layouts."""
         out = {"calls": self.calls, "buckets": {}}
         for b, st in self.buckets.items():
             out["buckets"][b] = {
@@ -125,24 +139,26 @@ class NangilaHookState:
                 "calls": st.calls,
                 "pred": None if st.pred is None else st.pred.detach().cpu().clone(),
                 "ef": None if st.ef is None else st.ef.detach().cpu().clone(),
+                "layout": None if st.layout is None else [list(x) for x in st.layout],
             }
         if self.comm is not None:
             out["epoch"] = int(self.comm.comm.epoch)
         return out
 
     def load_state_dict(self, sd: dict) -> None:
+        """Restore a ``state_dict``; each bucket takes its state when the hook
+        next sees it (a bucket of the same index, size and layout whole, any
+        other bucket parameter by parameter)."""
         self.calls = int(sd.get("calls", 0))
-        for b, d in sd["buckets"].items():
-            st = self.buckets.get(int(b))
-            if st is None or st.numel != d["numel"]:
-                st = _BucketState(d["numel"], ("restored", d["numel"]), None, None)
-                self.buckets[int(b)] = st
-            st.calls = int(d["calls"])
-            dev = self.comm.device if self.comm is not None else torch.device("cpu")
-            st.pred = None if d["pred"] is None else d["pred"].to(dev).clone()
-            st.ef = None if d["ef"] is None else d["ef"].to(dev).clone()
+        self.buckets = {}
+        self.restore = {"buckets": {int(b): d for b, d in sd["buckets"].items()}}
         if self.comm is not None and "epoch" in sd:
             self.comm.comm.epoch = int(sd["epoch"])
+
+    def _snapshot(self) -> dict:
+        """The current bucket states as a restore source (no copies)."""
+        return {"buckets": {b: {"numel": st.numel, "calls": st.calls, "pred": st.pred, "ef": st.ef,
+                                "layout": st.layout} for b, st in self.buckets.items()}}
 
 
 def _bucket_sig(bucket) -> tuple:
@@ -153,17 +169,92 @@ def _bucket_sig(bucket) -> tuple:
         return (bucket.buffer().numel(),)
 
 
-def _get_state(hs: NangilaHookState, bidx: int, buf: torch.Tensor, sig: tuple, want_pred: bool,
+def _layout(bucket, buf: torch.Tensor, param_index: dict) -> tuple | None:
+    """((parameter index, offset, numel), ...) of a DDP bucket from its
+    gradient views into the flat buffer; None when the bucket does not name
+    its parameters or a view lies outside the buffer."""
+    if not param_index:
+        return None
+    try:
+        params, grads = bucket.parameters(), bucket.gradients()
+    except Exception:
+        return None
+    if not params or len(params) != len(grads):
+        return None
+    base, es, n = buf.data_ptr(), buf.element_size(), buf.numel()
+    out = []
+    for p, g in zip(params, grads):
+        pi = param_index.get(p.data_ptr())
+        off, rem = divmod(g.data_ptr() - base, es)
+        if pi is None or rem or off < 0 or off + g.numel() > n:
+            return None
+        out.append((pi, off, g.numel()))
+    return tuple(out)
+
+
+def _restored(hs: NangilaHookState, bidx: int, buf: torch.Tensor, layout, want_pred: bool,
+              want_ef: bool) -> _BucketState | None:
+    src = hs.restore
+    if not src:
+        return None
+    saved = src["buckets"]
+    n, dev = buf.numel(), buf.device
+
+    def dev_copy(t, want):
+        return t.to(dev, torch.float32).clone() if (want and t is not None) else (
+            torch.zeros(n, dtype=torch.float32, device=dev) if want else None)
+
+    d = saved.get(bidx)
+    if d is not None and d["numel"] == n:
+        sl = d.get("layout")
+        if layout is None or sl is None or tuple(tuple(x) for x in sl) == layout:
+            return _BucketState(n, (), dev_copy(d["pred"], want_pred), dev_copy(d["ef"], want_ef),
+                                int(d["calls"]), layout)
+    if layout is None:
+        return None
+    where = src.get("where")
+    if where is None:
+        where = {pi: (b, off, num) for b, dd in saved.items() for pi, off, num in (dd.get("layout") or ())}
+        src["where"] = where
+    if not all(pi in where and where[pi][2] == num for pi, _, num in layout):
+        return None
+    pred = torch.zeros(n, dtype=torch.float32, device=dev) if want_pred else None
+    ef = torch.zeros(n, dtype=torch.float32, device=dev) if want_ef else None
+    calls = 0
+    for pi, off, num in layout:
+        b, soff, _ = where[pi]
+        dd = saved[b]
+        for dst, key in ((pred, "pred"), (ef, "ef")):
+            if dst is not None and dd[key] is not None:
+                dst[off:off + num].copy_(dd[key][soff:soff + num])
+        calls = max(calls, int(dd["calls"]))
+    return _BucketState(n, (), pred, ef, calls, layout)
+
+
+def _get_state(hs: NangilaHookState, bidx: int, buf: torch.Tensor, bucket, want_pred: bool,
                want_ef: bool) -> tuple[_BucketState, bool]:
+    sig = _bucket_sig(bucket)
     st = hs.buckets.get(bidx)
-    fresh = st is None or st.numel != buf.numel() or (st.sig != sig and st.sig[0] != "restored")
-    if fresh:
-        pred = torch.zeros(buf.numel(), dtype=torch.float32, device=buf.device) if want_pred else None
-        ef = torch.zeros(buf.numel(), dtype=torch.float32, device=buf.device) if want_ef else None
-        st = _BucketState(buf.numel(), sig, pred, ef, 0)
-        hs.buckets[bidx] = st
-    elif st.sig != sig:
+    if hs.restore is not None:
+        served = hs.restore.setdefault("served", set())
+        if bidx in served:
+            hs.restore = None  # a bucket index came round again: a new step, all states taken over
+        else:
+            served.add(bidx)
+    if st is None or st.numel != buf.numel() or st.sig != sig:
+        if st is not None and hs.restore is None:
+            # DDP replaced its buckets (the rebuild after the first iteration):
+            # the new ones take their parameters' state from the old ones
+            hs.restore = hs._snapshot()
+            hs.restore["served"] = {bidx}
+        layout = _layout(bucket, buf, hs.param_index)
+        st = _restored(hs, bidx, buf, layout, want_pred, want_ef)
+        if st is None:
+            pred = torch.zeros(buf.numel(), dtype=torch.float32, device=buf.device) if want_pred else None
+            ef = torch.zeros(buf.numel(), dtype=torch.float32, device=buf.device) if want_ef else None
+            st = _BucketState(buf.numel(), sig, pred, ef, 0, layout)
         st.sig = sig
+        hs.buckets[bidx] = st
     first = st.calls == 0
     st.calls += 1
     return st, first
@@ -228,7 +319,7 @@ def _fused_hook(hs: NangilaHookState, bucket):
     st_code = hs.comm.poll_status()
     if st_code != 0:
         hs.comm.check()  # synchronizes and raises CommError with the details
-    st, first = _get_state(hs, bidx, buf, _bucket_sig(bucket), cfg.use_momentum, cfg.error_feedback)
+    st, first = _get_state(hs, bidx, buf, bucket, cfg.use_momentum, cfg.error_feedback)
     hs.calls += 1
     if getattr(hs, "autotune_pending", False):
         # First bucket: time one-shot vs two-shot at bucket-like sizes on this
@@ -313,7 +404,7 @@ def _host_hook(hs: NangilaHookState, bucket):
     bidx = bucket.index()
     world = dist.get_world_size(hs.group)
     rank = dist.get_rank(hs.group)
-    st, first = _get_state(hs, bidx, buf, _bucket_sig(bucket), cfg.use_momentum, cfg.error_feedback)
+    st, first = _get_state(hs, bidx, buf, bucket, cfg.use_momentum, cfg.error_feedback)
     hs.calls += 1
     g = buf.detach().float().cpu().numpy()
     pred = st.pred.cpu().numpy() if st.pred is not None else None
@@ -418,6 +509,7 @@ def register_nangila_hook(
                      topo_drop_percent, topo_seed, impl, True if error_feedback is None else bool(error_feedback),
                      variant, timeout_s, verbose, max_ctas)
     hs = NangilaHookState(cfg, process_group)
+    hs.param_index = {p.data_ptr(): i for i, p in enumerate(model.parameters())}
     if impl == "fused":
         if dev.type != "cuda":
             raise RuntimeError("impl='fused' needs a CUDA model; use impl='host' on CPU")

@@ -156,6 +156,20 @@ class DDPTrainer:
             losses.append(float(pending[0]))
         return losses
 
+    def state_dict(self) -> dict:
+        """Everything a resumed run needs: model, optimizer, the hook's
+        predictor / error-feedback state and counters, steps done."""
+        return {"model": self.model.state_dict(), "optimizer": self.opt.state_dict(),
+                "hook": self.hook_state.state_dict() if self.hook_state is not None else None,
+                "steps_done": self.steps_done}
+
+    def load_state_dict(self, sd: dict) -> None:
+        self.model.load_state_dict(sd["model"])
+        self.opt.load_state_dict(sd["optimizer"])
+        if self.hook_state is not None and sd.get("hook") is not None:
+            self.hook_state.load_state_dict(sd["hook"])
+        self.steps_done = int(sd.get("steps_done", 0))
+
     def kernel_launches(self) -> int:
         hs = self.hook_state
         if hs is not None and getattr(hs, "comm", None) is not None:
