@@ -88,6 +88,41 @@ def test_grpc_twin_end_to_end(tmp_path):
         assert lines[0].startswith("tick,0,len,6,raw,24,comp,")
 
 
+def test_grpc_server_under_concurrent_clients(tmp_path):
+    """Frames from several client threads at once (the server's handler runs
+    on a thread pool): every frame is counted and every CSV line is whole."""
+    pytest.importorskip("grpc")
+    import threading
+
+    from mini_nangila_b200.twin.rotor_net import RotorClient, RotorServer, imu_sample
+
+    srv = RotorServer(metrics_path=str(tmp_path / "s.csv"))
+    server, port = srv.serve("127.0.0.1:0", max_workers=8)
+    errors = []
+
+    def client(k):
+        try:
+            c = RotorClient(f"127.0.0.1:{port}")
+            for tick in range(25):
+                assert c.send(imu_sample((100 * k + tick) / 50), 100 * k + tick)
+            c.close()
+        except Exception as e:  # noqa: BLE001
+            errors.append(e)
+
+    try:
+        ts = [threading.Thread(target=client, args=(k,)) for k in range(4)]
+        for t in ts:
+            t.start()
+        for t in ts:
+            t.join()
+    finally:
+        server.stop(0)
+    assert not errors and srv.frames == 100
+    lines = open(tmp_path / "s.csv").read().splitlines()
+    assert len(lines) == 100 and all(line.startswith("tick,") and line.count(",") == 9 for line in lines)
+    assert sorted(int(line.split(",")[1]) for line in lines) == sorted(100 * k + t for k in range(4) for t in range(25))
+
+
 def test_train_nano_two_cpu_ranks(tmp_path):
     import socket
     import subprocess
