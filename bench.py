@@ -88,35 +88,61 @@ class _HFLoss(torch.nn.Module):
         return torch.nn.functional.cross_entropy(logits.view(-1, logits.size(-1)).float(), y.reshape(-1))
 
 
-def build_reference(args, device):
-    """Reference arm: unmodified nangila_ddp hook from baseline/_ref on a stock
-    transformers GPT-2 small (the reference ships no GPT-2 model)."""
+def build_reference(args, device, tiny: bool = False):
+    """Reference arm: the unmodified nangila_ddp hook from baseline/_ref on a
+    stock transformers model of the same architecture (the reference ships
+    no GPT-2 or Llama model): GPT-2 small with the INT4 + EMA hook, or the
+    Llama-style 1.1B (bf16 weights) with the hook in top-k mode.  ``tiny``
+    swaps in small models of the same families (CPU tests of this arm)."""
     ref = os.path.join(ROOT, "baseline", "_ref")
     if not os.path.isdir(os.path.join(ref, "nangila_ddp")):
-        return None, "baseline/_ref/nangila_ddp is not installed"
+        return None, "baseline/_ref/nangila_ddp is not installed", ""
     sys.path.insert(0, ref)
     from nangila_ddp import register_nangila_hook as ref_register  # noqa: E402
-    from transformers import GPT2Config, GPT2LMHeadModel  # noqa: E402
 
-    cfg = GPT2Config(vocab_size=50257, n_positions=1024, n_embd=768, n_layer=12, n_head=12, n_inner=3072,
-                     resid_pdrop=0.0, embd_pdrop=0.0, attn_pdrop=0.0, initializer_range=0.02)
-    cfg._attn_implementation = "sdpa"
-    model = _HFLoss(GPT2LMHeadModel(cfg)).to(device)
-    ddp = torch.nn.parallel.DistributedDataParallel(model, device_ids=[device.index], bucket_cap_mb=25)
-    # Same call the reference's trainer makes (train_nano.py:133-143), with
-    # the per-bucket EMA predictor enabled.
-    ref_register(ddp, beta=0.9, bits=4, stochastic=True, use_fp16_transport=False, use_momentum=True)
+    if args.model == "gpt2":
+        from transformers import GPT2Config, GPT2LMHeadModel  # noqa: E402
+
+        dims = dict(vocab_size=512, n_positions=64, n_embd=64, n_layer=2, n_head=4, n_inner=256) if tiny else \
+            dict(vocab_size=50257, n_positions=1024, n_embd=768, n_layer=12, n_head=12, n_inner=3072)
+        cfg = GPT2Config(**dims, resid_pdrop=0.0, embd_pdrop=0.0, attn_pdrop=0.0, initializer_range=0.02)
+        cfg._attn_implementation = "sdpa"
+        model = _HFLoss(GPT2LMHeadModel(cfg)).to(device)
+        autocast = True
+    else:
+        from transformers import LlamaConfig as HFLlamaConfig  # noqa: E402
+        from transformers import LlamaForCausalLM  # noqa: E402
+
+        from mini_nangila_b200.models import LlamaConfig
+
+        c = LlamaConfig.tiny() if tiny else LlamaConfig.b1_1()
+        cfg = HFLlamaConfig(vocab_size=c.vocab_size, hidden_size=c.d_model, intermediate_size=c.d_ff,
+                            num_hidden_layers=c.n_layer, num_attention_heads=c.n_head,
+                            num_key_value_heads=c.n_kv_head, max_position_embeddings=c.max_seq,
+                            rms_norm_eps=c.eps, rope_theta=c.rope_theta, initializer_range=c.init_std,
+                            tie_word_embeddings=False)
+        cfg._attn_implementation = "sdpa"
+        model = _HFLoss(LlamaForCausalLM(cfg)).to(device=device, dtype=torch.bfloat16)
+        autocast = False
+    ddp = torch.nn.parallel.DistributedDataParallel(
+        model, device_ids=[device.index] if device.type == "cuda" else None, bucket_cap_mb=25)
+    topk = args.topk if args.mode == "topk" else 0.0
+    momentum = args.momentum == "on" or (args.momentum == "auto" and args.mode != "topk")
+    # Same call the reference's trainer makes (train_nano.py:133-143)
+    ref_register(ddp, beta=0.9, bits=4, stochastic=True, use_fp16_transport=False, use_momentum=momentum,
+                 topk_percent=topk)
     opt = torch.optim.AdamW(ddp.parameters(), lr=6e-4)
 
     def step(x, y):
-        with torch.autocast("cuda", dtype=torch.bfloat16):
+        with torch.autocast(device.type, dtype=torch.bfloat16, enabled=autocast):
             loss = ddp(x, y)
         opt.zero_grad(set_to_none=True)
         loss.backward()
         opt.step()
         return loss.detach()
 
-    return step, None
+    name = "reference-nangila_ddp-int4" + ("-ema" if momentum else "") + (f"-topk{topk:g}" if topk else "")
+    return step, None, name
 
 
 def main():
@@ -147,18 +173,12 @@ def main():
     quiet = contextlib.redirect_stdout(open(os.devnull, "w")) if args.impl == "reference" else contextlib.nullcontext()
     trainer = None
     if args.impl == "reference":
-        if args.model != "gpt2":
-            if rank == 0:
-                print(json.dumps({"impl": "reference", "unavailable": "the reference arm is defined for GPT-2 small"}))
-            dist.destroy_process_group()
-            return
-        step_fn, why = build_reference(args, device)
+        step_fn, why, hook_name = build_reference(args, device)
         if step_fn is None:
             if rank == 0:
                 print(json.dumps({"impl": "reference", "unavailable": why}))
             dist.destroy_process_group()
             return
-        hook_name = "reference-nangila_ddp-int4-momentum"
     else:
         model = GPT2(mcfg) if args.model == "gpt2" else Llama(mcfg)
         if args.model == "llama":
