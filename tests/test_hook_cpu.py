@@ -109,11 +109,26 @@ def _oracle_worker(rank, world, port, outdir):
         dist.destroy_process_group()
 
 
-def test_host_hook_matches_oracle(tmp_path):
-    mp.start_processes(_oracle_worker, args=(2, _port(), str(tmp_path)), nprocs=2, join=True, start_method="spawn")
-    for r in range(2):
+@pytest.mark.parametrize("world", [2, 3, 4])
+def test_host_hook_matches_oracle(world, tmp_path):
+    mp.start_processes(_oracle_worker, args=(world, _port(), str(tmp_path)), nprocs=world, join=True,
+                       start_method="spawn")
+    for r in range(world):
         got, ref = np.load(tmp_path / f"o{r}.npy")
         assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+
+@pytest.mark.parametrize("mode", ["int4", "topk+topo"])
+def test_ddp_hook_ranks_stay_identical_world3(mode, tmp_path):
+    """An odd world size: rank-ordered sums and per-rank noise keys still give
+    every rank the same parameters and predictor states."""
+    mp.start_processes(_train_worker, args=(3, _port(), "host", mode, str(tmp_path)), nprocs=3, join=True,
+                       start_method="spawn")
+    rs = [torch.load(tmp_path / f"r{r}.pt") for r in range(3)]
+    for r in rs[1:]:
+        assert torch.equal(rs[0]["params"], r["params"])
+        assert all(torch.equal(a, b) for a, b in zip(rs[0]["preds"], r["preds"]))
+    assert all(np.isfinite(rs[0]["losses"]))
 
 
 def _metrics_worker(rank, world, port, outdir):
