@@ -1,0 +1,36 @@
+"""The reference package's module paths (python/nangila_ddp/*) resolve to
+this framework: the hook, the trainers and the two plot scripts."""
+import importlib
+
+
+def test_module_paths():
+    import nangila_ddp
+    from mini_nangila_b200.apps import minigpt_train, train_nano
+    from mini_nangila_b200.parallel.hook import register_nangila_hook
+
+    assert nangila_ddp.register_nangila_hook is register_nangila_hook
+    assert importlib.import_module("nangila_ddp.comm_hook").register_nangila_hook is register_nangila_hook
+    assert importlib.import_module("nangila_ddp.train_nano").main is train_nano.main
+    assert importlib.import_module("nangila_ddp.examples.minigpt_train").main is minigpt_train.main
+
+
+def test_plot_scripts_summarise_without_matplotlib(tmp_path, capsys):
+    from nangila_ddp import plot_metrics, plot_train_and_compression
+
+    m = tmp_path / "ddp_metrics.csv"
+    m.write_text("ts,100.5,hook_idx,1,bucket_elems,10,raw_bytes,40,comp_bytes,5,ratio,8.0,res_mean_abs,1e-3\n"
+                 "ts,101.5,hook_idx,2,bucket_elems,10,raw_bytes,40,comp_bytes,4,ratio,10.0,res_mean_abs,2e-3\n")
+    t = tmp_path / "train_log.csv"
+    t.write_text("ts,step,loss,lr,tokens_per_sec,step_ms\n100.0,1,4.2,0.0006,1000,10\n101.0,2,4.0,0.0006,1000,10\n")
+    plot_metrics.main([str(m)])
+    plot_train_and_compression.main([str(t), str(m)])
+    out = capsys.readouterr().out
+    try:
+        import matplotlib  # noqa: F401
+
+        assert "Saved" in out
+    except ImportError:
+        assert '"median": 9.0' in out and '"loss"' in out
+    empty = tmp_path / "empty.csv"
+    empty.write_text("nothing here\n")
+    assert plot_metrics.main([str(empty)]) is None
