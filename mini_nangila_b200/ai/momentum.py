@@ -14,6 +14,8 @@ from ..core.predictor import PredictorShapeMismatch
 
 
 class MomentumPredictor:
+    """EMA predictor in Q8.23 (nangila-ai/src/momentum.rs:9-61): the first update copies
+    the observation, later ones ``state * beta + obs * (1 - beta)`` with ``mul_scalar``."""
     def __init__(self, beta: float):
         self.beta = float(np.float32(beta))
         self._state: FixedPointBuffer | None = None

@@ -66,6 +66,8 @@ def _decode_chunks(blob, offsets, scales, total_len: int, epsilon: float) -> np.
 
 
 def write_chunked_dataset(path: str, dataset: str, data, chunk: int, epsilon: float, codec: str) -> None:
+    """Chunked error-bounded dataset (nangila-checkpoint/src/lib.rs:29-83): group ``dataset`` with
+    ``blob``, ``offsets``, ``scales`` and attributes; the codes are always EB INT16."""
     data = np.ascontiguousarray(np.asarray(data, np.float32).reshape(-1))
     blob, offsets, scales = _encode_chunks(data, chunk, epsilon)
     attrs = {"total_len": np.uint64(data.size), "chunk": np.uint64(max(1, int(chunk))), "codec": codec,
@@ -86,6 +88,7 @@ def write_chunked_dataset(path: str, dataset: str, data, chunk: int, epsilon: fl
 
 
 def read_compressed_1d(path: str, dataset: str) -> np.ndarray:
+    """Decode a chunked dataset back to f32 (nangila-checkpoint/src/lib.rs:94-133)."""
     if h5py is not None:
         with h5py.File(path, "r") as f:
             g = f[dataset]
@@ -97,6 +100,7 @@ def read_compressed_1d(path: str, dataset: str) -> np.ndarray:
 
 
 def write_dataset(path: str, dataset: str, data, epsilon: float, codec: str) -> None:
+    """Plain 1-D f32 dataset with ``epsilon`` and ``codec`` attributes (nangila-checkpoint/src/lib.rs:14-26)."""
     data = np.asarray(data, np.float32).reshape(-1)
     if h5py is not None:
         with h5py.File(path, "a") as f:
@@ -118,6 +122,7 @@ def write_dataset(path: str, dataset: str, data, epsilon: float, codec: str) -> 
 
 
 def read_dataset(path: str, dataset: str) -> np.ndarray:
+    """Read a plain dataset written by ``write_dataset``."""
     if h5py is not None:
         with h5py.File(path, "r") as f:
             return f[dataset][()]

@@ -17,10 +17,12 @@ from .._ext import host
 
 
 class DumpFormatError(ValueError):
+    """A malformed LAMMPS dump; the message is the reference reader's."""
     pass
 
 
 def read_dump(path: str) -> list[np.ndarray]:
+    """One flattened ``[x0, y0, z0, ...]`` snapshot per ``ITEM: TIMESTEP`` block of a dump file."""
     if not os.path.isfile(path):
         raise FileNotFoundError(path)
     try:

@@ -27,6 +27,7 @@ CODEC_NAMES = {1: "ErrorBoundedINT16", 2: "ErrorBoundedINT16_RLE", 3: "ErrorBoun
 
 @dataclass
 class NzHeader:
+    """The 14-byte ``.nz`` header (examples/lammps_compress/src/main.rs:90-99)."""
     version: int
     codec: int
     particles: int
@@ -34,6 +35,7 @@ class NzHeader:
 
 
 def codec_id(codec) -> int:
+    """``"eb" | "rle" | "bs" | "bsrle"`` or 1-4 -> the header's codec byte."""
     if isinstance(codec, str):
         return CODECS[codec]
     return int(codec)
@@ -47,15 +49,19 @@ def compress(data, particles: int, steps: int, codec="eb", epsilon: float = 1e-3
 
 
 def read_header(b) -> NzHeader:
+    """Parse the header of an ``.nz`` image (raises on a bad magic)."""
     v, c, p, s = host().nz_read_header(np.frombuffer(bytes(b[:14]), dtype=np.uint8))
     return NzHeader(v, c, p, s)
 
 
 def decompress(b, add_back: bool = True) -> np.ndarray:
+    """All steps of an ``.nz`` image as f32: reconstructed values, or with ``add_back=False``
+    the residual stream the reference's decoder returns (main.rs:249-309)."""
     return host().nz_decompress(np.frombuffer(bytes(b), dtype=np.uint8), bool(add_back))
 
 
 def write(path: str, data, particles: int, steps: int, codec="eb", epsilon: float = 1e-3) -> dict:
+    """``compress`` to a file; returns the stats."""
     b, stats = compress(data, particles, steps, codec, epsilon)
     with open(path, "wb") as fh:
         fh.write(b)
@@ -63,6 +69,7 @@ def write(path: str, data, particles: int, steps: int, codec="eb", epsilon: floa
 
 
 def read(path: str, add_back: bool = True) -> np.ndarray:
+    """``decompress`` of a file."""
     with open(path, "rb") as fh:
         return decompress(fh.read(), add_back)
 

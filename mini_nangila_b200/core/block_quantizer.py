@@ -21,6 +21,7 @@ from .quantizer import as_u8
 
 
 class BlockStochasticQuantizer:
+    """The fused hook's per-256-block INT4/INT8 format as a standalone quantizer (see the module docstring)."""
     def __init__(self, seed: int = 0, bits: int = 4, stochastic: bool = True, rank: int = 0, stream: int = 0):
         if bits not in (4, 8):
             raise ValueError("bits must be 4 or 8")

@@ -21,10 +21,12 @@ SCALE_FACTOR = float(1 << FRACTIONAL_BITS)
 
 
 class FixedPointError(ValueError):
+    """Base error of the Q8.23 layer (``MathError`` in nangila-math)."""
     pass
 
 
 class ShapeMismatch(FixedPointError):
+    """Element-wise op on buffers of different lengths (ops.rs:7-9)."""
     def __init__(self, a: int, b: int):
         super().__init__(f"Shape mismatch: {a} vs {b}")
         self.a, self.b = a, b
@@ -49,6 +51,11 @@ def _dev_ops():
 
 
 class FixedPointBuffer:
+    """Q8.23 values as an int32 tensor (nangila-math/src/fixed_point.rs:14-17).
+
+    ``from_f32`` / ``to_f32`` convert (fixed_point.rs:34-60); ``add``, ``sub`` and
+    ``mul_scalar`` are the saturating ops of ops.rs:6-49.  A CPU buffer runs the
+    C++ host library, a CUDA buffer the sm_100a kernels; both give the same bits."""
     __slots__ = ("data",)
 
     def __init__(self, data):

@@ -7,15 +7,18 @@ from .fixed_point import FixedPointBuffer, FixedPointError
 
 
 class PredictorError(ValueError):
+    """Predictor failure (``NangilaError`` of nangila-core/src/predictor.rs)."""
     pass
 
 
 class PredictorShapeMismatch(PredictorError):
+    """An observation of another length than the predictor's state."""
     pass
 
 
 @runtime_checkable
 class Predictor(Protocol):
+    """``predict`` / ``update`` / ``reset`` (nangila-core/src/predictor.rs:4-21)."""
     def predict(self) -> FixedPointBuffer:
         """Prediction from the internal state (empty before any update)."""
 

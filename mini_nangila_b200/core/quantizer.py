@@ -16,6 +16,8 @@ from .fixed_point import FixedPointBuffer
 
 @runtime_checkable
 class Quantizer(Protocol):
+    """``quantize(residual) -> (bytes, scale)`` and ``dequantize(bytes, scale)``
+    (nangila-core/src/quantizer.rs:3-12)."""
     def quantize(self, residual: FixedPointBuffer) -> tuple[bytes, float]:
         ...
 
@@ -33,8 +35,10 @@ def as_u8(b) -> np.ndarray:
 
 
 def to_bytes(a) -> bytes:
+    """numpy array or bytes-like -> ``bytes``."""
     return a.tobytes() if isinstance(a, np.ndarray) else bytes(a)
 
 
 def host_i32(r: FixedPointBuffer) -> np.ndarray:
+    """The buffer's Q8.23 values as a host int32 array."""
     return r.data.cpu().numpy()

@@ -14,6 +14,8 @@ from .._ext import host
 
 
 class TopologyMask:
+    """Driver / passenger split of a model's layers (nangila-core/src/topology.rs:11-163),
+    backed by the C++ host library; fields and bincode bytes as the Rust struct."""
     def __init__(self, native=None):
         self._m = native if native is not None else host().TopologyMask()
 

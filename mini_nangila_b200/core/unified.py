@@ -25,17 +25,20 @@ from .quantizer import as_u8, host_i32, to_bytes
 
 @dataclass(frozen=True)
 class Stochastic:
+    """Stochastic INT4/INT8 with the fmix64 counter PRNG (unified_quantizer.rs:171-250)."""
     seed: int = 0
     bits: int = 4
 
 
 @dataclass(frozen=True)
 class ErrorBounded:
+    """INT16 codes with scale 2 * epsilon (unified_quantizer.rs:253-279)."""
     epsilon: float = 1e-3
 
 
 @dataclass(frozen=True)
 class TopK:
+    """Keep the |x| >= k-th largest, ``[u32 n]`` + per-32 masks + int8 (unified_quantizer.rs:285-375)."""
     k_percent: float = 0.1
 
 
@@ -59,6 +62,11 @@ def _dev_codecs():
 
 
 class UnifiedQuantizer:
+    """One quantizer whose mode switches at runtime (nangila-core/src/unified_quantizer.rs:68-166).
+
+    The stochastic mode's counter persists across calls and restarts at 0 on
+    ``set_mode``; element i of a call uses counter (elements quantized before) + i.
+    CUDA residuals are quantized by the sm_100a kernels (same bytes)."""
     def __init__(self, mode):
         self._mode = mode
         self._counter = 0  # persistent PRNG counter of the stochastic mode

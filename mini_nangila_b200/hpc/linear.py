@@ -8,6 +8,7 @@ from ..core.predictor import PredictorShapeMismatch
 
 
 class LinearPredictor:
+    """``2 s_t - s_{t-1}`` extrapolation (nangila-hpc/src/linear.rs:10-57)."""
     def __init__(self):
         self.s_t: FixedPointBuffer | None = None
         self.s_t_minus_1: FixedPointBuffer | None = None

@@ -51,19 +51,23 @@ class _EBBase:
 
 
 class ErrorBoundedQuantizer(_EBBase):
+    """INT16 codes ``round(r / 2eps)``, little endian (nangila-hpc/src/error_bounded.rs:29-68)."""
     _name = "eb"
 
 
 class RunLengthQuantizer(_EBBase):
+    """EB codes as runs of zeros / literals of up to 128, no header (nangila-hpc/src/rle.rs:21-99)."""
     _name = "rle"
 
 
 class BlockSparseQuantizer(_EBBase):
+    """``[u32 n]`` then per 32 codes a mask and the nonzero i16 codes (nangila-hpc/src/block_sparse.rs:21-92)."""
     _name = "bs"
     block_size = 32
 
 
 class BlockSparseRleQuantizer(_EBBase):
+    """BlockSparse blocks grouped into zero-mask runs and literal runs (nangila-hpc/src/block_sparse_rle.rs:26-131)."""
     _name = "bsrle"
     block_size = 32
 
@@ -73,8 +77,10 @@ class QuantizerError(ValueError):
 
 
 def rle_encode_i16(q) -> bytes:
+    """Element RLE of raw i16 codes (the rotor twin's top-k path, rotor_twin_net client.rs:41-66)."""
     return to_bytes(host().rle_encode_i16(np.ascontiguousarray(np.asarray(q, dtype=np.int16))))
 
 
 def rle_decode_i16(b) -> np.ndarray:
+    """Inverse of ``rle_encode_i16``."""
     return host().rle_decode_i16(as_u8(b))

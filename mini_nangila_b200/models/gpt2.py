@@ -22,6 +22,7 @@ import torch.nn.functional as F
 
 @dataclass
 class GPT2Config:
+    """GPT-2 dimensions; ``small()`` is the 124M model (12 layers, d 768, 12 heads, vocab 50257)."""
     vocab_size: int = 50257
     n_positions: int = 1024
     n_layer: int = 12
@@ -88,6 +89,7 @@ class Block(nn.Module):
 
 
 class GPT2(nn.Module):
+    """Causal GPT-2 with tied embeddings; ``forward(x, y)`` returns the mean cross-entropy."""
     def __init__(self, cfg: GPT2Config):
         super().__init__()
         self.cfg = cfg

@@ -14,6 +14,7 @@ import torch.nn.functional as F
 
 @dataclass
 class LlamaConfig:
+    """Llama-style dimensions; ``b1_1()`` is the 1.1B model (22 layers, d 2048, 32 heads, 4 KV heads)."""
     vocab_size: int = 32000
     max_seq: int = 2048
     n_layer: int = 22
@@ -106,6 +107,7 @@ class Layer(nn.Module):
 
 
 class Llama(nn.Module):
+    """Llama-style decoder (RMSNorm, RoPE, grouped-query attention, SwiGLU); ``forward(x, y)`` returns the loss."""
     def __init__(self, cfg: LlamaConfig):
         super().__init__()
         self.cfg = cfg

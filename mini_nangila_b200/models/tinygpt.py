@@ -10,6 +10,7 @@ import torch.nn as nn
 
 
 class TinyGPT(nn.Module):
+    """The reference trainer's TinyGPT (python/nangila_ddp/train_nano.py:44-56)."""
     def __init__(self, d_model=256, nhead=4, nlayers=4, vocab=5000, block_size=128, causal=False):
         super().__init__()
         self.causal = causal

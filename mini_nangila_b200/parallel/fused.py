@@ -45,6 +45,7 @@ STATUS_NAMES = {
 
 
 class CommError(RuntimeError):
+    """A fused exchange gave up (a bounded wait expired, a tag or bounds check failed)."""
     pass
 
 
@@ -116,6 +117,7 @@ MAX_COLS = 2048  # flag columns (max CTAs of one launch)
 
 @dataclass
 class Layout:
+    """Offsets of the flags, inboxes and result slots inside each rank's symmetric region."""
     max_numel: int
     flags_off: int
     inbox_off: int

@@ -59,6 +59,7 @@ class _BucketState:
 
 @dataclass
 class HookConfig:
+    """Keyword arguments of ``register_nangila_hook`` (python/nangila_ddp/comm_hook.py:47-60, plus this framework's)."""
     beta: float = 0.9
     bits: int = 4
     stochastic: bool = True
@@ -89,6 +90,8 @@ class HookConfig:
 
 @dataclass
 class NangilaHookState:
+    """What ``register_nangila_hook`` returns: per-bucket predictor / EF state,
+    byte counters, metrics and the communicator."""
     config: HookConfig
     group: object = None
     comm: FusedAllReduce | None = None

@@ -26,6 +26,7 @@ _PREFIX = "ngl/monitor"
 
 
 class RankMonitor:
+    """Per-step membership handshake in the process group's store; see the module docstring."""
     def __init__(self, group=None, store=None, comms=(), timeout_s: float = 10.0):
         self.group = group
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0

@@ -15,6 +15,7 @@ from .._ext import cuda as _cuda
 
 
 class SymmetricRegion:
+    """One device allocation per rank, mapped into every peer through CUDA IPC handles."""
     def __init__(self, nbytes: int, group=None, device: torch.device | None = None):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1

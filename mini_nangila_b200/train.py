@@ -57,6 +57,7 @@ def init_distributed(backend: str | None = None, timeout_s: float = 300.0) -> tu
 
 
 class DDPTrainer:
+    """DDP + gradient hook + AdamW (+ bf16 autocast) training steps; see the module docstring."""
     def __init__(
         self,
         model: torch.nn.Module,

@@ -11,10 +11,13 @@ from ..core.fixed_point import FixedPointBuffer, ShapeMismatch
 
 
 class SyncError(ValueError):
+    """A closed-loop step failed (shape mismatch or a malformed payload)."""
     pass
 
 
 class EdgeNode:
+    """Sender of the closed loop (nangila-twin/src/edge_sync.rs:29-63): predict, quantize
+    the residual, and update the predictor with the reconstruction the receiver computes."""
     def __init__(self, predictor, quantizer):
         self.predictor = predictor
         self.quantizer = quantizer
@@ -33,6 +36,7 @@ class EdgeNode:
 
 
 class CloudNode:
+    """Receiver of the closed loop (nangila-twin/src/edge_sync.rs:83-102); mirrors ``EdgeNode``."""
     def __init__(self, predictor, quantizer):
         self.predictor = predictor
         self.quantizer = quantizer

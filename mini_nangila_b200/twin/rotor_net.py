@@ -111,10 +111,12 @@ class Frame:
 
 
 def encode_ack(ok: bool) -> bytes:
+    """Protobuf bytes of ``Ack { ok }`` (rotor.proto)."""
     return b"\x08\x01" if ok else b""
 
 
 def decode_ack(b: bytes) -> bool:
+    """Parse ``Ack`` bytes."""
     i, ok = 0, False
     while i < len(b):
         key, i = _read_varint(b, i)
@@ -125,6 +127,7 @@ def decode_ack(b: bytes) -> bool:
 
 
 def imu_sample(t: float) -> np.ndarray:
+    """The client's synthetic 6-DOF IMU reading at time t (rotor_twin_net client.rs)."""
     w = np.float32(t) * np.float32(2.0) * np.float32(np.pi) * np.float32(1.67)
     s, c = np.sin(w), np.cos(w)
     return np.array([s, c, 0.01, s * np.float32(5.0), c * np.float32(5.0), 0.0], dtype=np.float32)

@@ -4,6 +4,7 @@ built tiny and stepped on CPU: GPT-2 with the INT4 + EMA hook and the
 Llama family with the hook in top-k mode."""
 import os
 import socket
+import sys
 import types
 
 import pytest
@@ -25,6 +26,7 @@ def test_reference_arm_steps(model, mode, name):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(s.getsockname()[1]))
     s.close()
     dist.init_process_group("gloo", rank=0, world_size=1)
+    saved_path = list(sys.path)
     try:
         args = types.SimpleNamespace(model=model, mode=mode, topk=0.05, momentum="auto")
         step, why, hook_name = bench.build_reference(args, torch.device("cpu"), tiny=True)
@@ -35,3 +37,9 @@ def test_reference_arm_steps(model, mode, name):
         assert all(torch.isfinite(torch.tensor(losses)))
     finally:
         dist.destroy_process_group()
+        # build_reference puts baseline/_ref first on sys.path and imports the
+        # reference's nangila_ddp; later tests in this process must get the shim
+        sys.path[:] = saved_path
+        for name in [m for m in sys.modules if m == "nangila_ddp" or m.startswith("nangila_ddp.")]:
+            if "_ref" in (getattr(sys.modules[name], "__file__", "") or ""):
+                del sys.modules[name]
