@@ -31,13 +31,14 @@ class ClockSampler:
     def start(self) -> "ClockSampler":
         fd, self.path = tempfile.mkstemp(prefix="ngl_clocks_", suffix=".csv")
         os.close(fd)
-        cmd = ["nvidia-smi", f"--query-gpu={','.join(FIELDS)}", "--format=csv,noheader,nounits", f"-lms", str(self.period_ms)]
+        cmd = ["nvidia-smi", f"--query-gpu={','.join(FIELDS)}", "--format=csv,noheader,nounits", "-lms",
+               str(self.period_ms)]
         if self.gpus:
             cmd += ["-i", ",".join(str(g) for g in self.gpus)]
         try:
-            self.proc = subprocess.Popen(cmd, stdout=open(self.path, "w"), stderr=subprocess.DEVNULL,
-                                         start_new_session=True)
-        except (OSError, FileNotFoundError):
+            with open(self.path, "w") as log:  # the child keeps its own descriptor
+                self.proc = subprocess.Popen(cmd, stdout=log, stderr=subprocess.DEVNULL, start_new_session=True)
+        except OSError:
             self.proc = None
         return self
 

@@ -123,6 +123,36 @@ def test_grpc_server_under_concurrent_clients(tmp_path):
     assert sorted(int(line.split(",")[1]) for line in lines) == sorted(100 * k + t for k in range(4) for t in range(25))
 
 
+def test_grpc_twin_cli_apps(tmp_path):
+    """The server and client CLIs with the reference's flags (the client
+    takes the reference's ``http://`` address form)."""
+    pytest.importorskip("grpc")
+    import socket
+    import subprocess
+    import sys
+
+    from mini_nangila_b200.apps import rotor_twin_client
+
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    srv = subprocess.Popen([sys.executable, "-u", "-m", "mini_nangila_b200.apps.rotor_twin_server", "--listen",
+                            f"127.0.0.1:{port}", "--metrics", str(tmp_path / "s.csv")], cwd=root,
+                           stdout=subprocess.PIPE, text=True)
+    try:
+        assert "listening" in srv.stdout.readline()
+        rotor_twin_client.main(["--server", f"http://127.0.0.1:{port}", "--duration", "1", "--rate-hz", "20",
+                                "--metrics", str(tmp_path / "c.csv")])
+    finally:
+        srv.terminate()
+        srv.wait(timeout=30)
+    n_client = len(open(tmp_path / "c.csv").read().splitlines())
+    n_server = len(open(tmp_path / "s.csv").read().splitlines())
+    assert n_client >= 10 and n_server >= 10 and abs(n_client - n_server) <= 1
+
+
 def test_train_nano_two_cpu_ranks(tmp_path):
     import socket
     import subprocess

@@ -1,0 +1,67 @@
+"""Measurement helpers: clock sampling (against a fake nvidia-smi that
+prints the queried fields), max over ranks on gloo, NVTX ranges without
+CUDA."""
+import os
+import socket
+import time
+
+import torch
+import torch.multiprocessing as mp
+
+from mini_nangila_b200.utils.clocks import FIELDS, ClockSampler
+from mini_nangila_b200.utils.nvtx import enabled, nvtx_range
+from mini_nangila_b200.utils.timing import WallTimer
+
+
+def test_clock_sampler_parses_samples_and_reasons(tmp_path, monkeypatch):
+    fake = tmp_path / "nvidia-smi"
+    loaded = "0, 1965, 1965, 700.5, 0x4, Not Active, Not Active, Not Active, Active"
+    idle = "0, 345, 1965, 95.0, 0x0, Not Active, Not Active, Not Active, Not Active"
+    fake.write_text("#!/bin/sh\n" + "".join(f"echo '{r}'\n" for r in (idle, loaded, loaded, loaded, idle))
+                    + "exec sleep 30\n")
+    fake.chmod(0o755)
+    monkeypatch.setenv("PATH", f"{tmp_path}:{os.environ['PATH']}")
+    s = ClockSampler([0], period_ms=50).start()
+    time.sleep(0.5)
+    out = s.stop()
+    assert len(loaded.split(",")) == len(FIELDS)
+    assert out["samples"] == 5 and out["sm_mhz"] == 1965.0 and out["sm_max_mhz"] == 1965.0
+    assert out["reasons"] == ["sw_power_cap"] and out["power_w_max"] == 700.5
+
+
+def test_clock_sampler_without_nvidia_smi(tmp_path, monkeypatch):
+    monkeypatch.setenv("PATH", str(tmp_path))
+    out = ClockSampler().start().stop()
+    assert out["samples"] == 0 and out["sm_mhz"] is None
+
+
+def _max_worker(rank, world, port, outdir):
+    import torch.distributed as dist
+
+    from mini_nangila_b200.utils.timing import barrier_sync, max_over_ranks
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        barrier_sync()
+        v = max_over_ranks(10.0 + rank)
+        torch.save(v, os.path.join(outdir, f"m{rank}.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_max_over_ranks(tmp_path):
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    mp.start_processes(_max_worker, args=(3, port, str(tmp_path)), nprocs=3, join=True, start_method="spawn")
+    assert [torch.load(tmp_path / f"m{r}.pt") for r in range(3)] == [12.0, 12.0, 12.0]
+
+
+def test_nvtx_range_and_wall_timer():
+    if not torch.cuda.is_available():
+        assert not enabled()
+    with nvtx_range("x"):
+        t = WallTimer().start()
+    assert t.stop() >= 0.0
