@@ -6,6 +6,7 @@
 
 #include "../common/ngl_scalar.h"
 #include "nangila_host.hpp"
+#include "fast_scalar.h"
 
 namespace ngl {
 namespace host {
@@ -35,12 +36,12 @@ inline size_t div_ceil(size_t a, size_t b) { return (a + b - 1) / b; }
 // ---------------------------------------------------------------- nangila-math
 Fixed q823_from_f32(const float* x, size_t n) {
   Fixed out(n);
-  for (size_t i = 0; i < n; ++i) out[i] = ngl::q823_from_f32(x[i]);
+  for (size_t i = 0; i < n; ++i) out[i] = fast::q823_from_f32(x[i]);
   return out;
 }
 Floats q823_to_f32(const int32_t* q, size_t n) {
   Floats out(n);
-  for (size_t i = 0; i < n; ++i) out[i] = ngl::q823_to_f32(q[i]);
+  for (size_t i = 0; i < n; ++i) out[i] = fast::q823_to_f32(q[i]);
   return out;
 }
 Fixed q823_add(const int32_t* a, size_t na, const int32_t* b, size_t nb) {
@@ -78,36 +79,32 @@ QuantOut stochastic_quantize(const int32_t* r, size_t n, int bits, uint64_t seed
   QuantOut out{{}, 1.0f};
   Floats f = to_f32(r, n);
   if (f.empty()) return out;
-  float max_val = 0.0f;
-  for (float x : f) max_val = f_max(max_val, f_abs(x));
+  const float max_val = fast::absmax(f.data(), f.size());
   float scale = 1.0f;
   if (max_val > 1e-9f) {
     int levels = (bits >= 1 && bits < 31) ? ((1 << bits) - 1) : 255;
     scale = max_val / ((float)levels / 2.0f);
   }
   out.scale = scale;
+  const uint64_t c0 = *counter;  // element i uses counter c0 + i
   if (bits == 4) {
-    out.bytes.reserve((n + 1) / 2);
-    for (size_t i = 0; i < n; i += 2) {
-      uint8_t byte = 0;
-      for (size_t j = 0; j < 2 && i + j < n; ++j) {
-        int32_t q = compat_stochastic_round(f[i + j] / scale, seed, *counter);
-        *counter += 1;
-        q = std::min(std::max(q, -8), 7);
-        uint8_t nibble = (uint8_t)((int8_t)q & 0x0F);
-        if (j == 0) byte |= (uint8_t)(nibble << 4);
-        else byte |= nibble;
-      }
-      out.bytes.push_back(byte);
-    }
-  } else if (bits == 8) {
-    out.bytes.reserve(n);
+    out.bytes.assign((n + 1) / 2, 0);
+    uint8_t* o = out.bytes.data();
     for (size_t i = 0; i < n; ++i) {
-      int32_t q = compat_stochastic_round(f[i] / scale, seed, *counter);
-      *counter += 1;
-      q = std::min(std::max(q, -128), 127);
-      out.bytes.push_back((uint8_t)(int8_t)q);
+      int32_t q = fast::stochastic_round(f[i] / scale, seed, c0 + i);
+      q = std::min(std::max(q, -8), 7);
+      const uint8_t nibble = (uint8_t)((int8_t)q & 0x0F);
+      o[i >> 1] |= (i & 1) ? nibble : (uint8_t)(nibble << 4);  // first element of a pair -> high nibble
     }
+    *counter = c0 + n;
+  } else if (bits == 8) {
+    out.bytes.resize(n);
+    uint8_t* o = out.bytes.data();
+    for (size_t i = 0; i < n; ++i) {
+      const int32_t q = fast::stochastic_round(f[i] / scale, seed, c0 + i);
+      o[i] = (uint8_t)(int8_t)std::min(std::max(q, -128), 127);
+    }
+    *counter = c0 + n;
   } else {
     // Fallback: deterministic INT8 rounding with Rust f32::clamp (NaN stays
     // NaN and then casts to 0).
@@ -123,21 +120,19 @@ QuantOut stochastic_quantize(const int32_t* r, size_t n, int bits, uint64_t seed
 
 // unified_quantizer.rs:225-250
 Fixed stochastic_dequantize(const uint8_t* b, size_t nb, float scale, int bits) {
-  Floats rec;
   if (bits == 4) {
-    rec.reserve(nb * 2);
+    Fixed out(nb * 2);  // two values per byte: an odd length gains a trailing 0 (Q10)
     for (size_t i = 0; i < nb; ++i) {
-      int8_t high = (int8_t)(uint8_t)(b[i] >> 4);
-      high = (int8_t)(high << 4);
-      rec.push_back((float)(high >> 4) * scale);
-      int8_t low = (int8_t)(uint8_t)(b[i] << 4);
-      rec.push_back((float)(low >> 4) * scale);
+      const int8_t high = (int8_t)(uint8_t)(b[i] & 0xF0);   // high nibble, sign in bit 7
+      const int8_t low = (int8_t)(uint8_t)(b[i] << 4);
+      out[2 * i] = fast::q823_from_f32((float)(high >> 4) * scale);
+      out[2 * i + 1] = fast::q823_from_f32((float)(low >> 4) * scale);
     }
-  } else {
-    rec.reserve(nb);
-    for (size_t i = 0; i < nb; ++i) rec.push_back((float)(int8_t)b[i] * scale);
+    return out;
   }
-  return from_f32(rec);
+  Fixed out(nb);
+  for (size_t i = 0; i < nb; ++i) out[i] = fast::q823_from_f32((float)(int8_t)b[i] * scale);
+  return out;
 }
 
 // unified_quantizer.rs:253-279 (same layout as nangila-hpc ErrorBounded)
@@ -226,13 +221,18 @@ Fixed topk_dequantize(const uint8_t* b, size_t nb, float scale) {
 QuantOut eb_quantize(const int32_t* r, size_t n, float eps) {
   const float scale = 2.0f * eps;
   QuantOut out{{}, scale};
-  out.bytes.reserve(n * 2);
-  for (size_t i = 0; i < n; ++i) put_i16(out.bytes, eb_code(ngl::q823_to_f32(r[i]), scale));
+  out.bytes.resize(n * 2);
+  uint8_t* o = out.bytes.data();
+  for (size_t i = 0; i < n; ++i) {
+    const uint16_t c = (uint16_t)fast::eb_code(fast::q823_to_f32(r[i]), scale);
+    o[2 * i] = (uint8_t)(c & 0xFF);
+    o[2 * i + 1] = (uint8_t)(c >> 8);
+  }
   return out;
 }
 Fixed eb_dequantize(const uint8_t* b, size_t nb, float scale) {
   Fixed out(nb / 2);
-  for (size_t i = 0; i + 2 <= nb; i += 2) out[i / 2] = ngl::q823_from_f32((float)get_i16(b + i) * scale);
+  for (size_t i = 0; i + 2 <= nb; i += 2) out[i / 2] = fast::q823_from_f32((float)get_i16(b + i) * scale);
   return out;
 }
 
@@ -243,7 +243,7 @@ QuantOut rle_quantize(const int32_t* r, size_t n, float eps) {
   const float scale = 2.0f * eps;
   out.scale = scale;
   std::vector<int16_t> q(n);
-  for (size_t i = 0; i < n; ++i) q[i] = eb_code(ngl::q823_to_f32(r[i]), scale);
+  for (size_t i = 0; i < n; ++i) q[i] = fast::eb_code(fast::q823_to_f32(r[i]), scale);
   out.bytes = rle_encode_i16(q.data(), n);
   return out;
 }
@@ -285,7 +285,7 @@ std::vector<int16_t> rle_decode_i16(const uint8_t* b, size_t nb) {
 Fixed rle_dequantize(const uint8_t* b, size_t nb, float scale) {
   std::vector<int16_t> q = rle_decode_i16(b, nb);
   Fixed out(q.size());
-  for (size_t i = 0; i < q.size(); ++i) out[i] = ngl::q823_from_f32((float)q[i] * scale);
+  for (size_t i = 0; i < q.size(); ++i) out[i] = fast::q823_from_f32((float)q[i] * scale);
   return out;
 }
 
@@ -301,7 +301,7 @@ QuantOut bs_quantize(const int32_t* r, size_t n, float eps) {
     int16_t vals[32];
     int nv = 0;
     for (size_t i = 0; i < len; ++i) {
-      int16_t q = eb_code(ngl::q823_to_f32(r[s + i]), scale);
+      int16_t q = fast::eb_code(fast::q823_to_f32(r[s + i]), scale);
       if (q != 0) {
         mask |= 1u << i;
         vals[nv++] = q;
@@ -348,7 +348,7 @@ QuantOut bsrle_quantize(const int32_t* r, size_t n, float eps) {
   const size_t num_blocks = div_ceil(n, 32);
   std::vector<uint32_t> masks(num_blocks);
   std::vector<int16_t> q(n);
-  for (size_t i = 0; i < n; ++i) q[i] = eb_code(ngl::q823_to_f32(r[i]), scale);
+  for (size_t i = 0; i < n; ++i) q[i] = fast::eb_code(fast::q823_to_f32(r[i]), scale);
   for (size_t blk = 0; blk < num_blocks; ++blk) {
     uint32_t m = 0;
     size_t s = blk * 32, len = std::min<size_t>(32, n - s);

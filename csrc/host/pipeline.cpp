@@ -5,6 +5,7 @@
 
 #include "../common/ngl_scalar.h"
 #include "nangila_host.hpp"
+#include "fast_scalar.h"
 
 namespace ngl {
 namespace host {
@@ -187,7 +188,7 @@ Bytes nz_compress(const float* data, size_t particles, size_t steps, int codec, 
     Fixed recon = p.empty() ? deq : q823_add(p.data(), p.size(), deq.data(), deq.size());
     pred.update(recon.data(), recon.size());
     for (size_t i = 0; i < particles && i < recon.size(); ++i) {
-      float e = std::fabs(ngl::q823_to_f32(buf[i]) - ngl::q823_to_f32(recon[i]));
+      float e = std::fabs(fast::q823_to_f32(buf[i]) - fast::q823_to_f32(recon[i]));
       if (e > st.max_abs_err) st.max_abs_err = e;
     }
     put_f32(out, q.scale);
