@@ -112,3 +112,24 @@ def test_baselines_app(tmp_path, monkeypatch):
     assert len(summary["0.001"]["tools"]) == 5  # four codecs and ZFP; the skipped SZ row is left out
     txt = open(os.path.join("baseline_results", "baseline_comparison.txt")).read()
     assert "Original size:" in txt and "Mini-Nangila (BlockSparse+RLE) (eps=0.001):" in txt and "SZ: SKIPPED" in txt
+
+
+def test_reader_on_random_text_raises_only_format_errors():
+    from hypothesis import given, settings
+    from hypothesis import strategies as st
+
+    base = _dump(["1 1 0.5 1.5 2.5", "2 1 -1 -2 -3"])
+    alphabet = st.sampled_from(list("ITEM: TIMESTEPNUMBEROFATOMSBXyzxyz0123456789.e+-\n \t"))
+
+    @settings(max_examples=300, deadline=None)
+    @given(st.integers(0, len(base)), st.lists(alphabet, max_size=120))
+    def run(cut, extra):
+        text = base[:cut] + "".join(extra)
+        try:
+            snaps = lammps.read_dump_text(text)
+        except lammps.DumpFormatError:
+            return
+        for s in snaps:
+            assert s.dtype == np.float32 and s.size % 3 == 0
+
+    run()
