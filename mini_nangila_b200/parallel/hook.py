@@ -26,8 +26,17 @@ their residual to the next step.  The reference drops single elements with a
 seeded ``randperm`` (``comm_hook.py:149-174``); ``impl="compat"`` does that.
 
 The hook state object returned by ``register_nangila_hook`` exposes
-``state_dict()/load_state_dict()`` (predictor and error-feedback buffers,
-call counters) so a resumed run continues bit-identically.
+``state_dict()/load_state_dict()``: the predictor and error-feedback
+buffers, the call counters (the noise keys), and each bucket's parameter
+layout. A resumed run continues bit-identically while the bucket layout
+matches. Otherwise each parameter's state follows it into the new buckets;
+this also happens in a live run when DDP rebuilds its buckets after the
+first iteration.
+
+With ``metrics_path`` set, rank 0 appends one line per bucket in the
+reference's ``key,value`` layout. Its ``res_mean_abs`` (mean |g - pred|) is
+computed on the device and written once it has landed, so logging adds no
+host sync.
 """
 from __future__ import annotations
 
