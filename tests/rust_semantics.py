@@ -60,7 +60,7 @@ def stochastic_int4(q, seed, counter):
             frac = F32(v - fl)
             h = fmix64((seed ^ counter) & M64)
             counter += 1
-            r = F32(F32(float(h)) / F32(18446744073709551616.0))
+            r = F32(np.uint64(h).astype(np.float32) / F32(18446744073709551616.0))  # one rounding, as Rust's `as f32`
             qq = int(fl) + 1 if r < frac else int(fl)
             qq = min(max(qq, -8), 7)
             nib = qq & 0xF
