@@ -3,6 +3,8 @@
 #include <pybind11/pybind11.h>
 #include <pybind11/stl.h>
 
+#include <string>
+
 #include "nangila_host.hpp"
 
 namespace py = pybind11;
@@ -24,6 +26,17 @@ const T* ptr(const carr<T>& a) {
   return a.size() ? a.data() : nullptr;
 }
 py::tuple qout(QuantOut&& q) { return py::make_tuple(to_np(std::move(q.bytes)), q.scale); }
+// An optional output array (None, or float32, C-contiguous, writable, n
+// elements) that a call writes in place instead of returning a new one.
+float* out_f32(const py::object& o, size_t n, const char* what) {
+  if (o.is_none()) return nullptr;
+  auto a = o.cast<py::array_t<float, py::array::c_style>>();
+  // a converted copy would be written and lost: the caller's array must already conform
+  if (a.ptr() != o.ptr()) throw std::runtime_error(std::string(what) + " must be a float32 C-contiguous array");
+  if ((size_t)a.size() != n) throw std::runtime_error(std::string(what) + " size mismatch");
+  if (!a.writeable()) throw std::runtime_error(std::string(what) + " is read-only");
+  return a.mutable_data();
+}
 }  // namespace
 
 PYBIND11_MODULE(_host, m) {
@@ -167,14 +180,17 @@ PYBIND11_MODULE(_host, m) {
     return py::make_tuple(t.a, t.b, t.ndrop);
   });
   m.def("product_encode", [](carr<float> g, py::object pred, py::object e_in, int bits, bool stochastic, bool ef,
-                             uint64_t seed, uint32_t rank, uint32_t bucket, uint64_t step, py::tuple topo) {
+                             uint64_t seed, uint32_t rank, uint32_t bucket, uint64_t step, py::tuple topo,
+                             py::object e_out_arr) {
     const size_t n = g.size();
     carr<float> pr = pred.is_none() ? carr<float>() : pred.cast<carr<float>>();
     carr<float> ei = e_in.is_none() ? carr<float>() : e_in.cast<carr<float>>();
     if (!pred.is_none() && (size_t)pr.size() != n) throw std::runtime_error("pred size mismatch");
     if (!e_in.is_none() && (size_t)ei.size() != n) throw std::runtime_error("e size mismatch");
     std::vector<uint8_t> wire(product_wire_bytes(n, bits == 4 ? 0 : 1, 0));
-    std::vector<float> e_out(ef ? n : 0);
+    float* e_dst = ef ? out_f32(e_out_arr, n, "e_out") : nullptr;
+    std::vector<float> e_out(ef && !e_dst ? n : 0);
+    if (ef && !e_dst) e_dst = e_out.data();
     ProductParams p;
     p.bits = bits;
     p.stochastic = stochastic;
@@ -188,31 +204,47 @@ PYBIND11_MODULE(_host, m) {
       p.topo_b = topo[1].cast<uint64_t>();
       p.topo_ndrop = topo[2].cast<int64_t>();
     }
+    // e_out may be e_in itself: each block's residuals are read before its
+    // error feedback is written, and blocks are disjoint
     product_encode(ptr(g), pred.is_none() ? nullptr : ptr(pr), e_in.is_none() ? nullptr : ptr(ei), n, p,
-                   wire.data(), ef ? e_out.data() : nullptr);
-    return py::make_tuple(to_np(std::move(wire)), to_np(std::move(e_out)));
+                   wire.data(), e_dst);
+    py::object e_ret = (ef && !e_out_arr.is_none()) ? e_out_arr : py::object(to_np(std::move(e_out)));
+    return py::make_tuple(to_np(std::move(wire)), e_ret);
   }, py::arg("g"), py::arg("pred"), py::arg("e_in"), py::arg("bits"), py::arg("stochastic"), py::arg("ef"),
-     py::arg("seed"), py::arg("rank"), py::arg("bucket"), py::arg("step"), py::arg("topo") = py::tuple());
+     py::arg("seed"), py::arg("rank"), py::arg("bucket"), py::arg("step"), py::arg("topo") = py::tuple(),
+     py::arg("e_out") = py::none());
   auto reduce_impl = [](bool twoshot) {
-    return [twoshot](std::vector<carr<uint8_t>> wires, size_t n, int bits, py::object pred, float inv_world) {
+    return [twoshot](std::vector<carr<uint8_t>> wires, size_t n, int bits, py::object pred, float inv_world,
+                     py::object out) -> py::object {
       const int W = (int)wires.size();
       std::vector<const uint8_t*> wp(W);
       for (int r = 0; r < W; ++r) wp[r] = ptr(wires[r]);
       carr<float> pr = pred.is_none() ? carr<float>() : pred.cast<carr<float>>();
-      std::vector<float> avg(n);
+      float* dst = out_f32(out, n, "out");
+      std::vector<float> avg(dst ? 0 : n);
+      if (!dst) dst = avg.data();
       if (twoshot)
-        product_reduce_twoshot(wp.data(), W, n, bits, pred.is_none() ? nullptr : ptr(pr), inv_world, avg.data());
+        product_reduce_twoshot(wp.data(), W, n, bits, pred.is_none() ? nullptr : ptr(pr), inv_world, dst);
       else
-        product_reduce(wp.data(), W, n, bits, pred.is_none() ? nullptr : ptr(pr), inv_world, avg.data());
-      return to_np(std::move(avg));
+        product_reduce(wp.data(), W, n, bits, pred.is_none() ? nullptr : ptr(pr), inv_world, dst);
+      return out.is_none() ? py::object(to_np(std::move(avg))) : out;
     };
   };
-  m.def("product_reduce", reduce_impl(false));
-  m.def("product_reduce_twoshot", reduce_impl(true));
+  m.def("product_reduce", reduce_impl(false), py::arg("wires"), py::arg("n"), py::arg("bits"), py::arg("pred"),
+        py::arg("inv_world"), py::arg("out") = py::none());
+  m.def("product_reduce_twoshot", reduce_impl(true), py::arg("wires"), py::arg("n"), py::arg("bits"), py::arg("pred"),
+        py::arg("inv_world"), py::arg("out") = py::none());
   m.def("product_ema", [](carr<float> state, carr<float> avg, float beta, bool first) {
     std::vector<float> s(state.data(), state.data() + state.size());
     product_ema(s.data(), ptr(avg), s.size(), beta, first);
     return to_np(std::move(s));
+  });
+  // In place on a float32 C-contiguous writable state array.
+  m.def("product_ema_", [](py::object state, carr<float> avg, float beta, bool first) {
+    const size_t n = (size_t)avg.size();
+    float* s = out_f32(state, n, "state");
+    if (!s) throw std::runtime_error("state is required");
+    product_ema(s, ptr(avg), n, beta, first);
   });
   m.def("product_topk_encode", [](carr<float> g, py::object pred, py::object e_in, int k, bool ef, py::tuple topo) {
     TopoChunks t;

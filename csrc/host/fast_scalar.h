@@ -21,6 +21,17 @@
 
 #include "../common/ngl_scalar.h"
 
+// Loops that use a fused multiply-add get an FMA-instruction clone next to
+// the baseline one (GCC function multiversioning, chosen once at load time).
+// Both compute the correctly rounded fma of the reference rule (the baseline
+// through libm's fmaf), so the results are identical; -ffp-contract=off
+// keeps every other multiply and add separate in both clones.
+#if defined(__GNUC__) && !defined(__clang__) && defined(__x86_64__)
+#define NGL_HOST_FMA_CLONES __attribute__((target_clones("fma", "default")))
+#else
+#define NGL_HOST_FMA_CLONES
+#endif
+
 namespace ngl {
 namespace host {
 namespace fast {

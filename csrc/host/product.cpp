@@ -1,6 +1,8 @@
 // Host oracle of the product wire format used by the fused all-reduce kernel
-// (csrc/cuda/fused_allreduce.cu).  Same per-element arithmetic
-// (csrc/common/ngl_product.h) in plain sequential loops.
+// (csrc/cuda/fused_kernels.cu).  Same per-element arithmetic
+// (csrc/common/ngl_product.h).  Blocks are independent and the noise is
+// counter-based, so the block loops run on host threads (parallel.h) with
+// results that do not depend on the thread count.
 #include <algorithm>
 #include <cmath>
 #include <cstring>
@@ -8,6 +10,8 @@
 
 #include "../common/ngl_product.h"
 #include "nangila_host.hpp"
+#include "fast_scalar.h"
+#include "parallel.h"
 
 namespace ngl {
 namespace host {
@@ -54,61 +58,69 @@ void product_encode(const float* g, const float* pred, const float* e_in, size_t
   const size_t bpb = p.bits == 4 ? kInt4BlockBytes : kInt8BlockBytes;
   const size_t cr = chunk_record_bytes(p.bits == 4 ? 0 : 1, 0);
   std::memset(wire, 0, nchunks_of(n) * cr);
-  float c[kBlock];
-  int32_t q[kBlock];
   const uint64_t nch = nchunks_of(n);
-  for (size_t b = 0; b < nblk; ++b) {
-    const size_t base = b * kBlock;
-    const size_t len = std::min<size_t>(kBlock, n - base);
-    if (topo_passenger(b / kChunkBlocks, p.topo_a, p.topo_b, p.topo_ndrop, nch)) {
-      // passenger: zero record, the whole residual goes to the error feedback
-      if (p.error_feedback && e_out)
-        for (size_t i = 0; i < len; ++i)
-          e_out[base + i] = product_residual(g[base + i], pred ? pred[base + i] : 0.0f, e_in ? e_in[base + i] : 0.0f);
-      continue;
-    }
-    float absmax = 0.0f;
-    for (size_t i = 0; i < kBlock; ++i) {
-      if (i < len) {
-        float pr = pred ? pred[base + i] : 0.0f;
-        float e = (p.error_feedback && e_in) ? e_in[base + i] : 0.0f;
-        c[i] = product_residual(g[base + i], pr, e);
-        absmax = f_max(absmax, f_abs(c[i]));
-      } else {
-        c[i] = 0.0f;
+  parallel_for(nblk, 64, [&](size_t lo, size_t hi) {
+    for (size_t b = lo; b < hi; ++b) {
+      float c[kBlock];
+      int32_t q[kBlock];
+      const size_t base = b * kBlock;
+      const size_t len = std::min<size_t>(kBlock, n - base);
+      if (topo_passenger(b / kChunkBlocks, p.topo_a, p.topo_b, p.topo_ndrop, nch)) {
+        // passenger: zero record, the whole residual goes to the error feedback
+        if (p.error_feedback && e_out)
+          for (size_t i = 0; i < len; ++i)
+            e_out[base + i] = product_residual(g[base + i], pred ? pred[base + i] : 0.0f, e_in ? e_in[base + i] : 0.0f);
+        continue;
       }
-    }
-    const float s = product_scale(absmax, qmaxf);
-    const float inv = product_inv(s);
-    *dense_scale(wire, b, cr) = s;
-    for (size_t i = 0; i < kBlock; i += 4) {
-      U32x4 r = {0, 0, 0, 0};
-      if (p.stochastic) r = product_noise4(p.seed, p.rank, p.bucket, p.step, (uint32_t)((base + i) / 4));
-      const uint32_t rb[4] = {r.x, r.y, r.z, r.w};
-      for (int j = 0; j < 4; ++j) {
-        const size_t k = i + j;
-        if (k >= len) {
-          q[k] = 0;
-          continue;
+      float absmax = 0.0f;
+      for (size_t i = 0; i < kBlock; ++i) {
+        if (i < len) {
+          float pr = pred ? pred[base + i] : 0.0f;
+          float e = (p.error_feedback && e_in) ? e_in[base + i] : 0.0f;
+          c[i] = product_residual(g[base + i], pr, e);
+          // maxNum fold; c is an arithmetic result, so never a signaling NaN
+          const float a = f_abs(c[i]);
+          absmax = a > absmax ? a : absmax;
+        } else {
+          c[i] = 0.0f;
         }
-        q[k] = p.stochastic ? product_code_sr(c[k], inv, u01_from_bits(rb[j]), qmax) : product_code_rn(c[k], inv, qmax);
-        if (p.error_feedback && e_out) e_out[base + k] = NGL_FSUB(c[k], product_deq(q[k], s));
+      }
+      const float s = product_scale(absmax, qmaxf);
+      const float inv = product_inv(s);
+      *dense_scale(wire, b, cr) = s;
+      for (size_t i = 0; i < kBlock; i += 4) {
+        U32x4 r = {0, 0, 0, 0};
+        if (p.stochastic) r = product_noise4(p.seed, p.rank, p.bucket, p.step, (uint32_t)((base + i) / 4));
+        const uint32_t rb[4] = {r.x, r.y, r.z, r.w};
+        for (int j = 0; j < 4; ++j) {
+          const size_t k = i + j;
+          if (k >= len) {
+            q[k] = 0;
+            continue;
+          }
+          q[k] = p.stochastic ? product_code_sr(c[k], inv, u01_from_bits(rb[j]), qmax) : product_code_rn(c[k], inv, qmax);
+          if (p.error_feedback && e_out) e_out[base + k] = NGL_FSUB(c[k], product_deq(q[k], s));
+        }
+      }
+      uint8_t* out = dense_codes(wire, b, cr, bpb);
+      if (p.bits == 4) {
+        for (size_t j = 0; j < kInt4BlockBytes; ++j) out[j] = (uint8_t)((nib(q[2 * j]) << 4) | nib(q[2 * j + 1]));
+      } else {
+        for (size_t j = 0; j < kInt8BlockBytes; ++j) out[j] = (uint8_t)(int8_t)q[j];
       }
     }
-    uint8_t* out = dense_codes(wire, b, cr, bpb);
-    if (p.bits == 4) {
-      for (size_t j = 0; j < kInt4BlockBytes; ++j) out[j] = (uint8_t)((nib(q[2 * j]) << 4) | nib(q[2 * j + 1]));
-    } else {
-      for (size_t j = 0; j < kInt8BlockBytes; ++j) out[j] = (uint8_t)(int8_t)q[j];
-    }
-  }
+  });
 }
 
-void product_reduce(const uint8_t* const* wires, int world, size_t n, int bits, const float* pred, float inv_world,
-                    float* avg_out) {
+namespace detail {
+// Range bodies of the loops that use a fused multiply-add: named functions,
+// so each carries its FMA clone (a lambda would not inherit it).
+NGL_HOST_FMA_CLONES
+void reduce_range(const uint8_t* const* wires, int world, int bits, const float* pred, float inv_world,
+                  float* avg_out, size_t lo, size_t hi) {
   const size_t bpb = bits == 4 ? kInt4BlockBytes : kInt8BlockBytes;
   const size_t cr = chunk_record_bytes(bits == 4 ? 0 : 1, 0);
-  for (size_t i = 0; i < n; ++i) {
+  for (size_t i = lo; i < hi; ++i) {
     const size_t b = i / kBlock, k = i % kBlock;
     float acc = 0.0f;
     for (int r = 0; r < world; ++r) {
@@ -126,9 +138,22 @@ void product_reduce(const uint8_t* const* wires, int world, size_t n, int bits, 
   }
 }
 
-void product_ema(float* state, const float* avg, size_t n, float beta, bool first) {
+NGL_HOST_FMA_CLONES
+void ema_range(float* state, const float* avg, float beta, bool first, size_t lo, size_t hi) {
   const float omb = 1.0f - beta;
-  for (size_t i = 0; i < n; ++i) state[i] = ngl::product_ema(state[i], avg[i], beta, omb, first);
+  for (size_t i = lo; i < hi; ++i) state[i] = ngl::product_ema(state[i], avg[i], beta, omb, first);
+}
+}  // namespace detail
+
+void product_reduce(const uint8_t* const* wires, int world, size_t n, int bits, const float* pred, float inv_world,
+                    float* avg_out) {
+  parallel_for(n, 1u << 15, [&](size_t lo, size_t hi) {
+    detail::reduce_range(wires, world, bits, pred, inv_world, avg_out, lo, hi);
+  });
+}
+
+void product_ema(float* state, const float* avg, size_t n, float beta, bool first) {
+  parallel_for(n, 1u << 15, [&](size_t lo, size_t hi) { detail::ema_range(state, avg, beta, first, lo, hi); });
 }
 
 namespace {
@@ -144,66 +169,70 @@ void product_topk_encode(const float* g, const float* pred, const float* e_in, s
   const size_t nblk = (n + kBlock - 1) / kBlock;
   const int rb = topk_record_bytes(k);
   std::memset(records, 0, nchunks_of(n) * kChunkBlocks * rb);
-  float c[kBlock];
-  uint32_t mag[kBlock];
   const uint64_t nch = nchunks_of(n);
-  for (size_t b = 0; b < nblk; ++b) {
-    const size_t base = b * kBlock;
-    const int len = (int)std::min<size_t>(kBlock, n - base);
-    if (topo_passenger(b / kChunkBlocks, topo.a, topo.b, topo.ndrop, nch)) {
-      if (ef && e_out)
-        for (int i = 0; i < len; ++i)
-          e_out[base + i] = product_residual(g[base + i], pred ? pred[base + i] : 0.0f, e_in ? e_in[base + i] : 0.0f);
-      continue;
-    }
-    float absmax = 0.0f;
-    for (int i = 0; i < len; ++i) {
-      c[i] = product_residual(g[base + i], pred ? pred[base + i] : 0.0f, (ef && e_in) ? e_in[base + i] : 0.0f);
-      mag[i] = fbits(f_abs(c[i]));
-      absmax = f_max(absmax, f_abs(c[i]));
-    }
-    const int keff = std::min(k, len);
-    // Threshold: largest T with count(mag >= T) >= keff (bitwise search).
-    uint32_t T = 0;
-    for (int bit = 31; bit >= 0; --bit) {
-      uint32_t cand = T | (1u << bit);
-      int cnt = 0;
-      for (int i = 0; i < len; ++i) cnt += mag[i] >= cand;
-      if (cnt >= keff) T = cand;
-    }
-    int gt = 0;
-    for (int i = 0; i < len; ++i) gt += mag[i] > T;
-    int eq_budget = keff - gt;
-    const float s = product_scale(absmax, 127.0f);
-    const float inv = product_inv(s);
-    uint8_t* rec = records + b * rb;
-    std::memcpy(rec, &s, 4);
-    int out = 0;
-    for (int i = 0; i < len; ++i) {
-      bool sel = mag[i] > T;
-      if (!sel && mag[i] == T && eq_budget > 0) {
-        sel = true;
-        --eq_budget;
+  parallel_for(nblk, 64, [&](size_t lo, size_t hi) {
+    for (size_t b = lo; b < hi; ++b) {
+      float c[kBlock];
+      uint32_t mag[kBlock];
+      const size_t base = b * kBlock;
+      const int len = (int)std::min<size_t>(kBlock, n - base);
+      if (topo_passenger(b / kChunkBlocks, topo.a, topo.b, topo.ndrop, nch)) {
+        if (ef && e_out)
+          for (int i = 0; i < len; ++i)
+            e_out[base + i] = product_residual(g[base + i], pred ? pred[base + i] : 0.0f, e_in ? e_in[base + i] : 0.0f);
+        continue;
       }
-      if (sel) {
-        int32_t q = product_code_rn(c[i], inv, 127);
-        rec[4 + out] = (uint8_t)i;
-        rec[4 + k + out] = (uint8_t)(int8_t)q;
-        ++out;
-        if (ef && e_out) e_out[base + i] = NGL_FSUB(c[i], product_deq(q, s));
-      } else if (ef && e_out) {
-        e_out[base + i] = c[i];
+      float absmax = 0.0f;
+      for (int i = 0; i < len; ++i) {
+        c[i] = product_residual(g[base + i], pred ? pred[base + i] : 0.0f, (ef && e_in) ? e_in[base + i] : 0.0f);
+        mag[i] = fbits(f_abs(c[i]));
+        const float a = f_abs(c[i]);  // maxNum fold; c is never a signaling NaN
+        absmax = a > absmax ? a : absmax;
+      }
+      const int keff = std::min(k, len);
+      // Threshold: largest T with count(mag >= T) >= keff (bitwise search).
+      uint32_t T = 0;
+      for (int bit = 31; bit >= 0; --bit) {
+        uint32_t cand = T | (1u << bit);
+        int cnt = 0;
+        for (int i = 0; i < len; ++i) cnt += mag[i] >= cand;
+        if (cnt >= keff) T = cand;
+      }
+      int gt = 0;
+      for (int i = 0; i < len; ++i) gt += mag[i] > T;
+      int eq_budget = keff - gt;
+      const float s = product_scale(absmax, 127.0f);
+      const float inv = product_inv(s);
+      uint8_t* rec = records + b * rb;
+      std::memcpy(rec, &s, 4);
+      int out = 0;
+      for (int i = 0; i < len; ++i) {
+        bool sel = mag[i] > T;
+        if (!sel && mag[i] == T && eq_budget > 0) {
+          sel = true;
+          --eq_budget;
+        }
+        if (sel) {
+          int32_t q = product_code_rn(c[i], inv, 127);
+          rec[4 + out] = (uint8_t)i;
+          rec[4 + k + out] = (uint8_t)(int8_t)q;
+          ++out;
+          if (ef && e_out) e_out[base + i] = NGL_FSUB(c[i], product_deq(q, s));
+        } else if (ef && e_out) {
+          e_out[base + i] = c[i];
+        }
       }
     }
-  }
+  });
 }
 
-void product_topk_reduce(const uint8_t* const* records, int world, size_t n, int k, const float* pred,
-                         float inv_world, float* avg_out) {
-  const size_t nblk = (n + kBlock - 1) / kBlock;
+namespace detail {
+NGL_HOST_FMA_CLONES
+void topk_reduce_range(const uint8_t* const* records, int world, size_t n, int k, const float* pred,
+                       float inv_world, float* avg_out, size_t lo, size_t hi) {
   const int rb = topk_record_bytes(k);
-  float acc[kBlock];
-  for (size_t b = 0; b < nblk; ++b) {
+  for (size_t b = lo; b < hi; ++b) {
+    float acc[kBlock];
     const size_t base = b * kBlock;
     const int len = (int)std::min<size_t>(kBlock, n - base);
     for (int i = 0; i < kBlock; ++i) acc[i] = 0.0f;
@@ -221,16 +250,24 @@ void product_topk_reduce(const uint8_t* const* records, int world, size_t n, int
     for (int i = 0; i < len; ++i) avg_out[base + i] = product_average(pred ? pred[base + i] : 0.0f, acc[i], inv_world);
   }
 }
+}  // namespace detail
 
-// Two-shot: the chunk owner reduces, re-encodes the mean residual as INT8
-// with per-block scales (round to nearest), every rank decodes that.
-void product_reduce_twoshot(const uint8_t* const* wires, int world, size_t n, int bits, const float* pred,
-                            float inv_world, float* avg_out) {
+void product_topk_reduce(const uint8_t* const* records, int world, size_t n, int k, const float* pred,
+                         float inv_world, float* avg_out) {
+  const size_t nblk = (n + kBlock - 1) / kBlock;
+  parallel_for(nblk, 64, [&](size_t lo, size_t hi) {
+      detail::topk_reduce_range(records, world, n, k, pred, inv_world, avg_out, lo, hi);
+  });
+}
+
+namespace detail {
+NGL_HOST_FMA_CLONES
+void twoshot_range(const uint8_t* const* wires, int world, size_t n, int bits, const float* pred, float inv_world,
+                   float* avg_out, size_t lo, size_t hi) {
   const size_t bpb = bits == 4 ? kInt4BlockBytes : kInt8BlockBytes;
   const size_t cr = chunk_record_bytes(bits == 4 ? 0 : 1, 0);
-  const size_t nblk = (n + kBlock - 1) / kBlock;
-  float m[kBlock];
-  for (size_t b = 0; b < nblk; ++b) {
+  for (size_t b = lo; b < hi; ++b) {
+    float m[kBlock];
     const size_t base = b * kBlock;
     const size_t len = std::min<size_t>(kBlock, n - base);
     float absmax = 0.0f;
@@ -250,7 +287,8 @@ void product_reduce_twoshot(const uint8_t* const* wires, int world, size_t n, in
         }
       }
       m[k] = NGL_FMUL(acc, inv_world);
-      absmax = f_max(absmax, f_abs(m[k]));
+      const float a = f_abs(m[k]);  // maxNum fold; m is never a signaling NaN
+      absmax = a > absmax ? a : absmax;
     }
     const float s2 = product_scale(absmax, 127.0f);
     const float inv2 = product_inv(s2);
@@ -259,6 +297,17 @@ void product_reduce_twoshot(const uint8_t* const* wires, int world, size_t n, in
       avg_out[base + k] = product_average(pred ? pred[base + k] : 0.0f, d, 1.0f);
     }
   }
+}
+}  // namespace detail
+
+// Two-shot: the chunk owner reduces, re-encodes the mean residual as INT8
+// with per-block scales (round to nearest), every rank decodes that.
+void product_reduce_twoshot(const uint8_t* const* wires, int world, size_t n, int bits, const float* pred,
+                            float inv_world, float* avg_out) {
+  const size_t nblk = (n + kBlock - 1) / kBlock;
+  parallel_for(nblk, 64, [&](size_t lo, size_t hi) {
+      detail::twoshot_range(wires, world, n, bits, pred, inv_world, avg_out, lo, hi);
+  });
 }
 
 }  // namespace host

@@ -407,6 +407,14 @@ def _unframe(x: torch.Tensor, src: int, n: int, step: int, bucket: int) -> np.nd
     return w
 
 
+def _np_view(t: torch.Tensor | None) -> np.ndarray | None:
+    """A writable numpy view of a CPU, contiguous fp32 tensor (None otherwise):
+    the host calls then write their outputs straight into the tensor."""
+    if t is None or t.device.type != "cpu" or t.dtype != torch.float32 or not t.is_contiguous():
+        return None
+    return t.detach().numpy()
+
+
 def _host_hook(hs: NangilaHookState, bucket):
     from .._ext import host
 
@@ -429,12 +437,15 @@ def _host_hook(hs: NangilaHookState, bucket):
         r = g - pred if (pred is not None and not first) else g
         res = float(np.abs(r, dtype=np.float64).mean()) if n else 0.0
     topo = topology(n, cfg.topo_drop_percent, cfg.topo_seed, bidx)
+    ef_view = _np_view(st.ef) if cfg.error_feedback else None
     if cfg.mode == "topk":
         wire, e_out = h.product_topk_encode(g, pred, ef, cfg.k, cfg.error_feedback, topo)
     else:
         bits = 4 if cfg.mode == "int4" else 8
+        # the new error feedback is written over the old one when it lives in
+        # a CPU fp32 tensor (each block is read before it is written)
         wire, e_out = h.product_encode(g, pred, ef, bits, cfg.stochastic, cfg.error_feedback,
-                                       cfg.seed & 0x7FFFFFFFFFFFFFFF, rank, bidx, st.calls, topo)
+                                       cfg.seed & 0x7FFFFFFFFFFFFFFF, rank, bidx, st.calls, topo, e_out=ef_view)
     payload = _frame(wire, n, st.calls, bidx, _fault(rank, hs.calls))
     gathered = [torch.empty_like(payload) for _ in range(world)]
     dist.all_gather(gathered, payload, group=hs.group)
@@ -442,15 +453,23 @@ def _host_hook(hs: NangilaHookState, bucket):
     # every rank checks every payload after the same collective, so all of
     # them raise together on a corrupt or mismatched one
     wires = [_unframe(x, r, n, st.calls, bidx) for r, x in enumerate(gathered)]
+    # the average is written straight into a CPU fp32 bucket (g, its view,
+    # is no longer needed)
+    out_view = _np_view(buf)
     if cfg.mode == "topk":
         avg = h.product_topk_reduce(wires, n, cfg.k, pred, float(inv_world))
     else:
-        avg = h.product_reduce(wires, n, bits, pred, float(inv_world))
+        avg = h.product_reduce(wires, n, bits, pred, float(inv_world), out=out_view)
     if st.pred is not None:
-        st.pred.copy_(torch.from_numpy(h.product_ema(st.pred.cpu().numpy(), avg, cfg.beta, first)))
-    if st.ef is not None:
+        pred_view = _np_view(st.pred)
+        if pred_view is not None:
+            h.product_ema_(pred_view, avg, cfg.beta, first)
+        else:
+            st.pred.copy_(torch.from_numpy(h.product_ema(st.pred.cpu().numpy(), avg, cfg.beta, first)))
+    if st.ef is not None and e_out is not ef_view:
         st.ef.copy_(torch.from_numpy(e_out))
-    buf.copy_(torch.from_numpy(avg).to(buf.dtype))
+    if avg is not out_view:
+        buf.copy_(torch.from_numpy(avg).to(buf.dtype))
     comp = wire_bytes(n, cfg.mode, cfg.k, cfg.topo_drop_percent, cfg.topo_seed, bidx)
     hs.raw_bytes += n * 4
     hs.comp_bytes += comp
