@@ -75,6 +75,24 @@ Floats fixedq_to_f32(const int32_t* q, size_t n) {
 
 // ------------------------------------------- UnifiedQuantizer: stochastic mode
 // unified_quantizer.rs:171-223
+namespace detail {
+// Stochastic codes of f / scale clamped to [qlo, qhi]: fast::stochastic_round
+// written out so the loop vectorizes (clones in fast_scalar.h).
+NGL_HOST_VEC_CLONES
+void stochastic_codes(const float* f, size_t n, float scale, uint64_t seed, uint64_t c0, int32_t qlo, int32_t qhi,
+                      int8_t* q) {
+  for (size_t i = 0; i < n; ++i) {
+    const float v = f[i] / scale;
+    const float fl = std::floor(v);
+    const float frac = v - fl;
+    const float r = (float)fmix64(seed ^ (c0 + i)) * 0x1p-64f;  // h / 2^64: exact scaling
+    const int32_t fi = sat_f32_to_i32(fl);
+    const int32_t qq = (r < frac) ? (int32_t)((uint32_t)fi + 1u) : fi;
+    q[i] = (int8_t)std::min(std::max(qq, qlo), qhi);
+  }
+}
+}  // namespace detail
+
 QuantOut stochastic_quantize(const int32_t* r, size_t n, int bits, uint64_t seed, uint64_t* counter) {
   QuantOut out{{}, 1.0f};
   Floats f = to_f32(r, n);
@@ -88,22 +106,18 @@ QuantOut stochastic_quantize(const int32_t* r, size_t n, int bits, uint64_t seed
   out.scale = scale;
   const uint64_t c0 = *counter;  // element i uses counter c0 + i
   if (bits == 4) {
+    std::vector<int8_t> q(n);
+    detail::stochastic_codes(f.data(), n, scale, seed, c0, -8, 7, q.data());
     out.bytes.assign((n + 1) / 2, 0);
     uint8_t* o = out.bytes.data();
-    for (size_t i = 0; i < n; ++i) {
-      int32_t q = fast::stochastic_round(f[i] / scale, seed, c0 + i);
-      q = std::min(std::max(q, -8), 7);
-      const uint8_t nibble = (uint8_t)((int8_t)q & 0x0F);
-      o[i >> 1] |= (i & 1) ? nibble : (uint8_t)(nibble << 4);  // first element of a pair -> high nibble
-    }
+    // first element of a pair -> high nibble
+    for (size_t j = 0; j < n / 2; ++j)
+      o[j] = (uint8_t)((((uint8_t)q[2 * j] & 0x0F) << 4) | ((uint8_t)q[2 * j + 1] & 0x0F));
+    if (n & 1) o[n / 2] = (uint8_t)(((uint8_t)q[n - 1] & 0x0F) << 4);
     *counter = c0 + n;
   } else if (bits == 8) {
     out.bytes.resize(n);
-    uint8_t* o = out.bytes.data();
-    for (size_t i = 0; i < n; ++i) {
-      const int32_t q = fast::stochastic_round(f[i] / scale, seed, c0 + i);
-      o[i] = (uint8_t)(int8_t)std::min(std::max(q, -128), 127);
-    }
+    detail::stochastic_codes(f.data(), n, scale, seed, c0, -128, 127, reinterpret_cast<int8_t*>(out.bytes.data()));
     *counter = c0 + n;
   } else {
     // Fallback: deterministic INT8 rounding with Rust f32::clamp (NaN stays

@@ -26,10 +26,15 @@
 // Both compute the correctly rounded fma of the reference rule (the baseline
 // through libm's fmaf), so the results are identical; -ffp-contract=off
 // keeps every other multiply and add separate in both clones.
+// Loops written to vectorize get AVX-512 and AVX2 clones the same way (the
+// AVX-512 one has 64-bit multiplies and a rounded u64 -> f32 conversion);
+// they hold only exact operations, so every clone gives the same bits.
 #if defined(__GNUC__) && !defined(__clang__) && defined(__x86_64__)
 #define NGL_HOST_FMA_CLONES __attribute__((target_clones("fma", "default")))
+#define NGL_HOST_VEC_CLONES __attribute__((target_clones("arch=x86-64-v4", "arch=x86-64-v3", "default")))
 #else
 #define NGL_HOST_FMA_CLONES
+#define NGL_HOST_VEC_CLONES
 #endif
 
 namespace ngl {

@@ -16,7 +16,7 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 @pytest.mark.skipif(shutil.which("g++") is None, reason="needs g++")
 def test_fast_paths_match_the_scalar_rules(tmp_path):
     exe = str(tmp_path / "fast_paths")
-    flags = ["-std=c++17", "-O2", "-ffp-contract=off", "-fno-fast-math", "-pthread"]
+    flags = ["-std=c++17", "-O2", "-ffp-contract=off", "-fno-fast-math", "-fno-trapping-math", "-pthread"]
     if platform.machine() in ("x86_64", "AMD64"):
         flags.append("-march=x86-64-v2")
     src = os.path.join(ROOT, "csrc", "host", "selftest", "fast_paths.cpp")
