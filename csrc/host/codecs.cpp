@@ -232,6 +232,15 @@ Fixed topk_dequantize(const uint8_t* b, size_t nb, float scale) {
 
 // ------------------------------------------------------------------ nangila-hpc
 // error_bounded.rs:294-333
+Bytes eb_pack_codes(const int16_t* q, size_t n) {
+  Bytes out(n * 2);
+  for (size_t i = 0; i < n; ++i) {
+    const uint16_t c = (uint16_t)q[i];
+    out[2 * i] = (uint8_t)(c & 0xFF);
+    out[2 * i + 1] = (uint8_t)(c >> 8);
+  }
+  return out;
+}
 QuantOut eb_quantize(const int32_t* r, size_t n, float eps) {
   const float scale = 2.0f * eps;
   QuantOut out{{}, scale};
@@ -304,27 +313,26 @@ Fixed rle_dequantize(const uint8_t* b, size_t nb, float scale) {
 }
 
 // block_sparse.rs:21-92
-QuantOut bs_quantize(const int32_t* r, size_t n, float eps) {
-  const float scale = 2.0f * eps;
-  QuantOut out{{}, scale};
-  out.bytes.reserve(4 + n * 2);
-  put_u32(out.bytes, (uint32_t)n);
+Bytes bs_pack_codes(const int16_t* q, size_t n) {
+  Bytes out;
+  out.reserve(4 + n * 2);
+  put_u32(out, (uint32_t)n);
   for (size_t s = 0; s < n; s += 32) {
-    size_t len = std::min<size_t>(32, n - s);
+    const size_t len = std::min<size_t>(32, n - s);
     uint32_t mask = 0;
-    int16_t vals[32];
-    int nv = 0;
-    for (size_t i = 0; i < len; ++i) {
-      int16_t q = fast::eb_code(fast::q823_to_f32(r[s + i]), scale);
-      if (q != 0) {
-        mask |= 1u << i;
-        vals[nv++] = q;
-      }
-    }
-    put_u32(out.bytes, mask);
-    for (int k = 0; k < nv; ++k) put_i16(out.bytes, vals[k]);
+    for (size_t i = 0; i < len; ++i)
+      if (q[s + i] != 0) mask |= 1u << i;
+    put_u32(out, mask);
+    for (size_t i = 0; i < len; ++i)
+      if (q[s + i] != 0) put_i16(out, q[s + i]);
   }
   return out;
+}
+QuantOut bs_quantize(const int32_t* r, size_t n, float eps) {
+  const float scale = 2.0f * eps;
+  std::vector<int16_t> q(n);
+  for (size_t i = 0; i < n; ++i) q[i] = fast::eb_code(fast::q823_to_f32(r[i]), scale);
+  return QuantOut{bs_pack_codes(q.data(), n), scale};
 }
 Fixed bs_dequantize(const uint8_t* b, size_t nb, float scale) {
   if (nb < 4) return Fixed();
@@ -356,13 +364,9 @@ Fixed bs_dequantize(const uint8_t* b, size_t nb, float scale) {
 }
 
 // block_sparse_rle.rs:137-242
-QuantOut bsrle_quantize(const int32_t* r, size_t n, float eps) {
-  const float scale = 2.0f * eps;
-  QuantOut out{{}, scale};
+Bytes bsrle_pack_codes(const int16_t* q, size_t n) {
   const size_t num_blocks = div_ceil(n, 32);
   std::vector<uint32_t> masks(num_blocks);
-  std::vector<int16_t> q(n);
-  for (size_t i = 0; i < n; ++i) q[i] = fast::eb_code(fast::q823_to_f32(r[i]), scale);
   for (size_t blk = 0; blk < num_blocks; ++blk) {
     uint32_t m = 0;
     size_t s = blk * 32, len = std::min<size_t>(32, n - s);
@@ -370,29 +374,36 @@ QuantOut bsrle_quantize(const int32_t* r, size_t n, float eps) {
       if (q[s + i] != 0) m |= 1u << i;
     masks[blk] = m;
   }
-  out.bytes.reserve(4 + num_blocks * 6);
-  put_u32(out.bytes, (uint32_t)n);
+  Bytes out;
+  out.reserve(4 + num_blocks * 6);
+  put_u32(out, (uint32_t)n);
   size_t blk = 0;
   while (blk < num_blocks) {
     size_t count = 1;
     if (masks[blk] == 0) {
       while (blk + count < num_blocks && masks[blk + count] == 0 && count < 128) ++count;
-      out.bytes.push_back((uint8_t)(0x80 | (count - 1)));
+      out.push_back((uint8_t)(0x80 | (count - 1)));
       blk += count;
       continue;
     }
     while (blk + count < num_blocks && masks[blk + count] != 0 && count < 128) ++count;
-    out.bytes.push_back((uint8_t)(count - 1));
+    out.push_back((uint8_t)(count - 1));
     for (size_t j = 0; j < count; ++j) {
       size_t bb = blk + j;
-      put_u32(out.bytes, masks[bb]);
+      put_u32(out, masks[bb]);
       size_t s = bb * 32, len = std::min<size_t>(32, n - s);
       for (size_t i = 0; i < len; ++i)
-        if (q[s + i] != 0) put_i16(out.bytes, q[s + i]);
+        if (q[s + i] != 0) put_i16(out, q[s + i]);
     }
     blk += count;
   }
   return out;
+}
+QuantOut bsrle_quantize(const int32_t* r, size_t n, float eps) {
+  const float scale = 2.0f * eps;
+  std::vector<int16_t> q(n);
+  for (size_t i = 0; i < n; ++i) q[i] = fast::eb_code(fast::q823_to_f32(r[i]), scale);
+  return QuantOut{bsrle_pack_codes(q.data(), n), scale};
 }
 Fixed bsrle_dequantize(const uint8_t* b, size_t nb, float scale) {
   if (nb < 4) return Fixed();

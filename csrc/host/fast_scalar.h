@@ -64,6 +64,19 @@ inline int16_t eb_code(float v, float scale) {
   return (int16_t)(int32_t)(d + (d < 0.0 ? -0.5 : 0.5));
 }
 
+// ngl::eb_code without a branch (for vectorized loops): round half away in
+// double (exact for every float: below 2^31 the +-0.5 sum is exact, above it
+// the value is already an integer and clamps), then the clamp as maxNum /
+// minNum.  "d >= -32768 ? d : -32768" sends NaN to -32768, as the reference's
+// f32::max(-32768.0) does; infinities clamp to the nearer end.
+inline int16_t eb_code_bf(float v, float scale) {
+  const double d = (double)(v / scale);
+  double r = std::trunc(d + (d < 0.0 ? -0.5 : 0.5));
+  r = r >= -32768.0 ? r : -32768.0;
+  r = r <= 32767.0 ? r : 32767.0;
+  return (int16_t)(int32_t)r;
+}
+
 // u64 -> f32 rounded to nearest even without a branch on the top bit (the
 // hash's top bit is random, so a branch mispredicts half the time): below
 // 2^63 the signed conversion is exact-rounded; at or above, halve with the

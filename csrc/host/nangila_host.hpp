@@ -59,6 +59,11 @@ QuantOut bs_quantize(const int32_t* r, size_t n, float eps);     // block_sparse
 Fixed bs_dequantize(const uint8_t* b, size_t nb, float scale);
 QuantOut bsrle_quantize(const int32_t* r, size_t n, float eps);  // block_sparse_rle.rs
 Fixed bsrle_dequantize(const uint8_t* b, size_t nb, float scale);
+// Byte streams of already computed error-bounded i16 codes (what the EB,
+// BlockSparse and BlockSparse+RLE quantizers emit for those codes).
+Bytes eb_pack_codes(const int16_t* q, size_t n);
+Bytes bs_pack_codes(const int16_t* q, size_t n);
+Bytes bsrle_pack_codes(const int16_t* q, size_t n);
 // Raw i16 element RLE used by the rotor twin's top-k path (client.rs:41-66).
 Bytes rle_encode_i16(const int16_t* q, size_t n);
 std::vector<int16_t> rle_decode_i16(const uint8_t* b, size_t nb);

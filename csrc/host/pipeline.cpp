@@ -146,15 +146,6 @@ TopologyMask TopologyMask::from_bytes(const uint8_t* p, size_t n) {
 
 // -------------------------------------------------- NZCP container (.nz files)
 namespace {
-QuantOut nz_quantize(int codec, const Fixed& r, float eps) {
-  switch (codec) {
-    case kNzEB: return eb_quantize(r.data(), r.size(), eps);
-    case kNzRLE: return rle_quantize(r.data(), r.size(), eps);
-    case kNzBS: return bs_quantize(r.data(), r.size(), eps);
-    case kNzBSRLE: return bsrle_quantize(r.data(), r.size(), eps);
-  }
-  throw std::runtime_error("unknown codec " + std::to_string(codec));
-}
 Fixed nz_dequantize(int codec, const uint8_t* b, size_t n, float scale) {
   switch (codec) {
     case kNzEB: return eb_dequantize(b, n, scale);
@@ -166,7 +157,40 @@ Fixed nz_dequantize(int codec, const uint8_t* b, size_t n, float scale) {
 }
 }  // namespace
 
-// examples/lammps_compress/src/main.rs:87-236
+namespace detail {
+// One closed-loop step of the LinearPredictor + error-bounded codes for n
+// values x (hist = snapshots in the predictor's history): the codes, the
+// reconstruction (the new history), and the largest |x - recon| as float
+// bits.  Every codec's decoder returns code * scale for each element, so the
+// reconstruction comes from the codes without decoding the step's bytes.
+// Written out so it vectorizes; only exact operations, and the error maximum
+// is an integer max of the bit patterns of non-negative floats, which does
+// not depend on the order.
+NGL_HOST_VEC_CLONES
+uint32_t hpc_step(const float* x, const int32_t* s_t, const int32_t* s_tm1, int hist, float scale, size_t n,
+                  int16_t* codes, int32_t* recon) {
+  uint32_t maxbits = 0;
+  for (size_t i = 0; i < n; ++i) {
+    const int32_t q = fast::q823_from_f32(x[i]);
+    const int32_t p = hist >= 2 ? sat_add_i32(s_t[i], sat_sub_i32(s_t[i], s_tm1[i])) : (hist == 1 ? s_t[i] : 0);
+    const int32_t r = hist >= 1 ? sat_sub_i32(q, p) : q;
+    const int16_t c = fast::eb_code_bf(fast::q823_to_f32(r), scale);
+    const int32_t d = fast::q823_from_f32((float)c * scale);
+    const int32_t rc = hist >= 1 ? sat_add_i32(p, d) : d;
+    codes[i] = c;
+    recon[i] = rc;
+    const float e = std::fabs(fast::q823_to_f32(q) - fast::q823_to_f32(rc));
+    uint32_t eb;
+    std::memcpy(&eb, &e, 4);
+    maxbits = eb > maxbits ? eb : maxbits;
+  }
+  return maxbits;
+}
+}  // namespace detail
+
+// examples/lammps_compress/src/main.rs:87-236: per step the LinearPredictor
+// prediction, the residual's error-bounded codes in the chosen container,
+// the reconstruction as the next history entry.
 Bytes nz_compress(const float* data, size_t particles, size_t steps, int codec, float eps, NzStats* stats) {
   if (codec < 1 || codec > 4) throw std::runtime_error("unknown codec " + std::to_string(codec));
   Bytes out;
@@ -175,26 +199,39 @@ Bytes nz_compress(const float* data, size_t particles, size_t steps, int codec, 
   out.push_back((uint8_t)codec);
   put_u32(out, (uint32_t)particles);
   put_u32(out, (uint32_t)steps);
-  LinearPredictor pred;
   NzStats st;
+  const float scale = 2.0f * eps;
+  // the RLE quantizer reports scale 1.0 for an empty input (rle.rs)
+  const float file_scale = (codec == kNzRLE && particles == 0) ? 1.0f : scale;
+  std::vector<int16_t> codes(particles);
+  Fixed hist_a(particles), hist_b(particles), hist_c(particles);
+  Fixed *s_t = &hist_a, *s_tm1 = &hist_b, *next = &hist_c;
+  int hist = 0;
+  uint32_t maxbits = 0;
   for (size_t t = 0; t < steps; ++t) {
-    Fixed buf = q823_from_f32(data + t * particles, particles);
     st.total_raw += particles * 4;
-    Fixed p = pred.predict();
-    Fixed residual = p.empty() ? buf : q823_sub(buf.data(), buf.size(), p.data(), p.size());
-    QuantOut q = nz_quantize(codec, residual, eps);
-    st.total_comp += q.bytes.size() + 8;
-    Fixed deq = nz_dequantize(codec, q.bytes.data(), q.bytes.size(), q.scale);
-    Fixed recon = p.empty() ? deq : q823_add(p.data(), p.size(), deq.data(), deq.size());
-    pred.update(recon.data(), recon.size());
-    for (size_t i = 0; i < particles && i < recon.size(); ++i) {
-      float e = std::fabs(fast::q823_to_f32(buf[i]) - fast::q823_to_f32(recon[i]));
-      if (e > st.max_abs_err) st.max_abs_err = e;
+    const uint32_t mb = detail::hpc_step(data + t * particles, s_t->data(), s_tm1->data(), hist, scale, particles,
+                                         codes.data(), next->data());
+    maxbits = std::max(maxbits, mb);
+    Bytes q;
+    switch (codec) {
+      case kNzEB: q = eb_pack_codes(codes.data(), particles); break;
+      case kNzRLE: q = rle_encode_i16(codes.data(), particles); break;
+      case kNzBS: q = bs_pack_codes(codes.data(), particles); break;
+      default: q = bsrle_pack_codes(codes.data(), particles); break;
     }
-    put_f32(out, q.scale);
-    put_u32(out, (uint32_t)q.bytes.size());
-    out.insert(out.end(), q.bytes.begin(), q.bytes.end());
+    st.total_comp += q.size() + 8;
+    // history: s_{t-1} <- s_t, s_t <- recon
+    Fixed* old = s_tm1;
+    s_tm1 = s_t;
+    s_t = next;
+    next = old;
+    hist = std::min(hist + 1, 2);
+    put_f32(out, file_scale);
+    put_u32(out, (uint32_t)q.size());
+    out.insert(out.end(), q.begin(), q.end());
   }
+  std::memcpy(&st.max_abs_err, &maxbits, 4);
   if (stats) *stats = st;
   return out;
 }

@@ -1,6 +1,6 @@
 // Exhaustive check of the host fast paths (csrc/host/fast_scalar.h) against
 // the scalar rules of csrc/common/ngl_scalar.h: q823_from_f32 and eb_code
-// (scale 1 and 2e-3) over all 2^32 float bit patterns, q823_to_f32 over all
+// (both forms, scale 1 and 2e-3) over all 2^32 float bit patterns, q823_to_f32 over all
 // 2^32 int32 values, stochastic rounding on 10^8 random (value, seed,
 // counter), absmax folds with NaN / inf / signed zeros, u64 -> f32 on 10^8
 // values of every magnitude.  Prints "fast paths ok" and exits 0 when every result matches.
@@ -35,6 +35,8 @@ void check_range(uint64_t lo, uint64_t hi) {
     bad += host::fast::q823_from_f32(x) != ngl::q823_from_f32(x);
     bad += host::fast::eb_code(x, 1.0f) != ngl::eb_code(x, 1.0f);
     bad += host::fast::eb_code(x, 2e-3f) != ngl::eb_code(x, 2e-3f);
+    bad += host::fast::eb_code_bf(x, 1.0f) != ngl::eb_code(x, 1.0f);
+    bad += host::fast::eb_code_bf(x, 2e-3f) != ngl::eb_code(x, 2e-3f);
     const float a = host::fast::q823_to_f32((int32_t)u), b = ngl::q823_to_f32((int32_t)u);
     bad += std::memcmp(&a, &b, 4) != 0;
   }

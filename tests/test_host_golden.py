@@ -10,7 +10,7 @@ import hashlib
 
 import numpy as np
 
-GOLDEN = "95d944d3f6f4d1b45cb78177dab222242f44aba267d33c714883a038bac31201"
+GOLDEN = "911e8eb33d9da559373f1ee94597a5d16bdfe8463b2f3a9250ce68ae4023e7f9"
 
 
 def outputs_digest(h) -> str:
@@ -59,7 +59,7 @@ def outputs_digest(h) -> str:
         data = f32(P * T, False)
         for codec in (1, 2, 3, 4):
             blob, st = h.nz_compress(data, P, T, codec, 1e-3)
-            add(blob, h.nz_decompress(blob, True), h.nz_decompress(blob, False))
+            add(blob, repr(sorted(dict(st).items())), h.nz_decompress(blob, True), h.nz_decompress(blob, False))
         g, pred, ef, g2 = x, f32(n, False), f32(n, False), f32(n, False)
         for bits in (4, 8):
             w, e = h.product_encode(g, pred, ef, bits, True, True, 9, 1, 2, trial)
