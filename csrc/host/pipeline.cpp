@@ -255,7 +255,12 @@ Floats nz_decompress(const uint8_t* b, size_t n, bool add_back) {
   size_t off = 14;
   Floats all;
   all.reserve((size_t)h.particles * h.steps);
-  LinearPredictor pred;
+  // The LinearPredictor closed loop in rotating buffers, with the checks of
+  // its predict / add in the same order: with two snapshots the history's
+  // sizes must agree (q823_sub), an empty prediction passes the decoded step
+  // through, any other prediction must match its size (q823_add).
+  Fixed s_t, s_tm1, next;
+  int hist = 0;
   for (uint32_t t = 0; t < h.steps; ++t) {
     if (off + 8 > n) throw std::runtime_error("read scale/len: unexpected end of file");
     float scale = get_f32(b + off);
@@ -264,16 +269,31 @@ Floats nz_decompress(const uint8_t* b, size_t n, bool add_back) {
     if (off + len > n) throw std::runtime_error("read bytes: unexpected end of file");
     Fixed deq = nz_dequantize(h.codec, b + off, len, scale);
     off += len;
-    if (add_back) {
-      Fixed p = pred.predict();
-      Fixed recon = p.empty() ? deq : q823_add(p.data(), p.size(), deq.data(), deq.size());
-      pred.update(recon.data(), recon.size());
-      Floats f = q823_to_f32(recon.data(), recon.size());
-      all.insert(all.end(), f.begin(), f.end());
-    } else {
-      Floats f = q823_to_f32(deq.data(), deq.size());
-      all.insert(all.end(), f.begin(), f.end());
+    const size_t m = deq.size();
+    if (!add_back) {
+      const size_t base = all.size();
+      all.resize(base + m);
+      for (size_t i = 0; i < m; ++i) all[base + i] = fast::q823_to_f32(deq[i]);
+      continue;
     }
+    if (hist >= 2 && s_t.size() != s_tm1.size()) throw ShapeMismatch(s_t.size(), s_tm1.size());
+    const bool use_p = hist >= 1 && !s_t.empty();
+    if (use_p && s_t.size() != m) throw ShapeMismatch(s_t.size(), m);
+    const size_t base = all.size();
+    all.resize(base + m);
+    next.resize(m);
+    for (size_t i = 0; i < m; ++i) {
+      int32_t rc = deq[i];
+      if (use_p) {
+        const int32_t p = hist >= 2 ? sat_add_i32(s_t[i], sat_sub_i32(s_t[i], s_tm1[i])) : s_t[i];
+        rc = sat_add_i32(p, deq[i]);
+      }
+      next[i] = rc;
+      all[base + i] = fast::q823_to_f32(rc);
+    }
+    if (hist >= 1) s_tm1.swap(s_t);  // LinearPredictor::update
+    s_t.swap(next);
+    hist = std::min(hist + 1, 2);
   }
   return all;
 }
