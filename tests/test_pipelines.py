@@ -158,3 +158,26 @@ def test_checkpoint_layout_roundtrip(tmp_path):
     p2 = str(tmp_path / "raw.h5")
     hdf5.write_dataset(p2, "traj_raw", data, 0.0, "raw")
     assert hdf5.read_dataset(p2, "traj_raw").size == n
+
+
+def test_nz_decoder_checks_step_sizes_like_the_predictor():
+    """Steps of other sizes glued under one header: after an empty step the
+    prediction is empty and the next step passes through; a step whose size
+    differs from the history raises the predictor's shape error
+    (LinearPredictor + FixedPointBuffer::add, main.rs:249-309)."""
+    import struct
+
+    from mini_nangila_b200.core import ShapeMismatch
+
+    def glue(*blobs):
+        steps = sum(struct.unpack_from("<I", x, 10)[0] for x in blobs)
+        return blobs[0][:10] + struct.pack("<I", steps) + b"".join(x[14:] for x in blobs)
+
+    empty, _ = nzcp.compress(np.zeros(0, np.float32), 0, 1, "eb", 1e-3)
+    six, _ = nzcp.compress(np.arange(6, dtype=np.float32), 6, 1, "eb", 1e-3)
+    four, _ = nzcp.compress(np.arange(4, dtype=np.float32), 4, 1, "eb", 1e-3)
+    out = nzcp.decompress(glue(empty, six))
+    assert out.size == 6 and np.abs(out - np.arange(6)).max() <= 1e-3 + 1e-6
+    with pytest.raises(ShapeMismatch, match="6 vs 4"):
+        nzcp.decompress(glue(six, four))
+    assert nzcp.decompress(glue(six, four), add_back=False).size == 10  # residuals need no history
