@@ -167,8 +167,6 @@ def test_nz_decoder_checks_step_sizes_like_the_predictor():
     (LinearPredictor + FixedPointBuffer::add, main.rs:249-309)."""
     import struct
 
-    from mini_nangila_b200.core import ShapeMismatch
-
     def glue(*blobs):
         steps = sum(struct.unpack_from("<I", x, 10)[0] for x in blobs)
         return blobs[0][:10] + struct.pack("<I", steps) + b"".join(x[14:] for x in blobs)
@@ -178,6 +176,6 @@ def test_nz_decoder_checks_step_sizes_like_the_predictor():
     four, _ = nzcp.compress(np.arange(4, dtype=np.float32), 4, 1, "eb", 1e-3)
     out = nzcp.decompress(glue(empty, six))
     assert out.size == 6 and np.abs(out - np.arange(6)).max() <= 1e-3 + 1e-6
-    with pytest.raises(ShapeMismatch, match="6 vs 4"):
+    with pytest.raises(ValueError, match="Shape mismatch: 6 vs 4"):  # the host library's ShapeMismatch
         nzcp.decompress(glue(six, four))
     assert nzcp.decompress(glue(six, four), add_back=False).size == 10  # residuals need no history
