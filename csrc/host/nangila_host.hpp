@@ -3,8 +3,12 @@
 // the NZCP container of examples/lammps_compress) plus the host oracle of the
 // product wire format used by the fused GPU all-reduce.
 //
-// It is the CPU test oracle for every kernel, the single-thread CPU baseline
-// the benches time, and the reader/writer of the on-disk formats.
+// It is the CPU test oracle for every kernel, the CPU baseline the benches
+// time (the codecs and the .nz pipeline run on one thread, as the reference's
+// binaries; the product-format oracle, which also carries the CPU DDP hook,
+// splits its block loops over NGL_HOST_THREADS / OMP_NUM_THREADS threads with
+// results that do not depend on the count), and the reader/writer of the
+// on-disk formats.
 #pragma once
 #include <cstddef>
 #include <cstdint>
