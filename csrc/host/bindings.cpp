@@ -49,6 +49,10 @@ PYBIND11_MODULE(_host, m) {
   m.def("q823_add", [](carr<int32_t> a, carr<int32_t> b) { return to_np(q823_add(ptr(a), a.size(), ptr(b), b.size())); });
   m.def("q823_sub", [](carr<int32_t> a, carr<int32_t> b) { return to_np(q823_sub(ptr(a), a.size(), ptr(b), b.size())); });
   m.def("q823_mul_scalar", [](carr<int32_t> a, float s) { return to_np(q823_mul_scalar(ptr(a), a.size(), s)); });
+  m.def("q823_momentum_update", [](carr<int32_t> state, carr<int32_t> obs, float beta, float one_minus_beta) {
+    if (state.size() != obs.size()) throw ShapeMismatch(state.size(), obs.size());
+    return to_np(q823_momentum_update(ptr(state), ptr(obs), state.size(), beta, one_minus_beta));
+  });
   m.def("fixedq_from_f32", [](carr<float> x) { return to_np(fixedq_from_f32(ptr(x), x.size())); });
   m.def("fixedq_to_f32", [](carr<int32_t> q) { return to_np(fixedq_to_f32(ptr(q), q.size())); });
 

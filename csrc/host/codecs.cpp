@@ -62,6 +62,15 @@ Fixed q823_mul_scalar(const int32_t* a, size_t n, float s) {
   for (size_t i = 0; i < n; ++i) out[i] = q823_mul_fixed(a[i], sf);
   return out;
 }
+// MomentumPredictor::update after the first observation (momentum.rs:41-48):
+// state.mul_scalar(beta).add(obs.mul_scalar(1 - beta)), element by element
+// in one pass with the same rules as the three buffer ops.
+Fixed q823_momentum_update(const int32_t* state, const int32_t* obs, size_t n, float beta, float one_minus_beta) {
+  const int64_t sb = q823_scalar_fixed(beta), so = q823_scalar_fixed(one_minus_beta);
+  Fixed out(n);
+  for (size_t i = 0; i < n; ++i) out[i] = sat_add_i32(q823_mul_fixed(state[i], sb), q823_mul_fixed(obs[i], so));
+  return out;
+}
 Fixed fixedq_from_f32(const float* x, size_t n) {
   Fixed out(n);
   for (size_t i = 0; i < n; ++i) out[i] = ngl::fixedq_from_f32(x[i]);

@@ -35,6 +35,8 @@ Floats q823_to_f32(const int32_t* q, size_t n);
 Fixed q823_add(const int32_t* a, size_t na, const int32_t* b, size_t nb);
 Fixed q823_sub(const int32_t* a, size_t na, const int32_t* b, size_t nb);
 Fixed q823_mul_scalar(const int32_t* a, size_t n, float s);
+// state.mul_scalar(beta).add(obs.mul_scalar(one_minus_beta)) in one pass.
+Fixed q823_momentum_update(const int32_t* state, const int32_t* obs, size_t n, float beta, float one_minus_beta);
 Fixed fixedq_from_f32(const float* x, size_t n);
 Floats fixedq_to_f32(const int32_t* q, size_t n);
 

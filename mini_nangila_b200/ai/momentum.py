@@ -8,7 +8,9 @@ first update).  Works on host and device buffers.
 from __future__ import annotations
 
 import numpy as np
+import torch
 
+from .._ext import host
 from ..core.fixed_point import FixedPointBuffer, ShapeMismatch
 from ..core.predictor import PredictorShapeMismatch
 
@@ -29,8 +31,17 @@ class MomentumPredictor:
         if self._state is None:
             self._state = observation.clone()
             return
+        omb = float(np.float32(1.0) - np.float32(self.beta))
+        obs = observation.to(self._state.device)
+        if self._state.device.type == "cpu":
+            # the same three ops fused in one host pass
+            if len(self._state) != len(obs):
+                raise PredictorShapeMismatch(f"Shape mismatch: {len(self._state)} vs {len(obs)}")
+            self._state = FixedPointBuffer(torch.from_numpy(host().q823_momentum_update(
+                self._state.numpy(), obs.numpy(), self.beta, omb)))
+            return
         decayed = self._state.mul_scalar(self.beta)
-        scaled = observation.to(self._state.device).mul_scalar(float(np.float32(1.0) - np.float32(self.beta)))
+        scaled = obs.mul_scalar(omb)
         try:
             self._state = decayed.add(scaled)
         except ShapeMismatch as e:

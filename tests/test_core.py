@@ -191,3 +191,20 @@ def test_prop_topology_determinism_coverage(v, drop):
     assert a.driver_indices == b.driver_indices and a.passenger_indices == b.passenger_indices
     assert len(a.driver_indices) + len(a.passenger_indices) == len(v)
     assert not set(a.driver_indices) & set(a.passenger_indices)
+
+
+@settings(max_examples=200, deadline=None)
+@given(st.lists(st.integers(-2**31, 2**31 - 1), min_size=0, max_size=200), st.integers(0, 2**32 - 1),
+       st.sampled_from([0.9, 0.5, 0.0, 1.0, 0.999, -0.3, 1.7, 1e6, 3e-8]))
+def test_fused_momentum_update_matches_the_three_ops(state, seed, beta):
+    """The host's one-pass momentum update equals
+    state.mul_scalar(beta).add(obs.mul_scalar(1 - beta)) bit for bit."""
+    from mini_nangila_b200 import _ext
+
+    h = _ext.host()
+    s = np.array(state, np.int32)
+    o = np.random.default_rng(seed).integers(-2**31, 2**31, s.size, dtype=np.int64).astype(np.int32)
+    b = float(np.float32(beta))
+    omb = float(np.float32(1.0) - np.float32(b))
+    want = h.q823_add(h.q823_mul_scalar(s, b), h.q823_mul_scalar(o, omb))
+    assert np.array_equal(h.q823_momentum_update(s, o, b, omb), want)
