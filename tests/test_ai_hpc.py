@@ -164,3 +164,16 @@ def test_prop_momentum_stable(vals):
     for v in vals:
         p.update(F([v]))
         assert abs(p.predict().to_f32()[0]) <= 300.0
+
+
+@settings(max_examples=40, deadline=None)
+@given(st.lists(st.floats(-50.0, 50.0, width=32), min_size=5, max_size=20))
+def test_prop_predictor_reset(vals):
+    """proptest_predictors.rs:66-89: after any history, reset leaves no
+    prediction (both predictors)."""
+    for p in (MomentumPredictor(0.9), LinearPredictor()):
+        for v in vals:
+            p.update(F([v]))
+        assert not p.predict().is_empty()
+        p.reset()
+        assert p.predict().is_empty()
