@@ -34,3 +34,13 @@ def test_plot_scripts_summarise_without_matplotlib(tmp_path, capsys):
     empty = tmp_path / "empty.csv"
     empty.write_text("nothing here\n")
     assert plot_metrics.main([str(empty)]) is None
+
+
+def test_package_metadata_and_lazy_subpackages():
+    import sys
+
+    import mini_nangila_b200 as m
+
+    assert m.__version__ == "0.1.0"
+    assert m.core.FixedPointBuffer is sys.modules["mini_nangila_b200.core"].FixedPointBuffer
+    assert "parallel" in m.__all__
