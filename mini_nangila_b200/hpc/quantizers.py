@@ -29,12 +29,34 @@ def _dev():
 
 
 class _EBBase:
+    """``strict=True`` raises ``QuantizerError`` instead of writing a code
+    that saturated at the INT16 ends, where the error bound no longer holds
+    (the reference declares ``FallbackRequired`` for this at
+    nangila-hpc/src/error_bounded.rs:5-11 but clamps silently,
+    :43-46)."""
     _name = ""
 
-    def __init__(self, epsilon: float):
+    def __init__(self, epsilon: float, strict: bool = False):
         self.epsilon = float(np.float32(epsilon))
+        self.strict = strict
+
+    def clamp_count(self, residual: FixedPointBuffer) -> int:
+        """How many codes of ``residual`` saturate: ``round(v / 2eps)``
+        (half away from zero) outside [-32768, 32767], i.e. the f32 quotient
+        at or beyond 32767.5 / -32768.5.  ``v`` is the Q8.23 value as f32,
+        as the quantizers see it; runs where the buffer lives."""
+        import torch
+
+        scale = np.float32(2.0) * np.float32(self.epsilon)
+        x = residual.data.to(torch.float32).mul_(2.0 ** -23).div_(float(scale))
+        return int(((x >= 32767.5) | (x <= -32768.5)).sum())
 
     def quantize(self, residual: FixedPointBuffer):
+        if self.strict:
+            k = self.clamp_count(residual)
+            if k:
+                raise QuantizerError(f"FallbackRequired: {k} of {residual.data.numel()} residuals exceed "
+                                     f"the INT16 code range at epsilon={self.epsilon:g}")
         if residual.data.is_cuda:
             return getattr(_dev(), f"{self._name}_quantize")(residual.data, self.epsilon)
         b, s = getattr(host(), f"{self._name}_quantize")(host_i32(residual), self.epsilon)
@@ -73,7 +95,8 @@ class BlockSparseRleQuantizer(_EBBase):
 
 
 class QuantizerError(ValueError):
-    """``FallbackRequired`` exists in the reference but is never produced."""
+    """``FallbackRequired``: raised by a ``strict`` error-bounded quantizer
+    when a residual is outside the INT16 code range."""
 
 
 def rle_encode_i16(q) -> bytes:

@@ -212,9 +212,10 @@ class RotorClient:
             idx = np.argsort(-np.abs(res), kind="stable")[:k]
             scale = np.float32(2.0) * np.float32(self.epsilon)
             q = np.zeros(n, np.int16)
-            for i in idx:
-                v = np.round(np.float32(res[i] / scale))
-                q[i] = np.int16(min(max(v, -32768.0), 32767.0))
+            # f32 quotient, rounded half away from zero (Rust's f32::round,
+            # client.rs:99; numpy's round is half to even), clamped to i16
+            d = (res[idx] / scale).astype(np.float64)
+            q[idx] = np.clip(np.where(d < 0, -np.floor(0.5 - d), np.floor(d + 0.5)), -32768, 32767)
             payload, sc = rle_encode_i16(q), -float(scale)
             deq = FixedPointBuffer.from_f32(q.astype(np.float32) * scale)
         else:

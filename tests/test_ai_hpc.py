@@ -177,3 +177,25 @@ def test_prop_predictor_reset(vals):
         assert not p.predict().is_empty()
         p.reset()
         assert p.predict().is_empty()
+
+
+def test_eb_clamp_count_and_strict_fallback():
+    """Codes that saturate at the INT16 ends are counted; a strict quantizer
+    raises instead of writing them (error_bounded.rs:5-11,43-46)."""
+    from mini_nangila_b200.hpc import QuantizerError
+
+    eps = 1e-3  # scale 2e-3: |v| up to ~65.53 fits
+    scale = np.float32(2) * np.float32(eps)
+    edge = [32767.5, -32768.5, 32767.4, -32768.4]  # quotients at and just inside the ends
+    vals = np.array([0.0, 1.0, -65.0, 70.0, -100.0, 255.0] + [np.float32(e) * scale for e in edge], np.float32)
+    r = FixedPointBuffer.from_f32(vals)
+    q = np.frombuffer(ErrorBoundedQuantizer(eps).quantize(r)[0], dtype="<i2")
+    x = r.to_f32() / scale
+    want = int(np.sum((x >= 32767.5) | (x <= -32768.5)))
+    assert want == int(np.sum(np.where(x < 0, -np.floor(-x + 0.5), np.floor(x + 0.5)) != q))
+    for cls in (ErrorBoundedQuantizer, RunLengthQuantizer, BlockSparseQuantizer, BlockSparseRleQuantizer):
+        assert cls(eps).clamp_count(r) == want >= 3
+        with pytest.raises(QuantizerError, match="FallbackRequired"):
+            cls(eps, strict=True).quantize(r)
+        ok = FixedPointBuffer.from_f32(vals[np.abs(x) < 32767])
+        assert cls(eps, strict=True).quantize(ok) == cls(eps).quantize(ok)

@@ -234,3 +234,23 @@ def test_analyze_reads_checkpoint(tmp_path):
     hdf5.write_chunked_dataset(p, "w", x, 1024, 1e-3, "eb")
     out = analyze.main(["checkpoint", p, "w"])
     assert out["n"] == 5000 and abs(out["first"][0] + 1.0) <= 1e-3
+
+
+def test_rotor_topk_codes_round_half_away_from_zero():
+    """The top-k path rounds the f32 quotient as Rust's f32::round does
+    (rotor_twin_net client.rs:99): 0.25 / 0.1 is 2.5 in f32 and codes as 3."""
+    pytest.importorskip("grpc")
+    from mini_nangila_b200.hpc import rle_decode_i16
+    from mini_nangila_b200.twin.rotor_net import RotorClient
+
+    for v, h in ((0.25, 2.5), (0.75, 7.5)):
+        assert np.float32(v) / np.float32(0.1) == np.float32(h)
+    c = RotorClient("127.0.0.1:1", epsilon=0.05, topk=0.5)
+    frame, _ = c.encode(np.array([0.25, -0.25, 0.75, 0.0, 0.125, 0.0], np.float32), 0)
+    assert frame.scale == -float(np.float32(0.1))
+    assert rle_decode_i16(frame.residual).tolist() == [3, -3, 8, 0, 0, 0]
+    c.close()
+    c = RotorClient("127.0.0.1:1", epsilon=1e-3, topk=0.34)  # k = 2; codes clamp at the i16 ends
+    frame, _ = c.encode(np.array([200.0, -200.0, 1.0, 0.0, 0.0, 0.0], np.float32), 0)
+    assert rle_decode_i16(frame.residual).tolist() == [32767, -32768, 0, 0, 0, 0]
+    c.close()

@@ -179,3 +179,14 @@ def test_eb_codes_match_host_at_near_ties(eps):
         dev = c.eb_codes(torch.from_numpy(r).cuda(), s).cpu().numpy()
         bad = np.flatnonzero(host != dev)
         assert bad.size == 0, (bad[:5], r[bad[:5]], host[bad[:5]], dev[bad[:5]])
+
+
+def test_eb_clamp_count_on_the_device_matches_the_host():
+    from mini_nangila_b200.hpc import QuantizerError
+
+    r = _resid(100003, 5, 0.5, scale=40.0)  # |v| up to ~200: many codes saturate at eps 1e-3
+    q = ErrorBoundedQuantizer(1e-3)
+    k = q.clamp_count(r)
+    assert k > 0 and q.clamp_count(r.cuda()) == k
+    with pytest.raises(QuantizerError, match=f"FallbackRequired: {k} of"):
+        ErrorBoundedQuantizer(1e-3, strict=True).quantize(r.cuda())
