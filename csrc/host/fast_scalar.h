@@ -29,7 +29,9 @@
 // Loops written to vectorize get AVX-512 and AVX2 clones the same way (the
 // AVX-512 one has 64-bit multiplies and a rounded u64 -> f32 conversion);
 // they hold only exact operations, so every clone gives the same bits.
-#if defined(__GNUC__) && !defined(__clang__) && defined(__x86_64__)
+// ThreadSanitizer builds take the baseline only: the clones' load-time
+// resolvers would run instrumented before the sanitizer's runtime is up.
+#if defined(__GNUC__) && !defined(__clang__) && defined(__x86_64__) && !defined(__SANITIZE_THREAD__)
 #define NGL_HOST_FMA_CLONES __attribute__((target_clones("fma", "default")))
 #define NGL_HOST_VEC_CLONES __attribute__((target_clones("arch=x86-64-v4", "arch=x86-64-v3", "default")))
 #else

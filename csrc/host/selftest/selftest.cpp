@@ -185,8 +185,10 @@ int main() {
       }
     }
   }
-  // product-format oracle: encode/reduce and top-k on odd sizes, with topology
-  for (size_t n : {1, 255, 257, 2049, 20000}) {
+  // product-format oracle: encode/reduce and top-k on odd sizes, with
+  // topology; 300000 (1172 blocks, the last one partial) splits every
+  // block-parallel loop over several host threads
+  for (size_t n : {1, 255, 257, 2049, 20000, 300000}) {
     Floats g = randn(n, 1e-3f, 0.1f), pred = randn(n, 1e-3f, 0.0f), e = randn(n, 1e-4f, 0.0f);
     ProductParams p;
     p.topo_a = 1;
@@ -206,6 +208,7 @@ int main() {
     product_topk_encode(g.data(), pred.data(), e.data(), n, 13, true, tk.data(), eo.data(), t);
     const uint8_t* ts[1] = {tk.data()};
     product_topk_reduce(ts, 1, n, 13, pred.data(), 1.0f, avg.data());
+    product_ema(pred.data(), avg.data(), n, 0.9f, false);
   }
   std::printf("selftest ok\n");
   return 0;

@@ -46,15 +46,17 @@ def _train_worker(rank, world, port, impl, mode, outdir):
             kw["error_feedback"] = True
         tr = DDPTrainer(GPT2(cfg), hook=impl, hook_kwargs=kw, device=torch.device("cpu"), bucket_cap_mb=0.05)
         g = torch.Generator().manual_seed(100 + rank)
-        losses = []
+        losses, grads = [], []
         for _ in range(3):
             t = torch.randint(0, cfg.vocab_size, (2, 17), generator=g)
             losses.append(float(tr.step(t[:, :-1], t[:, 1:])))
+            # the gradients are views of the buckets: the hook's averages
+            grads.append(torch.cat([p.grad.reshape(-1) for p in tr.model.parameters()]).clone())
         params = torch.cat([p.detach().reshape(-1) for p in tr.model.parameters()])
         hs = tr.hook_state
         preds = [st.pred.clone() for _, st in sorted(hs.buckets.items())] if impl == "host" else \
             [v.clone() for _, v in sorted(hs.compat_states.items())]
-        torch.save({"params": params, "preds": preds, "losses": losses, "ratio": hs.compression_ratio()},
+        torch.save({"params": params, "grads": grads, "preds": preds, "losses": losses, "ratio": hs.compression_ratio()},
                    os.path.join(outdir, f"r{rank}.pt"))
     finally:
         dist.destroy_process_group()
@@ -67,10 +69,17 @@ def test_ddp_hook_ranks_stay_identical(impl, mode, tmp_path):
     mp.start_processes(_train_worker, args=(2, _port(), impl, mode, str(tmp_path)), nprocs=2, join=True,
                        start_method="spawn")
     r0, r1 = torch.load(tmp_path / "r0.pt"), torch.load(tmp_path / "r1.pt")
-    # Identical averaged gradients -> identical parameters on both ranks.
-    assert torch.equal(r0["params"], r1["params"])
+    # What the hook guarantees: every rank gets the same averaged gradients
+    # and keeps the same predictor state, bit for bit.
+    for a, b in zip(r0["grads"], r1["grads"]):
+        assert torch.equal(a.view(torch.int32), b.view(torch.int32))
     for a, b in zip(r0["preds"], r1["preds"]):
         assert torch.equal(a, b)
+    # The parameters are the optimizer's: torch's CPU AdamW step has been seen
+    # to give one rank slightly different values (about 1e-4 of the update,
+    # within one intra-op thread's chunk) from bit-identical parameters,
+    # gradients and optimizer state, so they are compared to a tolerance.
+    assert torch.allclose(r0["params"], r1["params"], rtol=0.0, atol=1e-5)
     assert r0["ratio"] > 3.0
     assert all(np.isfinite(r0["losses"]))
 
@@ -121,13 +130,15 @@ def test_host_hook_matches_oracle(world, tmp_path):
 @pytest.mark.parametrize("mode", ["int4", "topk+topo"])
 def test_ddp_hook_ranks_stay_identical_world3(mode, tmp_path):
     """An odd world size: rank-ordered sums and per-rank noise keys still give
-    every rank the same parameters and predictor states."""
+    every rank the same averaged gradients and predictor states (and the same
+    parameters, to the optimizer's tolerance above)."""
     mp.start_processes(_train_worker, args=(3, _port(), "host", mode, str(tmp_path)), nprocs=3, join=True,
                        start_method="spawn")
     rs = [torch.load(tmp_path / f"r{r}.pt") for r in range(3)]
     for r in rs[1:]:
-        assert torch.equal(rs[0]["params"], r["params"])
+        assert all(torch.equal(a.view(torch.int32), b.view(torch.int32)) for a, b in zip(rs[0]["grads"], r["grads"]))
         assert all(torch.equal(a, b) for a, b in zip(rs[0]["preds"], r["preds"]))
+        assert torch.allclose(rs[0]["params"], r["params"], rtol=0.0, atol=1e-5)
     assert all(np.isfinite(rs[0]["losses"]))
 
 
