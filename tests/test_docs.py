@@ -28,3 +28,19 @@ def test_every_doc_is_listed_or_has_no_python():
     for name in sorted(os.listdir(os.path.join(ROOT, "docs"))):
         if name.endswith(".md"):
             assert isinstance(_blocks(name), list)
+
+
+def test_example_commands_name_existing_modules_and_flags():
+    """Every `python -m`/`torchrun -m` command of docs/examples.md names an
+    app module that exists, and every --flag it passes is one that module
+    (or bench.py) declares."""
+    text = open(os.path.join(ROOT, "docs", "examples.md")).read()
+    spans = re.findall(r"`([^`]*(?:-m mini_nangila_b200\.apps\.\w+|python bench\.py)[^`]*)`", text)
+    assert len(spans) >= 20
+    for cmd in spans:
+        m = re.search(r"mini_nangila_b200\.apps\.(\w+)", cmd)
+        path = os.path.join(ROOT, "mini_nangila_b200", "apps", m.group(1) + ".py") if m else os.path.join(ROOT, "bench.py")
+        assert os.path.exists(path), cmd
+        src = open(path).read()
+        for flag in re.findall(r"(?<![\w-])(--[a-z][\w-]*)", cmd.split("mini_nangila_b200.apps.")[-1]):
+            assert f'"{flag}"' in src, (cmd, flag)
