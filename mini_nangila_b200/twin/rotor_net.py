@@ -133,6 +133,12 @@ def imu_sample(t: float) -> np.ndarray:
     return np.array([s, c, 0.01, s * np.float32(5.0), c * np.float32(5.0), 0.0], dtype=np.float32)
 
 
+def _f32_display(x: np.float32) -> str:
+    """An f32 as Rust's ``{}`` prints it: the shortest digits that read back
+    as the same f32, positional, without a trailing ``.0`` (2.0 -> "2")."""
+    return np.format_float_positional(np.float32(x), unique=True, trim="-")
+
+
 # ------------------------------------------------------------------ server
 class RotorServer:
     """Cloud side: predictor + error-bounded decoder; logs the reference's
@@ -162,8 +168,9 @@ class RotorServer:
             self.frames += 1
             if self.metrics:
                 raw, comp = frame.length * 4, len(frame.residual) + 4
+                ratio = float(np.float32(raw) / np.float32(comp))  # f32, as server.rs:70
                 self.metrics.write(f"tick,{frame.tick},len,{frame.length},raw,{raw},comp,{comp},"
-                                   f"ratio,{raw / comp:.4f}\n")
+                                   f"ratio,{ratio:.4f}\n")
                 self.metrics.flush()
         return True
 
@@ -233,7 +240,7 @@ class RotorClient:
         self.pred.update(recon)
         if self.metrics:
             raw, comp = data.size * 4, len(frame.residual) + 4
-            self.metrics.write(f"{tick},{data.size},{raw},{comp},{raw / comp}\n")
+            self.metrics.write(f"{tick},{data.size},{raw},{comp},{_f32_display(np.float32(raw) / np.float32(comp))}\n")
         return ok
 
     def run(self, duration: float, rate_hz: int, sleep: bool = True) -> int:

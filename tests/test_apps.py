@@ -64,7 +64,8 @@ def test_rotor_twin_and_nano_gpt():
 
 def test_grpc_twin_end_to_end(tmp_path):
     grpc = pytest.importorskip("grpc")  # noqa: F841
-    from mini_nangila_b200.twin.rotor_net import Frame, RotorClient, RotorServer, decode_ack, encode_ack, imu_sample
+    from mini_nangila_b200.twin.rotor_net import (Frame, RotorClient, RotorServer, _f32_display, decode_ack, encode_ack,
+                                                  imu_sample)
 
     f = Frame(7, 6, -0.5, b"\x01\x02\x03")
     assert Frame.decode(f.encode()) == f and decode_ack(encode_ack(True)) is True
@@ -86,6 +87,19 @@ def test_grpc_twin_end_to_end(tmp_path):
         assert srv.frames == 40
         lines = open(tmp_path / f"s{topk}.csv").read().splitlines()
         assert lines[0].startswith("tick,0,len,6,raw,24,comp,")
+        # the ratio columns as the Rust programs print an f32: "{:.4}" on the
+        # server (server.rs:74), "{}" on the client (client.rs:124)
+        for line in lines:
+            f = line.split(",")
+            assert f[9] == f"{float(np.float32(int(f[5])) / np.float32(int(f[7]))):.4f}"
+        rows = open(tmp_path / f"c{topk}.csv").read().splitlines()
+        assert rows[0] == "tick,len,raw,comp,ratio" and len(rows) == 41
+        for row in rows[1:]:
+            t, n, raw, comp, ratio = row.split(",")
+            assert ratio == _f32_display(np.float32(int(raw)) / np.float32(int(comp)))
+            assert not ratio.endswith(".0")
+    assert [_f32_display(np.float32(a) / np.float32(b)) for a, b in ((24, 12), (24, 14), (1, 3))] == \
+        ["2", "1.7142857", "0.33333334"]
 
 
 def test_grpc_server_under_concurrent_clients(tmp_path):
