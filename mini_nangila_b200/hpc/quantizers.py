@@ -48,7 +48,11 @@ class _EBBase:
         import torch
 
         scale = np.float32(2.0) * np.float32(self.epsilon)
-        x = residual.data.to(torch.float32).mul_(2.0 ** -23).div_(float(scale))
+        x = residual.data.to(torch.float32).mul_(2.0 ** -23)
+        # a divisor tensor on the buffer's device: a correctly rounded f32
+        # division, as the quantizers do (a Python scalar divisor may be
+        # applied as a multiply by its reciprocal)
+        x = x / torch.full((1,), float(scale), dtype=torch.float32, device=x.device)
         return int(((x >= 32767.5) | (x <= -32768.5)).sum())
 
     def quantize(self, residual: FixedPointBuffer):
