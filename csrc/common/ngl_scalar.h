@@ -181,7 +181,7 @@ NGL_HD int32_t fixedq_from_f32(float x) {
 NGL_HD float fixedq_to_f32(int32_t y) { return NGL_FMUL((float)y, 1.0f / kQScale); }
 
 // Error-bounded INT16 code: round(v / scale) clamped with max/min then `as i16`
-// (error_bounded.rs:306-311, block_sparse.rs:38-39, rle.rs:510-511).
+// (error_bounded.rs:41-46, block_sparse.rs:38-39, rle.rs:30-31).
 NGL_HD int16_t eb_code(float v, float scale) {
   float q = f_round(NGL_FDIV(v, scale));
   float c = f_min(f_max(q, -32768.0f), 32767.0f);

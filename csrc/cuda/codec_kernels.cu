@@ -4,10 +4,10 @@
 //
 // Reference hot loops restated here (all scalar Rust loops in the reference):
 //   nangila-math/src/fixed_point.rs:34-60, ops.rs:6-49        -> q823_* kernels
-//   nangila-hpc/src/error_bounded.rs:294-333, linear.rs:26-57  -> hpc_step, eb_*
+//   nangila-hpc/src/error_bounded.rs:29-68, linear.rs:26-57     -> hpc_step, eb_*
 //   nangila-hpc/src/block_sparse.rs:21-92                      -> bs_encode + walker
-//   nangila-hpc/src/block_sparse_rle.rs:137-242                -> bsrle_encode + walker
-//   nangila-hpc/src/rle.rs:500-579                             -> rle_encode + walker
+//   nangila-hpc/src/block_sparse_rle.rs:26-131                 -> bsrle_encode + walker
+//   nangila-hpc/src/rle.rs:21-99                               -> rle_encode + walker
 //   nangila-core/src/unified_quantizer.rs:171-375              -> stochastic_*, topk_*
 //
 // Variable-length encoders compute every item's output offset with a
@@ -344,7 +344,7 @@ __device__ uint64_t lookback(uint64_t* status_arr, int64_t tile, uint64_t agg, i
         base -= 32;
       }
       if (timed_out) {
-        if (lane == 0) dev::set_status(status, dev::kBounds, (int)tile, -1);
+        if (lane == 0) dev::set_status(status, dev::kTimeoutLookback, (int)tile, -1);
         excl = Op::id();
       }
       if (lane == 0) st_release_gpu(&status_arr[tile], kStInc | (Op::op(excl, agg) & kValMask));

@@ -23,6 +23,7 @@ enum Status : int {
   kBadHeader = 3,        // payload header did not match (n / epoch)
   kBounds = 4,           // bounds check failed (NGL_BOUNDS_CHECK builds)
   kTimeoutCopy = 5,      // a bulk copy into shared memory never completed
+  kTimeoutLookback = 6,  // a scan's look-back wait on a predecessor tile expired
 };
 
 __device__ __forceinline__ uint64_t globaltimer() {

@@ -10,8 +10,11 @@
 namespace {
 
 constexpr int64_t kMaxN = int64_t(1) << 26;  // 64 Mi codes
+// One status word per tile of kPackTileBlocks * 32 = 16384 codes (4096 tiles
+// at kMaxN), the tile counter and spare words: 4104 u64 = 32,832 bytes.
 constexpr int64_t kScratchWords =
     ((kMaxN + 31) / 32 + ngl::codec::kPackTileBlocks - 1) / ngl::codec::kPackTileBlocks + 8;
+static_assert(kScratchWords == 4104, "scratch size documented in noalloc.h");
 
 // The scratch itself.  In host code `g_scratch` only names a host-side stand-in
 // for the symbol, never a device address: kernels get the address from
@@ -50,6 +53,12 @@ extern "C" int ngl_bs_encode_noalloc(const int16_t* codes, int64_t n, uint8_t* o
   uint64_t* scratch = nullptr;
   cudaError_t e = scratch_for_current_device(&scratch);
   if (e != cudaSuccess) return (int)e;
+  // The kernel only records errors (first one wins), so the success value
+  // comes from clearing the caller's status words here.  Allocates nothing.
+  if (status != nullptr) {
+    e = cudaMemsetAsync(status, 0, 4 * sizeof(int), stream);
+    if (e != cudaSuccess) return (int)e;
+  }
   // The encoder clears the scratch words it uses (cudaMemsetAsync) before its
   // kernel runs, so the previous call's contents do not leak into this one.
   e = ngl::codec::bs_encode(codes, n, out, scratch, total_bytes, status, stream);

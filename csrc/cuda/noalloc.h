@@ -17,8 +17,9 @@ extern "C" {
 #endif
 
 // Largest number of int16 codes one call accepts (64 Mi).  The scratch array
-// behind it holds one status word per tile of 4096 codes plus a tile counter
-// (about 128 KiB), and every GPU that loads this library keeps it until exit.
+// behind it holds one look-back status word per tile of 16384 codes (4096
+// tiles at the limit), a tile counter and a few spare words: 4104 u64, about
+// 32 KiB, which every GPU that loads this library keeps until exit.
 int64_t ngl_bs_encode_noalloc_max_n(void);
 
 // Encode `n` int16 error-bounded codes into the BlockSparse byte stream
@@ -26,14 +27,23 @@ int64_t ngl_bs_encode_noalloc_max_n(void);
 //   codes        device pointer, n int16 values
 //   out          device pointer, capacity of at least 4 + 68 * ceil(n / 32) bytes
 //   total_bytes  device pointer to one uint64: receives the stream length
-//   status       device pointer to int32[4]: 0 on success, else an error code
-//                recorded by the kernel (it never traps)
+//   status       device pointer to int32[4]; each call clears it on `stream`
+//                before its kernel runs, then the kernel records the first
+//                error it meets (it never traps).  After the stream has
+//                finished, status[0] is
+//                  0  success
+//                  4  an output or scratch bound was exceeded
+//                  6  a look-back wait on a predecessor tile gave up after
+//                     2 s (the stream is then incomplete)
+//                and status[1] holds the tile concerned.
 // Returns 0 (cudaSuccess) when the work was enqueued, the CUDA error code of a
 // failed set-up or launch, or -2 when n exceeds ngl_bs_encode_noalloc_max_n().
 //
 // The first call on a device looks up the scratch array's device address
-// (cudaGetSymbolAddress, with that device current); make that first call
-// before any stream capture.  No call allocates or frees memory.  All calls
+// (cudaGetSymbolAddress, with that device current) and keeps it for the
+// process; make that first call before any stream capture.  cudaDeviceReset
+// after that first call is not supported: it unloads the module, and the
+// kept address would be stale.  No call allocates or frees memory.  All calls
 // share the one scratch array, which keeps the last call's contents (each call
 // clears the part it needs before its kernel runs); calls that overlap on the
 // GPU, e.g. on two streams at once, race on it and must be serialised by the

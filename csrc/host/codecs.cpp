@@ -240,7 +240,7 @@ Fixed topk_dequantize(const uint8_t* b, size_t nb, float scale) {
 }
 
 // ------------------------------------------------------------------ nangila-hpc
-// error_bounded.rs:294-333
+// error_bounded.rs:29-68
 Bytes eb_pack_codes(const int16_t* q, size_t n) {
   Bytes out(n * 2);
   for (size_t i = 0; i < n; ++i) {
@@ -268,7 +268,7 @@ Fixed eb_dequantize(const uint8_t* b, size_t nb, float scale) {
   return out;
 }
 
-// rle.rs:500-579
+// rle.rs:21-99
 QuantOut rle_quantize(const int32_t* r, size_t n, float eps) {
   QuantOut out{{}, 1.0f};
   if (n == 0) return out;
@@ -372,7 +372,7 @@ Fixed bs_dequantize(const uint8_t* b, size_t nb, float scale) {
   return from_f32(rec);
 }
 
-// block_sparse_rle.rs:137-242
+// block_sparse_rle.rs:26-131
 Bytes bsrle_pack_codes(const int16_t* q, size_t n) {
   const size_t num_blocks = div_ceil(n, 32);
   std::vector<uint32_t> masks(num_blocks);

@@ -1,6 +1,9 @@
 """Toy DDP training on random tokens with the compression hook
-(python/nangila_ddp/examples/minigpt_train.py); runs on CUDA (fused hook) or
-CPU (host hook)."""
+(python/nangila_ddp/examples/minigpt_train.py): a TinyGPT stepped by
+``DDPTrainer``, on CUDA with the fused hook or on CPU with the host hook.
+
+    torchrun --nproc-per-node 2 --master-addr 127.0.0.1 -m mini_nangila_b200.apps.minigpt_train --steps 20
+"""
 from __future__ import annotations
 
 import argparse
@@ -8,38 +11,27 @@ import argparse
 import torch
 import torch.distributed as dist
 
+from ..data import uniform_tokens
 from ..models import TinyGPT
 from ..train import DDPTrainer, init_distributed
-
-
-class _LM(torch.nn.Module):
-    def __init__(self, vocab):
-        super().__init__()
-        self.m = TinyGPT(vocab=vocab)
-        self.vocab = vocab
-
-    def forward(self, x, y):
-        return torch.nn.functional.cross_entropy(self.m(x).reshape(-1, self.vocab), y.reshape(-1))
+from ..utils.trainlog import TrainLog
 
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--vocab", type=int, default=5000)
+    ap.add_argument("--train_log", default="")
     a = ap.parse_args(argv)
     cuda = torch.cuda.is_available()
     rank, world, local = init_distributed("nccl" if cuda else "gloo")
     dev = torch.device("cuda", local) if cuda else torch.device("cpu")
-    tr = DDPTrainer(_LM(a.vocab), lr=3e-4, hook="fused" if cuda else "host", device=dev,
+    tr = DDPTrainer(TinyGPT(vocab=a.vocab), lr=3e-4, hook="fused" if cuda else "host", device=dev,
                     hook_kwargs=dict(beta=0.9, bits=4, stochastic=True, use_fp16_transport=True),
                     autocast_dtype=None)
-    g = torch.Generator(device=dev).manual_seed(rank)
-    for step in range(a.steps):
-        x = torch.randint(0, a.vocab, (8, 128), device=dev, generator=g)
-        y = torch.randint(0, a.vocab, (8, 128), device=dev, generator=g)
-        loss = tr.step(x, y)
-        if rank == 0 and step % 10 == 0:
-            print(f"step {step} loss {loss.item():.4f}")
+    log = TrainLog(a.train_log or None, enabled=rank == 0, echo_every=10 if rank == 0 else 0)
+    tr.fit(lambda step: uniform_tokens(a.vocab, 8, 128, seed=1000 * step + rank, device=dev), a.steps, log=log,
+           first_step=0)
     dist.destroy_process_group()
 
 

@@ -1,49 +1,43 @@
-"""Character-level TinyGPT DDP training with the compression hook
-(python/nangila_ddp/train_nano.py).
+"""Character-level TinyGPT DDP training with the compression hook.
 
-    torchrun --nproc-per-node 2 --master-addr 127.0.0.1 -m mini_nangila_b200.apps.train_nano \
+    torchrun --nproc-per-node 2 --master-addr 127.0.0.1 -m mini_nangila_b200.apps.train_nano \\
         --device cpu --steps 50 --use_momentum
 
-Same flags and CSV outputs as the reference (``train_log.csv`` with
-``ts,step,loss,lr,tokens_per_sec,step_ms``; the hook's metrics CSV).  There
-is no network here: without ``--data`` the reference's synthetic fallback
-text is used.  On CUDA the hook is the fused sm_100a kernel (``--impl``
-selects fused / compat / host).
+The command line and both CSV outputs are the reference trainer's
+(python/nangila_ddp/train_nano.py:66-82 flags; ``train_log.csv`` with
+``ts,step,loss,lr,tokens_per_sec,step_ms``; the hook's metrics CSV), so its
+plot scripts read these logs.  The rest is this framework's:
+
+* data: ``data.CharCorpus`` — every rank reads the same text (``--data``,
+  else the reference's offline fallback text; there is no network here) and
+  draws random windows keyed by (seed, rank, step), so no broadcast or
+  sampler is needed;
+* the step: ``train.DDPTrainer`` (DDP with bucket views, the hook, AdamW),
+  fp32 like the reference;
+* logging: ``utils.trainlog.TrainLog`` on rank 0, step time from CUDA events
+  on GPUs.
+
+``--impl`` picks the hook (fused sm_100a kernel on CUDA, the C++ host path
+on CPU, or the reference-compatible ``compat``).  ``--topo_drop`` without
+``--impl`` uses ``compat``, whose element-granular drop matches the
+reference's; fused/host drop whole 2048-element chunks.
 """
 from __future__ import annotations
 
 import argparse
-import os
-import time
 
 import torch
 import torch.distributed as dist
-from torch.nn.parallel import DistributedDataParallel as DDP
-from torch.utils.data import DataLoader, Dataset
 
+from ..data import CharCorpus
 from ..models import TinyGPT
-from ..parallel import register_nangila_hook
-from ..train import init_distributed
+from ..train import DDPTrainer, init_distributed
+from ..utils.trainlog import TrainLog
 
 
-class CharDataset(Dataset):
-    def __init__(self, text: str, block_size: int):
-        self.block = block_size
-        self.chars = sorted(set(text))
-        self.c2i = {c: i for i, c in enumerate(self.chars)}
-        self.vocab = len(self.chars)
-        self.data = torch.tensor([self.c2i[c] for c in text], dtype=torch.long)
-
-    def __len__(self):
-        return max(0, self.data.numel() - self.block - 1)
-
-    def __getitem__(self, i):
-        return self.data[i:i + self.block], self.data[i + 1:i + 1 + self.block]
-
-
-def main(argv=None):
-    ap = argparse.ArgumentParser(description="NanoGPT DDP with the compression hook")
-    ap.add_argument("--data", default="")
+def parse(argv=None):
+    ap = argparse.ArgumentParser(description="TinyGPT DDP training with the compression hook")
+    ap.add_argument("--data", default="", help="text file; empty: the offline fallback text")
     ap.add_argument("--block_size", type=int, default=128)
     ap.add_argument("--d_model", type=int, default=256)
     ap.add_argument("--nhead", type=int, default=4)
@@ -59,64 +53,29 @@ def main(argv=None):
     ap.add_argument("--topk", type=float, default=0.0)
     ap.add_argument("--topo_drop", type=float, default=0.0)
     ap.add_argument("--impl", default=None, choices=[None, "fused", "compat", "host"])
-    a = ap.parse_args(argv)
-    dev = a.device if a.device != "auto" else ("cuda" if torch.cuda.is_available() else "cpu")
-    rank, world, local = init_distributed("nccl" if dev == "cuda" else "gloo")
-    device = torch.device("cuda", local) if dev == "cuda" else torch.device("cpu")
-    torch.manual_seed(a.seed + rank)
-    if rank == 0:
-        if a.data and os.path.exists(a.data):
-            text = open(a.data, encoding="utf-8").read()
-        else:
-            text = "abc def ghi " * 100000
-    else:
-        text = ""
-    lens = torch.tensor([len(text)], dtype=torch.long, device=device)
-    dist.broadcast(lens, src=0)
-    buf = torch.empty(int(lens.item()), dtype=torch.uint8, device=device)
-    if rank == 0:
-        buf.copy_(torch.tensor(list(text.encode("utf-8")), dtype=torch.uint8, device=device))
-    dist.broadcast(buf, src=0)
-    text = bytes(buf.cpu().tolist()).decode("utf-8")
-    ds = CharDataset(text, a.block_size)
-    sampler = torch.utils.data.distributed.DistributedSampler(ds, num_replicas=world, rank=rank, shuffle=True)
-    loader = DataLoader(ds, batch_size=a.batch_size, sampler=sampler, drop_last=True)
-    model = TinyGPT(a.d_model, a.nhead, a.nlayers, ds.vocab, a.block_size).to(device)
-    model = DDP(model, device_ids=[local]) if dev == "cuda" else DDP(model)
-    impl = a.impl or ("fused" if dev == "cuda" else "host")
-    if a.topo_drop > 0.0:
-        impl = "compat"
-    register_nangila_hook(model, beta=0.9, bits=4, stochastic=True, use_fp16_transport=False,
-                          metrics_path=a.metrics_path, use_momentum=a.use_momentum, topk_percent=a.topk,
-                          topo_drop_percent=a.topo_drop, impl=impl)
-    opt = torch.optim.AdamW(model.parameters(), lr=a.lr)
-    loss_fn = torch.nn.CrossEntropyLoss()
-    if rank == 0:
-        with open(a.train_log, "w") as fh:
-            fh.write("ts,step,loss,lr,tokens_per_sec,step_ms\n")
-    step, tok = 0, a.batch_size * a.block_size
-    for epoch in range(1_000_000):
-        sampler.set_epoch(epoch)
-        for xb, yb in loader:
-            step += 1
-            xb, yb = xb.to(device), yb.to(device)
-            t0 = time.time()
-            logits = model(xb)
-            loss = loss_fn(logits.view(-1, ds.vocab), yb.view(-1))
-            opt.zero_grad(set_to_none=True)
-            loss.backward()
-            opt.step()
-            ms = (time.time() - t0) * 1000.0
-            if rank == 0:
-                with open(a.train_log, "a") as fh:
-                    fh.write(f"{time.time():.6f},{step},{loss.item():.6f},{a.lr},{tok / max(1e-6, ms / 1000):.2f},"
-                             f"{ms:.2f}\n")
-                if step % 10 == 0:
-                    print(f"step {step} loss {loss.item():.4f} tps {tok / max(1e-6, ms / 1000):.1f} tokens/s")
-            if step >= a.steps:
-                break
-        if step >= a.steps:
-            break
+    return ap.parse_args(argv)
+
+
+def main(argv=None):
+    a = parse(argv)
+    use_cuda = a.device == "cuda" or (a.device == "auto" and torch.cuda.is_available())
+    rank, world, local = init_distributed("nccl" if use_cuda else "gloo")
+    device = torch.device("cuda", local) if use_cuda else torch.device("cpu")
+    torch.manual_seed(a.seed)  # same initial weights on every rank (DDP also broadcasts them)
+    corpus = CharCorpus.from_path(a.data or None)
+    impl = a.impl or ("compat" if a.topo_drop > 0.0 else ("fused" if use_cuda else "host"))
+    hook_kwargs = dict(beta=0.9, bits=4, stochastic=True, use_fp16_transport=False, metrics_path=a.metrics_path,
+                       use_momentum=a.use_momentum, topk_percent=a.topk, topo_drop_percent=a.topo_drop)
+    trainer = DDPTrainer(TinyGPT(a.d_model, a.nhead, a.nlayers, corpus.vocab, a.block_size), lr=a.lr, hook=impl,
+                         hook_kwargs=hook_kwargs, autocast_dtype=None, device=device)
+    log = TrainLog(a.train_log, enabled=rank == 0, echo_every=10 if rank == 0 else 0)
+
+    def next_batch(step):
+        return corpus.batch(a.batch_size, a.block_size, seed=a.seed, rank=rank, step=step, device=device)
+
+    trainer.fit(next_batch, a.steps, log=log, lr=a.lr)
+    if trainer.hook_state is not None and getattr(trainer.hook_state, "comm", None) is not None:
+        trainer.hook_state.comm.check()
     dist.destroy_process_group()
 
 

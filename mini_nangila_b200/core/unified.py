@@ -136,7 +136,7 @@ class UnifiedQuantizer:
 
         m = self._mode
         c = _dev_codecs()
-        t = torch.from_numpy(b).to(device)
+        t = torch.from_numpy(np.require(b, requirements="W")).to(device)  # bytes-backed arrays are read-only
         if isinstance(m, Stochastic):
             return FixedPointBuffer(c.stochastic_dequantize(t, float(scale), int(m.bits)))
         if isinstance(m, ErrorBounded):

@@ -71,7 +71,10 @@ class _EBBase:
         if device is not None and str(device).startswith("cuda"):
             import torch
 
-            return FixedPointBuffer(getattr(_dev(), f"{self._name}_dequantize")(torch.from_numpy(b).to(device),
+            # a writable copy: torch.from_numpy of a read-only array (bytes
+            # from a file or a bytes object) is undefined if written
+            w = np.require(b, requirements="W")
+            return FixedPointBuffer(getattr(_dev(), f"{self._name}_dequantize")(torch.from_numpy(w).to(device),
                                                                                float(scale)))
         return FixedPointBuffer(getattr(host(), f"{self._name}_dequantize")(b, float(np.float32(scale))))
 

@@ -20,8 +20,13 @@ class TinyGPT(nn.Module):
         self.enc = nn.TransformerEncoder(layer, nlayers, enable_nested_tensor=False)
         self.lm = nn.Linear(d_model, vocab)
 
-    def forward(self, x):
+    def forward(self, x, targets=None):
+        """Logits for ``x``; with ``targets``, the mean cross-entropy instead
+        (the form ``DDPTrainer`` steps)."""
         h = self.emb(x) + self.pos[:, : x.size(1), :]
         mask = nn.Transformer.generate_square_subsequent_mask(x.size(1), device=x.device) if self.causal else None
         h = self.enc(h, mask=mask, is_causal=self.causal)
-        return self.lm(h)
+        logits = self.lm(h)
+        if targets is None:
+            return logits
+        return nn.functional.cross_entropy(logits.reshape(-1, logits.size(-1)), targets.reshape(-1))

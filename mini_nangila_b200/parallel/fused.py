@@ -41,6 +41,7 @@ STATUS_NAMES = {
     5: "timeout of a bulk copy into shared memory",
     3: "payload tag mismatch (ranks disagree on bucket size or order)",
     4: "bounds check",
+    6: "timeout of a scan's look-back wait",
 }
 
 

@@ -157,6 +157,27 @@ class DDPTrainer:
             losses.append(float(pending[0]))
         return losses
 
+    def fit(self, next_batch, steps: int, log=None, lr: float | None = None, first_step: int = 1) -> list[float]:
+        """Run ``steps`` training steps.  ``next_batch(step)`` returns the
+        step's (x, y) on the device; each step is timed on the device
+        (``utils.trainlog.StepTimer``) and, with a ``TrainLog``, logged as one
+        row.  Returns the losses (read every step, so this loop waits for
+        each step; ``train_steps`` is the pipelined form)."""
+        from .utils.trainlog import StepTimer
+
+        timer = StepTimer(self.device)
+        lr = lr if lr is not None else self.opt.param_groups[0]["lr"]
+        losses = []
+        for step in range(first_step, first_step + steps):
+            x, y = next_batch(step)
+            timer.start()
+            loss = self.step(x, y)
+            ms = timer.stop_ms()
+            losses.append(float(loss))
+            if log is not None:
+                log.row(step, losses[-1], lr, x.numel(), ms)
+        return losses
+
     def state_dict(self) -> dict:
         """Everything a resumed run needs: model, optimizer, the hook's
         predictor / error-feedback state and counters, steps done."""

@@ -42,9 +42,12 @@ def _noalloc_encode(lib, codes):
     nblk = (n + 31) // 32
     out = torch.zeros(4 + 68 * nblk, dtype=torch.uint8, device="cuda")
     total = torch.zeros(1, dtype=torch.int64, device="cuda")
-    status = torch.zeros(4, dtype=torch.int32, device="cuda")
+    # Garbage in the status words: the entry point clears them itself, so a
+    # caller need not.
+    status = torch.full((4,), -7, dtype=torch.int32, device="cuda")
     stream = torch.cuda.current_stream().cuda_stream
-    rc = lib.ngl_bs_encode_noalloc(codes.data_ptr(), n, out.data_ptr(), total.data_ptr(), status.data_ptr(), stream)
+    ptr = codes.data_ptr() if n else 0
+    rc = lib.ngl_bs_encode_noalloc(ptr, n, out.data_ptr(), total.data_ptr(), status.data_ptr(), stream)
     assert rc == 0, lib.ngl_bs_encode_noalloc_error(rc).decode()
     torch.cuda.synchronize()
     assert int(status[0]) == 0, status.tolist()
@@ -62,6 +65,22 @@ def test_noalloc_matches_regular_encoder_two_calls():
         got = _noalloc_encode(lib, codes)
         ref = _ext.cuda().pack_codes(codes, 0).cpu().numpy().tobytes()
         assert got == ref
+
+
+def test_noalloc_edge_sizes():
+    """Empty input (header only), one code past a whole 16384-code tile,
+    and the largest accepted size, which uses the whole scratch array."""
+    from mini_nangila_b200 import _ext
+
+    lib = _lib()
+    empty = _noalloc_encode(lib, torch.zeros(0, dtype=torch.int16, device="cuda"))
+    assert empty == b"\x00\x00\x00\x00"  # [u32 n = 0], total 4 bytes
+    for n, seed, sp in ((16385, 3, 0.5), (lib.ngl_bs_encode_noalloc_max_n(), 4, 0.9)):
+        codes = _codes(n, seed, sp)
+        got = _noalloc_encode(lib, codes)
+        ref = _ext.cuda().pack_codes(codes, 0).cpu().numpy().tobytes()
+        assert got == ref
+        del codes
 
 
 def test_noalloc_rejects_oversized_input():
