@@ -18,6 +18,22 @@ end-to-end figure runs the same K steps through ``DDPTrainer.step_host``:
 H2D copy of the step's tokens from pinned memory, the step, and a D2H read
 of the loss, timed on the host between synchronized points (max over ranks).
 
+The repo arm also times, on the same box and in the same process, two
+comparison arms (``--no-arms`` skips them) and prints them as extra keys:
+
+* ``nccl_fp32``: the same model, optimizer and DDP settings with DDP's own
+  uncompressed NCCL fp32 all-reduce and AdamW after backward (the plain
+  baseline);
+* ``hook_on_reference_model``: this framework's fused hook on exactly the
+  reference arm's setup (stock ``transformers`` model, foreach AdamW,
+  default DDP arguments), so its ratio to the reference arm isolates the
+  hook from the model and optimizer.
+
+The product arm applies AdamW per bucket from the hook (``--overlap-opt``)
+and caps the exchange grid of buckets that overlap backward
+(``--inflight-ctas``).  ``--timeline FILE`` records one more step's
+per-bucket device timeline on every rank (``utils.timeline``).
+
 Rank 0 prints one JSON line.
 """
 from __future__ import annotations
@@ -53,6 +69,12 @@ def parse():
     ap.add_argument("--max-ctas", type=int, default=0)
     ap.add_argument("--momentum", choices=["auto", "on", "off"], default="auto",
                     help="EMA predictor in the hook (auto: on for int4/int8, off for top-k, which uses error feedback)")
+    ap.add_argument("--overlap-opt", choices=["on", "off"], default="on",
+                    help="fused hook: apply AdamW per bucket from the hook, overlapping backward")
+    ap.add_argument("--inflight-ctas", type=int, default=None,
+                    help="grid cap of exchange kernels that overlap backward (default: the hook's choice)")
+    ap.add_argument("--no-arms", action="store_true", help="skip the same-box NCCL and same-model comparison arms")
+    ap.add_argument("--timeline", default="", help="write one step's per-bucket device timeline (JSON) here")
     return ap.parse_args()
 
 
@@ -88,18 +110,11 @@ class _HFLoss(torch.nn.Module):
         return torch.nn.functional.cross_entropy(logits.view(-1, logits.size(-1)).float(), y.reshape(-1))
 
 
-def build_reference(args, device, tiny: bool = False):
-    """Reference arm: the unmodified nangila_ddp hook from baseline/_ref on a
-    stock transformers model of the same architecture (the reference ships
-    no GPT-2 or Llama model): GPT-2 small with the INT4 + EMA hook, or the
-    Llama-style 1.1B (bf16 weights) with the hook in top-k mode.  ``tiny``
-    swaps in small models of the same families (CPU tests of this arm)."""
-    ref = os.path.join(ROOT, "baseline", "_ref")
-    if not os.path.isdir(os.path.join(ref, "nangila_ddp")):
-        return None, "baseline/_ref/nangila_ddp is not installed", ""
-    sys.path.insert(0, ref)
-    from nangila_ddp import register_nangila_hook as ref_register  # noqa: E402
-
+def build_hf_model(args, device, tiny: bool = False):
+    """The stock ``transformers`` model of the workload's family (the
+    reference ships no GPT-2 or Llama model): GPT-2 small (fp32 weights, bf16
+    autocast) or the Llama-style 1.1B (bf16 weights), each wrapped as
+    forward(x, y) -> loss.  Returns (module, autocast)."""
     if args.model == "gpt2":
         from transformers import GPT2Config, GPT2LMHeadModel  # noqa: E402
 
@@ -124,6 +139,21 @@ def build_reference(args, device, tiny: bool = False):
         cfg._attn_implementation = "sdpa"
         model = _HFLoss(LlamaForCausalLM(cfg)).to(device=device, dtype=torch.bfloat16)
         autocast = False
+    return model, autocast
+
+
+def build_reference(args, device, tiny: bool = False):
+    """Reference arm: the unmodified nangila_ddp hook from baseline/_ref on
+    the stock model of ``build_hf_model``: GPT-2 small with the INT4 + EMA
+    hook, or the Llama-style 1.1B with the hook in top-k mode.  ``tiny``
+    swaps in small models of the same families (CPU tests of this arm)."""
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "nangila_ddp")):
+        return None, "baseline/_ref/nangila_ddp is not installed", ""
+    sys.path.insert(0, ref)
+    from nangila_ddp import register_nangila_hook as ref_register  # noqa: E402
+
+    model, autocast = build_hf_model(args, device, tiny)
     ddp = torch.nn.parallel.DistributedDataParallel(
         model, device_ids=[device.index] if device.type == "cuda" else None, bucket_cap_mb=25)
     topk = args.topk if args.mode == "topk" else 0.0
@@ -143,6 +173,90 @@ def build_reference(args, device, tiny: bool = False):
 
     name = "reference-nangila_ddp-int4" + ("-ema" if momentum else "") + (f"-topk{topk:g}" if topk else "")
     return step, None, name
+
+
+def build_hook_on_reference_model(args, device, tiny: bool = False):
+    """This framework's fused hook on exactly the reference arm's setup:
+    the same stock model, default DDP arguments and foreach AdamW, with the
+    hook's mode set as the reference arm sets its own.  Returns (step, hook
+    state, name)."""
+    from mini_nangila_b200.parallel import register_nangila_hook
+
+    model, autocast = build_hf_model(args, device, tiny)
+    ddp = torch.nn.parallel.DistributedDataParallel(
+        model, device_ids=[device.index] if device.type == "cuda" else None, bucket_cap_mb=25)
+    topk = args.topk if args.mode == "topk" else 0.0
+    momentum = args.momentum == "on" or (args.momentum == "auto" and args.mode != "topk")
+    hs = register_nangila_hook(ddp, beta=0.9, bits=4, stochastic=True, use_momentum=momentum, topk_percent=topk,
+                               seed=12345, error_feedback=True, variant=args.variant,
+                               impl="fused" if device.type == "cuda" else "host")
+    opt = torch.optim.AdamW(ddp.parameters(), lr=6e-4)
+
+    def step(x, y):
+        with torch.autocast(device.type, dtype=torch.bfloat16, enabled=autocast):
+            loss = ddp(x, y)
+        opt.zero_grad(set_to_none=True)
+        loss.backward()
+        opt.step()
+        return loss.detach()
+
+    name = "fused-int4" + ("-ema" if momentum else "") + "-ef" + (f"-keep{topk:g}" if topk else "")
+    return step, hs, name
+
+
+def time_steps(step_fn, batches, warmup: int, steps: int, device) -> float:
+    """Milliseconds for ``steps`` steps after ``warmup`` (CUDA events, max over ranks)."""
+    from mini_nangila_b200.utils import barrier_sync, max_over_ranks
+
+    for i in range(warmup):
+        step_fn(*batches[i % len(batches)])
+    barrier_sync(device)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(steps):
+        step_fn(*batches[i % len(batches)])
+    e.record()
+    barrier_sync(device)
+    return max_over_ranks(s.elapsed_time(e), device)
+
+
+def comparison_arms(args, device, world: int, mb: int, seq: int, batches, mcfg) -> dict:
+    """Time the same-box NCCL fp32 arm and the hook-on-reference-model arm."""
+    import gc
+
+    from mini_nangila_b200.models import GPT2, Llama
+    from mini_nangila_b200.train import DDPTrainer
+
+    out = {}
+    tokens = world * mb * seq * args.steps
+    # plain NCCL fp32: same model class, optimizer and DDP settings as the product arm
+    model = GPT2(mcfg) if args.model == "gpt2" else Llama(mcfg).to(torch.bfloat16)
+    tr = DDPTrainer(model, lr=6e-4, hook="nccl", bucket_cap_mb=25.0,
+                    autocast_dtype=torch.bfloat16 if args.model == "gpt2" else None, device=device)
+    ms = time_steps(tr.step, batches, args.warmup, args.steps, device)
+    out["nccl_fp32"] = {"value": tokens / (ms / 1000.0), "ms_per_step": ms / args.steps,
+                        "hook": "DDP built-in NCCL fp32 all-reduce, AdamW (fused) after backward"}
+    del tr, model
+    gc.collect()
+    torch.cuda.empty_cache()
+    try:
+        step, hs, name = build_hook_on_reference_model(args, device)
+    except ImportError as e:  # transformers missing
+        out["hook_on_reference_model"] = {"unavailable": str(e)}
+        return out
+    ms = time_steps(step, batches, args.warmup, args.steps, device)
+    if hs is not None and getattr(hs, "comm", None) is not None:
+        hs.comm.check()
+    out["hook_on_reference_model"] = {
+        "value": tokens / (ms / 1000.0), "ms_per_step": ms / args.steps, "hook": name,
+        "model": "transformers " + ("GPT2LMHeadModel" if args.model == "gpt2" else "LlamaForCausalLM"),
+        "optimizer": "AdamW (foreach) after backward", "ddp": "default arguments, bucket_cap_mb 25"}
+    if hs is not None and getattr(hs, "comm", None) is not None:
+        hs.comm.close()
+    del step, hs
+    gc.collect()
+    torch.cuda.empty_cache()
+    return out
 
 
 def main():
@@ -189,8 +303,12 @@ def main():
             hk = dict(beta=0.9, bits=8 if args.mode == "int8" else 4, stochastic=True, use_momentum=momentum,
                       topk_percent=args.topk if args.mode == "topk" else 0.0, seed=12345,
                       error_feedback=True, variant=args.variant, max_ctas=args.max_ctas)
+            if args.hook == "fused":
+                hk["inflight_ctas"] = args.inflight_ctas
+        overlap = args.hook == "fused" and args.overlap_opt == "on"
         trainer = DDPTrainer(model, lr=6e-4, hook=args.hook, hook_kwargs=hk, bucket_cap_mb=25.0,
-                             autocast_dtype=torch.bfloat16 if args.model == "gpt2" else None, device=device)
+                             autocast_dtype=torch.bfloat16 if args.model == "gpt2" else None, device=device,
+                             overlap_optimizer=overlap)
         step_fn = trainer.step
         hook_name = {"fused": f"fused-{args.mode}", "nccl": "nccl-fp32-allreduce", "compat": f"compat-{args.mode}"}[args.hook]
         if args.hook != "nccl":
@@ -254,11 +372,41 @@ def main():
                 "h2d_bytes_per_step": int(xb.numel() * xb.element_size() + yb.numel() * yb.element_size()),
                 "d2h_bytes_per_step": 4,
             }
+    timeline = None
+    if args.timeline and trainer is not None:
+        from mini_nangila_b200.utils.timeline import summarize
+
+        step_fn(*batches[0])
+        trainer.timeline_next_step()
+        step_fn(*batches[1])
+        tl = trainer.timeline.collect()
+        per_rank = [None] * world
+        dist.all_gather_object(per_rank, {"rank": rank, "summary": summarize(tl), "timeline": tl})
+        timeline = per_rank
     hs = trainer.hook_state if trainer else None
     if trainer is not None and hs is not None and getattr(hs, "comm", None) is not None:
         hs.comm.check()
     tokens = world * mb * seq * args.steps
     value = tokens / (ms / 1000.0)
+    arms = None
+    if trainer is not None and not args.no_arms:
+        ratio_fields = (hs.compression_ratio() if hs is not None and hs.raw_bytes else None,
+                        hs.last_variant if hs is not None else None,
+                        (hs.comm.twoshot_min_bytes if hs is not None and getattr(hs, "comm", None) is not None
+                         and hs.comm.world > 1 else None))
+        if hs is not None and getattr(hs, "comm", None) is not None:
+            hs.comm.close()
+        trainer = None
+        import gc
+
+        gc.collect()
+        torch.cuda.empty_cache()
+        arms = comparison_arms(args, device, world, mb, seq, batches, mcfg)
+    else:
+        ratio_fields = (hs.compression_ratio() if hs is not None and hs.raw_bytes else None,
+                        hs.last_variant if hs is not None else None,
+                        (hs.comm.twoshot_min_bytes if hs is not None and getattr(hs, "comm", None) is not None
+                         and hs.comm.world > 1 else None))
     if rank == 0:
         out = {
             "metric": METRIC,
@@ -289,18 +437,28 @@ def main():
         }
         if args.impl == "reference":
             out["impl"] = "reference"
-        if hs is not None and hs.raw_bytes:
-            out["compression_ratio"] = hs.compression_ratio()
-            out["config"]["variant"] = hs.last_variant
-            if getattr(hs, "comm", None) is not None and hs.comm.world > 1:
-                out["config"]["twoshot_from_mb"] = (None if hs.comm.twoshot_min_bytes >= (1 << 60)
-                                                    else hs.comm.twoshot_min_bytes / 2 ** 20)
+        ratio, variant, twoshot_from = ratio_fields
+        if ratio is not None:
+            out["compression_ratio"] = ratio
+            out["config"]["variant"] = variant
+            if twoshot_from is not None:
+                out["config"]["twoshot_from_mb"] = None if twoshot_from >= (1 << 60) else twoshot_from / 2 ** 20
+        if trainer is not None or arms is not None:
+            out["config"]["optimizer_overlap"] = bool(args.hook == "fused" and args.overlap_opt == "on")
         if clocks is not None:
             out["clocks"] = clocks
         if e2e is not None:
             out["e2e"] = e2e
+        if arms is not None:
+            out.update(arms)
+            if "value" in arms.get("nccl_fp32", {}):
+                out["vs_nccl_fp32_same_box"] = value / arms["nccl_fp32"]["value"]
+        if timeline is not None:
+            with open(args.timeline, "w") as fh:
+                json.dump(timeline, fh)
+            out["timeline"] = {"file": args.timeline, "rank0": timeline[0]["summary"]}
         print(json.dumps(out), flush=True)
-    if hs is not None and getattr(hs, "comm", None) is not None:
+    if trainer is not None and hs is not None and getattr(hs, "comm", None) is not None:
         hs.comm.close()
     dist.barrier()
     dist.destroy_process_group()

@@ -224,8 +224,12 @@ class FusedAllReduce:
         tag: int | None = None,
         topo_drop: float = 0.0,
         topo_seed: int = 0,
+        max_ctas: int | None = None,
     ) -> str:
         """Average ``grad`` across ranks in place on the current stream.
+
+        ``max_ctas`` caps this launch's grid (default: the communicator's);
+        every rank must pass the same value for the same bucket.
 
         Buckets longer than ``capacity`` run as several launches over
         segments; segment s of bucket b draws its noise from stream
@@ -243,7 +247,7 @@ class FusedAllReduce:
                     mode=mode, k=k, variant=variant, stochastic=stochastic, seed=seed,
                     bucket=(bucket * 65536 + si) & 0xFFFFFFFF, step=step, beta=beta, first=first,
                     tag=None if tag is None else (tag + si) & 0xFFFFFFFF, topo_drop=topo_drop,
-                    topo_seed=topo_seed,
+                    topo_seed=topo_seed, max_ctas=max_ctas,
                 )
             return v
         v = self.choose_variant(n, mode, variant)
@@ -251,7 +255,8 @@ class FusedAllReduce:
             tag = self.tag_for(n, bucket)
         self.comm.run(
             grad, pred, ef, MODES[mode], int(k), VARIANTS[v], bool(stochastic), int(seed) & 0x7FFFFFFFFFFFFFFF,
-            int(bucket), int(step), float(beta), bool(first), self.max_ctas, self.timeout_ns, int(tag),
+            int(bucket), int(step), float(beta), bool(first), self.max_ctas if max_ctas is None else int(max_ctas),
+            self.timeout_ns, int(tag),
             list(topology(n, topo_drop, topo_seed, bucket)) if topo_drop > 0.0 else [],
         )
         self.launches += 1

@@ -85,6 +85,9 @@ class HookConfig:
     timeout_s: float = 10.0
     verbose: bool = False
     max_ctas: int = 0
+    # CTAs of the exchange kernels of buckets that are not the last one,
+    # which run while backward still computes (0: the whole grid)
+    inflight_ctas: int = 0
 
     @property
     def mode(self) -> str:
@@ -118,6 +121,12 @@ class NangilaHookState:
     # bucket states (a loaded state_dict, or the buckets DDP just replaced)
     # that new buckets take their predictor / EF state from, per parameter
     restore: dict | None = None
+    # fused: called as after_reduce(bucket) on the hook stream right after
+    # the bucket's exchange kernel, before its future completes (the
+    # trainer's per-bucket optimizer update)
+    after_reduce: object = None
+    # fused: a utils.timeline.StepTimeline that receives each bucket's events
+    timeline: object = None
 
     def compression_ratio(self) -> float:
         return self.raw_bytes / max(1, self.comp_bytes)
@@ -340,6 +349,24 @@ def _fused_hook(hs: NangilaHookState, bucket):
         with nvtx_range("nangila/autotune"):
             autotune_twoshot(hs.comm, sizes_mb=(4, 16, 32, 64, 128, 256))
     cur = torch.cuda.current_stream(buf.device)
+    # Buckets before the last one run while backward still computes: their
+    # kernels get a capped grid so backward keeps most SMs.  The last bucket
+    # (the first layers' gradients) runs when backward is over and gets the
+    # whole grid.  is_last() is the same on every rank, so the grids (part
+    # of the flag tags) agree.
+    last = bool(bucket.is_last()) if hasattr(bucket, "is_last") else True
+    ctas = cfg.max_ctas if (last or not cfg.inflight_ctas) else cfg.inflight_ctas
+    tl = hs.timeline
+    trec = None
+    if tl is not None:
+        variant = hs.comm.choose_variant(buf.numel(), cfg.mode, cfg.variant)
+        from .._ext import cuda as _cuda
+
+        grid = _cuda().fused_grid(buf.numel(), {"int4": 0, "int8": 1, "topk": 2}[cfg.mode],
+                                  buf.dtype == torch.bfloat16, {"single": 0, "oneshot": 1, "twoshot": 2}[variant],
+                                  ctas, buf.device.index)
+        trec = tl.bucket(bucket=bidx, numel=buf.numel(), variant=variant, grid=grid, last=last)
+        tl.event(trec, "ready", cur)
     hs.stream.wait_stream(cur)
     with torch.cuda.stream(hs.stream), nvtx_range(f"nangila/bucket{bidx}/{buf.numel()}"):
         # mean |g - pred| of this rank's bucket, the reference's res_mean_abs
@@ -351,11 +378,19 @@ def _fused_hook(hs: NangilaHookState, bucket):
                 res = (buf.float() - st.pred).abs_().mean()
             else:
                 res = buf.float().abs().mean()
+        if trec is not None:
+            tl.event(trec, "start", hs.stream)
         hs.last_variant = hs.comm.allreduce_(
             buf, st.pred, st.ef, mode=cfg.mode, k=cfg.k, variant=cfg.variant, stochastic=cfg.stochastic,
             seed=cfg.seed, bucket=bidx, step=st.calls, beta=cfg.beta, first=first,
-            topo_drop=cfg.topo_drop_percent, topo_seed=cfg.topo_seed,
+            topo_drop=cfg.topo_drop_percent, topo_seed=cfg.topo_seed, max_ctas=ctas,
         )
+        if trec is not None:
+            tl.event(trec, "end", hs.stream)
+        if hs.after_reduce is not None:
+            hs.after_reduce(bucket)
+            if trec is not None:
+                tl.event(trec, "opt_end", hs.stream)
         fut = torch.futures.Future(devices=[buf.device])
         fut.set_result(buf)
         comp = wire_bytes(buf.numel(), cfg.mode, cfg.k, cfg.topo_drop_percent, cfg.topo_seed, bidx)
@@ -474,6 +509,8 @@ def _host_hook(hs: NangilaHookState, bucket):
     hs.raw_bytes += n * 4
     hs.comp_bytes += comp
     _log(hs, bidx, n, comp, res)
+    if hs.after_reduce is not None:
+        hs.after_reduce(bucket)
     fut = torch.futures.Future()
     fut.set_result(buf)
     return fut
@@ -514,8 +551,13 @@ def register_nangila_hook(
     max_ctas: int = 0,
     process_group=None,
     autotune: bool = True,
+    inflight_ctas: int | None = None,
 ) -> NangilaHookState:
     """Register a predictive-residual compression comm hook on a DDP model.
+
+    ``inflight_ctas`` caps the grid of the exchange kernels of every bucket
+    but the last (they overlap backward); None picks 32 with more than one
+    rank and no cap on one rank, 0 disables the cap.
 
     Returns the hook state (metrics, ``state_dict``/``load_state_dict``).
     """
@@ -536,9 +578,12 @@ def register_nangila_hook(
         hs = NangilaHookState(cfg, process_group)
         model.register_comm_hook(state=None, hook=make_compat_hook(hs))
         return hs
+    world = dist.get_world_size(process_group) if dist.is_initialized() else 1
+    if inflight_ctas is None:
+        inflight_ctas = 32 if world > 1 else 0
     cfg = HookConfig(beta, bits, stochastic, use_fp16_transport, seed, metrics_path, use_momentum, topk_percent,
                      topo_drop_percent, topo_seed, impl, True if error_feedback is None else bool(error_feedback),
-                     variant, timeout_s, verbose, max_ctas)
+                     variant, timeout_s, verbose, max_ctas, int(inflight_ctas))
     hs = NangilaHookState(cfg, process_group)
     hs.param_index = {p.data_ptr(): i for i, p in enumerate(model.parameters())}
     if impl == "fused":

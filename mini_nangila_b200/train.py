@@ -56,8 +56,83 @@ def init_distributed(backend: str | None = None, timeout_s: float = 300.0) -> tu
     return dist.get_rank(), dist.get_world_size(), int(os.environ.get("LOCAL_RANK", "0"))
 
 
+class BucketAdamW:
+    """The trainer's AdamW applied to one DDP bucket's parameters, from the
+    gradient hook, with PyTorch's fused AdamW kernel on the current (hook)
+    stream: each bucket's update runs as soon as its averaged gradients
+    land, overlapping the rest of backward, and only the last bucket's
+    update follows the end of backward.
+
+    The state lives in the ``torch.optim.AdamW`` object (``exp_avg``,
+    ``exp_avg_sq`` and a device ``step`` per parameter, created as that
+    optimizer creates them for ``fused=True``), so its ``state_dict`` is
+    unchanged and either path can resume the other.  Hyper-parameters are
+    read from the parameter's group at every call (schedulers work).  What
+    cannot work with an update per bucket: anything that needs every
+    gradient before the first update (global-norm clipping, a skipped step).
+    """
+
+    def __init__(self, opt: torch.optim.Optimizer):
+        self.opt = opt
+        self.group_of = {id(p): g for g in opt.param_groups for p in g["params"]}
+        self.updated: set[int] = set()  # ids of parameters updated in this step
+        self._cache: dict = {}
+
+    def _lists(self, params, grads):
+        key = tuple(p.data_ptr() for p in params) + tuple(g.data_ptr() for g in grads)
+        hit = self._cache.get(key)
+        if hit is not None:
+            return hit
+        by_group: dict[int, tuple] = {}
+        for p, g in zip(params, grads):
+            grp = self.group_of[id(p)]
+            st = self.opt.state[p]
+            if len(st) == 0:
+                st["step"] = torch.zeros((), dtype=torch.float32, device=p.device)
+                st["exp_avg"] = torch.zeros_like(p, memory_format=torch.preserve_format)
+                st["exp_avg_sq"] = torch.zeros_like(p, memory_format=torch.preserve_format)
+            lists = by_group.setdefault(id(grp), (grp, [], [], [], [], []))
+            lists[1].append(p)
+            lists[2].append(g.view_as(p))
+            lists[3].append(st["exp_avg"])
+            lists[4].append(st["exp_avg_sq"])
+            lists[5].append(st["step"])
+        out = list(by_group.values())
+        if len(self._cache) > 4096:
+            self._cache.clear()
+        self._cache[key] = out
+        return out
+
+    def apply(self, params, grads) -> None:
+        with torch.no_grad():
+            for grp, ps, gs, ms, vs, steps in self._lists(params, grads):
+                b1, b2 = grp["betas"]
+                torch._foreach_add_(steps, 1)
+                torch._fused_adamw_(ps, gs, ms, vs, [], steps, lr=float(grp["lr"]), beta1=float(b1),
+                                    beta2=float(b2), weight_decay=float(grp["weight_decay"]), eps=float(grp["eps"]),
+                                    amsgrad=False, maximize=bool(grp.get("maximize", False)))
+        self.updated.update(id(p) for p in params)
+
+    def __call__(self, bucket) -> None:
+        self.apply(bucket.parameters(), bucket.gradients())
+
+    def finish_step(self, all_params) -> None:
+        """Update the parameters no bucket carried this step (if any), then
+        start the next step's bookkeeping."""
+        rest = [p for p in all_params if p.grad is not None and id(p) not in self.updated]
+        if rest:
+            self.apply(rest, [p.grad for p in rest])
+        self.updated.clear()
+
+
 class DDPTrainer:
-    """DDP + gradient hook + AdamW (+ bf16 autocast) training steps; see the module docstring."""
+    """DDP + gradient hook + AdamW (+ bf16 autocast) training steps; see the module docstring.
+
+    ``overlap_optimizer=True`` (fused hook on CUDA) applies AdamW per bucket
+    from the hook (``BucketAdamW``) instead of once after backward.
+    ``timeline_next_step()`` records the next step's device timeline
+    (``utils.timeline.StepTimeline``).
+    """
     def __init__(
         self,
         model: torch.nn.Module,
@@ -70,6 +145,7 @@ class DDPTrainer:
         device: torch.device | None = None,
         fused_optimizer: bool = True,
         monitor: bool = False,
+        overlap_optimizer: bool = False,
     ):
         self.device = device or (torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available()
                                  else torch.device("cpu"))
@@ -95,6 +171,18 @@ class DDPTrainer:
         use_fused = fused_optimizer and self.device.type == "cuda"
         self.opt = torch.optim.AdamW(self.ddp.parameters(), lr=lr, fused=use_fused)
         self.autocast_dtype = autocast_dtype if self.device.type == "cuda" else None
+        self.bucket_opt = None
+        if overlap_optimizer:
+            if hook not in ("fused", "host"):
+                raise ValueError("overlap_optimizer needs the fused (CUDA) or host (CPU) hook")
+            self.bucket_opt = BucketAdamW(self.opt)
+            self.hook_state.after_reduce = self.bucket_opt
+        self.timeline = None
+        self._timeline_next = False
+
+    def timeline_next_step(self) -> None:
+        """Record the next ``step``'s timeline into ``self.timeline``."""
+        self._timeline_next = True
 
     @property
     def model(self) -> torch.nn.Module:
@@ -103,6 +191,15 @@ class DDPTrainer:
     def step(self, x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
         if self.monitor is not None:
             self.monitor.check(self.steps_done)  # a peer that left is noticed before any launch
+        tl = None
+        if self._timeline_next and self.device.type == "cuda":
+            from .utils.timeline import StepTimeline
+
+            tl = self.timeline = StepTimeline()
+            tl.mark("forward")
+            if self.hook_state is not None and hasattr(self.hook_state, "timeline"):
+                self.hook_state.timeline = tl
+        self._timeline_next = False
         with nvtx_range("forward"):
             if self.autocast_dtype is not None:
                 with torch.autocast(self.device.type, dtype=self.autocast_dtype):
@@ -110,10 +207,22 @@ class DDPTrainer:
             else:
                 loss = self.ddp(x, y)
         self.opt.zero_grad(set_to_none=False)
+        if tl is not None:
+            tl.mark("backward")
         with nvtx_range("backward"):
             loss.backward()
+        if tl is not None:
+            tl.mark("backward_done")
         with nvtx_range("optimizer"):
-            self.opt.step()
+            if self.bucket_opt is not None:
+                self.bucket_opt.finish_step(self.opt.param_groups[0]["params"] if len(self.opt.param_groups) == 1
+                                            else [p for g in self.opt.param_groups for p in g["params"]])
+            else:
+                self.opt.step()
+        if tl is not None:
+            tl.mark("step_done")
+            if self.hook_state is not None and hasattr(self.hook_state, "timeline"):
+                self.hook_state.timeline = None
         self.steps_done += 1
         return loss.detach()
 

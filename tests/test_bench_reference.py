@@ -43,3 +43,25 @@ def test_reference_arm_steps(model, mode, name):
         for name in [m for m in sys.modules if m == "nangila_ddp" or m.startswith("nangila_ddp.")]:
             if "_ref" in (getattr(sys.modules[name], "__file__", "") or ""):
                 del sys.modules[name]
+
+
+def test_hook_on_reference_model_arm_steps():
+    """bench.py's same-model arm: this framework's hook on the stock
+    transformers GPT-2 with foreach AdamW and default DDP (tiny, CPU host hook)."""
+    import bench
+
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(s.getsockname()[1]))
+    s.close()
+    dist.init_process_group("gloo", rank=0, world_size=1)
+    try:
+        args = types.SimpleNamespace(model="gpt2", mode="int4", topk=0.05, momentum="auto", variant="auto")
+        step, hs, name = bench.build_hook_on_reference_model(args, torch.device("cpu"), tiny=True)
+        assert name == "fused-int4-ema-ef"
+        g = torch.Generator().manual_seed(0)
+        x, y = torch.randint(0, 512, (2, 16), generator=g), torch.randint(0, 512, (2, 16), generator=g)
+        losses = [float(step(x, y)) for _ in range(2)]
+        assert all(torch.isfinite(torch.tensor(losses))) and hs.raw_bytes > 0
+    finally:
+        dist.destroy_process_group()

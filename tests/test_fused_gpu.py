@@ -201,3 +201,80 @@ def test_prefetch_pipeline_copies_every_chunk(n, grid, vec):
     torch.cuda.synchronize()
     assert status.tolist()[0] == 0
     assert torch.equal(dst, src)
+
+
+def _twoshot_emulation(n, mode, world, drop=0.0, grid_cap=0):
+    """Rank 0 of a ``world``-rank two-shot all-reduce on one GPU.
+
+    Every rank's region is a local buffer.  Ranks world-1 .. 1 run first,
+    each with every other rank's phase-A payload and every payload and
+    result flag pre-delivered into its own region, so none of them waits on
+    anything unset; their phase-A records, phase-B INT8 results and flags
+    land in rank 0's region through the same stores as over NVLink.  Rank 0
+    runs last, with everything delivered, and its average, predictor and
+    error feedback are compared with the host two-shot oracle."""
+    from mini_nangila_b200.parallel.fused import MAX_COLS, MODES, VARIANTS, FusedAllReduce, make_layout, topology
+
+    h, c = _ext()
+    dev = torch.device("cuda")
+    k = 13
+    topo = topology(n, drop, 5, 6)
+    tl = list(topo) if drop else []
+    L = make_layout(world, n, k, modes=(mode,))
+    regs = [torch.zeros(L.total, dtype=torch.uint8, device=dev) for _ in range(world)]
+    ptrs = [r.data_ptr() for r in regs]
+    bits = 8 if mode == "int8" else 4
+    mcode = MODES[mode]
+    tag = FusedAllReduce.tag_for(n, 6)
+    grid = c.fused_grid(n, mcode, False, VARIANTS["twoshot"], grid_cap, 0)
+    epoch, parity = 1, 1
+    ftag = (tag ^ ((grid * 0x9E3779B1) & 0xFFFFFFFF)) & 0xFFFFFFFF
+    val = (ftag << 32) | epoch
+    if val >= 1 << 63:
+        val -= 1 << 64
+    pred = _data(n, 40)
+    efs = [_data(n, 50 + r, 1e-4) for r in range(world)]
+    gs = [_data(n, 60 + r) for r in range(world)]
+    seed, bucket, step = 21, 6, 3
+    payloads = [c.product_encode(torch.from_numpy(gs[r]).to(dev), torch.from_numpy(pred).to(dev),
+                                 torch.from_numpy(efs[r]).to(dev), mcode, k, True, seed, r, bucket, step, tl)[0]
+                for r in range(world)]
+    outs = {}
+    for r in list(range(world - 1, 0, -1)) + [0]:
+        if r != 0:
+            reg = regs[r]
+            flags = reg[L.flags_off:].view(torch.int64)
+            for src in range(world):
+                if src == r:
+                    continue
+                slot = L.inbox_off + (parity * world + src) * L.slot_bytes
+                reg[slot: slot + payloads[src].numel()] = payloads[src]
+                for kind in (0, 1):
+                    base = ((parity * 2 + kind) * world + src) * MAX_COLS
+                    flags[base: base + grid] = val
+        status = torch.zeros(4, dtype=torch.int32, device=dev)
+        comm = c.FusedComm(world, r, ptrs, L.flags_off, L.inbox_off, L.slot_bytes, L.result_off, L.result_bytes,
+                           status)
+        gd = torch.from_numpy(gs[r].copy()).to(dev)
+        pd = torch.from_numpy(pred.copy()).to(dev)
+        ed = torch.from_numpy(efs[r].copy()).to(dev)
+        torch.cuda.synchronize()
+        comm.run(gd, pd, ed, mcode, k, VARIANTS["twoshot"], True, seed, bucket, step, 0.9, False, grid_cap,
+                 int(2e9), tag, tl)
+        torch.cuda.synchronize()
+        outs[r] = (status.cpu().tolist(), gd.cpu().numpy(), pd.cpu().numpy(), ed.cpu().numpy())
+    inv = float(np.float32(1.0) / np.float32(world))
+    encs = [h.product_encode(gs[r], pred, efs[r], bits, True, True, seed, r, bucket, step, topo) for r in range(world)]
+    avg = h.product_reduce_twoshot([e[0] for e in encs], n, bits, pred, inv)
+    return outs[0], avg, h.product_ema(pred, avg, 0.9, False), encs[0][1]
+
+
+@pytest.mark.parametrize("mode", ["int4", "int8"])
+@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("n,drop,cap", [(70001, 0.0, 0), (70001, 0.4, 0), (300_000, 0.0, 7)])
+def test_twoshot_kernel_with_predelivered_peers(mode, world, n, drop, cap):
+    (st, out, pred_out, ef_out), avg, pred_ref, ef_ref = _twoshot_emulation(n, mode, world, drop, cap)
+    assert st[0] == 0, st
+    assert np.array_equal(_bits(out), _bits(avg)), int(np.sum(_bits(out) != _bits(avg)))
+    assert np.array_equal(_bits(pred_out), _bits(pred_ref))
+    assert np.array_equal(_bits(ef_out), _bits(ef_ref))

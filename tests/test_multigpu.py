@@ -56,7 +56,8 @@ def _worker(rank, world, port, cases, errfile):
                 gs = [_data(n, 100 * step + r) for r in range(world)]
                 gd = torch.from_numpy(gs[rank].copy()).to(dev)
                 comm.allreduce_(gd, pred_d, ef_d, mode=mode, k=k, variant=variant, seed=11, bucket=3, step=step,
-                                beta=0.9, first=(step == 0), topo_drop=drop, topo_seed=8)
+                                beta=0.9, first=(step == 0), topo_drop=drop, topo_seed=8,
+                                max_ctas=7 if step == 1 else None)
                 if mode == "topk":
                     encs = [h.product_topk_encode(gs[r], pred, efs[r], k, True, topo) for r in range(world)]
                     avg = h.product_topk_reduce([e[0] for e in encs], n, k, pred, inv)
@@ -83,7 +84,7 @@ def _worker(rank, world, port, cases, errfile):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_fused_allreduce_matches_oracle_across_ranks(world, tmp_path):
     import torch.multiprocessing as mp
 
