@@ -5,6 +5,7 @@
 
 #include <string>
 
+#include "hdf5_io.hpp"
 #include "nangila_host.hpp"
 
 namespace py = pybind11;
@@ -37,9 +38,63 @@ float* out_f32(const py::object& o, size_t n, const char* what) {
   if (!a.writeable()) throw std::runtime_error(std::string(what) + " is read-only");
   return a.mutable_data();
 }
+// HDF5 objects <-> Python: a value is (kind, size, shape, bytes); an object
+// is (is_group, name, parent, value or None, [(attr name, value), ...]).
+ngl::h5::Value h5_value(const py::tuple& t) {
+  ngl::h5::Value v;
+  const std::string kind = t[0].cast<std::string>();
+  if (kind.size() != 1) throw std::runtime_error("HDF5 value kind must be one character");
+  v.kind = kind[0];
+  v.size = t[1].cast<int>();
+  v.shape = t[2].cast<std::vector<uint64_t>>();
+  v.bytes = t[3].cast<std::string>();
+  return v;
+}
+py::tuple h5_tuple(const ngl::h5::Value& v) {
+  return py::make_tuple(std::string(1, v.kind), v.size, v.shape, py::bytes(v.bytes));
+}
 }  // namespace
 
 PYBIND11_MODULE(_host, m) {
+  py::register_exception<ngl::h5::Error>(m, "H5Error", PyExc_ValueError);
+  m.def("h5_write", [](const py::list& objs) {
+    std::vector<ngl::h5::Object> v;
+    for (const auto& it : objs) {
+      const auto t = it.cast<py::tuple>();
+      ngl::h5::Object o;
+      o.is_group = t[0].cast<bool>();
+      o.name = t[1].cast<std::string>();
+      o.parent = t[2].cast<int>();
+      if (!t[3].is_none()) o.data = h5_value(t[3].cast<py::tuple>());
+      for (const auto& a : t[4].cast<py::list>()) {
+        const auto at = a.cast<py::tuple>();
+        o.attrs.push_back({at[0].cast<std::string>(), h5_value(at[1].cast<py::tuple>())});
+      }
+      v.push_back(std::move(o));
+    }
+    std::string out;
+    {
+      py::gil_scoped_release nogil;
+      out = ngl::h5::write_file(v);
+    }
+    return py::bytes(out);
+  }, py::arg("objects"), "HDF5 file bytes of a flat object list (objects[0] is the root group)");
+  m.def("h5_read", [](const py::bytes& file) {
+    const std::string f = file;
+    std::vector<ngl::h5::Object> v;
+    {
+      py::gil_scoped_release nogil;
+      v = ngl::h5::read_file(f);
+    }
+    py::list out;
+    for (const auto& o : v) {
+      py::list attrs;
+      for (const auto& a : o.attrs) attrs.append(py::make_tuple(a.name, h5_tuple(a.value)));
+      out.append(py::make_tuple(o.is_group, o.name, o.parent, o.is_group ? py::object(py::none())
+                                                                           : py::object(h5_tuple(o.data)), attrs));
+    }
+    return out;
+  }, py::arg("file"), "Flat object list of an HDF5 file image");
   m.doc() = "Native host library: bit-exact codecs, predictors, topology, NZCP, product-format oracle";
   py::register_exception<ShapeMismatch>(m, "ShapeMismatch", PyExc_ValueError);
 

@@ -3,18 +3,21 @@
 // within its bound), every decoder on random garbage and on truncations of
 // valid streams (no out-of-bounds access, no undefined arithmetic), the NZCP
 // container, TopologyMask bincode (including malformed input), the LAMMPS
-// dump reader (valid, truncated and random text), and the product-format
-// oracle.  Exit status 0 and "selftest ok" on success.
+// dump reader (valid, truncated and random text), the HDF5 writer and
+// reader (round trip, every truncation and random byte flips of a written
+// file), and the product-format oracle.  Exit status 0 and "selftest ok" on success.
 //
 //   g++ -std=c++17 -O1 -g -fsanitize=address,undefined -fno-sanitize-recover=all \
 //       -fno-omit-frame-pointer -Icsrc csrc/host/codecs.cpp csrc/host/pipeline.cpp \
-//       csrc/host/product.cpp csrc/host/lammps_io.cpp csrc/host/selftest/selftest.cpp -o selftest && ./selftest
+//       csrc/host/product.cpp csrc/host/lammps_io.cpp csrc/host/hdf5_io.cpp csrc/host/selftest/selftest.cpp \
+//       -o selftest && ./selftest
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
 #include <random>
 #include <string>
 
+#include "../hdf5_io.hpp"
 #include "../nangila_host.hpp"
 
 using namespace ngl::host;
@@ -209,6 +212,72 @@ int main() {
     const uint8_t* ts[1] = {tk.data()};
     product_topk_reduce(ts, 1, n, 13, pred.data(), 1.0f, avg.data());
     product_ema(pred.data(), avg.data(), n, 0.9f, false);
+  }
+  // HDF5: a tree with nested groups, more links than one symbol table node
+  // holds, every element type and scalar / N-D / empty values; then every
+  // truncation and random byte flips of the file must fail cleanly
+  {
+    namespace h5 = ngl::h5;
+    auto val = [](char kind, int size, std::vector<uint64_t> shape) {
+      h5::Value v;
+      v.kind = kind;
+      v.size = size;
+      v.shape = shape;
+      uint64_t n = 1;
+      for (uint64_t d : shape) n *= d;
+      v.bytes.resize(n * size);
+      for (auto& c : v.bytes) c = (char)(rng() & 0x7f);
+      return v;
+    };
+    std::vector<h5::Object> objs(1);
+    objs[0].attrs.push_back({"root_attr", val('f', 8, {})});
+    h5::Object g;
+    g.name = "grp";
+    g.parent = 0;
+    g.attrs.push_back({"codec", val('S', 17, {})});
+    g.attrs.push_back({"total_len", val('u', 8, {})});
+    objs.push_back(g);
+    for (int i = 0; i < 21; ++i) {
+      h5::Object d;
+      d.is_group = false;
+      d.name = "d" + std::to_string(i);
+      d.parent = i % 2 ? 1 : 0;
+      const char kinds[] = {'u', 'i', 'f', 'S'};
+      const char k = kinds[i % 4];
+      const int size = k == 'f' ? (i % 8 < 4 ? 4 : 8) : (k == 'S' ? 5 : 1 << (i % 4));
+      d.data = val(k, size, i % 5 == 0 ? std::vector<uint64_t>{} : std::vector<uint64_t>{(uint64_t)(i * 7 % 13), 3});
+      d.attrs.push_back({"a", val('i', 4, {2})});
+      objs.push_back(d);
+    }
+    h5::Object sub;
+    sub.name = "sub";
+    sub.parent = 1;
+    objs.push_back(sub);
+    const std::string file = h5::write_file(objs);
+    const std::vector<h5::Object> back = h5::read_file(file);
+    CHECK(back.size() == objs.size());
+    size_t checked = 0;
+    for (const auto& b : back)
+      for (const auto& o : objs)
+        if (o.name == b.name && !o.is_group && !b.is_group) {
+          CHECK(o.data.bytes == b.data.bytes && o.data.shape == b.data.shape && o.data.kind == b.data.kind);
+          ++checked;
+        }
+    CHECK(checked == 21);
+    for (size_t cut = 0; cut < file.size(); cut += 1 + file.size() / 257) {
+      try {
+        (void)h5::read_file(file.substr(0, cut));
+      } catch (const std::exception&) {
+      }
+    }
+    for (int t = 0; t < 400; ++t) {
+      std::string f = file;
+      for (int k = 0; k < 1 + t % 4; ++k) f[rng() % f.size()] = (char)(rng() & 0xff);
+      try {
+        (void)h5::read_file(f);
+      } catch (const std::exception&) {
+      }
+    }
   }
   std::printf("selftest ok\n");
   return 0;

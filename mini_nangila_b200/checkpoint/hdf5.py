@@ -10,9 +10,11 @@ label) and stores, under group ``dataset``:
 * ``scales`` f32[num_chunks]
 * attrs ``total_len`` (u64), ``chunk`` (u64), ``codec`` (str), ``epsilon`` (f32)
 
-``read_compressed_1d`` reverses it.  With h5py installed the file is HDF5
-with exactly these names; without it the same arrays and attributes go into
-an ``.npz`` archive (keys ``<dataset>/blob`` ... and ``<dataset>/@attr``).
+``read_compressed_1d`` reverses it.  The file is always HDF5 with exactly
+these names: through h5py when it is installed, otherwise through this
+framework's native HDF5 writer and reader (``checkpoint.h5file``, no libhdf5
+needed), whose files h5py reads and which reads files libhdf5 wrote.  Like
+the reference's ``File::create``, the writers replace an existing file.
 """
 from __future__ import annotations
 
@@ -20,6 +22,8 @@ import numpy as np
 
 from ..core.fixed_point import FixedPointBuffer
 from ..hpc import ErrorBoundedQuantizer, LinearPredictor
+
+from . import h5file
 
 try:  # optional dependency
     import h5py  # type: ignore
@@ -81,10 +85,13 @@ def write_chunked_dataset(path: str, dataset: str, data, chunk: int, epsilon: fl
             for k, v in attrs.items():
                 g.attrs[k] = v
         return
-    arrays = {f"{dataset}/blob": blob, f"{dataset}/offsets": offsets, f"{dataset}/scales": scales}
-    arrays.update({f"{dataset}/@{k}": np.asarray(v) for k, v in attrs.items()})
-    with open(path, "wb") as fh:
-        np.savez(fh, **arrays)
+    root = h5file.Group()
+    g = root.create_group(dataset)
+    g.create_dataset("blob", blob)
+    g.create_dataset("offsets", offsets)
+    g.create_dataset("scales", scales)
+    g.attrs.update(attrs)
+    h5file.save(path, root)
 
 
 def read_compressed_1d(path: str, dataset: str) -> np.ndarray:
@@ -94,31 +101,23 @@ def read_compressed_1d(path: str, dataset: str) -> np.ndarray:
             g = f[dataset]
             return _decode_chunks(g["blob"][()], g["offsets"][()], g["scales"][()], int(g.attrs["total_len"]),
                                   float(g.attrs["epsilon"]))
-    with np.load(path) as z:
-        return _decode_chunks(z[f"{dataset}/blob"], z[f"{dataset}/offsets"], z[f"{dataset}/scales"],
-                              int(z[f"{dataset}/@total_len"]), float(z[f"{dataset}/@epsilon"]))
+    g = h5file.load(path)[dataset]
+    return _decode_chunks(g["blob"].data, g["offsets"].data, g["scales"].data, int(g.attrs["total_len"]),
+                          float(g.attrs["epsilon"]))
 
 
 def write_dataset(path: str, dataset: str, data, epsilon: float, codec: str) -> None:
     """Plain 1-D f32 dataset with ``epsilon`` and ``codec`` attributes (nangila-checkpoint/src/lib.rs:14-26)."""
     data = np.asarray(data, np.float32).reshape(-1)
     if h5py is not None:
-        with h5py.File(path, "a") as f:
+        with h5py.File(path, "w") as f:
             ds = f.create_dataset(dataset, data=data)
             ds.attrs["epsilon"] = np.float32(epsilon)
             ds.attrs["codec"] = codec
         return
-    existing = {}
-    try:
-        with np.load(path) as z:
-            existing = {k: z[k] for k in z.files}
-    except (OSError, ValueError):
-        pass
-    existing[dataset] = data
-    existing[f"{dataset}@epsilon"] = np.float32(epsilon)
-    existing[f"{dataset}@codec"] = np.asarray(codec)
-    with open(path, "wb") as fh:
-        np.savez(fh, **existing)
+    root = h5file.Group()
+    root.create_dataset(dataset, data, attrs={"epsilon": np.float32(epsilon), "codec": codec})
+    h5file.save(path, root)
 
 
 def read_dataset(path: str, dataset: str) -> np.ndarray:
@@ -126,5 +125,4 @@ def read_dataset(path: str, dataset: str) -> np.ndarray:
     if h5py is not None:
         with h5py.File(path, "r") as f:
             return f[dataset][()]
-    with np.load(path) as z:
-        return z[dataset]
+    return h5file.load(path)[dataset].data

@@ -13,7 +13,8 @@ import pytest
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
-SRC = [os.path.join(ROOT, "csrc", "host", f) for f in ("codecs.cpp", "pipeline.cpp", "product.cpp", "lammps_io.cpp")]
+SRC = [os.path.join(ROOT, "csrc", "host", f) for f in ("codecs.cpp", "pipeline.cpp", "product.cpp", "lammps_io.cpp",
+                                                 "hdf5_io.cpp")]
 SRC.append(os.path.join(ROOT, "csrc", "host", "selftest", "selftest.cpp"))
 
 
