@@ -71,8 +71,11 @@ def parse():
                     help="EMA predictor in the hook (auto: on for int4/int8, off for top-k, which uses error feedback)")
     ap.add_argument("--overlap-opt", choices=["on", "off"], default="on",
                     help="fused hook: apply AdamW per bucket from the hook, overlapping backward")
-    ap.add_argument("--inflight-ctas", type=int, default=None,
-                    help="grid cap of exchange kernels that overlap backward (default: the hook's choice)")
+    ap.add_argument("--inflight-ctas", type=int, default=0,
+                    help="grid cap of exchange kernels that overlap backward (0: the whole grid)")
+    ap.add_argument("--stream-priority", type=int, default=-1, help="hook stream priority (-1 high, 0 normal)")
+    ap.add_argument("--l2-keep-mb", type=float, default=48.0,
+                    help="predictor MB an exchange kernel keeps in L2 between its phases (0: no L2 policy)")
     ap.add_argument("--no-arms", action="store_true", help="skip the same-box NCCL and same-model comparison arms")
     ap.add_argument("--timeline", default="", help="write one step's per-bucket device timeline (JSON) here")
     return ap.parse_args()
@@ -304,7 +307,8 @@ def main():
                       topk_percent=args.topk if args.mode == "topk" else 0.0, seed=12345,
                       error_feedback=True, variant=args.variant, max_ctas=args.max_ctas)
             if args.hook == "fused":
-                hk["inflight_ctas"] = args.inflight_ctas
+                hk.update(inflight_ctas=args.inflight_ctas, stream_priority=args.stream_priority,
+                          l2_keep_mb=args.l2_keep_mb)
         overlap = args.hook == "fused" and args.overlap_opt == "on"
         trainer = DDPTrainer(model, lr=6e-4, hook=args.hook, hook_kwargs=hk, bucket_cap_mb=25.0,
                              autocast_dtype=torch.bfloat16 if args.model == "gpt2" else None, device=device,

@@ -37,6 +37,9 @@ struct QParams {
   int use_ef;
   int use_pred;
   Topo topo;
+  // Exchange kernels: fraction of the predictor's lines read in phase 1 with
+  // the L2 evict_last policy, so phase 2's re-read hits L2 (0: no policy).
+  float pred_keep;
 };
 struct FParams {
   float inv_world;
@@ -45,6 +48,7 @@ struct FParams {
   int first;
   int use_pred;
   Topo topo;
+  int pred_stream;  // phase 2 reads the predictor with the evict_first policy
 };
 
 // Symmetric region of every rank (same layout on all ranks):

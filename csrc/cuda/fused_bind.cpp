@@ -5,6 +5,7 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include <algorithm>
 #include <cstring>
 
 #include "common/ngl_product.h"
@@ -138,6 +139,12 @@ class FusedComm {
     P.f.use_pred = P.pred != nullptr;
     P.q.topo = topo_of(topo, P.nchunks);
     P.f.topo = P.q.topo;
+    // Exchange kernels read the predictor in both phases: keep (at most
+    // l2_keep_bytes of) it in L2 between them.
+    P.q.pred_keep = 0.0f;
+    if (variant != kVariantSingle && P.pred != nullptr && l2_keep_bytes_ > 0 && n > 0)
+      P.q.pred_keep = (float)std::min(1.0, (double)l2_keep_bytes_ / (4.0 * (double)n));
+    P.f.pred_stream = P.q.pred_keep > 0.0f ? 1 : 0;
     P.timeout_ns = (uint64_t)timeout_ns;
     if (P.nblk == 0) return epoch_;
     const c10::cuda::CUDAGuard guard(grad.device());
@@ -150,8 +157,13 @@ class FusedComm {
 
   int64_t epoch() const { return epoch_; }
   void set_epoch(int64_t e) { epoch_ = e; }
+  int64_t l2_keep_bytes() const { return l2_keep_bytes_; }
+  void set_l2_keep_bytes(int64_t b) { l2_keep_bytes_ = b < 0 ? 0 : b; }
 
  private:
+  // Predictor bytes held in L2 between the phases of an exchange kernel
+  // (48 MB of the 126 MB L2 by default; 0 turns the policy off).
+  int64_t l2_keep_bytes_ = int64_t(48) << 20;
   int64_t world_, rank_;
   torch::Tensor status_;
   FusedParams base_;
@@ -179,6 +191,7 @@ std::vector<torch::Tensor> product_encode_cuda(torch::Tensor g, c10::optional<to
   qp.use_ef = ef.has_value();
   qp.use_pred = pred.has_value();
   qp.topo = topo_of(topo, nchunks_of(n));
+  qp.pred_keep = 0.0f;
   if (pred.has_value()) check_dev(*pred, "pred");
   if (ef.has_value()) check_dev(*ef, "ef");
   if (nblk == 0) return {out, ef_out};
@@ -215,6 +228,7 @@ torch::Tensor product_reduce_cuda(std::vector<torch::Tensor> payloads, int64_t n
   fp.first = first;
   fp.use_pred = pred.has_value();
   fp.topo = topo_of(topo, nchunks_of(n));
+  fp.pred_stream = 0;
   if (pred.has_value()) check_dev(*pred, "pred");
   const c10::cuda::CUDAGuard guard(payloads[0].device());
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
@@ -237,7 +251,8 @@ void register_fused(pybind11::module& m) {
            pybind11::arg("seed"), pybind11::arg("bucket"), pybind11::arg("step"), pybind11::arg("beta"),
            pybind11::arg("first"), pybind11::arg("max_ctas"), pybind11::arg("timeout_ns"), pybind11::arg("tag"),
            pybind11::arg("topo") = std::vector<int64_t>{})
-      .def_property("epoch", &FusedComm::epoch, &FusedComm::set_epoch);
+      .def_property("epoch", &FusedComm::epoch, &FusedComm::set_epoch)
+      .def_property("l2_keep_bytes", &FusedComm::l2_keep_bytes, &FusedComm::set_l2_keep_bytes);
   m.def("product_encode", &product_encode_cuda, pybind11::arg("g"), pybind11::arg("pred"), pybind11::arg("ef"),
         pybind11::arg("mode"), pybind11::arg("k"), pybind11::arg("stochastic"), pybind11::arg("seed"),
         pybind11::arg("rank"), pybind11::arg("bucket"), pybind11::arg("step"),

@@ -64,15 +64,27 @@ struct ChunkSrc {
 };
 
 // Residual c = g - pred + e of the lane's 8 consecutive elements of a block.
-template <typename T>
+// kL2Policy compiles the L2-policy loads in (dense modes; the top-k kernels
+// keep their registers for the selection).
+template <typename T, bool kL2Policy = true>
 __device__ __forceinline__ int load_residual(const ChunkSrc<T>& s, int64_t n, int blk, int lane, const QParams& qp,
                                              float (&c)[8]) {
   const int64_t e0 = (int64_t)blk * kBlock + lane * 8;
   const int valid = (int)min64(8, max64(0, n - e0));
   float gv[8], pv[8], ev[8];
-  load8<T>(s.g, e0 - s.roff, valid, true, gv);
-  if (qp.use_pred) load8<float>(s.pred, e0 - s.roff, valid, true, pv);
-  if (qp.use_ef) load8<float>(s.ef, e0 - s.roff, valid, true, ev);
+  if (kL2Policy && qp.pred_keep > 0.0f && s.roff == 0) {
+    // Exchange kernels, global source: the predictor is read again in
+    // phase 2, so its lines are kept in L2; gradient and EF stream through.
+    const uint64_t stream = l2_policy_evict_first();
+    if constexpr (sizeof(T) == 4) load8_policy(reinterpret_cast<const float*>(s.g), e0, valid, stream, gv);
+    else load8<T>(s.g, e0, valid, true, gv);
+    if (qp.use_pred) load8_policy(s.pred, e0, valid, l2_policy_evict_last(qp.pred_keep), pv);
+    if (qp.use_ef) load8_policy(s.ef, e0, valid, stream, ev);
+  } else {
+    load8<T>(s.g, e0 - s.roff, valid, true, gv);
+    if (qp.use_pred) load8<float>(s.pred, e0 - s.roff, valid, true, pv);
+    if (qp.use_ef) load8<float>(s.ef, e0 - s.roff, valid, true, ev);
+  }
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     const float p = qp.use_pred ? pv[j] : 0.0f;
@@ -88,7 +100,7 @@ __device__ __forceinline__ void passenger_block(const ChunkSrc<T>& s, float* ef_
                                                 const QParams& qp) {
   if (!qp.use_ef) return;
   float cv[8];
-  const int valid = load_residual<T>(s, n, blk, lane, qp, cv);
+  const int valid = load_residual<T, false>(s, n, blk, lane, qp, cv);
   store8<float>(ef_w, (int64_t)blk * kBlock + lane * 8, valid, true, cv);
 }
 
@@ -241,14 +253,17 @@ __device__ __forceinline__ void accum_dense(const uint8_t* rec, int warp, int la
 }
 
 // avg = pred + acc / W -> bucket; EMA update of the predictor state.
-template <typename T>
+template <typename T, bool kL2Policy = true>
 __device__ __forceinline__ void finalize(T* grad, float* pred, int64_t n, int blk, int lane, const float (&acc)[8],
                                          const FParams& fp) {
   const int64_t e0 = (int64_t)blk * kBlock + lane * 8;
   const int valid = (int)min64(8, max64(0, n - e0));
   if (valid <= 0) return;
   float p[8], avg[8];
-  if (fp.use_pred) load8<float>(pred, e0, valid, true, p);
+  if (fp.use_pred) {
+    if (kL2Policy && fp.pred_stream) load8_policy(pred, e0, valid, l2_policy_evict_first(), p);
+    else load8<float>(pred, e0, valid, true, p);
+  }
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     if (!fp.use_pred) p[j] = 0.0f;
@@ -428,7 +443,7 @@ __device__ __forceinline__ void encode_chunk(const ChunkSrc<T>& src, float* ef_w
     uint8_t* r = rec + warp * rec_bytes;
     if (blk < nblk) {
       float cv[8];
-      const int valid = load_residual<T>(src, n, blk, lane, qp, cv);
+      const int valid = load_residual<T, false>(src, n, blk, lane, qp, cv);
       topk_select(cv, valid, blk, lane, k, n, qp, ef_w, r, rec_bytes);
     } else {
       for (int w = lane; w < rec_bytes / 4; w += 32) reinterpret_cast<uint32_t*>(r)[w] = 0u;
@@ -483,7 +498,7 @@ __device__ __forceinline__ void decode_chunk(const RecOf& rec_of, int world, T* 
     constexpr int BITS = MODE == kInt4 ? 4 : 8;
     for (int src = 0; src < world; ++src) accum_dense<BITS>(rec_of(src), warp, lane, acc);
   }
-  finalize<T>(grad, pred, n, blk, lane, acc, fp);
+  finalize<T, MODE != kTopK>(grad, pred, n, blk, lane, acc, fp);
 }
 
 // ---------------------------------------------------------- flag addressing
@@ -687,7 +702,7 @@ __device__ __forceinline__ void single_chunk(const FusedParams& P, const ChunkSr
   const int blk = ch * kChunkBlocks + warp;
   if (blk >= P.nblk) return;
   float c[8], acc[8];
-  const int valid = load_residual<T>(in, P.n, blk, lane, P.q, c);
+  const int valid = load_residual<T, false>(in, P.n, blk, lane, P.q, c);
   if (passenger(P.q.topo, ch, P.nchunks)) {
     if (P.q.use_ef) store8<float>(P.ef, (int64_t)blk * kBlock + lane * 8, valid, true, c);
 #pragma unroll

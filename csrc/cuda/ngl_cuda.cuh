@@ -188,6 +188,40 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* m, uint32_t parity, uint64_t
   return true;
 }
 
+// ---- L2 eviction-priority loads (createpolicy + ld.global.L2::cache_hint)
+// A policy marks a fraction of the accessed lines evict_first (streamed
+// once) or evict_last (read again soon by this kernel: kept over normal
+// lines).  fp32 only; the caller checks alignment (16 bytes).
+__device__ __forceinline__ uint64_t l2_policy_evict_last(float fraction) {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, %1;" : "=l"(p) : "f"(fraction));
+  return p;
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ float4 ld_f4_policy(const float* p, uint64_t pol) {
+  float4 v;
+  asm volatile("ld.global.L2::cache_hint.v4.f32 {%0, %1, %2, %3}, [%4], %5;"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(p), "l"(pol));
+  return v;
+}
+// 8 fp32 elements at base + e0 through an L2 policy (scalar tail as load8).
+__device__ __forceinline__ void load8_policy(const float* base, int64_t e0, int valid, uint64_t pol,
+                                             float (&v)[8]) {
+  if (valid == 8) {
+    const float4 a = ld_f4_policy(base + e0, pol), b = ld_f4_policy(base + e0 + 4, pol);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = (j < valid) ? base[e0 + j] : 0.0f;
+  }
+}
+
 template <typename T>
 __device__ __forceinline__ void load8(const T* base, int64_t e0, int valid, bool vec_ok, float (&v)[8]) {
   if (valid == 8 && vec_ok) {

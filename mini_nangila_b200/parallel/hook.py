@@ -551,13 +551,19 @@ def register_nangila_hook(
     max_ctas: int = 0,
     process_group=None,
     autotune: bool = True,
-    inflight_ctas: int | None = None,
+    inflight_ctas: int = 0,
+    stream_priority: int = -1,
+    l2_keep_mb: float = 48.0,
 ) -> NangilaHookState:
     """Register a predictive-residual compression comm hook on a DDP model.
 
     ``inflight_ctas`` caps the grid of the exchange kernels of every bucket
-    but the last (they overlap backward); None picks 32 with more than one
-    rank and no cap on one rank, 0 disables the cap.
+    but the last (they overlap backward); 0 (the default) leaves them the
+    whole grid, which measured fastest on B200s: a capped exchange kernel
+    lacks the memory parallelism to finish early and holds its SMs longer.
+    ``stream_priority`` is the hook stream's CUDA priority (-1 high, 0
+    normal).  ``l2_keep_mb`` bounds the predictor bytes an exchange kernel
+    keeps in L2 between its two phases (0 turns the L2 policy off).
 
     Returns the hook state (metrics, ``state_dict``/``load_state_dict``).
     """
@@ -578,9 +584,6 @@ def register_nangila_hook(
         hs = NangilaHookState(cfg, process_group)
         model.register_comm_hook(state=None, hook=make_compat_hook(hs))
         return hs
-    world = dist.get_world_size(process_group) if dist.is_initialized() else 1
-    if inflight_ctas is None:
-        inflight_ctas = 32 if world > 1 else 0
     cfg = HookConfig(beta, bits, stochastic, use_fp16_transport, seed, metrics_path, use_momentum, topk_percent,
                      topo_drop_percent, topo_seed, impl, True if error_feedback is None else bool(error_feedback),
                      variant, timeout_s, verbose, max_ctas, int(inflight_ctas))
@@ -595,7 +598,8 @@ def register_nangila_hook(
         max_numel = bucket_cap // 4 + max(p.numel() for p in model.parameters()) + 8192
         hs.comm = FusedAllReduce(max_numel, group=process_group, device=dev, topk_k=max(cfg.k, 1),
                                  timeout_s=timeout_s, max_ctas=max_ctas, modes=(cfg.mode,))
-        hs.stream = torch.cuda.Stream(device=dev, priority=-1)
+        hs.comm.comm.l2_keep_bytes = int(max(0.0, l2_keep_mb) * (1 << 20))
+        hs.stream = torch.cuda.Stream(device=dev, priority=int(stream_priority))
         hs.autotune_pending = bool(autotune) and hs.comm.world > 2 and variant == "auto" and cfg.mode != "topk"
 
         def hook(_state, bucket):

@@ -268,3 +268,33 @@ def test_rotor_topk_codes_round_half_away_from_zero():
     frame, _ = c.encode(np.array([200.0, -200.0, 1.0, 0.0, 0.0, 0.0], np.float32), 0)
     assert rle_decode_i16(frame.residual).tolist() == [32767, -32768, 0, 0, 0, 0]
     c.close()
+
+
+def test_loss_curves_app_two_cpu_ranks(tmp_path):
+    """apps.loss_curves on two gloo ranks with a tiny GPT-2: every setting
+    starts from the same loss (same weights and batches) and the summary
+    names its difference to the uncompressed all-reduce."""
+    import json
+    import socket
+    import subprocess
+    import sys
+
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    out = tmp_path / "curves.json"
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+           "--master-addr", "127.0.0.1", "--master-port", str(port), "-m", "mini_nangila_b200.apps.loss_curves",
+           "--tiny", "--steps", "4", "--micro-batch", "2", "--seq", "16", "--warmup", "2",
+           "--settings", "nccl,int4-oneshot,topk5,compat", "--out", str(out), "--log-dir", str(tmp_path)]
+    env = dict(os.environ, PYTHONPATH=os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    r = subprocess.run(cmd, capture_output=True, text=True, timeout=600, env=env)
+    assert r.returncode == 0, r.stderr[-3000:]
+    res = json.loads(out.read_text())
+    curves = res["curves"]
+    assert set(curves) == {"nccl", "int4-oneshot", "topk5", "compat"}
+    first = {k: v[0] for k, v in curves.items()}
+    assert max(first.values()) - min(first.values()) < 1e-5  # same weights, same first batch
+    assert res["summary"]["nccl"]["delta_vs_nccl"] == 0.0
+    assert (tmp_path / "train_log_topk5.csv").read_text().startswith("ts,step,loss,lr,tokens_per_sec,step_ms")
