@@ -10,8 +10,8 @@
 
 The reference's plotting snippets (python/snippets/*.py,
 python/nangila_ddp/plot_*.py, benchmarks/plot_baselines.py) as one CLI:
-prints a JSON summary; ``--plot`` also writes the PNGs when matplotlib is
-installed.
+prints a JSON summary; ``--plot`` also writes the reference's PNGs (drawn by
+``utils.plot``, no plotting library needed).
 """
 from __future__ import annotations
 
@@ -40,21 +40,21 @@ def main(argv=None):
         out["ratio"] = A._stats(r)
         if a.plot:
             out["plot"] = A.plot_series(np.arange(r.size), r, "hook call index", "compression ratio",
-                                        a.files[0].replace(".csv", "_ratio.png"))
+                                        a.files[0].replace(".csv", "_ratio.png"), title="DDP hook compression ratio")
     elif a.kind == "hpc":
         out.update(A.summarize_hpc(a.files[0]))
         if a.plot:
-            s, r, _ = A.parse_hpc_log(a.files[0])
-            out["plot"] = A.plot_series(s, r, "step", "compression ratio", "hpc_ratio.png")
+            out["plot"] = A.plot_hpc(a.files[0])
     elif a.kind == "twin":
         out["client"] = A.summarize_ticks(a.files[0])
         if len(a.files) > 1:
             out["server"] = A.summarize_ticks(a.files[1])
         if a.plot:
-            t, r = A.load_tick_ratio_csv(a.files[0])
-            out["plot"] = A.plot_series(t, r, "tick", "compression ratio", "rotor_net_ratio.png")
+            out["plot"] = A.plot_twin(a.files[0], a.files[1] if len(a.files) > 1 else None)
     elif a.kind == "entropy":
         out.update(A.entropy_reduction())
+        if a.plot:
+            out["plot"] = A.plot_entropy()
     elif a.kind == "baselines":
         out.update(A.summarize_baselines(a.files[0]))
         if a.plot:

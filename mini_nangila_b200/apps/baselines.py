@@ -27,7 +27,7 @@ per second.  Writes ``baseline_comparison.txt`` and
 ``baseline_comparison.csv`` (the reference's columns ``tool, epsilon,
 codec, compressed_bytes, ratio, comp_time_s, throughput_MBps, status`` plus
 ``codec_time_s`` and ``device``) into the results directory; ``--plot``
-also writes ``baseline_comparison.png`` when matplotlib is installed.
+also writes ``baseline_comparison.png``.
 """
 from __future__ import annotations
 

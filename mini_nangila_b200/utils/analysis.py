@@ -10,8 +10,7 @@ twin metric CSVs with the tick first and the ratio last
 (python/snippets/plot_rotor_net.py:6-19), the compression-baseline CSV of
 ``apps/baselines`` (benchmarks/plot_baselines.py:8-16)), numeric summaries
 of each, and
-optional PNG plots when matplotlib is importable (it is optional: every
-summary works without it).  ``entropy_reduction`` restates the reference's
+PNG or SVG plots drawn by ``utils.plot`` (no plotting library needed).  ``entropy_reduction`` restates the reference's
 entropy illustration (python/snippets/entropy_plot.py:5-33) as numbers: the
 histogram entropy of a signal and of its EMA-prediction residual.
 """
@@ -176,70 +175,113 @@ def entropy_reduction(x: np.ndarray | None = None, beta: float = 0.9, bins: int 
 
 
 # -------------------------------------------------------------------- plots
-def _plt():
-    try:
-        import matplotlib
-
-        matplotlib.use("Agg")
-        import matplotlib.pyplot as plt
-    except ImportError as e:  # optional dependency
-        raise RuntimeError("plots need matplotlib, which is not installed; the summaries do not") from e
-    return plt
-
-
+# Drawn by utils.plot (PNG or SVG by the output's extension); no plotting
+# library is needed.
 def plot_training(train_csv: str, metrics_csv: str, out: str = "train_and_compression.png") -> str:
-    plt = _plt()
+    """Loss over time with the hook's compression ratio (and mean |residual|)
+    on a second axis (python/nangila_ddp/plot_train_and_compression.py:8-95)."""
+    from .plot import Figure
+
     ts, _, loss = load_train_log(train_csv)
     m = load_hook_metrics(metrics_csv)
     d_ts, ratio = m.get("ts", np.array([])), m.get("ratio", np.array([]))
     t0 = min(ts.min() if ts.size else math.inf, d_ts.min() if d_ts.size else math.inf)
-    fig, ax1 = plt.subplots(figsize=(9, 4))
-    ax1.plot(ts - t0, loss, color="tab:blue")
-    ax1.set_xlabel("time (s)")
-    ax1.set_ylabel("loss")
-    ax2 = ax1.twinx()
-    ax2.plot(d_ts - t0, ratio, ".", alpha=0.3, color="tab:orange")
-    ax2.set_ylabel("compression ratio")
-    fig.tight_layout()
-    fig.savefig(out)
-    plt.close(fig)
-    return out
+    t0 = 0.0 if not math.isfinite(t0) else t0
+    fig = Figure(900, 420)
+    ax = fig.add_axes(title="training loss and compression", xlabel="time (s)", ylabel="loss")
+    ax.line(ts - t0, loss, color="tab:blue", label="loss")
+    ax2 = ax.twin(ylabel="compression ratio")
+    ax2.points(d_ts - t0, ratio, color="tab:orange", alpha=0.3, label="ratio (raw/comp)")
+    if ratio.size >= 10:
+        k = max(1, ratio.size // 50)
+        smooth = np.convolve(ratio, np.ones(k) / k, mode="same")
+        ax2.line(d_ts - t0, smooth, color="tab:orange")
+    return fig.save(out)
 
 
-def plot_series(x, y, xlabel: str, ylabel: str, out: str) -> str:
-    plt = _plt()
-    fig = plt.figure(figsize=(8, 4))
-    plt.plot(x, y, "-o", alpha=0.7)
-    plt.xlabel(xlabel)
-    plt.ylabel(ylabel)
-    plt.grid(True, alpha=0.3)
-    fig.tight_layout()
-    fig.savefig(out)
-    plt.close(fig)
-    return out
+def plot_series(x, y, xlabel: str, ylabel: str, out: str, title: str = "", labels=None) -> str:
+    """One or several y series against x (a list of arrays with ``labels``)."""
+    from .plot import Figure
+
+    fig = Figure(800, 400)
+    ax = fig.add_axes(title=title, xlabel=xlabel, ylabel=ylabel)
+    if labels is None:
+        ax.line(x, y, marker=np.size(x) <= 200)
+    else:
+        for xi, yi, lab in zip(x, y, labels):
+            ax.line(xi, yi, label=lab)
+    return fig.save(out)
+
+
+def plot_histogram(values, xlabel: str, out: str, bins: int = 20, title: str = "") -> str:
+    from .plot import Figure
+
+    v = np.asarray(values, float)
+    v = v[np.isfinite(v)]
+    counts, edges = np.histogram(v, bins=bins) if v.size else (np.zeros(1), np.array([0.0, 1.0]))
+    fig = Figure(640, 400)
+    ax = fig.add_axes(title=title, xlabel=xlabel, ylabel="count")
+    centers = (edges[:-1] + edges[1:]) / 2
+    ax.bars([f"{c:.3g}" if i % max(1, bins // 5) == 0 else "" for i, c in enumerate(centers)], counts)
+    return fig.save(out)
+
+
+def plot_hpc(log_path: str, out_prefix: str = "hpc") -> list[str]:
+    """Ratio per step and the max-error histogram of an HPC bench log
+    (python/snippets/plot_hpc_logs.py:22-46)."""
+    steps, ratios, errs = parse_hpc_log(log_path)
+    return [plot_series(steps, ratios, "step", "compression ratio (raw/comp)", f"{out_prefix}_ratio.png",
+                        title="HPC compression ratio vs step"),
+            plot_histogram(errs, "max error per step", f"{out_prefix}_eps_hist.png",
+                           title="HPC max error distribution")]
+
+
+def plot_twin(client_csv: str, server_csv: str | None = None, out: str = "rotor_net_ratio.png") -> str:
+    """Client (and server) compression ratio per tick (python/snippets/plot_rotor_net.py:22-42)."""
+    t, r = load_tick_ratio_csv(client_csv)
+    xs, ys, labels = [t], [r], ["client ratio"]
+    if server_csv:
+        t2, r2 = load_tick_ratio_csv(server_csv)
+        xs.append(t2)
+        ys.append(r2)
+        labels.append("server ratio")
+    return plot_series(xs, ys, "tick", "compression ratio (raw/comp)", out, title="rotor twin network compression",
+                       labels=labels)
+
+
+def plot_entropy(out: str = "entropy_reduction.png", bins: int = 100) -> str:
+    """Histograms of a signal and of its EMA-prediction residual, the
+    reference's entropy illustration (python/snippets/entropy_plot.py:5-33)."""
+    from .plot import Figure
+
+    t = np.arange(100_000)
+    x = (np.sin(t * 0.01) + 0.1 * np.sin(t * 0.05) + 0.01 * np.random.default_rng(0).standard_normal(t.size)
+         ).astype(np.float32)
+    r = ema_residual(x)
+    fig = Figure(900, 640)
+    for vals, name in ((x, "signal"), (r, "EMA residual")):
+        counts, edges = np.histogram(vals, bins=bins)
+        ax = fig.add_axes(title=f"{name}: entropy {histogram_entropy(vals, bins):.2f} bits", xlabel="value",
+                          ylabel="count")
+        ax.line((edges[:-1] + edges[1:]) / 2, counts)
+    return fig.save(out)
 
 
 def plot_baselines(csv_path: str, out: str = "baseline_comparison.png") -> str:
-    """Ratio bars and throughput line per epsilon group, one panel each."""
-    plt = _plt()
+    """Ratio bars and throughput per tool, one panel per epsilon
+    (benchmarks/plot_baselines.py)."""
+    from .plot import Figure
+
     groups: dict = {}
     for r in load_baseline_rows(csv_path):
         groups.setdefault(r.get("epsilon") or "", []).append(r)
     if not groups:
         raise RuntimeError(f"no OK rows in {csv_path}")
-    fig, axes = plt.subplots(len(groups), 1, figsize=(9, 4 * len(groups)), squeeze=False)
-    for ax, (eps, rs) in zip(axes[:, 0], groups.items()):
-        x = range(len(rs))
-        ax.bar(x, [_float(r["ratio"]) for r in rs], color="tab:blue", alpha=0.7, label="ratio")
-        ax2 = ax.twinx()
-        ax2.plot(x, [_float(r["throughput_MBps"]) for r in rs], color="tab:orange", marker="o", label="throughput")
-        ax.set_xticks(list(x))
-        ax.set_xticklabels([r["tool"] for r in rs], rotation=20, ha="right")
-        ax.set_ylabel("ratio (raw/comp)")
-        ax2.set_ylabel("throughput (MB/s)")
-        ax.set_title(f"Baseline Comparison (epsilon={eps})" if eps else "Baseline Comparison")
-        ax.grid(True, axis="y", alpha=0.3)
-    fig.tight_layout()
-    fig.savefig(out)
-    plt.close(fig)
-    return out
+    fig = Figure(900, 400 * len(groups))
+    for eps, rs in groups.items():
+        ax = fig.add_axes(title=f"baseline comparison (epsilon={eps})" if eps else "baseline comparison",
+                          ylabel="ratio (raw/comp)")
+        ax.bars([r["tool"] for r in rs], [_float(r["ratio"]) for r in rs], color="tab:blue", label="ratio")
+        ax.twin(ylabel="throughput (MB/s)").line(range(len(rs)), [_float(r["throughput_MBps"]) for r in rs],
+                                                 color="tab:orange", marker=True, label="throughput")
+    return fig.save(out)

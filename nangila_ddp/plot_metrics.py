@@ -1,7 +1,7 @@
 """``nangila_ddp/plot_metrics.py``: compression ratio per hook call from a
 metrics CSV (both the key,value layout and the older ``step,`` prefix).
-Writes ``<csv>_ratio.png`` when matplotlib is installed, else prints the
-ratio summary."""
+Writes ``<csv>_ratio.png`` (drawn by ``utils.plot``) and prints the ratio
+summary."""
 import json
 import sys
 
@@ -17,15 +17,11 @@ def main(argv=None):
     if ratio.size == 0:
         print("No metrics found in", path)
         return None
-    try:
-        out = analysis.plot_series(np.arange(ratio.size), ratio, "hook call index", "compression ratio (raw/comp)",
-                                   path.replace(".csv", "_ratio.png"))
-        print("Saved plot:", out)
-        return out
-    except RuntimeError as e:  # matplotlib is optional
-        print(e)
-        print(json.dumps(analysis._stats(ratio)))
-        return None
+    out = analysis.plot_series(np.arange(ratio.size), ratio, "hook call index", "compression ratio (raw/comp)",
+                               path.replace(".csv", "_ratio.png"), title="DDP hook compression ratio")
+    print("Saved plot:", out)
+    print(json.dumps(analysis._stats(ratio)))
+    return out
 
 
 if __name__ == "__main__":

@@ -14,7 +14,7 @@ def test_module_paths():
     assert importlib.import_module("nangila_ddp.examples.minigpt_train").main is minigpt_train.main
 
 
-def test_plot_scripts_summarise_without_matplotlib(tmp_path, capsys):
+def test_plot_scripts_plot_and_summarise(tmp_path, capsys, monkeypatch):
     from nangila_ddp import plot_metrics, plot_train_and_compression
 
     m = tmp_path / "ddp_metrics.csv"
@@ -22,15 +22,12 @@ def test_plot_scripts_summarise_without_matplotlib(tmp_path, capsys):
                  "ts,101.5,hook_idx,2,bucket_elems,10,raw_bytes,40,comp_bytes,4,ratio,10.0,res_mean_abs,2e-3\n")
     t = tmp_path / "train_log.csv"
     t.write_text("ts,step,loss,lr,tokens_per_sec,step_ms\n100.0,1,4.2,0.0006,1000,10\n101.0,2,4.0,0.0006,1000,10\n")
-    plot_metrics.main([str(m)])
-    plot_train_and_compression.main([str(t), str(m)])
+    monkeypatch.chdir(tmp_path)
+    assert plot_metrics.main([str(m)]).endswith("_ratio.png")
+    assert plot_train_and_compression.main([str(t), str(m)]) == "train_and_compression.png"
     out = capsys.readouterr().out
-    try:
-        import matplotlib  # noqa: F401
-
-        assert "Saved" in out
-    except ImportError:
-        assert '"median": 9.0' in out and '"loss"' in out
+    assert "Saved" in out and '"median": 9.0' in out and '"loss"' in out
+    assert (tmp_path / "train_and_compression.png").read_bytes()[:8] == b"\x89PNG\r\n\x1a\n"
     empty = tmp_path / "empty.csv"
     empty.write_text("nothing here\n")
     assert plot_metrics.main([str(empty)]) is None
