@@ -11,7 +11,12 @@ choice) and top-k 1/5/10 %, and NCCL all_reduce of the fp32 and bf16 bucket.
 
 Reported per row: time per call, effective GB/s of uncompressed fp32 data
 reduced, compressed bytes each rank sends over NVLink, and the fraction of
-the roofline max(HBM bytes / measured HBM bandwidth, NVLink bytes / 770 GB/s).
+the roofline max(HBM bytes / measured HBM bandwidth, NVLink bytes / 900 GB/s
+per direction, the nominal NVLink 5 figure), with the fraction against the
+770 GB/s peer copy measured on these machines as a second column.  With
+``--nvlink`` every rank also reads its GPU's NVLink data counters (NVML,
+``utils.nvlink``) around the timed calls and the row carries the measured
+bytes sent and received per call (mean and max over ranks).
 """
 from __future__ import annotations
 
@@ -23,7 +28,8 @@ import os
 import torch
 import torch.distributed as dist
 
-NVLINK_GBS = 770.0  # measured peer copy per direction on this pool
+NVLINK_GBS = 900.0  # NVLink 5 per direction per GPU (nominal): the roofline
+NVLINK_MEASURED_GBS = 770.0  # peer copy per direction measured on these B200s
 
 
 def hbm_peak_gbs() -> float:
@@ -36,7 +42,8 @@ def hbm_peak_gbs() -> float:
         return 6650.0
 
 
-def roofline_ms(n: int, world: int, mode: str, variant: str, k: int) -> tuple[float, int]:
+def roofline_ms(n: int, world: int, mode: str, variant: str, k: int,
+                link_gbs: float = NVLINK_GBS) -> tuple[float, int]:
     from ..parallel.fused import dense_payload_bytes, payload_bytes
 
     P = payload_bytes(n, mode, k)
@@ -53,13 +60,14 @@ def roofline_ms(n: int, world: int, mode: str, variant: str, k: int) -> tuple[fl
     else:
         nvl = (world - 1) * P
         hbm = 24 * n + 2 * world * P
-    t = max(hbm / (hbm_peak_gbs() * 1e6), nvl / (NVLINK_GBS * 1e6))
+    t = max(hbm / (hbm_peak_gbs() * 1e6), nvl / (link_gbs * 1e6))
     return t, int(nvl)
 
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--sizes-mb", default="1,4,16,64,256,1024")
+    ap.add_argument("--sizes-mb", default="1,4,16,25,64,154,256,1024")
+    ap.add_argument("--nvlink", action="store_true", help="read NVLink data counters around the timed calls")
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--modes", default="int4,topk1,topk5,topk10")
@@ -75,6 +83,11 @@ def main():
     sizes = [int(float(s) * (1 << 20)) // 4 for s in args.sizes_mb.split(",")]
     comm = FusedAllReduce(max(sizes), device=dev, topk_k=topk_per_block(0.10), timeout_s=30.0,
                           max_ctas=args.max_ctas)
+    counter = None
+    if args.nvlink:
+        from ..utils.nvlink import NvlinkCounter
+
+        counter = NvlinkCounter(dev)
     rows = []
     g = torch.Generator(device=dev)
     for n in sizes:
@@ -96,6 +109,7 @@ def main():
             pred.zero_()
             ef.zero_()
             total = 0.0
+            link = [0, 0]
             for step in range(args.warmup + args.steps):
                 # AR(1): sig <- 0.9 sig + sqrt(1 - 0.81) * N(0, 1e-3^2)
                 sig.mul_(0.9).add_(torch.randn(n, device=dev, generator=g), alpha=math.sqrt(0.19) * 1e-3)
@@ -104,6 +118,9 @@ def main():
                 else:
                     buf.copy_(sig)
                 torch.cuda.synchronize(dev)
+                if counter is not None and step >= args.warmup:
+                    dist.barrier()  # the peers' traffic of the previous call has ended
+                    c0 = counter.read()
                 s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 s.record()
                 if mode == "nccl_fp32":
@@ -119,6 +136,11 @@ def main():
                 e.synchronize()
                 if step >= args.warmup:
                     total += s.elapsed_time(e)
+                    if counter is not None:
+                        dist.barrier()  # every peer's stores into this GPU have landed
+                        c1 = counter.read()
+                        link[0] += c1[0] - c0[0]
+                        link[1] += c1[1] - c0[1]
             ms = total / args.steps
             t = torch.tensor([ms], device=dev, dtype=torch.float64)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -127,9 +149,23 @@ def main():
                                     variant if world > 1 else "single", max(k, 1))
             if mode.startswith("nccl"):
                 roof, nvl = roofline_ms(n, world, "int4", variant, 1)
+            roof_meas, _ = roofline_ms(n, world, mode if mode in ("int4", "topk") else "int4",
+                                       variant if world > 1 else "single", max(k, 1), NVLINK_MEASURED_GBS)
+            if mode.startswith("nccl"):
+                roof_meas, _ = roofline_ms(n, world, "int4", variant, 1, NVLINK_MEASURED_GBS)
             row = dict(n_gpus=world, bucket_mb=n * 4 / (1 << 20), mode=mode if mode != "topk" else f"topk_k{k}",
                        variant=variant, ms=ms, eff_gbs=n * 4 / (ms * 1e6), nvlink_bytes_per_rank=nvl,
-                       roofline_ms=roof, roofline_frac=roof / ms if ms > 0 else None)
+                       roofline_ms=roof, roofline_frac=roof / ms if ms > 0 else None,
+                       roofline_frac_measured_link=roof_meas / ms if ms > 0 else None)
+            if counter is not None:
+                lt = torch.tensor([link[0] / args.steps, link[1] / args.steps], device=dev, dtype=torch.float64)
+                lmax = lt.clone()
+                dist.all_reduce(lt)
+                dist.all_reduce(lmax, op=dist.ReduceOp.MAX)
+                row.update(nvlink_counters=counter.available,
+                           nvlink_tx_bytes_measured_mean=float(lt[0]) / world,
+                           nvlink_rx_bytes_measured_mean=float(lt[1]) / world,
+                           nvlink_tx_bytes_measured_max=float(lmax[0]))
             rows.append(row)
             if rank == 0:
                 print(json.dumps(row), flush=True)

@@ -4,7 +4,9 @@
 
 Ops: fused_single (INT4, world 1), fused_oneshot (rank 0 of a 2-rank one-shot
 all-reduce with the peer's payload and flags pre-delivered into local memory,
-so the exchange kernel runs in full on one GPU), fused_topk_single,
+so the exchange kernel runs in full on one GPU), fused_twoshot (rank 0 of a
+--world-rank two-shot all-reduce: every peer's phase-A records, its INT8
+result records and both kinds of flags pre-delivered), fused_topk_single,
 fused_topk_oneshot, hpc_step, bs_encode, bsrle_encode, rle_encode,
 bs_decode, bsrle_decode, stochastic_encode, topk_encode, nz_encode_eb / nz_encode_bs /
 nz_encode_bsrle (whole-trajectory device .nz encode, --steps snapshots of
@@ -102,6 +104,63 @@ def _emulated_oneshot(n, mode, k):
     return setup, run, algo, status
 
 
+def _emulated_twoshot(n, world, l2_keep_mb):
+    """Rank 0 of a ``world``-rank two-shot launch.  Rank 0's region holds
+    every peer's payload (phase A reads the chunks rank 0 owns) and INT8
+    result records (phase C reads the chunks the peers own); the payload
+    and result flags of every peer are written before every call."""
+    from mini_nangila_b200 import _ext
+    from mini_nangila_b200.parallel.fused import MAX_COLS, MODES, VARIANTS, FusedAllReduce, make_layout
+
+    c = _ext.cuda()
+    dev = torch.device("cuda")
+    L = make_layout(world, n, 1, ("int4",))
+    regs = [torch.zeros(L.total, dtype=torch.uint8, device=dev) for _ in range(world)]
+    status = torch.zeros(4, dtype=torch.int32, device=dev)
+    comm = c.FusedComm(world, 0, [r.data_ptr() for r in regs], L.flags_off, L.inbox_off, L.slot_bytes,
+                       L.result_off, L.result_bytes, status)
+    comm.l2_keep_bytes = int(l2_keep_mb * (1 << 20))
+    mcode = MODES["int4"]
+    grid = c.fused_grid(n, mcode, False, VARIANTS["twoshot"], 0, 0)
+    tag = FusedAllReduce.tag_for(n, 0)
+    reg0 = regs[0]
+    peer = torch.randn(n, device=dev) * 1e-3
+    p1, _ = c.product_encode(peer, None, None, mcode, 1, True, 3, 1, 0, 0)
+    res, _ = c.product_encode(peer * 0.5, None, None, MODES["int8"], 1, False, 3, 1, 0, 0)
+    for par in (0, 1):
+        for src in range(1, world):
+            slot = L.inbox_off + (par * world + src) * L.slot_bytes
+            reg0[slot: slot + p1.numel()] = p1
+        r0 = L.result_off + par * L.result_bytes
+        reg0[r0: r0 + res.numel()] = res
+    g = torch.randn(n, device=dev) * 1e-3
+    pred = torch.randn(n, device=dev) * 1e-3
+    ef = torch.zeros(n, device=dev)
+    flags = reg0[L.flags_off:].view(torch.int64)
+    ftag = tag ^ ((grid * 0x9E3779B1) & 0xFFFFFFFF)
+
+    def setup():
+        epoch = comm.epoch + 1
+        par = epoch & 1
+        val = (ftag << 32) | epoch
+        if val >= 1 << 63:
+            val -= 1 << 64
+        for kind in (0, 1):
+            for src in range(1, world):
+                base = ((par * 2 + kind) * world + src) * MAX_COLS
+                flags[base: base + grid] = val
+
+    def run():
+        comm.run(g, pred, ef, mcode, 1, VARIANTS["twoshot"], True, 3, 0, 1, 0.9, False, 0, int(5e9), tag)
+
+    P, R = p1.numel(), res.numel()
+    # g, pred, ef read, ef written (16n); own records (P) written; the owned
+    # chunks' W records read (P); INT8 results written to every rank (R) and
+    # read back (R); pred read again and grad, pred written (12n)
+    algo = 28 * n + 2 * P + 2 * R
+    return setup, run, algo, status
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--op", required=True)
@@ -110,6 +169,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--k", type=int, default=13, help="top-k kept per 256-block")
     ap.add_argument("--steps", type=int, default=100, help="snapshots for the trajectory ops")
+    ap.add_argument("--world", type=int, default=8, help="emulated ranks of fused_twoshot")
+    ap.add_argument("--l2-keep-mb", type=float, default=48.0,
+                    help="fused_twoshot: predictor MB kept in L2 between phases (0: no L2 policy)")
     args = ap.parse_args()
     torch.cuda.set_device(0)
     from mini_nangila_b200 import _ext
@@ -130,6 +192,8 @@ def main():
     elif args.op in ("fused_oneshot", "fused_topk_oneshot"):
         mode = "topk" if "topk" in args.op else "int4"
         setup, run, algo, status = _emulated_oneshot(n, mode, args.k)
+    elif args.op == "fused_twoshot":
+        setup, run, algo, status = _emulated_twoshot(n, args.world, args.l2_keep_mb)
     elif args.op == "hpc_step":
         x = torch.rand(n, device=dev) * 100
         st = c.q823_from_f32(x)

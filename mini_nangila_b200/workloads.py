@@ -64,7 +64,9 @@ class ModeSwitchingAR1:
 class AllReduceSweep:
     """Compressed all-reduce of fp32 buckets whose contents evolve as AR(1)."""
 
-    sizes_mb: tuple = (1, 4, 16, 64, 256, 1024)
+    # 1 MB to 1 GB, plus the GPT-2 small bucket sizes (25 MB, and the 154 MB
+    # tied-embedding bucket)
+    sizes_mb: tuple = (1, 4, 16, 25, 64, 154, 256, 1024)
     steps: int = 20
     rho: float = 0.9
     sigma: float = 1e-3

@@ -117,55 +117,12 @@ def test_fused_single_rank_matches_oracle(mode, n, drop):
 
 
 def _two_rank_emulation(n, mode, k, bad_tag=False, deliver=True, timeout_s=0.2, drop=0.0):
-    """Run rank 0 of a 2-rank one-shot all-reduce on one GPU with rank 1's
-    payload and column flags pre-delivered into rank 0's region."""
-    from mini_nangila_b200.parallel.fused import MAX_COLS, MODES, VARIANTS, FusedAllReduce, make_layout, topology
+    """Rank 0 of a 2-rank one-shot all-reduce on one GPU, rank 1's payload
+    and column flags pre-delivered (parallel/emulate.py)."""
+    from mini_nangila_b200.parallel import emulate
 
-    topo = topology(n, drop, 3, 4)
-    tl = list(topo) if drop else []
-
-    h, c = _ext()
-    dev = torch.device("cuda")
-    L = make_layout(2, n, k)
-    reg0 = torch.zeros(L.total, dtype=torch.uint8, device=dev)
-    reg1 = torch.zeros(L.total, dtype=torch.uint8, device=dev)
-    status = torch.zeros(4, dtype=torch.int32, device=dev)
-    comm = c.FusedComm(2, 0, [reg0.data_ptr(), reg1.data_ptr()], L.flags_off, L.inbox_off, L.slot_bytes,
-                       L.result_off, L.result_bytes, status)
-    epoch = comm.epoch + 1
-    parity = epoch & 1
-    tag = FusedAllReduce.tag_for(n, 4)
-    g0, g1 = _data(n, 1), _data(n, 2)
-    bits = 8 if mode == "int8" else 4
-    mcode = MODES[mode]
-    grid = c.fused_grid(n, mcode, False, VARIANTS["oneshot"], 0, 0)
-    if deliver:
-        p1, _ = c.product_encode(torch.from_numpy(g1).to(dev), None, None, mcode, k, True, 99, 1, 4, 7, tl)
-        slot = L.inbox_off + (parity * 2 + 1) * L.slot_bytes
-        reg0[slot: slot + p1.numel()] = p1
-        flags = reg0[L.flags_off:].view(torch.int64)
-        ftag = (tag ^ ((grid * 0x9E3779B1) & 0xFFFFFFFF)) ^ (1 if bad_tag else 0)
-        val = (ftag << 32) | epoch
-        if val >= 1 << 63:
-            val -= 1 << 64
-        base = ((parity * 2 + 0) * 2 + 1) * MAX_COLS  # kind payload, src 1
-        flags[base: base + grid] = val
-    torch.cuda.synchronize()
-    gd = torch.from_numpy(g0).to(dev)
-    comm.run(gd, None, None, mcode, k, VARIANTS["oneshot"], True, 99, 4, 7, 0.9, True, 0, int(timeout_s * 1e9), tag,
-             tl)
-    torch.cuda.synchronize()
-    st = status.cpu().tolist()
-    inv = float(np.float32(0.5))
-    if mode == "topk":
-        r0, _ = h.product_topk_encode(g0, None, None, k, False, topo)
-        r1, _ = h.product_topk_encode(g1, None, None, k, False, topo)
-        ref = h.product_topk_reduce([r0, r1], n, k, None, inv)
-    else:
-        w0, _ = h.product_encode(g0, None, None, bits, True, False, 99, 0, 4, 7, topo)
-        w1, _ = h.product_encode(g1, None, None, bits, True, False, 99, 1, 4, 7, topo)
-        ref = h.product_reduce([w0, w1], n, bits, None, inv)
-    return st, gd.cpu().numpy(), ref
+    r = emulate.oneshot(n, mode, k, drop=drop, bad_tag=bad_tag, deliver=deliver, timeout_s=timeout_s)
+    return r["status"], r["avg"], r["ref_avg"]
 
 
 @pytest.mark.parametrize("mode", ["int4", "int8", "topk"])
@@ -204,69 +161,13 @@ def test_prefetch_pipeline_copies_every_chunk(n, grid, vec):
 
 
 def _twoshot_emulation(n, mode, world, drop=0.0, grid_cap=0):
-    """Rank 0 of a ``world``-rank two-shot all-reduce on one GPU.
+    """Rank 0 of a ``world``-rank two-shot all-reduce on one GPU: ranks
+    world-1 .. 1 run first with everything they wait for pre-delivered, and
+    their stores fill rank 0's region (parallel/emulate.py)."""
+    from mini_nangila_b200.parallel import emulate
 
-    Every rank's region is a local buffer.  Ranks world-1 .. 1 run first,
-    each with every other rank's phase-A payload and every payload and
-    result flag pre-delivered into its own region, so none of them waits on
-    anything unset; their phase-A records, phase-B INT8 results and flags
-    land in rank 0's region through the same stores as over NVLink.  Rank 0
-    runs last, with everything delivered, and its average, predictor and
-    error feedback are compared with the host two-shot oracle."""
-    from mini_nangila_b200.parallel.fused import MAX_COLS, MODES, VARIANTS, FusedAllReduce, make_layout, topology
-
-    h, c = _ext()
-    dev = torch.device("cuda")
-    k = 13
-    topo = topology(n, drop, 5, 6)
-    tl = list(topo) if drop else []
-    L = make_layout(world, n, k, modes=(mode,))
-    regs = [torch.zeros(L.total, dtype=torch.uint8, device=dev) for _ in range(world)]
-    ptrs = [r.data_ptr() for r in regs]
-    bits = 8 if mode == "int8" else 4
-    mcode = MODES[mode]
-    tag = FusedAllReduce.tag_for(n, 6)
-    grid = c.fused_grid(n, mcode, False, VARIANTS["twoshot"], grid_cap, 0)
-    epoch, parity = 1, 1
-    ftag = (tag ^ ((grid * 0x9E3779B1) & 0xFFFFFFFF)) & 0xFFFFFFFF
-    val = (ftag << 32) | epoch
-    if val >= 1 << 63:
-        val -= 1 << 64
-    pred = _data(n, 40)
-    efs = [_data(n, 50 + r, 1e-4) for r in range(world)]
-    gs = [_data(n, 60 + r) for r in range(world)]
-    seed, bucket, step = 21, 6, 3
-    payloads = [c.product_encode(torch.from_numpy(gs[r]).to(dev), torch.from_numpy(pred).to(dev),
-                                 torch.from_numpy(efs[r]).to(dev), mcode, k, True, seed, r, bucket, step, tl)[0]
-                for r in range(world)]
-    outs = {}
-    for r in list(range(world - 1, 0, -1)) + [0]:
-        if r != 0:
-            reg = regs[r]
-            flags = reg[L.flags_off:].view(torch.int64)
-            for src in range(world):
-                if src == r:
-                    continue
-                slot = L.inbox_off + (parity * world + src) * L.slot_bytes
-                reg[slot: slot + payloads[src].numel()] = payloads[src]
-                for kind in (0, 1):
-                    base = ((parity * 2 + kind) * world + src) * MAX_COLS
-                    flags[base: base + grid] = val
-        status = torch.zeros(4, dtype=torch.int32, device=dev)
-        comm = c.FusedComm(world, r, ptrs, L.flags_off, L.inbox_off, L.slot_bytes, L.result_off, L.result_bytes,
-                           status)
-        gd = torch.from_numpy(gs[r].copy()).to(dev)
-        pd = torch.from_numpy(pred.copy()).to(dev)
-        ed = torch.from_numpy(efs[r].copy()).to(dev)
-        torch.cuda.synchronize()
-        comm.run(gd, pd, ed, mcode, k, VARIANTS["twoshot"], True, seed, bucket, step, 0.9, False, grid_cap,
-                 int(2e9), tag, tl)
-        torch.cuda.synchronize()
-        outs[r] = (status.cpu().tolist(), gd.cpu().numpy(), pd.cpu().numpy(), ed.cpu().numpy())
-    inv = float(np.float32(1.0) / np.float32(world))
-    encs = [h.product_encode(gs[r], pred, efs[r], bits, True, True, seed, r, bucket, step, topo) for r in range(world)]
-    avg = h.product_reduce_twoshot([e[0] for e in encs], n, bits, pred, inv)
-    return outs[0], avg, h.product_ema(pred, avg, 0.9, False), encs[0][1]
+    r = emulate.twoshot(n, mode, world, drop, grid_cap)
+    return (r["status"], r["avg"], r["pred"], r["ef"]), r["ref_avg"], r["ref_pred"], r["ref_ef"]
 
 
 @pytest.mark.parametrize("mode", ["int4", "int8"])
