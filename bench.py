@@ -125,7 +125,8 @@ def build_hf_model(args, device, tiny: bool = False):
             dict(vocab_size=50257, n_positions=1024, n_embd=768, n_layer=12, n_head=12, n_inner=3072)
         cfg = GPT2Config(**dims, resid_pdrop=0.0, embd_pdrop=0.0, attn_pdrop=0.0, initializer_range=0.02)
         cfg._attn_implementation = "sdpa"
-        model = _HFLoss(GPT2LMHeadModel(cfg)).to(device)
+        with torch.device(device):  # initialised on the device: every rank builds its copy in parallel
+            model = _HFLoss(GPT2LMHeadModel(cfg))
         autocast = True
     else:
         from transformers import LlamaConfig as HFLlamaConfig  # noqa: E402
@@ -140,7 +141,8 @@ def build_hf_model(args, device, tiny: bool = False):
                             rms_norm_eps=c.eps, rope_theta=c.rope_theta, initializer_range=c.init_std,
                             tie_word_embeddings=False)
         cfg._attn_implementation = "sdpa"
-        model = _HFLoss(LlamaForCausalLM(cfg)).to(device=device, dtype=torch.bfloat16)
+        with torch.device(device):
+            model = _HFLoss(LlamaForCausalLM(cfg)).to(dtype=torch.bfloat16)
         autocast = False
     return model, autocast
 
@@ -233,7 +235,8 @@ def comparison_arms(args, device, world: int, mb: int, seq: int, batches, mcfg) 
     out = {}
     tokens = world * mb * seq * args.steps
     # plain NCCL fp32: same model class, optimizer and DDP settings as the product arm
-    model = GPT2(mcfg) if args.model == "gpt2" else Llama(mcfg).to(torch.bfloat16)
+    with torch.device(device):
+        model = GPT2(mcfg) if args.model == "gpt2" else Llama(mcfg).to(torch.bfloat16)
     tr = DDPTrainer(model, lr=6e-4, hook="nccl", bucket_cap_mb=25.0,
                     autocast_dtype=torch.bfloat16 if args.model == "gpt2" else None, device=device)
     ms = time_steps(tr.step, batches, args.warmup, args.steps, device)
@@ -297,7 +300,8 @@ def main():
             dist.destroy_process_group()
             return
     else:
-        model = GPT2(mcfg) if args.model == "gpt2" else Llama(mcfg)
+        with torch.device(device):  # initialised on the device (fast for the 1.1B model)
+            model = GPT2(mcfg) if args.model == "gpt2" else Llama(mcfg)
         if args.model == "llama":
             model = model.to(torch.bfloat16)
         hk = None
