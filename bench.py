@@ -71,6 +71,8 @@ def parse():
                     help="EMA predictor in the hook (auto: on for int4/int8, off for top-k, which uses error feedback)")
     ap.add_argument("--overlap-opt", choices=["on", "off"], default="on",
                     help="fused hook: apply AdamW per bucket from the hook, overlapping backward")
+    ap.add_argument("--opt-in-kernel", choices=["on", "off"], default="on",
+                    help="with --overlap-opt: AdamW inside the exchange kernel (fp32 parameters)")
     ap.add_argument("--inflight-ctas", type=int, default=0,
                     help="grid cap of exchange kernels that overlap backward (0: the whole grid)")
     ap.add_argument("--stream-priority", type=int, default=-1, help="hook stream priority (-1 high, 0 normal)")
@@ -316,7 +318,7 @@ def main():
         overlap = args.hook == "fused" and args.overlap_opt == "on"
         trainer = DDPTrainer(model, lr=6e-4, hook=args.hook, hook_kwargs=hk, bucket_cap_mb=25.0,
                              autocast_dtype=torch.bfloat16 if args.model == "gpt2" else None, device=device,
-                             overlap_optimizer=overlap)
+                             overlap_optimizer=overlap, optimizer_in_kernel=args.opt_in_kernel == "on")
         step_fn = trainer.step
         hook_name = {"fused": f"fused-{args.mode}", "nccl": "nccl-fp32-allreduce", "compat": f"compat-{args.mode}"}[args.hook]
         if args.hook != "nccl":
@@ -453,6 +455,8 @@ def main():
                 out["config"]["twoshot_from_mb"] = None if twoshot_from >= (1 << 60) else twoshot_from / 2 ** 20
         if trainer is not None or arms is not None:
             out["config"]["optimizer_overlap"] = bool(args.hook == "fused" and args.overlap_opt == "on")
+            out["config"]["optimizer_in_kernel"] = bool(out["config"]["optimizer_overlap"]
+                                                        and args.opt_in_kernel == "on" and args.model == "gpt2")
         if clocks is not None:
             out["clocks"] = clocks
         if e2e is not None:

@@ -41,6 +41,25 @@ struct QParams {
   // the L2 evict_last policy, so phase 2's re-read hits L2 (0: no policy).
   float pred_keep;
 };
+// One fp32 parameter of a bucket for the optimizer fused into the decode
+// phase: its gradient occupies bucket elements [off, off + numel).
+struct OptSeg {
+  int64_t off;
+  int64_t numel;
+  float* p;
+  float* m;  // first moment
+  float* v;  // second moment
+};
+// AdamW with decoupled weight decay (Loshchilov & Hutter), applied to every
+// averaged gradient element as it is written: segs == nullptr turns it off.
+// Host-computed per step: decay = 1 - lr * weight_decay, step_size =
+// lr / (1 - beta1^t), inv_bc2_sqrt = 1 / sqrt(1 - beta2^t).
+struct OptParams {
+  const OptSeg* segs;  // device array sorted by off
+  int nsegs;
+  int64_t base;        // bucket element of this launch's element 0 (segmented buckets)
+  float beta1, beta2, eps, decay, step_size, inv_bc2_sqrt;
+};
 struct FParams {
   float inv_world;
   float beta;
@@ -49,6 +68,7 @@ struct FParams {
   int use_pred;
   Topo topo;
   int pred_stream;  // phase 2 reads the predictor with the evict_first policy
+  OptParams opt;
 };
 
 // Symmetric region of every rank (same layout on all ranks):
@@ -91,7 +111,8 @@ enum Variant : int { kVariantSingle = 0, kVariantOneShot = 1, kVariantTwoShot = 
 
 // Grid used for a launch: a pure function of (nchunks, mode, dtype, variant,
 // cap) on a given GPU model, so every rank launches the same grid.
-int fused_grid(int nchunks, int mode, int dtype, int variant, int cap, int device);
+// opt: the instance that applies the fused optimizer (its occupancy differs).
+int fused_grid(int nchunks, int mode, int dtype, int variant, int cap, int device, int opt = 0);
 cudaError_t launch_fused(const FusedParams& P, int mode, int dtype, int variant, int grid, cudaStream_t stream);
 cudaError_t launch_encode(const void* g, const float* pred, const float* ef_in, float* ef_out, int64_t n, int k,
                           const QParams& qp, uint8_t* out, int mode, int dtype, int grid, cudaStream_t stream);

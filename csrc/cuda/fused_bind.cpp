@@ -83,9 +83,14 @@ class FusedComm {
 
   // Launch the fused kernel on the current stream; returns the epoch used.
   // variant: 0 = auto-single (world 1), 1 = one-shot, 2 = two-shot.
+  // opt_segs: optional uint8 CUDA tensor holding opt_nsegs OptSeg records
+  // (the fused AdamW of the decode phase); opt_hyper = (beta1, beta2, eps,
+  // decay, step_size, inv_bc2_sqrt); opt_base = bucket element of grad[0].
   int64_t run(torch::Tensor grad, c10::optional<torch::Tensor> pred, c10::optional<torch::Tensor> ef, int64_t mode,
               int64_t k, int64_t variant, bool stochastic, int64_t seed, int64_t bucket, int64_t step, double beta,
-              bool first, int64_t max_ctas, int64_t timeout_ns, int64_t tag, std::vector<int64_t> topo) {
+              bool first, int64_t max_ctas, int64_t timeout_ns, int64_t tag, std::vector<int64_t> topo,
+              c10::optional<torch::Tensor> opt_segs, int64_t opt_nsegs, int64_t opt_base,
+              std::vector<double> opt_hyper) {
     check_dev(grad, "bucket");
     const int64_t n = grad.numel();
     FusedParams P = base_;
@@ -145,12 +150,32 @@ class FusedComm {
     if (variant != kVariantSingle && P.pred != nullptr && l2_keep_bytes_ > 0 && n > 0)
       P.q.pred_keep = (float)std::min(1.0, (double)l2_keep_bytes_ / (4.0 * (double)n));
     P.f.pred_stream = P.q.pred_keep > 0.0f ? 1 : 0;
+    std::memset(&P.f.opt, 0, sizeof(P.f.opt));
+    if (opt_segs.has_value()) {
+      TORCH_CHECK(opt_segs->is_cuda() && opt_segs->scalar_type() == torch::kUInt8 && opt_segs->is_contiguous(),
+                  "optimizer segments must be a contiguous uint8 CUDA tensor");
+      TORCH_CHECK(opt_nsegs >= 1 && opt_segs->numel() == opt_nsegs * (int64_t)sizeof(OptSeg),
+                  "optimizer segment table size mismatch");
+      TORCH_CHECK(opt_hyper.size() == 6, "optimizer scalars must be (beta1, beta2, eps, decay, step_size, "
+                                         "inv_bc2_sqrt)");
+      TORCH_CHECK(grad.scalar_type() == torch::kFloat32, "the fused optimizer needs an fp32 bucket");
+      P.f.opt.segs = reinterpret_cast<const OptSeg*>(opt_segs->data_ptr());
+      P.f.opt.nsegs = (int)opt_nsegs;
+      P.f.opt.base = opt_base;
+      P.f.opt.beta1 = (float)opt_hyper[0];
+      P.f.opt.beta2 = (float)opt_hyper[1];
+      P.f.opt.eps = (float)opt_hyper[2];
+      P.f.opt.decay = (float)opt_hyper[3];
+      P.f.opt.step_size = (float)opt_hyper[4];
+      P.f.opt.inv_bc2_sqrt = (float)opt_hyper[5];
+    }
     P.timeout_ns = (uint64_t)timeout_ns;
     if (P.nblk == 0) return epoch_;
     const c10::cuda::CUDAGuard guard(grad.device());
     cudaStream_t stream = at::cuda::getCurrentCUDAStream();
     const int dev = grad.get_device();
-    const int grid = fused_grid(P.nchunks, (int)mode, dtype_code(grad.scalar_type()), (int)variant, (int)max_ctas, dev);
+    const int grid = fused_grid(P.nchunks, (int)mode, dtype_code(grad.scalar_type()), (int)variant, (int)max_ctas, dev,
+                                P.f.opt.segs != nullptr ? 1 : 0);
     check_launch(launch_fused(P, (int)mode, dtype_code(grad.scalar_type()), (int)variant, grid, stream), "fused");
     return epoch_;
   }
@@ -229,6 +254,7 @@ torch::Tensor product_reduce_cuda(std::vector<torch::Tensor> payloads, int64_t n
   fp.use_pred = pred.has_value();
   fp.topo = topo_of(topo, nchunks_of(n));
   fp.pred_stream = 0;
+  std::memset(&fp.opt, 0, sizeof(fp.opt));
   if (pred.has_value()) check_dev(*pred, "pred");
   const c10::cuda::CUDAGuard guard(payloads[0].device());
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
@@ -250,7 +276,9 @@ void register_fused(pybind11::module& m) {
            pybind11::arg("mode"), pybind11::arg("k"), pybind11::arg("variant"), pybind11::arg("stochastic"),
            pybind11::arg("seed"), pybind11::arg("bucket"), pybind11::arg("step"), pybind11::arg("beta"),
            pybind11::arg("first"), pybind11::arg("max_ctas"), pybind11::arg("timeout_ns"), pybind11::arg("tag"),
-           pybind11::arg("topo") = std::vector<int64_t>{})
+           pybind11::arg("topo") = std::vector<int64_t>{},
+           pybind11::arg("opt_segs") = c10::optional<torch::Tensor>(), pybind11::arg("opt_nsegs") = 0,
+           pybind11::arg("opt_base") = 0, pybind11::arg("opt_hyper") = std::vector<double>{})
       .def_property("epoch", &FusedComm::epoch, &FusedComm::set_epoch)
       .def_property("l2_keep_bytes", &FusedComm::l2_keep_bytes, &FusedComm::set_l2_keep_bytes);
   m.def("product_encode", &product_encode_cuda, pybind11::arg("g"), pybind11::arg("pred"), pybind11::arg("ef"),
@@ -261,6 +289,7 @@ void register_fused(pybind11::module& m) {
         pybind11::arg("k"), pybind11::arg("pred"), pybind11::arg("beta"), pybind11::arg("first"),
         pybind11::arg("inv_world"), pybind11::arg("out_dtype"), pybind11::arg("topo") = std::vector<int64_t>{});
   m.def("payload_bytes", &payload_bytes);
+  m.def("opt_seg_bytes", []() { return (int64_t)sizeof(OptSeg); });
   m.def("pipe_copy", [](torch::Tensor src, int64_t grid, torch::Tensor status, bool vec) {
     check_dev(src, "src");
     TORCH_CHECK(src.scalar_type() == torch::kFloat32, "src must be float32");
@@ -271,8 +300,9 @@ void register_fused(pybind11::module& m) {
                  "pipe_copy");
     return dst;
   });
-  m.def("fused_grid", [](int64_t n, int64_t mode, bool bf16, int64_t variant, int64_t cap, int64_t device) {
+  m.def("fused_grid", [](int64_t n, int64_t mode, bool bf16, int64_t variant, int64_t cap, int64_t device, bool opt) {
     const int nchunks = (int)nchunks_of(n);
-    return fused_grid(nchunks, (int)mode, bf16 ? kBF16 : kF32, (int)variant, (int)cap, (int)device);
-  });
+    return fused_grid(nchunks, (int)mode, bf16 ? kBF16 : kF32, (int)variant, (int)cap, (int)device, opt ? 1 : 0);
+  }, pybind11::arg("n"), pybind11::arg("mode"), pybind11::arg("bf16"), pybind11::arg("variant"), pybind11::arg("cap"),
+     pybind11::arg("device"), pybind11::arg("opt") = false);
 }

@@ -252,8 +252,67 @@ __device__ __forceinline__ void accum_dense(const uint8_t* rec, int warp, int la
   }
 }
 
-// avg = pred + acc / W -> bucket; EMA update of the predictor state.
-template <typename T, bool kL2Policy = true>
+// ------------------------------------------------------ fused optimizer
+// One AdamW step of parameter element x with gradient g (decoupled weight
+// decay, bias-corrected moments; see OptParams).
+__device__ __forceinline__ void adamw1(const OptParams& o, float g, float& x, float& m, float& v) {
+  x = x * o.decay;
+  m = o.beta1 * m + (1.0f - o.beta1) * g;
+  v = o.beta2 * v + (1.0f - o.beta2) * (g * g);
+  const float denom = sqrtf(v) * o.inv_bc2_sqrt + o.eps;
+  x = x - o.step_size * (m / denom);
+}
+
+// Index of the segment holding bucket element e (the last with off <= e).
+__device__ __forceinline__ int opt_seg(const OptParams& o, int64_t e) {
+  int lo = 0, hi = o.nsegs - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (__ldg(&o.segs[mid].off) <= e) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
+}
+
+// AdamW on the lane's 8 averaged gradients (elements e0 .. e0 + valid - 1 of
+// this launch).  Whole vectors when the 8 lie in one parameter at a 16-byte
+// boundary (every GPT-2 / Llama parameter has a multiple of 8 elements);
+// element by element otherwise.  Elements outside every segment are skipped.
+__device__ __forceinline__ void adamw8(const OptParams& o, int64_t e0, int valid, const float (&g)[8]) {
+  const int64_t b0 = o.base + e0;
+  const int si = opt_seg(o, b0);
+  const OptSeg s = o.segs[si];
+  const int64_t rel = b0 - s.off;
+  if (valid == 8 && rel >= 0 && rel + 8 <= s.numel && (rel & 7) == 0 &&
+      ((reinterpret_cast<uintptr_t>(s.p) | reinterpret_cast<uintptr_t>(s.m) | reinterpret_cast<uintptr_t>(s.v)) &
+       15u) == 0) {
+    float x[8], m[8], v[8];
+    load8<float>(s.p, rel, 8, true, x);
+    load8<float>(s.m, rel, 8, true, m);
+    load8<float>(s.v, rel, 8, true, v);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) adamw1(o, g[j], x[j], m[j], v[j]);
+    store8<float>(s.p, rel, 8, true, x);
+    store8<float>(s.m, rel, 8, true, m);
+    store8<float>(s.v, rel, 8, true, v);
+    return;
+  }
+  for (int j = 0; j < valid; ++j) {
+    const int sj = opt_seg(o, b0 + j);
+    const OptSeg t = o.segs[sj];
+    const int64_t r = b0 + j - t.off;
+    if (r < 0 || r >= t.numel) continue;
+    float x = t.p[r], m = t.m[r], v = t.v[r];
+    adamw1(o, g[j], x, m, v);
+    t.p[r] = x;
+    t.m[r] = m;
+    t.v[r] = v;
+  }
+}
+
+// avg = pred + acc / W -> bucket; EMA update of the predictor state; with
+// kOpt, AdamW on the bucket's parameters from the averaged gradient.
+template <typename T, bool kL2Policy = true, bool kOpt = false>
 __device__ __forceinline__ void finalize(T* grad, float* pred, int64_t n, int blk, int lane, const float (&acc)[8],
                                          const FParams& fp) {
   const int64_t e0 = (int64_t)blk * kBlock + lane * 8;
@@ -270,6 +329,7 @@ __device__ __forceinline__ void finalize(T* grad, float* pred, int64_t n, int bl
     avg[j] = product_average(p[j], acc[j], fp.inv_world);
   }
   store8<T>(grad, e0, valid, true, avg);
+  if constexpr (kOpt) adamw8(fp.opt, e0, valid, avg);
   if (fp.use_pred) {
 #pragma unroll
     for (int j = 0; j < 8; ++j) p[j] = product_ema(p[j], avg[j], fp.beta, fp.omb, fp.first != 0);
@@ -470,7 +530,7 @@ __device__ __forceinline__ void copy_record(uint8_t* dst, const uint8_t* rec, in
 }
 
 // Decode chunk c: accumulate the W records in rank order, finalize.
-template <int MODE, typename T, typename RecOf>
+template <int MODE, typename T, bool kOpt, typename RecOf>
 __device__ __forceinline__ void decode_chunk(const RecOf& rec_of, int world, T* grad, float* pred, int64_t n, int nblk,
                                              int nchunks, int k, int rec_bytes, const FParams& fp, int c,
                                              uint8_t* stage_smem, float* acc_smem) {
@@ -498,7 +558,7 @@ __device__ __forceinline__ void decode_chunk(const RecOf& rec_of, int world, T* 
     constexpr int BITS = MODE == kInt4 ? 4 : 8;
     for (int src = 0; src < world; ++src) accum_dense<BITS>(rec_of(src), warp, lane, acc);
   }
-  finalize<T, MODE != kTopK>(grad, pred, n, blk, lane, acc, fp);
+  finalize<T, MODE != kTopK, kOpt>(grad, pred, n, blk, lane, acc, fp);
 }
 
 // ---------------------------------------------------------- flag addressing
@@ -597,7 +657,7 @@ __device__ __forceinline__ void encode_owned(const FusedParams& P, uint8_t* rec,
   }
 }
 
-template <int MODE, typename T>
+template <int MODE, typename T, bool kOpt>
 __global__ void __launch_bounds__(kThreads) oneshot_kernel(FusedParams P) {
   __shared__ int s_abort;
   __shared__ __align__(16) uint8_t rec[Smem<MODE>::kRec];
@@ -625,12 +685,12 @@ __global__ void __launch_bounds__(kThreads) oneshot_kernel(FusedParams P) {
   auto rec_of = [&](int src) { return slot_rec(P, P.rank, src, 0); };
   for (int c = blockIdx.x; c < P.nchunks; c += gridDim.x) {
     auto rc = [&](int src) { return rec_of(src) + (int64_t)c * P.chunk_bytes; };
-    decode_chunk<MODE, T>(rc, P.world, reinterpret_cast<T*>(P.grad), P.pred, P.n, P.nblk, P.nchunks, P.k,
+    decode_chunk<MODE, T, kOpt>(rc, P.world, reinterpret_cast<T*>(P.grad), P.pred, P.n, P.nblk, P.nchunks, P.k,
                           P.rec_bytes, P.f, c, stage, acc_smem);
   }
 }
 
-template <int MODE, typename T>
+template <int MODE, typename T, bool kOpt>
 __global__ void __launch_bounds__(kThreads) twoshot_kernel(FusedParams P) {
   constexpr int BITS = MODE == kInt4 ? 4 : 8;
   __shared__ int s_abort;
@@ -691,12 +751,12 @@ __global__ void __launch_bounds__(kThreads) twoshot_kernel(FusedParams P) {
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
     if (!passenger(P.f.topo, c, P.nchunks)) accum_dense<8>(result_rec(P, P.rank, c), warp, lane, acc);
-    finalize<T>(reinterpret_cast<T*>(P.grad), P.pred, P.n, blk, lane, acc, f);
+    finalize<T, true, kOpt>(reinterpret_cast<T*>(P.grad), P.pred, P.n, blk, lane, acc, f);
   }
 }
 
 // One chunk of the single-rank kernel: encode + decode in registers.
-template <int MODE, typename T>
+template <int MODE, typename T, bool kOpt>
 __device__ __forceinline__ void single_chunk(const FusedParams& P, const ChunkSrc<T>& in, int ch, uint8_t* rec_smem) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int blk = ch * kChunkBlocks + warp;
@@ -719,7 +779,7 @@ __device__ __forceinline__ void single_chunk(const FusedParams& P, const ChunkSr
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[j] = product_accum(0.0f, q[j], s);
   }
-  finalize<T>(reinterpret_cast<T*>(P.grad), P.pred, P.n, blk, lane, acc, P.f);
+  finalize<T, false, kOpt>(reinterpret_cast<T*>(P.grad), P.pred, P.n, blk, lane, acc, P.f);
 }
 
 // Single rank: encode + decode in registers (no exchange); inputs of whole
@@ -733,7 +793,7 @@ inline constexpr bool kPrefetch = !kExchange && MODE != kTopK;
 // Top-k: 64 registers without spills, four CTAs per SM (0.42 ms at 64M
 // elements against 0.46 ms at 76 registers and three).  The one-shot top-k
 // kernel spills at 64 and is no faster, so it keeps the default bound.
-template <int MODE, typename T>
+template <int MODE, typename T, bool kOpt>
 __global__ void __launch_bounds__(kThreads, MODE == kTopK ? 4 : 1) single_kernel(FusedParams P) {
   __shared__ __align__(16) uint8_t rec_smem[MODE == kTopK ? kWarps * kTopkMaxRec : 16];
   __shared__ __align__(8) uint64_t mbar[2];
@@ -743,7 +803,7 @@ __global__ void __launch_bounds__(kThreads, MODE == kTopK ? 4 : 1) single_kernel
   const float* pp = P.q.use_pred ? P.pred : nullptr;
   const float* pe = P.q.use_ef ? P.ef : nullptr;
   if constexpr (!kPrefetch<MODE, false>) {
-    for (int ch = blockIdx.x; ch < P.nchunks; ch += gridDim.x) single_chunk<MODE, T>(P, gsrc, ch, rec_smem);
+    for (int ch = blockIdx.x; ch < P.nchunks; ch += gridDim.x) single_chunk<MODE, T, kOpt>(P, gsrc, ch, rec_smem);
     return;
   }
   ChunkPipe<T> pipe{mbar, dsm};
@@ -761,9 +821,9 @@ __global__ void __launch_bounds__(kThreads, MODE == kTopK ? 4 : 1) single_kernel
         pipe.drain(P.timeout_ns);
         return;
       }
-      single_chunk<MODE, T>(P, pipe.buffer_source(b, ch), ch, rec_smem);
+      single_chunk<MODE, T, kOpt>(P, pipe.buffer_source(b, ch), ch, rec_smem);
     } else {
-      single_chunk<MODE, T>(P, gsrc, ch, rec_smem);
+      single_chunk<MODE, T, kOpt>(P, gsrc, ch, rec_smem);
     }
     __syncthreads();  // buffer b is reused two iterations on
   }
@@ -802,7 +862,7 @@ __global__ void __launch_bounds__(kThreads) reduce_kernel(ReduceSrcs srcs, int w
   __shared__ __align__(16) float acc_smem[Smem<MODE>::kAcc];
   for (int c = blockIdx.x; c < nchunks; c += gridDim.x) {
     auto rc = [&](int src) { return srcs.p[src] + (int64_t)c * chunk_bytes; };
-    decode_chunk<MODE, T>(rc, world, out, pred, n, nblk, nchunks, k, rec_bytes, fp, c, stage, acc_smem);
+    decode_chunk<MODE, T, false>(rc, world, out, pred, n, nblk, nchunks, k, rec_bytes, fp, c, stage, acc_smem);
   }
 }
 
@@ -888,37 +948,53 @@ constexpr int dsmem_of() {
   return kPrefetch<M, kExchange> ? ChunkPipe<T>::kBytes : 0;
 }
 
-// Two-shot exists for the dense modes only; these wrappers keep the top-k
-// instance from being referenced (discarded branches inside a template).
-template <int M, typename T>
-int twoshot_occupancy() {
+// Kernel instances.  Two-shot exists for the dense modes only, and the
+// fused optimizer for fp32 dense buckets only; these helpers keep the other
+// instances from being referenced (discarded branches inside a template).
+template <int M, typename T, bool kOpt>
+constexpr bool kHasOpt = !kOpt || (M != kTopK && sizeof(T) == 4);
+
+template <int M, typename T, bool kOpt>
+int occupancy_of(int variant) {
   int v = 1;
-  if constexpr (M != kTopK)
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, twoshot_kernel<M, T>, kThreads, dsmem_of<M, T, true>());
+  if constexpr (kHasOpt<M, T, kOpt>) {
+    if (variant == kVariantTwoShot) {
+      if constexpr (M != kTopK)
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, twoshot_kernel<M, T, kOpt>, kThreads, dsmem_of<M, T, true>());
+    } else if (variant == kVariantOneShot) {
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, oneshot_kernel<M, T, kOpt>, kThreads, dsmem_of<M, T, true>());
+    } else {
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+          &v, single_kernel<M, T, kOpt>, kThreads,
+          prepare_dsmem<single_kernel<M, T, kOpt>>(dsmem_of<M, T, false>()));
+    }
+  }
   return v;
 }
-template <int M, typename T>
-void twoshot_launch(const FusedParams& P, int grid, cudaStream_t stream) {
-  if constexpr (M != kTopK) twoshot_kernel<M, T><<<grid, kThreads, dsmem_of<M, T, true>(), stream>>>(P);
+
+template <int M, typename T, bool kOpt>
+void launch_instance(const FusedParams& P, int variant, int grid, cudaStream_t stream) {
+  if constexpr (kHasOpt<M, T, kOpt>) {
+    if (variant == kVariantSingle) {
+      const int dyn = prepare_dsmem<single_kernel<M, T, kOpt>>(dsmem_of<M, T, false>());
+      single_kernel<M, T, kOpt><<<grid, kThreads, dyn, stream>>>(P);
+    } else if (variant == kVariantTwoShot) {
+      if constexpr (M != kTopK) twoshot_kernel<M, T, kOpt><<<grid, kThreads, dsmem_of<M, T, true>(), stream>>>(P);
+    } else {
+      oneshot_kernel<M, T, kOpt><<<grid, kThreads, dsmem_of<M, T, true>(), stream>>>(P);
+    }
+  }
 }
 
-int fused_grid(int nchunks, int mode, int dtype, int variant, int cap, int device) {
-  static int occ_cache[3][2][3] = {};
+int fused_grid(int nchunks, int mode, int dtype, int variant, int cap, int device, int opt) {
+  static int occ_cache[2][3][2][3] = {};
   static int sms = 0;
   if (sms == 0) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-  int& occ = occ_cache[variant][dtype][mode];
+  opt = (opt && dtype == kF32 && mode != kTopK) ? 1 : 0;
+  int& occ = occ_cache[opt][variant][dtype][mode];
   if (occ == 0) {
     int v = 1;
-    NGL_DISPATCH(mode, dtype, [&] {
-      if (variant == kVariantTwoShot) {
-        v = twoshot_occupancy<M, T>();
-      } else if (variant == kVariantOneShot) {
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, oneshot_kernel<M, T>, kThreads, dsmem_of<M, T, true>());
-      } else {
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, single_kernel<M, T>, kThreads,
-                                                      prepare_dsmem<single_kernel<M, T>>(dsmem_of<M, T, false>()));
-      }
-    });
+    NGL_DISPATCH(mode, dtype, [&] { v = opt ? occupancy_of<M, T, true>(variant) : occupancy_of<M, T, false>(variant); });
     occ = v > 0 ? v : 1;
   }
   int g = occ * sms;
@@ -934,16 +1010,12 @@ int fused_grid(int nchunks, int mode, int dtype, int variant, int cap, int devic
 }
 
 cudaError_t launch_fused(const FusedParams& P, int mode, int dtype, int variant, int grid, cudaStream_t stream) {
-  if (variant == kVariantSingle) {
-    NGL_DISPATCH(mode, dtype, [&] {
-      const int dyn = prepare_dsmem<single_kernel<M, T>>(dsmem_of<M, T, false>());
-      single_kernel<M, T><<<grid, kThreads, dyn, stream>>>(P);
-    });
-  } else if (variant == kVariantTwoShot) {
-    NGL_DISPATCH(mode, dtype, [&] { twoshot_launch<M, T>(P, grid, stream); });
-  } else {
-    NGL_DISPATCH(mode, dtype, [&] { oneshot_kernel<M, T><<<grid, kThreads, dsmem_of<M, T, true>(), stream>>>(P); });
-  }
+  const bool opt = P.f.opt.segs != nullptr;
+  if (opt && (dtype != kF32 || mode == kTopK)) return cudaErrorInvalidValue;
+  NGL_DISPATCH(mode, dtype, [&] {
+    if (opt) launch_instance<M, T, true>(P, variant, grid, stream);
+    else launch_instance<M, T, false>(P, variant, grid, stream);
+  });
   return cudaGetLastError();
 }
 

@@ -84,9 +84,48 @@ def oneshot(n: int, mode: str = "int4", k: int = 13, drop: float = 0.0, bad_tag:
     return {"status": status.cpu().tolist(), "avg": gd.cpu().numpy(), "ref_avg": np.asarray(ref, np.float32)}
 
 
-def twoshot(n: int, mode: str = "int4", world: int = 4, drop: float = 0.0, grid_cap: int = 0) -> dict:
+def adamw_reference(p, m, v, g, hyper):
+    """AdamW with decoupled weight decay in float64, with the scalars of
+    ``parallel.fused.FusedOpt.hyper``."""
+    b1, b2, eps, decay, step_size, inv_bc2 = hyper
+    p, m, v, g = (np.asarray(a, np.float64) for a in (p, m, v, g))
+    p = p * decay
+    m = b1 * m + (1 - b1) * g
+    v = b2 * v + (1 - b2) * g * g
+    p = p - step_size * m / (np.sqrt(v) * inv_bc2 + eps)
+    return p, m, v
+
+
+def _opt_segments(n: int, dev, seed: int = 9):
+    """Parameters covering the bucket in four segments, one boundary not
+    on a multiple of 8 elements (the element-by-element path), with random
+    weights and moments; returns (FusedOpt without scalars, tensors)."""
+    from .fused import FusedOpt
+
+    cuts = sorted({0, n // 3, n // 3 + 13, (2 * n) // 3, n})
+    rng = np.random.default_rng(seed)
+    rows, tensors = [], []
+    for a, b in zip(cuts[:-1], cuts[1:]):
+        if b <= a:
+            continue
+        p = torch.from_numpy((rng.standard_normal(b - a) * 0.02).astype(np.float32)).to(dev)
+        m = torch.from_numpy((rng.standard_normal(b - a) * 1e-4).astype(np.float32)).to(dev)
+        v = torch.from_numpy((rng.random(b - a) * 1e-7).astype(np.float32)).to(dev)
+        rows.append((a, b - a, p.data_ptr(), m.data_ptr(), v.data_ptr()))
+        tensors.append((a, b, p, m, v))
+    table = np.array(rows, dtype=[("off", "<i8"), ("numel", "<i8"), ("p", "<u8"), ("m", "<u8"), ("v", "<u8")])
+    segs = torch.from_numpy(np.frombuffer(table.tobytes(), np.uint8).copy()).to(dev)
+    t = 3
+    hyper = [0.9, 0.999, 1e-8, 1.0 - 6e-4 * 0.01, 6e-4 / (1 - 0.9 ** t), 1.0 / np.sqrt(1 - 0.999 ** t)]
+    return FusedOpt(segs, len(rows), hyper), tensors
+
+
+def twoshot(n: int, mode: str = "int4", world: int = 4, drop: float = 0.0, grid_cap: int = 0,
+            optimizer: bool = False) -> dict:
     """Rank 0 of a ``world``-rank two-shot all-reduce with a predictor and
-    error feedback (see the module docstring)."""
+    error feedback (see the module docstring).  ``optimizer`` also applies
+    AdamW in rank 0's decode phase; the result then carries the updated and
+    the float64 reference parameters and moments."""
     h, c = _host(), _cuda()
     dev = torch.device("cuda")
     k = 13
@@ -97,7 +136,9 @@ def twoshot(n: int, mode: str = "int4", world: int = 4, drop: float = 0.0, grid_
     ptrs = [r.data_ptr() for r in regs]
     mcode = MODES[mode]
     tag = FusedAllReduce.tag_for(n, 6)
-    grid = c.fused_grid(n, mcode, False, VARIANTS["twoshot"], grid_cap, 0)
+    # the optimizer instance has its own occupancy, hence grid; every rank
+    # runs the same instance, as in a real run
+    grid = c.fused_grid(n, mcode, False, VARIANTS["twoshot"], grid_cap, 0, optimizer)
     epoch, parity = 1, 1  # every communicator below is new: its first launch
     val = _flag_value(tag, grid, epoch)
     pred = _data(n, 40)
@@ -126,13 +167,20 @@ def twoshot(n: int, mode: str = "int4", world: int = 4, drop: float = 0.0, grid_
         gd = torch.from_numpy(gs[r].copy()).to(dev)
         pd = torch.from_numpy(pred.copy()).to(dev)
         ed = torch.from_numpy(efs[r].copy()).to(dev)
+        opt, tensors = _opt_segments(n, dev, seed=9 + r) if optimizer else (None, [])
+        before = [(a, b, p.cpu().numpy(), m.cpu().numpy(), v.cpu().numpy()) for a, b, p, m, v in tensors]
         torch.cuda.synchronize()
         comm.run(gd, pd, ed, mcode, k, VARIANTS["twoshot"], True, seed, bucket, step, 0.9, False, grid_cap,
-                 int(2e9), tag, tl)
+                 int(2e9), tag, tl, None if opt is None else opt.segs, 0 if opt is None else opt.nsegs, 0,
+                 [] if opt is None else opt.hyper)
         torch.cuda.synchronize()
         if r == 0:
             out = {"status": status.cpu().tolist(), "avg": gd.cpu().numpy(), "pred": pd.cpu().numpy(),
                    "ef": ed.cpu().numpy()}
+            if opt is not None:
+                out["opt"] = [(a, b, p.cpu().numpy(), m.cpu().numpy(), v.cpu().numpy(), before[i][2:])
+                              for i, (a, b, p, m, v) in enumerate(tensors)]
+                out["opt_hyper"] = opt.hyper
     bits = 8 if mode == "int8" else 4
     inv = float(np.float32(1.0) / np.float32(world))
     encs = [h.product_encode(gs[r], pred, efs[r], bits, True, True, seed, r, bucket, step, topo) for r in range(world)]

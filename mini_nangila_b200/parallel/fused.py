@@ -45,6 +45,19 @@ STATUS_NAMES = {
 }
 
 
+@dataclass
+class FusedOpt:
+    """AdamW fused into the decode phase of one launch: ``segs`` is a uint8
+    CUDA tensor of ``nsegs`` packed segment records (bucket offset, numel,
+    parameter / first-moment / second-moment pointers), ``hyper`` the step's
+    (beta1, beta2, eps, 1 - lr*wd, lr / (1 - beta1^t), 1 / sqrt(1 - beta2^t)),
+    ``base`` the bucket element of the launch's first element."""
+    segs: torch.Tensor
+    nsegs: int
+    hyper: list
+    base: int = 0
+
+
 class CommError(RuntimeError):
     """A fused exchange gave up (a bounded wait expired, a tag or bounds check failed)."""
     pass
@@ -225,11 +238,14 @@ class FusedAllReduce:
         topo_drop: float = 0.0,
         topo_seed: int = 0,
         max_ctas: int | None = None,
+        opt: FusedOpt | None = None,
     ) -> str:
         """Average ``grad`` across ranks in place on the current stream.
 
         ``max_ctas`` caps this launch's grid (default: the communicator's);
-        every rank must pass the same value for the same bucket.
+        every rank must pass the same value for the same bucket.  ``opt``
+        applies AdamW to the bucket's parameters as each averaged gradient
+        element is written (fp32 buckets).
 
         Buckets longer than ``capacity`` run as several launches over
         segments; segment s of bucket b draws its noise from stream
@@ -248,6 +264,7 @@ class FusedAllReduce:
                     bucket=(bucket * 65536 + si) & 0xFFFFFFFF, step=step, beta=beta, first=first,
                     tag=None if tag is None else (tag + si) & 0xFFFFFFFF, topo_drop=topo_drop,
                     topo_seed=topo_seed, max_ctas=max_ctas,
+                    opt=None if opt is None else FusedOpt(opt.segs, opt.nsegs, opt.hyper, opt.base + s0),
                 )
             return v
         v = self.choose_variant(n, mode, variant)
@@ -258,6 +275,8 @@ class FusedAllReduce:
             int(bucket), int(step), float(beta), bool(first), self.max_ctas if max_ctas is None else int(max_ctas),
             self.timeout_ns, int(tag),
             list(topology(n, topo_drop, topo_seed, bucket)) if topo_drop > 0.0 else [],
+            None if opt is None else opt.segs, 0 if opt is None else int(opt.nsegs),
+            0 if opt is None else int(opt.base), [] if opt is None else [float(x) for x in opt.hyper],
         )
         self.launches += 1
         self._status_host.copy_(self.status, non_blocking=True)

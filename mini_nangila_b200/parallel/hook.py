@@ -127,6 +127,10 @@ class NangilaHookState:
     after_reduce: object = None
     # fused: a utils.timeline.StepTimeline that receives each bucket's events
     timeline: object = None
+    # fused: kernel_opt(bucket) -> parallel.fused.FusedOpt or None (AdamW in
+    # the exchange kernel's decode phase), then kernel_opt_done(bucket)
+    kernel_opt: object = None
+    kernel_opt_done: object = None
 
     def compression_ratio(self) -> float:
         return self.raw_bytes / max(1, self.comp_bytes)
@@ -356,6 +360,7 @@ def _fused_hook(hs: NangilaHookState, bucket):
     # of the flag tags) agree.
     last = bool(bucket.is_last()) if hasattr(bucket, "is_last") else True
     ctas = cfg.max_ctas if (last or not cfg.inflight_ctas) else cfg.inflight_ctas
+    kopt = hs.kernel_opt(bucket) if hs.kernel_opt is not None else None
     tl = hs.timeline
     trec = None
     if tl is not None:
@@ -364,8 +369,9 @@ def _fused_hook(hs: NangilaHookState, bucket):
 
         grid = _cuda().fused_grid(buf.numel(), {"int4": 0, "int8": 1, "topk": 2}[cfg.mode],
                                   buf.dtype == torch.bfloat16, {"single": 0, "oneshot": 1, "twoshot": 2}[variant],
-                                  ctas, buf.device.index)
-        trec = tl.bucket(bucket=bidx, numel=buf.numel(), variant=variant, grid=grid, last=last)
+                                  ctas, buf.device.index, kopt is not None)
+        trec = tl.bucket(bucket=bidx, numel=buf.numel(), variant=variant, grid=grid, last=last,
+                         optimizer_in_kernel=kopt is not None)
         tl.event(trec, "ready", cur)
     hs.stream.wait_stream(cur)
     with torch.cuda.stream(hs.stream), nvtx_range(f"nangila/bucket{bidx}/{buf.numel()}"):
@@ -383,11 +389,13 @@ def _fused_hook(hs: NangilaHookState, bucket):
         hs.last_variant = hs.comm.allreduce_(
             buf, st.pred, st.ef, mode=cfg.mode, k=cfg.k, variant=cfg.variant, stochastic=cfg.stochastic,
             seed=cfg.seed, bucket=bidx, step=st.calls, beta=cfg.beta, first=first,
-            topo_drop=cfg.topo_drop_percent, topo_seed=cfg.topo_seed, max_ctas=ctas,
+            topo_drop=cfg.topo_drop_percent, topo_seed=cfg.topo_seed, max_ctas=ctas, opt=kopt,
         )
         if trec is not None:
             tl.event(trec, "end", hs.stream)
-        if hs.after_reduce is not None:
+        if kopt is not None:
+            hs.kernel_opt_done(bucket)
+        elif hs.after_reduce is not None:
             hs.after_reduce(bucket)
             if trec is not None:
                 tl.event(trec, "opt_end", hs.stream)

@@ -17,9 +17,11 @@ Reference: python/nangila_ddp/train_nano.py:126-181 (DDP + hook + AdamW loop).
 """
 from __future__ import annotations
 
+import math
 import os
 from datetime import timedelta
 
+import numpy as np
 import torch
 
 from .utils.nvtx import nvtx_range
@@ -77,6 +79,8 @@ class BucketAdamW:
         self.group_of = {id(p): g for g in opt.param_groups for p in g["params"]}
         self.updated: set[int] = set()  # ids of parameters updated in this step
         self._cache: dict = {}
+        self._kcache: dict = {}
+        self._pending = None
 
     def _lists(self, params, grads):
         key = tuple(p.data_ptr() for p in params) + tuple(g.data_ptr() for g in grads)
@@ -116,6 +120,69 @@ class BucketAdamW:
     def __call__(self, bucket) -> None:
         self.apply(bucket.parameters(), bucket.gradients())
 
+    # ------------------------------------------- AdamW inside the exchange kernel
+    def kernel_args(self, bucket):
+        """The bucket's update as a ``parallel.fused.FusedOpt`` for the
+        exchange kernel to apply as it writes each averaged gradient, or
+        None when the bucket does not qualify (parameters not fp32 CUDA
+        tensors of one group, amsgrad or maximize, a non-float lr)."""
+        from .parallel.fused import FusedOpt
+
+        params, grads = bucket.parameters(), bucket.gradients()
+        buf = bucket.buffer()
+        if not params or buf.dtype != torch.float32 or not buf.is_cuda:
+            return None
+        key = (buf.data_ptr(), buf.numel()) + tuple(p.data_ptr() for p in params)
+        hit = self._kcache.get(key)
+        if hit is None:
+            grp = self.group_of.get(id(params[0]))
+            if grp is None or grp.get("amsgrad") or grp.get("maximize") or not isinstance(grp["lr"], float):
+                return None
+            rows = []
+            steps = []
+            for p, g in zip(params, grads):
+                if (self.group_of.get(id(p)) is not grp or p.dtype != torch.float32 or not p.is_cuda
+                        or not p.is_contiguous() or g.dtype != torch.float32):
+                    return None
+                off, rem = divmod(g.data_ptr() - buf.data_ptr(), 4)
+                if rem or off < 0 or off + g.numel() > buf.numel() or g.numel() != p.numel():
+                    return None
+                st = self.opt.state[p]
+                if len(st) == 0:
+                    st["step"] = torch.zeros((), dtype=torch.float32, device=p.device)
+                    st["exp_avg"] = torch.zeros_like(p, memory_format=torch.preserve_format)
+                    st["exp_avg_sq"] = torch.zeros_like(p, memory_format=torch.preserve_format)
+                rows.append((off, p.numel(), p.data_ptr(), st["exp_avg"].data_ptr(), st["exp_avg_sq"].data_ptr()))
+                steps.append(st["step"])
+            rows.sort()
+            table = np.array(rows, dtype=[("off", "<i8"), ("numel", "<i8"), ("p", "<u8"), ("m", "<u8"),
+                                          ("v", "<u8")])
+            segs = torch.from_numpy(np.frombuffer(table.tobytes(), np.uint8).copy()).to(buf.device)
+            # all of a bucket's parameters step together; the count is read
+            # from the device once, then kept on the host
+            t = int(steps[0].item())
+            hit = {"segs": segs, "n": len(rows), "steps": steps, "t": t, "grp": grp, "params": list(params)}
+            if len(self._kcache) > 4096:
+                self._kcache.clear()
+            self._kcache[key] = hit
+        grp = hit["grp"]
+        t = hit["t"] + 1
+        b1, b2 = grp["betas"]
+        lr, wd = float(grp["lr"]), float(grp["weight_decay"])
+        hyper = [float(b1), float(b2), float(grp["eps"]), 1.0 - lr * wd, lr / (1.0 - float(b1) ** t),
+                 1.0 / math.sqrt(1.0 - float(b2) ** t)]
+        self._pending = hit
+        return FusedOpt(hit["segs"], hit["n"], hyper)
+
+    def kernel_done(self, bucket) -> None:
+        """After the kernel launch that applied ``kernel_args``: advance the
+        step counters (device tensors, as torch's AdamW keeps them)."""
+        hit = self._pending
+        self._pending = None
+        hit["t"] += 1
+        torch._foreach_add_(hit["steps"], 1)
+        self.updated.update(id(p) for p in hit["params"])
+
     def finish_step(self, all_params) -> None:
         """Update the parameters no bucket carried this step (if any), then
         start the next step's bookkeeping."""
@@ -129,7 +196,9 @@ class DDPTrainer:
     """DDP + gradient hook + AdamW (+ bf16 autocast) training steps; see the module docstring.
 
     ``overlap_optimizer=True`` (fused hook on CUDA) applies AdamW per bucket
-    from the hook (``BucketAdamW``) instead of once after backward.
+    from the hook (``BucketAdamW``) instead of once after backward; with
+    ``optimizer_in_kernel`` (the default) the exchange kernel itself applies
+    it to fp32 parameters as it writes each averaged gradient.
     ``timeline_next_step()`` records the next step's device timeline
     (``utils.timeline.StepTimeline``).
     """
@@ -146,6 +215,7 @@ class DDPTrainer:
         fused_optimizer: bool = True,
         monitor: bool = False,
         overlap_optimizer: bool = False,
+        optimizer_in_kernel: bool = True,
     ):
         self.device = device or (torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available()
                                  else torch.device("cpu"))
@@ -177,6 +247,12 @@ class DDPTrainer:
                 raise ValueError("overlap_optimizer needs the fused (CUDA) or host (CPU) hook")
             self.bucket_opt = BucketAdamW(self.opt)
             self.hook_state.after_reduce = self.bucket_opt
+            if optimizer_in_kernel and hook == "fused":
+                # AdamW inside the exchange kernel's decode phase when the
+                # bucket qualifies (fp32 parameters); the separate update
+                # above otherwise
+                self.hook_state.kernel_opt = self.bucket_opt.kernel_args
+                self.hook_state.kernel_opt_done = self.bucket_opt.kernel_done
         self.timeline = None
         self._timeline_next = False
 

@@ -179,3 +179,23 @@ def test_twoshot_kernel_with_predelivered_peers(mode, world, n, drop, cap):
     assert np.array_equal(_bits(out), _bits(avg)), int(np.sum(_bits(out) != _bits(avg)))
     assert np.array_equal(_bits(pred_out), _bits(pred_ref))
     assert np.array_equal(_bits(ef_out), _bits(ef_ref))
+
+
+@pytest.mark.parametrize("world", [2, 8])
+def test_twoshot_kernel_applies_adamw_in_its_decode_phase(world):
+    """AdamW fused into the two-shot kernel's decode phase: with the
+    kernel's own averaged gradient (bit-identical to the oracle's), the
+    parameters and moments match a float64 AdamW step, on four parameters
+    of which one boundary is off the 8-element grid."""
+    from mini_nangila_b200.parallel import emulate
+
+    r = emulate.twoshot(70001, "int4", world, optimizer=True)
+    assert r["status"][0] == 0
+    assert emulate.bit_equal(r["avg"], r["ref_avg"])
+    g = r["ref_avg"]
+    for a, b, p, m, v, (p0, m0, v0) in r["opt"]:
+        rp, rm, rv = emulate.adamw_reference(p0, m0, v0, g[a:b], r["opt_hyper"])
+        assert np.allclose(m, rm, rtol=1e-5, atol=1e-12)
+        assert np.allclose(v, rv, rtol=1e-5, atol=1e-18)
+        assert np.allclose(p, rp, rtol=0, atol=1e-7)
+        assert np.abs(p - p0).max() > 1e-4  # the step moved the weights

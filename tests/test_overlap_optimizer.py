@@ -90,7 +90,8 @@ def test_bucket_adamw_fused_hook_matches_step_after_backward():
         for overlap in (False, True):
             torch.manual_seed(0)
             tr = DDPTrainer(GPT2(cfg), hook="fused", device=dev, bucket_cap_mb=0.25,
-                            hook_kwargs=dict(use_momentum=True), overlap_optimizer=overlap)
+                            hook_kwargs=dict(use_momentum=True), overlap_optimizer=overlap,
+                            optimizer_in_kernel=False)
             g = torch.Generator(device=dev).manual_seed(1)
             for i in range(4):
                 t = torch.randint(0, cfg.vocab_size, (2, 65), generator=g, device=dev)
@@ -108,5 +109,44 @@ def test_bucket_adamw_fused_hook_matches_step_after_backward():
             tr.hook_state.comm.close()
         for a, b in zip(res[False], res[True]):
             assert torch.equal(a, b)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_adamw_inside_the_exchange_kernel_tracks_adamw_after_backward():
+    """World 1 on a GPU: AdamW applied by the fused kernel as it writes each
+    averaged gradient stays within rounding of PyTorch's AdamW after
+    backward over several steps, moves the weights, and keeps the step
+    counters and moments in the optimizer's own state."""
+    import torch.distributed as dist
+
+    from mini_nangila_b200.models import GPT2, GPT2Config
+    from mini_nangila_b200.train import DDPTrainer, init_distributed
+
+    init_distributed("nccl")
+    try:
+        dev = torch.device("cuda", 0)
+        cfg = GPT2Config(vocab_size=1024, n_positions=128, n_layer=2, n_head=4, n_embd=128, n_inner=512)
+        res, init = {}, None
+        for in_kernel in (False, True):
+            torch.manual_seed(0)
+            tr = DDPTrainer(GPT2(cfg), hook="fused", device=dev, bucket_cap_mb=0.25,
+                            hook_kwargs=dict(use_momentum=True), overlap_optimizer=in_kernel,
+                            optimizer_in_kernel=in_kernel)
+            init = [p.detach().clone() for p in tr.model.parameters()]
+            g = torch.Generator(device=dev).manual_seed(1)
+            for _ in range(4):
+                t = torch.randint(0, cfg.vocab_size, (2, 65), generator=g, device=dev)
+                tr.step(t[:, :-1].contiguous(), t[:, 1:].contiguous())
+            torch.cuda.synchronize()
+            tr.hook_state.comm.check()
+            res[in_kernel] = ([p.detach().clone() for p in tr.model.parameters()],
+                              [tr.opt.state[p]["step"].item() for p in tr.model.parameters()])
+            tr.hook_state.comm.close()
+        for a, b, p0 in zip(res[False][0], res[True][0], init):
+            assert torch.allclose(a, b, rtol=0, atol=2e-6), float((a - b).abs().max())
+            assert float((b - p0).abs().max()) > 1e-5
+        assert res[True][1] == res[False][1] == [4.0] * len(res[True][1])
     finally:
         dist.destroy_process_group()
