@@ -2,9 +2,11 @@
 
     python -m mini_nangila_b200.apps.kernel_bench --op fused_oneshot --n 67108864
 
-Ops: fused_single (INT4, world 1), fused_oneshot (rank 0 of a 2-rank one-shot
-all-reduce with the peer's payload and flags pre-delivered into local memory,
-so the exchange kernel runs in full on one GPU), fused_twoshot (rank 0 of a
+Ops: fused_single (INT4, world 1), fused_oneshot (rank 0 of a --world-rank
+one-shot all-reduce, 2 by default, with the peers' payloads and flags
+pre-delivered into local memory, so the exchange kernel runs in full on one
+GPU; --dtype bf16 and --no-pred give the top-k configuration of a bf16
+model), fused_twoshot (rank 0 of a
 --world-rank two-shot all-reduce: every peer's phase-A records, its INT8
 result records and both kinds of flags pre-delivered), fused_topk_single,
 fused_topk_oneshot, hpc_step, bs_encode, bsrle_encode, rle_encode,
@@ -57,33 +59,37 @@ def _time(fn, iters, warmup, setup=None):
     return statistics.median(out)
 
 
-def _emulated_oneshot(n, mode, k):
-    """Rank 0 of a 2-rank one-shot launch; the peer's record and column flags
-    are written into rank 0's region before every call."""
+def _emulated_oneshot(n, mode, k, world=2, dtype=torch.float32, use_pred=True):
+    """Rank 0 of a ``world``-rank one-shot launch; every peer's record and
+    column flag are written into rank 0's region before every call, so the
+    kernel runs in full (encode, pushes, waits, rank-ordered decode of all
+    ``world`` records) on one GPU.  ``dtype`` is the bucket's; without
+    ``use_pred`` there is no predictor state (the top-k configuration)."""
     from mini_nangila_b200 import _ext
     from mini_nangila_b200.parallel.fused import MAX_COLS, MODES, VARIANTS, FusedAllReduce, make_layout
 
     c = _ext.cuda()
     dev = torch.device("cuda")
-    L = make_layout(2, n, k, (mode,))
-    reg0 = torch.zeros(L.total, dtype=torch.uint8, device=dev)
-    reg1 = torch.zeros(L.total, dtype=torch.uint8, device=dev)
+    L = make_layout(world, n, k, (mode,))
+    regs = [torch.zeros(L.total, dtype=torch.uint8, device=dev) for _ in range(world)]
     status = torch.zeros(4, dtype=torch.int32, device=dev)
-    comm = c.FusedComm(2, 0, [reg0.data_ptr(), reg1.data_ptr()], L.flags_off, L.inbox_off, L.slot_bytes,
+    comm = c.FusedComm(world, 0, [r.data_ptr() for r in regs], L.flags_off, L.inbox_off, L.slot_bytes,
                        L.result_off, L.result_bytes, status)
     mcode = MODES[mode]
-    grid = c.fused_grid(n, mcode, False, VARIANTS["oneshot"], 0, 0)
+    grid = c.fused_grid(n, mcode, dtype == torch.bfloat16, VARIANTS["oneshot"], 0, 0)
     tag = FusedAllReduce.tag_for(n, 0)
+    reg0 = regs[0]
     g1 = torch.randn(n, device=dev) * 1e-3
     p1, _ = c.product_encode(g1, None, None, mcode, k, True, 3, 1, 0, 0)
-    g = torch.randn(n, device=dev) * 1e-3
-    pred = torch.zeros(n, device=dev)
+    g = (torch.randn(n, device=dev) * 1e-3).to(dtype)
+    pred = torch.zeros(n, device=dev) if use_pred else None
     ef = torch.zeros(n, device=dev)
     flags = reg0[L.flags_off:].view(torch.int64)
     ftag = tag ^ ((grid * 0x9E3779B1) & 0xFFFFFFFF)
     for par in (0, 1):
-        slot = L.inbox_off + (par * 2 + 1) * L.slot_bytes
-        reg0[slot: slot + p1.numel()] = p1
+        for src in range(1, world):
+            slot = L.inbox_off + (par * world + src) * L.slot_bytes
+            reg0[slot: slot + p1.numel()] = p1
 
     def setup():
         epoch = comm.epoch + 1
@@ -91,16 +97,19 @@ def _emulated_oneshot(n, mode, k):
         val = (ftag << 32) | epoch
         if val >= 1 << 63:
             val -= 1 << 64
-        base = ((par * 2 + 0) * 2 + 1) * MAX_COLS
-        flags[base: base + grid] = val
+        for src in range(1, world):
+            base = ((par * 2 + 0) * world + src) * MAX_COLS
+            flags[base: base + grid] = val
 
     def run():
         comm.run(g, pred, ef, mcode, k, VARIANTS["oneshot"], True, 3, 0, 1, 0.9, False, 0, int(5e9), tag)
 
     wire = p1.numel()
-    # g, pred, ef read; ef, g, pred written; own record written twice (self + "peer"),
-    # two records read.
-    algo = 24 * n + 4 * wire
+    es = g.element_size()
+    # g read and written back (the average), ef read and written, pred read
+    # and written; own record written to every slot (world copies, the
+    # peers' over NVLink in a real run), world records read.
+    algo = 2 * es * n + 8 * n + (8 * n if use_pred else 0) + 2 * world * wire
     return setup, run, algo, status
 
 
@@ -169,7 +178,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--k", type=int, default=13, help="top-k kept per 256-block")
     ap.add_argument("--steps", type=int, default=100, help="snapshots for the trajectory ops")
-    ap.add_argument("--world", type=int, default=8, help="emulated ranks of fused_twoshot")
+    ap.add_argument("--world", type=int, default=None,
+                    help="emulated ranks of fused_twoshot (default 8) / fused_oneshot (default 2)")
+    ap.add_argument("--dtype", choices=["fp32", "bf16"], default="fp32", help="bucket dtype of fused_oneshot")
+    ap.add_argument("--no-pred", action="store_true", help="fused_oneshot without predictor state")
     ap.add_argument("--l2-keep-mb", type=float, default=48.0,
                     help="fused_twoshot: predictor MB kept in L2 between phases (0: no L2 policy)")
     args = ap.parse_args()
@@ -191,9 +203,11 @@ def main():
         status = comm.status
     elif args.op in ("fused_oneshot", "fused_topk_oneshot"):
         mode = "topk" if "topk" in args.op else "int4"
-        setup, run, algo, status = _emulated_oneshot(n, mode, args.k)
+        setup, run, algo, status = _emulated_oneshot(
+            n, mode, args.k, args.world or 2, torch.bfloat16 if args.dtype == "bf16" else torch.float32,
+            not args.no_pred)
     elif args.op == "fused_twoshot":
-        setup, run, algo, status = _emulated_twoshot(n, args.world, args.l2_keep_mb)
+        setup, run, algo, status = _emulated_twoshot(n, args.world or 8, args.l2_keep_mb)
     elif args.op == "hpc_step":
         x = torch.rand(n, device=dev) * 100
         st = c.q823_from_f32(x)

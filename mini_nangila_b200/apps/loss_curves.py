@@ -10,8 +10,10 @@ the workload's lr with a short linear warm-up, identical for all settings.
 Settings (``--settings``, comma-separated):
 
 * ``nccl``: DDP's uncompressed NCCL fp32 all-reduce (the baseline);
-* ``int4-oneshot`` / ``int4-auto``: the fused INT4 + EMA + error-feedback
-  hook, one-shot only or the size-based one-shot / two-shot choice;
+* ``int4-oneshot`` / ``int4-auto`` / ``int4-twoshot``: the fused INT4 +
+  EMA + error-feedback hook, one-shot only, the size-based one-shot /
+  two-shot choice, or two-shot only (every bucket takes the second,
+  round-to-nearest INT8 stage, which error feedback does not see);
 * ``topk5``: the fused per-block top-k 5 % + error-feedback hook;
 * ``compat``: the reference-compatible hook (INT4, global scale, no EF).
 
@@ -38,6 +40,7 @@ SETTINGS = {
     "nccl": dict(hook="nccl"),
     "int4-oneshot": dict(hook="fused", hook_kwargs=dict(use_momentum=True, error_feedback=True, variant="oneshot")),
     "int4-auto": dict(hook="fused", hook_kwargs=dict(use_momentum=True, error_feedback=True, variant="auto")),
+    "int4-twoshot": dict(hook="fused", hook_kwargs=dict(use_momentum=True, error_feedback=True, variant="twoshot")),
     "topk5": dict(hook="fused", hook_kwargs=dict(use_momentum=False, error_feedback=True, topk_percent=0.05)),
     "compat": dict(hook="compat", hook_kwargs=dict(use_momentum=True, bits=4)),
 }
@@ -96,7 +99,7 @@ def summarize(curves: dict, every: int = 100, tail: int = 20) -> dict:
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--steps", type=int, default=300)
-    ap.add_argument("--settings", default="nccl,int4-oneshot,int4-auto,topk5,compat")
+    ap.add_argument("--settings", default="nccl,int4-oneshot,int4-auto,int4-twoshot,topk5,compat")
     ap.add_argument("--micro-batch", type=int, default=8)
     ap.add_argument("--seq", type=int, default=1024)
     ap.add_argument("--lr", type=float, default=6e-4)

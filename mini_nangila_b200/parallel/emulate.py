@@ -86,12 +86,15 @@ def oneshot(n: int, mode: str = "int4", k: int = 13, drop: float = 0.0, bad_tag:
 
 def adamw_reference(p, m, v, g, hyper):
     """AdamW with decoupled weight decay in float64, with the scalars of
-    ``parallel.fused.FusedOpt.hyper``."""
-    b1, b2, eps, decay, step_size, inv_bc2 = hyper
+    ``parallel.fused.FusedOpt.hyper`` as the kernel receives them: rounded to
+    float32, and 1 - beta formed in float32."""
+    b1, b2, eps, decay, step_size, inv_bc2 = (float(np.float32(x)) for x in hyper)
+    omb1 = float(np.float32(1) - np.float32(b1))
+    omb2 = float(np.float32(1) - np.float32(b2))
     p, m, v, g = (np.asarray(a, np.float64) for a in (p, m, v, g))
     p = p * decay
-    m = b1 * m + (1 - b1) * g
-    v = b2 * v + (1 - b2) * g * g
+    m = b1 * m + omb1 * g
+    v = b2 * v + omb2 * g * g
     p = p - step_size * m / (np.sqrt(v) * inv_bc2 + eps)
     return p, m, v
 

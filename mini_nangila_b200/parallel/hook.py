@@ -360,7 +360,8 @@ def _fused_hook(hs: NangilaHookState, bucket):
     # of the flag tags) agree.
     last = bool(bucket.is_last()) if hasattr(bucket, "is_last") else True
     ctas = cfg.max_ctas if (last or not cfg.inflight_ctas) else cfg.inflight_ctas
-    kopt = hs.kernel_opt(bucket) if hs.kernel_opt is not None else None
+    # AdamW in the kernel's decode phase: dense (INT4/INT8) fp32 buckets only
+    kopt = hs.kernel_opt(bucket) if (hs.kernel_opt is not None and cfg.mode != "topk") else None
     tl = hs.timeline
     trec = None
     if tl is not None:

@@ -70,3 +70,36 @@ def test_error_feedback_bounds_accumulated_error():
     total = steps * g.astype(np.float64)
     assert np.abs(sent + ef - total).max() < 1e-6 * steps
     assert np.abs(ef).max() < 3 * np.abs(g).max()
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("W", [2, 4, 8])
+def test_twoshot_average_within_both_stages_bound(bits, W):
+    """Two-shot: each chunk owner sums the ranks' stochastic codes, then
+    re-encodes the mean as INT8 with round-to-nearest and one scale per
+    256-block, which every rank decodes.  Against the float64 mean, the error
+    is at most the first stage's one step per rank (averaged) plus half a
+    step of the second stage (block absmax of the mean / 127).  That second
+    rounding is not seen by error feedback, so its bound is checked alone too:
+    the two-shot result is within half a second-stage step of the one-shot
+    average that it re-encodes."""
+    h = _ext.host()
+    n = 5000
+    gs = _ranks(W, n, 2)
+    wires = [h.product_encode(gs[r], None, None, bits, True, False, 13, r, 0, 0)[0] for r in range(W)]
+    inv = float(np.float32(1) / np.float32(W))
+    one = h.product_reduce(wires, n, bits, None, inv).astype(np.float64)
+    two = h.product_reduce_twoshot(wires, n, bits, None, inv).astype(np.float64)
+    exact = np.mean(np.stack(gs).astype(np.float64), axis=0)
+    nblk = (n + 255) // 256
+    amax = np.array([np.abs(one[b * 256:(b + 1) * 256]).max() for b in range(nblk)])
+    half2 = np.repeat(amax / 127.0 / 2.0, 256)[:n]
+    stage1 = np.zeros(n)
+    for r in range(W):
+        stage1 += np.repeat(_scales(wires[r], n, bits).astype(np.float64), 256)[:n]
+    stage1 /= W
+    assert np.all(np.abs(two - one) <= half2 * (1 + 1e-5) + 1e-12)
+    assert np.all(np.abs(two - exact) <= (stage1 + half2) * (1 + 1e-5) + 1e-12)
+    # the second stage is round-to-nearest: its error is no larger than the
+    # first stage's stochastic error on average
+    assert np.abs(two - one).mean() < np.abs(one - exact).mean()

@@ -193,9 +193,15 @@ def test_twoshot_kernel_applies_adamw_in_its_decode_phase(world):
     assert r["status"][0] == 0
     assert emulate.bit_equal(r["avg"], r["ref_avg"])
     g = r["ref_avg"]
+    b1, b2 = r["opt_hyper"][:2]
+    ulp = 2.0 ** -24
     for a, b, p, m, v, (p0, m0, v0) in r["opt"]:
         rp, rm, rv = emulate.adamw_reference(p0, m0, v0, g[a:b], r["opt_hyper"])
-        assert np.allclose(m, rm, rtol=1e-5, atol=1e-12)
-        assert np.allclose(v, rv, rtol=1e-5, atol=1e-18)
+        gg = np.asarray(g[a:b], np.float64)
+        # fp32 error of each moment relative to the size of its two terms:
+        # b1*m0 and (1-b1)*g may nearly cancel, so the error bound is a few
+        # ulps of the terms, not of the result
+        assert np.all(np.abs(m - rm) <= 4 * ulp * (b1 * np.abs(m0) + (1 - b1) * np.abs(gg)) + 1e-30)
+        assert np.all(np.abs(v - rv) <= 4 * ulp * (b2 * v0 + (1 - b2) * gg * gg) + 1e-36)
         assert np.allclose(p, rp, rtol=0, atol=1e-7)
-        assert np.abs(p - p0).max() > 1e-4  # the step moved the weights
+        assert np.abs(p - p0).max() > 1e-5  # the step moved the weights (updates are ~5e-5 here)
