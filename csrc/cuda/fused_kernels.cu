@@ -228,27 +228,61 @@ __device__ __forceinline__ void put_dense(uint8_t* rec, int warp, int lane, floa
   else reinterpret_cast<uint2*>(codes)[lane] = make_uint2(w[0], w[1]);
 }
 
+// The lane's codes and the scale of warp `warp`'s block in one dense chunk
+// record (global memory).
+struct DenseLane {
+  uint2 x;  // INT4: x.x holds the lane's 8 nibbles; INT8: 8 bytes
+  float s;
+};
+template <int BITS>
+__device__ __forceinline__ DenseLane load_dense(const uint8_t* rec, int warp, int lane) {
+  constexpr int bpb = BITS == 4 ? kInt4BlockBytes : kInt8BlockBytes;
+  const uint8_t* codes = rec + 4 * kChunkBlocks + warp * bpb;
+  DenseLane d;
+  d.s = __ldcg(reinterpret_cast<const float*>(rec) + warp);
+  if (BITS == 4) d.x = make_uint2(__ldcg(reinterpret_cast<const unsigned int*>(codes) + lane), 0u);
+  else d.x = __ldcg(reinterpret_cast<const uint2*>(codes) + lane);
+  return d;
+}
+template <int BITS>
+__device__ __forceinline__ void accum_lane(const DenseLane& d, float (&acc)[8]) {
+  if (BITS == 4) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t byte = (d.x.x >> (8 * j)) & 0xffu;
+      acc[2 * j] = product_accum(acc[2 * j], sext4(byte >> 4), d.s);
+      acc[2 * j + 1] = product_accum(acc[2 * j + 1], sext4(byte & 0xfu), d.s);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      acc[j] = product_accum(acc[j], (int32_t)(int8_t)((d.x.x >> (8 * j)) & 0xffu), d.s);
+      acc[4 + j] = product_accum(acc[4 + j], (int32_t)(int8_t)((d.x.y >> (8 * j)) & 0xffu), d.s);
+    }
+  }
+}
 // Accumulate warp `warp`'s block of one dense chunk record (global memory).
 template <int BITS>
 __device__ __forceinline__ void accum_dense(const uint8_t* rec, int warp, int lane, float (&acc)[8]) {
-  constexpr int bpb = BITS == 4 ? kInt4BlockBytes : kInt8BlockBytes;
-  const uint8_t* codes = rec + 4 * kChunkBlocks + warp * bpb;
-  const float s = __ldcg(reinterpret_cast<const float*>(rec) + warp);
-  if (BITS == 4) {
-    const uint32_t x = __ldcg(reinterpret_cast<const unsigned int*>(codes) + lane);
+  accum_lane<BITS>(load_dense<BITS>(rec, warp, lane), acc);
+}
+// The same over `world` records (rec_of(src), src = 0 .. world-1), four
+// ranks at a time: a group's loads are all issued before its first sum, so
+// their round trips overlap (two instead of eight at eight ranks, with 8-12
+// more live registers rather than 16-24); the sums run in rank order (the
+// same FMA sequence as one record at a time).
+constexpr int kRankGroup = 4;
+template <int BITS, typename RecOf>
+__device__ __forceinline__ void accum_dense_ranks(const RecOf& rec_of, int world, int warp, int lane,
+                                                  float (&acc)[8]) {
+  for (int g0 = 0; g0 < world; g0 += kRankGroup) {
+    DenseLane d[kRankGroup];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const uint32_t byte = (x >> (8 * j)) & 0xffu;
-      acc[2 * j] = product_accum(acc[2 * j], sext4(byte >> 4), s);
-      acc[2 * j + 1] = product_accum(acc[2 * j + 1], sext4(byte & 0xfu), s);
-    }
-  } else {
-    const uint2 x = __ldcg(reinterpret_cast<const uint2*>(codes) + lane);
+    for (int i = 0; i < kRankGroup; ++i)
+      if (g0 + i < world) d[i] = load_dense<BITS>(rec_of(g0 + i), warp, lane);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      acc[j] = product_accum(acc[j], (int32_t)(int8_t)((x.x >> (8 * j)) & 0xffu), s);
-      acc[4 + j] = product_accum(acc[4 + j], (int32_t)(int8_t)((x.y >> (8 * j)) & 0xffu), s);
-    }
+    for (int i = 0; i < kRankGroup; ++i)
+      if (g0 + i < world) accum_lane<BITS>(d[i], acc);
   }
 }
 
@@ -482,6 +516,44 @@ __device__ __forceinline__ void topk_accum_global(const uint8_t* rec_g, uint8_t*
   __syncwarp();
 }
 
+// Add `world` ranks' records of one block (rec_of(src) + block offset, global
+// memory) into the warp accumulator `acc` (shared memory), in rank order.
+// A record of R = rec_bytes / 4 <= 32 words is read with one load per lane
+// and rank, all issued before the first sum; each kept entry's index and
+// code bytes then reach their lane by shuffles.  Longer records (k > 62)
+// are staged rank by rank.
+template <typename RecOf>
+__device__ __forceinline__ void topk_accum_ranks(const RecOf& rec_of, int world, int64_t boff, uint8_t* stage, int k,
+                                                 int keff, int rec_bytes, float* acc, int lane) {
+  const int R = rec_bytes >> 2;
+  if (R > 32) {
+    for (int src = 0; src < world; ++src) topk_accum_global(rec_of(src) + boff, stage, k, keff, rec_bytes, acc, lane);
+    return;
+  }
+  uint32_t wv[kMaxWorld];
+#pragma unroll
+  for (int src = 0; src < kMaxWorld; ++src)
+    wv[src] = (src < world && lane < R) ? __ldcg(reinterpret_cast<const unsigned int*>(rec_of(src) + boff) + lane)
+                                        : 0u;
+#pragma unroll
+  for (int src = 0; src < kMaxWorld; ++src) {
+    if (src >= world) break;
+    const float s = __uint_as_float(__shfl_sync(kFull, wv[src], 0));
+    for (int base = 0; base < keff; base += 32) {
+      const int j = base + lane;
+      const int bi = 4 + j, bq = 4 + k + j;  // byte offsets of entry j's index and code
+      const uint32_t wi = __shfl_sync(kFull, wv[src], min(bi >> 2, 31));
+      const uint32_t wq = __shfl_sync(kFull, wv[src], min(bq >> 2, 31));
+      if (j < keff) {
+        const int idx = (int)((wi >> (8 * (bi & 3))) & 0xffu);
+        const int32_t q = (int32_t)(int8_t)((wq >> (8 * (bq & 3))) & 0xffu);
+        acc[idx] = product_accum(acc[idx], q, s);
+      }
+    }
+    __syncwarp();  // this rank's sums land before the next rank's
+  }
+}
+
 // ------------------------------------------------------------- chunk level
 // Encode chunk c into the shared-memory record `rec` (all threads; ends
 // with __syncthreads).  Blocks past the end are written as empty blocks.
@@ -523,6 +595,73 @@ __device__ __forceinline__ void encode_chunk(const ChunkSrc<T>& src, float* ef_w
   __syncthreads();
 }
 
+// Phase 1 of the exchange kernels, one warp: encode block `warp` of chunk c
+// and store this block's part of the chunk record straight into each of
+// `ndst` destination chunk records (dst(i), i = 0 .. ndst-1): no CTA-wide
+// staging, so warps go through their chunks independently.  Dense blocks:
+// the scale (lane 0) and the lane's code word, coalesced across the warp.
+// Top-k blocks: the record is assembled in the warp's shared-memory slot
+// `wrec`, then copied out in 16-byte (or 4-byte) words.  Blocks past the
+// end are written as empty blocks; a passenger chunk writes nothing (its
+// residual goes to the error feedback).  The layout is encode_chunk's.
+// Inputs are read with direct loads: the prefetch pipeline of the
+// single-rank kernel measured slower here, since the exchange phases want
+// the occupancy its buffers would take.
+template <int MODE, typename T, typename Dst>
+__device__ __forceinline__ void encode_push_block(const FusedParams& P, int c, uint8_t* wrec, int ndst,
+                                                  const Dst& dst) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int blk = c * kChunkBlocks + warp;
+  const ChunkSrc<T> src{reinterpret_cast<const T*>(P.grad), P.pred, P.ef, 0};
+  if (passenger(P.q.topo, c, P.nchunks)) {
+    if (blk < P.nblk) passenger_block<T>(src, P.ef, P.n, blk, lane, P.q);
+    return;
+  }
+  if constexpr (MODE == kTopK) {
+    if (blk < P.nblk) {
+      float cv[8];
+      const int valid = load_residual<T, false>(src, P.n, blk, lane, P.q, cv);
+      topk_select(cv, valid, blk, lane, P.k, P.n, P.q, P.ef, wrec, P.rec_bytes);
+    } else {
+      for (int w = lane; w < P.rec_bytes / 4; w += 32) reinterpret_cast<uint32_t*>(wrec)[w] = 0u;
+      __syncwarp();
+    }
+    const int64_t boff = (int64_t)warp * P.rec_bytes;
+    if ((P.rec_bytes & 15) == 0) {
+      const int Q = P.rec_bytes >> 4;
+      for (int i = lane; i < Q * ndst; i += 32) {
+        const int d = i / Q, q = i - d * Q;
+        reinterpret_cast<uint4*>(dst(d) + boff)[q] = reinterpret_cast<const uint4*>(wrec)[q];
+      }
+    } else {
+      const int Q = P.rec_bytes >> 2;
+      for (int i = lane; i < Q * ndst; i += 32) {
+        const int d = i / Q, q = i - d * Q;
+        reinterpret_cast<uint32_t*>(dst(d) + boff)[q] = reinterpret_cast<const uint32_t*>(wrec)[q];
+      }
+    }
+    __syncwarp();  // the slot is read out before the next block rewrites it
+  } else {
+    constexpr int BITS = MODE == kInt4 ? 4 : 8;
+    constexpr int bpb = BITS == 4 ? kInt4BlockBytes : kInt8BlockBytes;
+    uint32_t w[2] = {0u, 0u};
+    float s = 0.0f;
+    if (blk < P.nblk) {
+      float cv[8];
+      int32_t q[8];
+      const int valid = load_residual<T>(src, P.n, blk, lane, P.q, cv);
+      s = encode_dense<BITS>(cv, valid, blk, lane, P.q, P.ef, w, q);
+    }
+    for (int d = 0; d < ndst; ++d) {
+      uint8_t* rec = dst(d);
+      uint8_t* codes = rec + 4 * kChunkBlocks + warp * bpb;
+      if (lane == 0) reinterpret_cast<float*>(rec)[warp] = s;
+      if (BITS == 4) reinterpret_cast<uint32_t*>(codes)[lane] = w[0];
+      else reinterpret_cast<uint2*>(codes)[lane] = make_uint2(w[0], w[1]);
+    }
+  }
+}
+
 __device__ __forceinline__ void copy_record(uint8_t* dst, const uint8_t* rec, int bytes) {
   const uint4* s = reinterpret_cast<const uint4*>(rec);
   uint4* d = reinterpret_cast<uint4*>(dst);
@@ -549,14 +688,13 @@ __device__ __forceinline__ void decode_chunk(const RecOf& rec_of, int world, T* 
     for (int j = 0; j < 8; ++j) a[lane * 8 + j] = 0.0f;
     __syncwarp();
     const int keff = min(k, (int)min64(kBlock, n - (int64_t)blk * kBlock));
-    for (int src = 0; src < world; ++src)
-      topk_accum_global(rec_of(src) + warp * rec_bytes, stage, k, keff, rec_bytes, a, lane);
+    topk_accum_ranks(rec_of, world, (int64_t)warp * rec_bytes, stage, k, keff, rec_bytes, a, lane);
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[j] = a[lane * 8 + j];
     __syncwarp();
   } else {
     constexpr int BITS = MODE == kInt4 ? 4 : 8;
-    for (int src = 0; src < world; ++src) accum_dense<BITS>(rec_of(src), warp, lane, acc);
+    accum_dense_ranks<BITS>(rec_of, world, warp, lane, acc);
   }
   finalize<T, MODE != kTopK, kOpt>(grad, pred, n, blk, lane, acc, fp);
 }
@@ -636,26 +774,20 @@ __device__ bool wait_column(const FusedParams& P, int kind, int* s_abort) {
 }
 
 // ------------------------------------------------------------------ kernels
+// Per-warp top-k record slot in shared memory: the largest record rounded up
+// to 16 bytes, so every slot starts on a 16-byte boundary (the one-shot
+// kernel copies records out of it in 16-byte words).
+constexpr int kTopkSlot = (kTopkMaxRec + 15) / 16 * 16;
+static_assert(kWarps * kTopkSlot >= kMaxChunkRec, "the slots also hold one whole chunk record");
+
 template <int MODE>
 struct Smem {
-  static constexpr int kRec = MODE == kTopK ? kMaxChunkRec : (MODE == kInt4 ? 1056 : 2080);
+  // encode_chunk's chunk record (the encode kernel); the one-shot kernel
+  // uses it as per-warp top-k record slots (kTopkSlot bytes each)
+  static constexpr int kRec = MODE == kTopK ? kWarps * kTopkSlot : (MODE == kInt4 ? 1056 : 2080);
   static constexpr int kStage = MODE == kTopK ? kWarps * kTopkMaxRec : 16;
   static constexpr int kAcc = MODE == kTopK ? kWarps * kBlock : 4;
 };
-
-// Phase-1 loop shared by the exchange kernels: encode every owned chunk
-// (direct loads: measured faster here than the prefetch pipeline, since the
-// exchange phases want the occupancy its buffers would take) and hand the
-// staged record to `send`.
-template <int MODE, typename T, typename Send>
-__device__ __forceinline__ void encode_owned(const FusedParams& P, uint8_t* rec, Send&& send) {
-  const ChunkSrc<T> gsrc{reinterpret_cast<const T*>(P.grad), P.pred, P.ef, 0};
-  int it = 0;
-  for (int c = blockIdx.x; c < P.nchunks; c += gridDim.x, ++it) {
-    encode_chunk<MODE, T>(gsrc, P.ef, P.n, P.nblk, P.nchunks, P.k, P.rec_bytes, P.q, c, rec);
-    send(c, it);
-  }
-}
 
 template <int MODE, typename T, bool kOpt>
 __global__ void __launch_bounds__(kThreads) oneshot_kernel(FusedParams P) {
@@ -669,16 +801,12 @@ __global__ void __launch_bounds__(kThreads) oneshot_kernel(FusedParams P) {
   NGL_BOUNDS_UNIFORM((int64_t)P.nchunks * P.chunk_bytes <= P.slot_bytes && P.world <= kMaxWorld, P.status,
                      P.nchunks, P.chunk_bytes);
   for (int r = 0; r < P.world; ++r) NGL_BOUNDS_UNIFORM(P.sym[r] != nullptr, P.status, -2, r);
-  // Phase 1: encode each owned chunk and push its record to every rank.
-  encode_owned<MODE, T>(P, rec, [&](int c, int) {
-    if (!passenger(P.q.topo, c, P.nchunks)) {
-      for (int i = 0; i < P.world; ++i) {
-        const int r = (P.rank + 1 + i) % P.world;  // self last
-        copy_record(slot_rec(P, r, P.rank, c), rec, P.chunk_bytes);
-      }
-    }
-    __syncthreads();
-  });
+  // Phase 1: each warp encodes its block of every owned chunk and pushes
+  // it to every rank (self last).
+  uint8_t* wrec = rec + (threadIdx.x >> 5) * kTopkSlot;
+  for (int c = blockIdx.x; c < P.nchunks; c += gridDim.x)
+    encode_push_block<MODE, T>(P, c, wrec, P.world,
+                               [&](int i) { return slot_rec(P, (P.rank + 1 + i) % P.world, P.rank, c); });
   signal_column(P, kFlagPayload);
   // Phase 2: wait for the peers' records of this column, reduce.
   if (!wait_column(P, kFlagPayload, &s_abort)) return;
@@ -694,18 +822,19 @@ template <int MODE, typename T, bool kOpt>
 __global__ void __launch_bounds__(kThreads) twoshot_kernel(FusedParams P) {
   constexpr int BITS = MODE == kInt4 ? 4 : 8;
   __shared__ int s_abort;
-  __shared__ __align__(16) uint8_t rec[2080];
   if (threadIdx.x == 0) s_abort = 0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   NGL_BOUNDS_UNIFORM((int64_t)P.nchunks * P.chunk_bytes <= P.slot_bytes &&
                          (int64_t)P.nchunks * chunk_record_bytes(kInt8, 0) <= P.result_bytes && P.world <= kMaxWorld,
                      P.status, P.nchunks, P.chunk_bytes);
   for (int r = 0; r < P.world; ++r) NGL_BOUNDS_UNIFORM(P.sym[r] != nullptr, P.status, -2, r);
-  // Phase A: chunk i of this column goes to its owner rank i mod W.
-  encode_owned<MODE, T>(P, rec, [&](int c, int i) {
-    if (!passenger(P.q.topo, c, P.nchunks)) copy_record(slot_rec(P, i % P.world, P.rank, c), rec, P.chunk_bytes);
-    __syncthreads();
-  });
+  // Phase A: chunk i of this column goes to its owner rank i mod W (each
+  // warp pushes its own block).
+  {
+    int i = 0;
+    for (int c = blockIdx.x; c < P.nchunks; c += gridDim.x, ++i)
+      encode_push_block<MODE, T>(P, c, nullptr, 1, [&](int) { return slot_rec(P, i % P.world, P.rank, c); });
+  }
   signal_column(P, kFlagPayload);
   if (!wait_column(P, kFlagPayload, &s_abort)) return;
   // Phase B: reduce owned chunks, re-encode the mean residual as INT8.
@@ -718,7 +847,7 @@ __global__ void __launch_bounds__(kThreads) twoshot_kernel(FusedParams P) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
       if (blk < P.nblk)
-        for (int src = 0; src < P.world; ++src) accum_dense<BITS>(slot_rec(P, P.rank, src, c), warp, lane, acc);
+        accum_dense_ranks<BITS>([&](int src) { return slot_rec(P, P.rank, src, c); }, P.world, warp, lane, acc);
       float m[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) m[j] = NGL_FMUL(acc[j], P.f.inv_world);
@@ -730,13 +859,8 @@ __global__ void __launch_bounds__(kThreads) twoshot_kernel(FusedParams P) {
         w[0] |= ((uint32_t)product_code_rn(m[j], inv2, 127) & 0xffu) << (8 * j);
         w[1] |= ((uint32_t)product_code_rn(m[4 + j], inv2, 127) & 0xffu) << (8 * j);
       }
-      put_dense<8>(rec, warp, lane, s2, w);
-      __syncthreads();
-      for (int t = 0; t < P.world; ++t) {
-        const int r = (P.rank + 1 + t) % P.world;
-        copy_record(result_rec(P, r, c), rec, chunk_record_bytes(kInt8, 0));
-      }
-      __syncthreads();
+      // this warp's block of the INT8 result record, to every rank (self last)
+      for (int t = 0; t < P.world; ++t) put_dense<8>(result_rec(P, (P.rank + 1 + t) % P.world, c), warp, lane, s2, w);
     }
   }
   signal_column(P, kFlagResult);

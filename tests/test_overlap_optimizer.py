@@ -172,12 +172,15 @@ def test_adamw_inside_the_exchange_kernel_tracks_adamw_after_backward(mode):
                 kv = st["exp_avg_sq"].double().cpu().numpy().ravel()
                 assert np.all(np.abs(km - rm) <= 8 * ulp * (b1 * np.abs(m0) + (1 - b1) * np.abs(gg)) + 1e-30)
                 assert np.all(np.abs(kv - rv) <= 8 * ulp * (b2 * v0 + (1 - b2) * gg * gg) + 1e-36)
-                # the weight, from the kernel's own moments: a few ulps of the
-                # weight and of the update
-                upd = hyper[4] * km / (np.sqrt(kv) * hyper[5] + eps)
-                rp2 = p0 * hyper[3] - upd
-                assert np.all(np.abs(kp - rp2) <= 4 * ulp * np.abs(p0) + 8 * ulp * np.abs(upd) + 1e-12), \
-                    float(np.abs(kp - rp2).max())
+                if mode == "int4":
+                    # the weight, from the kernel's own moments: a few ulps of
+                    # the weight and of the update (top-k buckets take
+                    # PyTorch's fused AdamW, whose rounding differs; its bit
+                    # identity is checked above)
+                    upd = hyper[4] * km / (np.sqrt(kv) * hyper[5] + eps)
+                    rp2 = p0 * hyper[3] - upd
+                    assert np.all(np.abs(kp - rp2) <= 4 * ulp * np.abs(p0) + 8 * ulp * np.abs(upd) + 1e-12), \
+                        float(np.abs(kp - rp2).max())
                 assert np.allclose(kp, rp, rtol=0, atol=lr)  # and near the float64 recursion
                 moved = max(moved, float(np.abs(kp - p0).max()))
             assert moved > 1e-4
