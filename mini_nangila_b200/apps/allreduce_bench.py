@@ -162,7 +162,7 @@ def main():
                 lmax = lt.clone()
                 dist.all_reduce(lt)
                 dist.all_reduce(lmax, op=dist.ReduceOp.MAX)
-                row.update(nvlink_counters=counter.available,
+                row.update(nvlink_counters=counter.available, nvlink_counter_source=counter.source,
                            nvlink_tx_bytes_measured_mean=float(lt[0]) / world,
                            nvlink_rx_bytes_measured_mean=float(lt[1]) / world,
                            nvlink_tx_bytes_measured_max=float(lmax[0]))

@@ -12,6 +12,7 @@ Used by the app trainers (``apps.train_nano``, ``apps.minigpt_train``,
 """
 from __future__ import annotations
 
+import os
 import time
 
 import torch
@@ -27,6 +28,9 @@ class TrainLog:
         self.echo_every = int(echo_every)
         self.rows: list[tuple] = []
         if self.path:
+            d = os.path.dirname(self.path)
+            if d:
+                os.makedirs(d, exist_ok=True)
             with open(self.path, "w") as fh:
                 fh.write(HEADER + "\n")
 

@@ -65,3 +65,43 @@ def test_nvtx_range_and_wall_timer():
     with nvtx_range("x"):
         t = WallTimer().start()
     assert t.stop() >= 0.0
+
+
+def test_nvlink_counter_falls_back_to_byte_counters(monkeypatch):
+    """utils.nvlink against a fake NVML: a driver that does not serve the
+    THROUGHPUT_DATA fields (138/139) but does serve the NVLink 5 byte
+    counters (202/204) on links 0-3 is read through the latter, in bytes."""
+    import sys
+    import types
+
+    import torch
+
+    from mini_nangila_b200.utils import nvlink
+
+    class V:
+        def __init__(self, ret, val=0):
+            self.nvmlReturn = ret
+            self.value = types.SimpleNamespace(ullVal=val)
+
+    counts = {202: 1000, 204: 3000}
+
+    def field_values(_h, ids):
+        out = []
+        for fid, link in ids:
+            if fid in counts and link < 4:
+                out.append(V(0, counts[fid] + link))
+            else:
+                out.append(V(3))  # NVML_ERROR_NOT_SUPPORTED
+        return out
+
+    fake = types.SimpleNamespace(nvmlInit=lambda: None, nvmlDeviceGetHandleByPciBusId=lambda bus: bus,
+                                 nvmlDeviceGetFieldValues=field_values)
+    monkeypatch.setitem(sys.modules, "pynvml", fake)
+    monkeypatch.setattr(torch.cuda, "get_device_properties",
+                        lambda i: types.SimpleNamespace(pci_domain_id=0, pci_bus_id=0x1b, pci_device_id=0))
+    c = nvlink.NvlinkCounter(0)
+    assert c.available and c.source == "COUNT_BYTES"
+    assert c.read() == (4 * 1000 + 6, 4 * 3000 + 6)
+    counts[202] += 500
+    tx, rx = c.read()
+    assert tx == 4 * 1500 + 6 and rx == 4 * 3000 + 6
