@@ -396,12 +396,12 @@ __device__ __forceinline__ uint32_t count_ge3(const uint32_t (&m)[8], uint32_t c
 // the same way, until hi = lo + 1 or exactly keff patterns are >= lo.
 // This takes about 4-6 dependent warp sums on gradient blocks instead of
 // the ~14 of a bit-at-a-time search.
-__device__ __forceinline__ uint32_t topk_threshold_bits(const uint32_t (&m)[8], int keff) {
-  if (keff <= 0) return 0xffffffffu;  // nothing is >= it: no element kept
+__device__ __forceinline__ uint32_t topk_threshold_bits(const uint32_t (&m)[8], int keff, uint32_t& M) {
   uint32_t mx = 0;
 #pragma unroll
   for (int j = 0; j < 8; ++j) mx = max(mx, m[j]);
-  const uint32_t M = __reduce_max_sync(kFull, mx);
+  M = __reduce_max_sync(kFull, mx);
+  if (keff <= 0) return 0xffffffffu;  // nothing is >= it: no element kept
   uint32_t lo = 0, hi = M + 1;  // M <= 0x7fffffff
   bool first = true;
   while (hi - lo > 1) {
@@ -456,7 +456,8 @@ __device__ __forceinline__ TopkSel topk_select(const float (&c)[8], int valid, i
   uint32_t m[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) m[j] = __float_as_uint(fabsf(c[j]));
-  const uint32_t T = topk_threshold_bits(m, keff);
+  uint32_t M;  // largest |c| bit pattern of the block (NaN above inf)
+  const uint32_t T = topk_threshold_bits(m, keff, M);
   int gt = 0, eq = 0;
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
@@ -476,7 +477,9 @@ __device__ __forceinline__ TopkSel topk_select(const float (&c)[8], int valid, i
     sel |= (uint32_t)sj << j;
   }
   const int out_base = warp_excl_scan(__popc(sel), lane);
-  r.s = product_scale(block_absmax(c), 127.0f);
+  // the block's absmax is the largest pattern when no |c| is NaN (maxNum
+  // folds skip NaN, so a NaN block takes the full fold)
+  r.s = product_scale(M <= 0x7f800000u ? __uint_as_float(M) : block_absmax(c), 127.0f);
   const float inv = product_inv(r.s);
   for (int w = lane; w < rec_bytes / 4; w += 32) reinterpret_cast<uint32_t*>(rec)[w] = 0u;
   __syncwarp();

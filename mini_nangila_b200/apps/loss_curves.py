@@ -5,7 +5,10 @@
 
 Every setting starts from the same weights (seed 0) and sees the same
 batches (``data.MarkovTokens``: a learnable synthetic Markov stream over the
-GPT-2 vocabulary, keyed by (seed, rank, step)); the optimizer is AdamW at
+first ``--corpus-vocab`` token ids of the GPT-2 vocabulary, 2048 by default,
+so that a few hundred steps reach the chain's entropy instead of stopping
+on the plateau of a 50,257-token table; batches are keyed by (seed, rank,
+step)); the optimizer is AdamW at
 the workload's lr with a short linear warm-up, identical for all settings.
 Settings (``--settings``, comma-separated):
 
@@ -107,13 +110,15 @@ def main(argv=None):
     ap.add_argument("--seed", type=int, default=7)
     ap.add_argument("--out", default="loss_curves.json")
     ap.add_argument("--log-dir", default="")
+    ap.add_argument("--corpus-vocab", type=int, default=2048,
+                    help="tokens the Markov chain uses (ids below this; the model keeps its full vocabulary)")
     ap.add_argument("--tiny", action="store_true", help="tiny GPT-2 (tests)")
     a = ap.parse_args(argv)
     use_cuda = torch.cuda.is_available()
     rank, world, local = init_distributed("nccl" if use_cuda else "gloo")
     device = torch.device("cuda", local) if use_cuda else torch.device("cpu")
     cfg = GPT2Config.small() if not a.tiny else GPT2Config.tiny()
-    corpus = MarkovTokens(cfg.vocab_size, seed=a.seed)
+    corpus = MarkovTokens(min(a.corpus_vocab, cfg.vocab_size), seed=a.seed)
     curves = {}
     for name in [s for s in a.settings.split(",") if s]:
         if name not in SETTINGS:
@@ -121,7 +126,8 @@ def main(argv=None):
         curves[name] = run_setting(name, a, corpus, rank, world, device)
     if rank == 0:
         res = {"world": world, "steps": a.steps, "micro_batch": a.micro_batch, "seq": a.seq, "lr": a.lr,
-               "warmup": a.warmup, "data": "MarkovTokens(vocab 50257, 4 successors, seed %d)" % a.seed,
+               "warmup": a.warmup, "data": "MarkovTokens(%d tokens of the model's %d, 4 successors, seed %d)" % (
+                   corpus.vocab, cfg.vocab_size, a.seed),
                "entropy_floor_nats": corpus.entropy_nats, "summary": summarize(curves), "curves": curves}
         with open(a.out, "w") as fh:
             json.dump(res, fh)
