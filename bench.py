@@ -76,8 +76,9 @@ def parse():
     ap.add_argument("--inflight-ctas", type=int, default=0,
                     help="grid cap of exchange kernels that overlap backward (0: the whole grid)")
     ap.add_argument("--stream-priority", type=int, default=-1, help="hook stream priority (-1 high, 0 normal)")
-    ap.add_argument("--l2-keep-mb", type=float, default=48.0,
-                    help="predictor MB an exchange kernel keeps in L2 between its phases (0: no L2 policy)")
+    ap.add_argument("--l2-keep-mb", type=float, default=0.0,
+                    help="predictor MB an exchange kernel keeps in L2 between its phases (0: no L2 policy, the "
+                         "default: the kept lines cost the concurrent backward more than they save)")
     ap.add_argument("--no-arms", action="store_true", help="skip the same-box NCCL and same-model comparison arms")
     ap.add_argument("--timeline", default="", help="write one step's per-bucket device timeline (JSON) here")
     return ap.parse_args()

@@ -792,8 +792,10 @@ struct Smem {
   static constexpr int kAcc = MODE == kTopK ? kWarps * kBlock : 4;
 };
 
+// Top-k: 64 registers without spills (four CTAs per SM instead of three at
+// 80); the dense instances keep the compiler's choice.
 template <int MODE, typename T, bool kOpt>
-__global__ void __launch_bounds__(kThreads) oneshot_kernel(FusedParams P) {
+__global__ void __launch_bounds__(kThreads, MODE == kTopK ? 4 : 0) oneshot_kernel(FusedParams P) {
   __shared__ int s_abort;
   __shared__ __align__(16) uint8_t rec[Smem<MODE>::kRec];
   __shared__ __align__(16) uint8_t stage[Smem<MODE>::kStage];

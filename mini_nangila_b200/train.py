@@ -238,7 +238,13 @@ class DDPTrainer:
 
             comm = getattr(self.hook_state, "comm", None) if self.hook_state is not None else None
             self.monitor = RankMonitor(comms=[comm] if comm is not None else [])
-        use_fused = fused_optimizer and self.device.type == "cuda"
+        # PyTorch's fused AdamW on CUDA and on CPU.  On CPU it also keeps the
+        # ranks' parameters bit-identical: the unfused CPU step runs its
+        # square root through a vector-math library split over the intra-op
+        # threads, and one thread's share of a tensor has been seen to come
+        # out about 1e-4 off (relative) on one rank of two from identical
+        # inputs, while a single-threaded replay of the same step was exact.
+        use_fused = fused_optimizer and self.device.type in ("cuda", "cpu")
         self.opt = torch.optim.AdamW(self.ddp.parameters(), lr=lr, fused=use_fused)
         self.autocast_dtype = autocast_dtype if self.device.type == "cuda" else None
         self.bucket_opt = None
