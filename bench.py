@@ -208,7 +208,8 @@ def build_hook_on_reference_model(args, device, tiny: bool = False):
         opt.step()
         return loss.detach()
 
-    name = "fused-int4" + ("-ema" if momentum else "") + "-ef" + (f"-keep{topk:g}" if topk else "")
+    name = ("fused-topk" if topk else "fused-int4") + ("-ema" if momentum else "") + "-ef" + \
+        (f"-keep{topk:g}" if topk else "")
     return step, hs, name
 
 
