@@ -66,6 +66,8 @@ def parse():
     ap.add_argument("--seq", type=int, default=None)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
+    ap.add_argument("--clock-period-ms", type=int, default=200,
+                    help="nvidia-smi sampling period during the timed region")
     ap.add_argument("--max-ctas", type=int, default=0)
     ap.add_argument("--momentum", choices=["auto", "on", "off"], default="auto",
                     help="EMA predictor in the hook (auto: on for int4/int8, off for top-k, which uses error feedback)")
@@ -333,7 +335,7 @@ def main():
         for i in range(args.warmup):
             step_fn(*batches[i % len(batches)])
         barrier_sync(device)
-        sampler = (ClockSampler(visible_gpu_indices(world), period_ms=50).start()
+        sampler = (ClockSampler(visible_gpu_indices(world), period_ms=args.clock_period_ms).start()
                    if (rank == 0 and not args.no_clocks) else None)
         launches0 = trainer.kernel_launches() if trainer else 0
         barrier_sync(device)
