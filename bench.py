@@ -82,6 +82,8 @@ def parse():
                     help="predictor MB an exchange kernel keeps in L2 between its phases (0: no L2 policy, the "
                          "default: the kept lines cost the concurrent backward more than they save)")
     ap.add_argument("--no-arms", action="store_true", help="skip the same-box NCCL and same-model comparison arms")
+    ap.add_argument("--bucket-mb", type=float, default=25.0,
+                    help="DDP bucket cap in MB for every arm (GPT-2's workload fixes 25)")
     ap.add_argument("--timeline", default="", help="write one step's per-bucket device timeline (JSON) here")
     return ap.parse_args()
 
@@ -165,7 +167,7 @@ def build_reference(args, device, tiny: bool = False):
 
     model, autocast = build_hf_model(args, device, tiny)
     ddp = torch.nn.parallel.DistributedDataParallel(
-        model, device_ids=[device.index] if device.type == "cuda" else None, bucket_cap_mb=25)
+        model, device_ids=[device.index] if device.type == "cuda" else None, bucket_cap_mb=args.bucket_mb)
     topk = args.topk if args.mode == "topk" else 0.0
     momentum = args.momentum == "on" or (args.momentum == "auto" and args.mode != "topk")
     # Same call the reference's trainer makes (train_nano.py:133-143)
@@ -194,7 +196,7 @@ def build_hook_on_reference_model(args, device, tiny: bool = False):
 
     model, autocast = build_hf_model(args, device, tiny)
     ddp = torch.nn.parallel.DistributedDataParallel(
-        model, device_ids=[device.index] if device.type == "cuda" else None, bucket_cap_mb=25)
+        model, device_ids=[device.index] if device.type == "cuda" else None, bucket_cap_mb=args.bucket_mb)
     topk = args.topk if args.mode == "topk" else 0.0
     momentum = args.momentum == "on" or (args.momentum == "auto" and args.mode != "topk")
     hs = register_nangila_hook(ddp, beta=0.9, bits=4, stochastic=True, use_momentum=momentum, topk_percent=topk,
@@ -243,7 +245,7 @@ def comparison_arms(args, device, world: int, mb: int, seq: int, batches, mcfg) 
     # plain NCCL fp32: same model class, optimizer and DDP settings as the product arm
     with torch.device(device):
         model = GPT2(mcfg) if args.model == "gpt2" else Llama(mcfg).to(torch.bfloat16)
-    tr = DDPTrainer(model, lr=6e-4, hook="nccl", bucket_cap_mb=25.0,
+    tr = DDPTrainer(model, lr=6e-4, hook="nccl", bucket_cap_mb=args.bucket_mb,
                     autocast_dtype=torch.bfloat16 if args.model == "gpt2" else None, device=device)
     ms = time_steps(tr.step, batches, args.warmup, args.steps, device)
     out["nccl_fp32"] = {"value": tokens / (ms / 1000.0), "ms_per_step": ms / args.steps,
@@ -262,7 +264,7 @@ def comparison_arms(args, device, world: int, mb: int, seq: int, batches, mcfg) 
     out["hook_on_reference_model"] = {
         "value": tokens / (ms / 1000.0), "ms_per_step": ms / args.steps, "hook": name,
         "model": "transformers " + ("GPT2LMHeadModel" if args.model == "gpt2" else "LlamaForCausalLM"),
-        "optimizer": "AdamW (foreach) after backward", "ddp": "default arguments, bucket_cap_mb 25"}
+        "optimizer": "AdamW (foreach) after backward", "ddp": f"default arguments, bucket_cap_mb {args.bucket_mb:g}"}
     if hs is not None and getattr(hs, "comm", None) is not None:
         hs.comm.close()
     del step, hs
@@ -320,7 +322,7 @@ def main():
                 hk.update(inflight_ctas=args.inflight_ctas, stream_priority=args.stream_priority,
                           l2_keep_mb=args.l2_keep_mb)
         overlap = args.hook == "fused" and args.overlap_opt == "on"
-        trainer = DDPTrainer(model, lr=6e-4, hook=args.hook, hook_kwargs=hk, bucket_cap_mb=25.0,
+        trainer = DDPTrainer(model, lr=6e-4, hook=args.hook, hook_kwargs=hk, bucket_cap_mb=args.bucket_mb,
                              autocast_dtype=torch.bfloat16 if args.model == "gpt2" else None, device=device,
                              overlap_optimizer=overlap, optimizer_in_kernel=args.opt_in_kernel == "on")
         step_fn = trainer.step
@@ -442,7 +444,7 @@ def main():
                 "seq_len": seq,
                 "parallelism": f"dp{world}",
                 "hook": hook_name,
-                "bucket_mb": 25,
+                "bucket_mb": args.bucket_mb,
                 "optimizer": "AdamW lr 6e-4",
                 "precision": "fp32 master weights, bf16 autocast" if args.model == "gpt2" else "bf16",
                 "l2": "no flush: each step reads/writes ~2 GB of weights, grads and optimizer state (> 126 MB L2)",

@@ -28,7 +28,7 @@ def test_reference_arm_steps(model, mode, name):
     dist.init_process_group("gloo", rank=0, world_size=1)
     saved_path = list(sys.path)
     try:
-        args = types.SimpleNamespace(model=model, mode=mode, topk=0.05, momentum="auto")
+        args = types.SimpleNamespace(model=model, mode=mode, topk=0.05, momentum="auto", bucket_mb=25.0)
         step, why, hook_name = bench.build_reference(args, torch.device("cpu"), tiny=True)
         assert why is None and hook_name == name
         g = torch.Generator().manual_seed(0)
@@ -56,7 +56,7 @@ def test_hook_on_reference_model_arm_steps():
     s.close()
     dist.init_process_group("gloo", rank=0, world_size=1)
     try:
-        args = types.SimpleNamespace(model="gpt2", mode="int4", topk=0.05, momentum="auto", variant="auto")
+        args = types.SimpleNamespace(model="gpt2", mode="int4", topk=0.05, momentum="auto", variant="auto", bucket_mb=25.0)
         step, hs, name = bench.build_hook_on_reference_model(args, torch.device("cpu"), tiny=True)
         assert name == "fused-int4-ema-ef"
         g = torch.Generator().manual_seed(0)
