@@ -18,7 +18,10 @@ def test_bench_prints_one_contract_line():
 
     if not torch.cuda.is_available():
         pytest.skip("needs a GPU")
-    env = dict(os.environ, MASTER_ADDR="127.0.0.1")
+    # a single rank of its own: no rendezvous variables left by earlier tests
+    env = {k: v for k, v in os.environ.items()
+           if k not in ("MASTER_PORT", "RANK", "WORLD_SIZE", "LOCAL_RANK", "LOCAL_WORLD_SIZE")}
+    env["MASTER_ADDR"] = "127.0.0.1"
     r = subprocess.run([sys.executable, "bench.py", "--steps", "10", "--warmup", "3", "--no-arms"], cwd=ROOT,
                        env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stderr[-2000:]
