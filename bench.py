@@ -66,8 +66,8 @@ def parse():
     ap.add_argument("--seq", type=int, default=None)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
-    ap.add_argument("--clock-period-ms", type=int, default=200,
-                    help="nvidia-smi sampling period during the timed region")
+    ap.add_argument("--clock-period-ms", type=int, default=100,
+                    help="nvidia-smi sampling period (the samples of the timed region are kept)")
     ap.add_argument("--max-ctas", type=int, default=0)
     ap.add_argument("--momentum", choices=["auto", "on", "off"], default="auto",
                     help="EMA predictor in the hook (auto: on for int4/int8, off for top-k, which uses error feedback)")
@@ -334,19 +334,26 @@ def main():
 
     batches = make_batches(vocab, mb, seq, 4, 1000 + rank, device)
     with quiet:
+        # nvidia-smi runs from before the warm-up, so that it is already
+        # printing samples when the timed region starts; only the samples
+        # of the timed region (begin / end) enter the clock record
+        sampler = (ClockSampler(visible_gpu_indices(world), period_ms=args.clock_period_ms).start()
+                   if (rank == 0 and not args.no_clocks) else None)
         for i in range(args.warmup):
             step_fn(*batches[i % len(batches)])
         barrier_sync(device)
-        sampler = (ClockSampler(visible_gpu_indices(world), period_ms=args.clock_period_ms).start()
-                   if (rank == 0 and not args.no_clocks) else None)
         launches0 = trainer.kernel_launches() if trainer else 0
         barrier_sync(device)
+        if sampler:
+            sampler.begin()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
         for i in range(args.steps):
             step_fn(*batches[i % len(batches)])
         e.record()
         barrier_sync(device)
+        if sampler:
+            sampler.end()
         ms_local = s.elapsed_time(e)
         launches = (trainer.kernel_launches() - launches0) if trainer else 0
         clocks = sampler.stop() if sampler else None

@@ -22,11 +22,36 @@ REASON_KEYS = {
 
 
 class ClockSampler:
+    """``nvidia-smi -lms`` in the background.  ``begin()`` / ``end()`` mark
+    the timed region: the statistics of ``stop()`` come from the samples
+    written between the marks (or, for a region shorter than the period,
+    the samples on either side of it), so the sampler can be started before
+    the warm-up steps and be producing samples when the region starts
+    (``nvidia-smi`` takes a noticeable time to print its first sample on a
+    multi-GPU query).  Without marks, every sample counts."""
+
     def __init__(self, gpus: list[int] | None = None, period_ms: int = 200):
         self.gpus = gpus
         self.period_ms = period_ms
         self.proc = None
         self.path = None
+        self._marks: list[int] = []
+
+    def _lines(self) -> int:
+        try:
+            with open(self.path) as fh:
+                return sum(1 for line in fh if line.endswith("\n"))
+        except (OSError, TypeError):
+            return 0
+
+    def begin(self) -> None:
+        """Mark the start of the timed region."""
+        self._marks = [self._lines()]
+
+    def end(self) -> None:
+        """Mark the end of the timed region."""
+        if self._marks:
+            self._marks = self._marks[:1] + [self._lines()]
 
     def start(self) -> "ClockSampler":
         fd, self.path = tempfile.mkstemp(prefix="ngl_clocks_", suffix=".csv")
@@ -52,13 +77,19 @@ class ClockSampler:
         out = {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
         if not self.path or not os.path.exists(self.path):
             return out
-        rows = []
         with open(self.path) as fh:
-            for line in fh:
-                parts = [p.strip() for p in line.split(",")]
-                if len(parts) == len(FIELDS):
-                    rows.append(dict(zip(FIELDS, parts)))
+            lines = [line for line in fh if line.endswith("\n")]
         os.unlink(self.path)
+        if len(self._marks) == 2:
+            # the timed region's lines (the marks count complete lines), or
+            # the samples just before and after a region shorter than the period
+            a, b = self._marks
+            lines = lines[a:b] or lines[max(0, a - 1): b + 1] or lines
+        rows = []
+        for line in lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) == len(FIELDS):
+                rows.append(dict(zip(FIELDS, parts)))
         if not rows:
             return out
         def num(x):

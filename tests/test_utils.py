@@ -105,3 +105,45 @@ def test_nvlink_counter_falls_back_to_byte_counters(monkeypatch):
     counts[202] += 500
     tx, rx = c.read()
     assert tx == 4 * 1500 + 6 and rx == 4 * 3000 + 6
+
+
+def test_clock_sampler_keeps_the_marked_region(tmp_path, monkeypatch):
+    """Samples written before begin() and after end() are left out; a region
+    that saw no sample of its own takes the samples on either side."""
+    fake = tmp_path / "nvidia-smi"
+    warm = "0, 900, 1965, 300.0, 0x0, Not Active, Not Active, Not Active, Not Active"
+    hot = "0, 1800, 1965, 990.0, 0x4, Not Active, Not Active, Not Active, Active"
+    cool = "0, 345, 1965, 95.0, 0x0, Not Active, Not Active, Not Active, Not Active"
+    gate = tmp_path / "go"
+    # two samples at once, then one per file that appears under tmp_path
+    script = "#!/bin/sh\n" + f"echo '{warm}'\necho '{warm}'\n"
+    script += f"while [ ! -e {gate}1 ]; do sleep 0.02; done\necho '{hot}'\necho '{hot}'\n"
+    script += f"while [ ! -e {gate}2 ]; do sleep 0.02; done\necho '{cool}'\nexec sleep 30\n"
+    fake.write_text(script)
+    fake.chmod(0o755)
+    monkeypatch.setenv("PATH", f"{tmp_path}:{os.environ['PATH']}")
+
+    def wait_lines(s, n):
+        t0 = time.time()
+        while s._lines() < n and time.time() - t0 < 10:
+            time.sleep(0.02)
+
+    s = ClockSampler([0], period_ms=50).start()
+    wait_lines(s, 2)
+    s.begin()
+    (tmp_path / "go1").write_text("")
+    wait_lines(s, 4)
+    s.end()
+    (tmp_path / "go2").write_text("")
+    wait_lines(s, 5)
+    out = s.stop()
+    assert out["samples"] == 2 and out["sm_mhz"] == 1800.0 and out["reasons"] == ["sw_power_cap"]
+
+    (tmp_path / "go1").unlink()
+    (tmp_path / "go2").unlink()
+    s = ClockSampler([0], period_ms=50).start()
+    wait_lines(s, 2)
+    s.begin()
+    s.end()  # nothing written in between
+    out = s.stop()
+    assert out["samples"] == 1 and out["sm_mhz"] == 900.0
